@@ -1,0 +1,277 @@
+"""B200 drop-in for the FFN half of the reference's ``engine.py``.
+
+* :class:`HotNeurons` -- one layer's hot FP8 neurons (the reference's hot file,
+  splitter.py:221-226 / engine.py:251-264) re-laid out once at load into the
+  kernel layout [n_hot][gate row | up row | down column] (12 KiB per neuron).
+* :class:`FFNStack` -- L layers of SparseFFNLayer.forward (engine.py:292-312)
+  with the predictor lookahead of DesdemonaEngine.forward (engine.py:421-438),
+  run by one persistent cooperative kernel per token (``hc_ffn_stack``) plus
+  the two predictor launches for layer 0's fetch set.
+* :class:`SparseFFNLayer` -- the reference's per-layer module (same
+  constructor) on the fused kernel.
+* :func:`sparse_ffn` -- the reference's function signature (engine.py:173-209)
+  for callers that already hold dense tensors.  It runs on CUDA tensors only.
+"""
+from __future__ import annotations
+
+from pathlib import Path
+from typing import Optional, Sequence
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+import hc_native as N
+from predictor import NeuronPredictor, PredictorRegistry, logit_threshold, unpack_mask
+from splitter import HIDDEN_DIM, ColdWeightStore, bits_to_words
+
+
+# ─── Hot neurons ──────────────────────────────────────────────────────────────
+class HotNeurons:
+    """Hot FP8 neurons of one layer in the fused kernel's layout."""
+
+    def __init__(self, neuron_ids: torch.Tensor, gate: torch.Tensor, up: torch.Tensor, down: torch.Tensor,
+                 scales: Optional[torch.Tensor] = None, device="cuda"):
+        """gate/up: [n, H] float8_e4m3fn; down: [H, n] float8_e4m3fn (the
+        reference's layouts); scales: optional fp32 [n, 3] per-neuron scales
+        of (gate, up, down) -- absent means the reference's direct cast."""
+        self.device = torch.device(device)
+        self.ids = neuron_ids.to(torch.int64).cpu()
+        n = int(self.ids.numel())
+        self.n = n
+        as_u8 = lambda t: t.view(torch.uint8) if t.dtype == torch.float8_e4m3fn else t.to(torch.float8_e4m3fn).view(torch.uint8)
+        g, u, d = (as_u8(t.to(self.device)) for t in (gate, up, down))
+        if g.shape != (n, HIDDEN_DIM) or u.shape != (n, HIDDEN_DIM) or d.shape != (HIDDEN_DIM, n):
+            raise ValueError("hot tensors must be gate/up [n, H] and down [H, n]")
+        self.packed = torch.stack([g, u, d.t()], dim=1).contiguous() if n else \
+            torch.zeros(1, 3, HIDDEN_DIM, dtype=torch.uint8, device=self.device)
+        self.scales = scales.to(self.device, torch.float32).contiguous() if scales is not None else None
+
+    @classmethod
+    def from_file(cls, path: str, device="cuda") -> "HotNeurons":
+        """Load ``hot_weights/layer_XXX_expert_000.pt`` (splitter.py:221-226)."""
+        w = torch.load(str(path), map_location="cpu")
+        return cls(w["neuron_ids"], w["gate"], w["up"], w["down"], w.get("scales"), device)
+
+    def decoded(self):
+        """fp32 (gate [n,H], up [n,H], down [H,n]) with scales applied."""
+        f = self.packed.view(torch.float8_e4m3fn).float()[: self.n]
+        if self.scales is not None:
+            f = f * self.scales[:, :, None]
+        return f[:, 0], f[:, 1], f[:, 2].t()
+
+
+# ─── Fused L-layer stack ──────────────────────────────────────────────────────
+class FFNStack:
+    """L layers of the hot/cold sparse FFN on one GPU, batch 1.
+
+    forward(x) computes, for l = 0..L-1, x <- x + sparse_ffn(RMSNorm_l(x))
+    with layer l's cold neurons = predictor_l(RMSNorm_l(x_{l-1})) & fetchable
+    (x_{-1} = x_0: the engine's lookahead, engine.py:421-438).  A layer
+    without a predictor fetches every cold neuron (engine.py:282-283).
+    """
+
+    def __init__(self, store: ColdWeightStore, hot: Sequence[HotNeurons], norms: Sequence[Optional[torch.Tensor]],
+                 predictors: Sequence[Optional[NeuronPredictor]], activation: str = "silu",
+                 act_on_both: bool = False, eps: float = 1e-5, threshold: float = 0.5,
+                 layer_ids: Optional[Sequence[int]] = None, grid: int = 0, inter: Optional[int] = None):
+        self.store = store
+        self.device = store.device
+        self.L = len(hot)
+        self.layer_ids = list(layer_ids) if layer_ids is not None else list(range(self.L))
+        self.inter = int(inter or store.I)
+        if self.inter % 4:
+            raise ValueError("the fused kernel needs intermediate_dim % 4 == 0")
+        self.words = (self.inter + 31) // 32
+        self.hot = list(hot)
+        self.norms = [n.to(self.device, torch.float32).contiguous() if n is not None else None for n in norms]
+        self.predictors = list(predictors)
+        self.act = N.HC_ACT_RELU if activation == "relu" else N.HC_ACT_SILU
+        self.act_on_both = bool(act_on_both)
+        self.eps = float(eps)
+        self.threshold = float(threshold)
+        self.thr = logit_threshold(self.threshold)
+        self.fetch = torch.stack([store.fetch_bits(li, h.ids, self.inter) for li, h in zip(self.layer_ids, self.hot)])
+        descs, self._keep = [], []
+        for l in range(self.L):
+            li = self.layer_ids[l]
+            p = self.predictors[l]
+            wdt = p.down_t() if p is not None else None
+            rec = store.section_records(li)
+            self._keep += [rec, wdt]
+            descs.append(N.LayerDesc(
+                hot=N.ptr(self.hot[l].packed), hot_scale=N.ptr(self.hot[l].scales), norm_w=N.ptr(self.norms[l]),
+                cold_records=N.ptr(rec), table=N.ptr(store.table[li]), fetch_bits=N.ptr(self.fetch[l]),
+                pred_w_down_t=N.ptr(wdt), pred_w_up=N.ptr(p.up.weight.data) if p is not None else None,
+                pred_b_up=N.ptr(p.up.bias.data) if p is not None else None,
+                n_hot=self.hot[l].n, n_records=int(store.n_rec_host[li]), inter=self.inter,
+                rank=p.rank if p is not None else 0))
+        self.desc_dev = N.layer_desc_array(descs, self.device)
+        self.grid = int(grid) if grid else int(N.lib.hc_ffn_stack_grid())
+        self.ws = torch.zeros(int(N.lib.hc_ffn_stack_workspace_bytes(self.grid, self.inter)), dtype=torch.uint8,
+                              device=self.device)
+        self.masks = torch.zeros(self.L, self.words, dtype=torch.int32, device=self.device)
+        self.status = N.new_status(self.device)
+        self.x_out = torch.empty(HIDDEN_DIM, dtype=torch.float32, device=self.device)
+        ones = torch.ones(self.inter, dtype=torch.bool)
+        self._all_ones = bits_to_words(ones.numpy(), self.inter).to(self.device)
+
+    def first_mask(self, x: torch.Tensor):
+        """Layer 0's predicted set from RMSNorm_0(x) (engine.py:422), on device."""
+        p0 = self.predictors[0]
+        if p0 is None:
+            self.masks[0].copy_(self._all_ones)
+        else:
+            p0.predict_words(x.view(1, -1), self.threshold, norm_w=self.norms[0], eps=self.eps,
+                             mask_out=self.masks[0:1])
+
+    def launch(self, x: torch.Tensor, masks_given: bool = False, x_hist: Optional[torch.Tensor] = None,
+               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        out = self.x_out if out is None else out
+        N.check(N.lib.hc_ffn_stack(N.ptr(self.desc_dev), self.L, self.inter, N.ptr(x), N.ptr(self.masks),
+                                   1 if masks_given else 0, N.ptr(out), N.ptr(x_hist), self.eps, self.act,
+                                   1 if self.act_on_both else 0, self.thr, self.grid, N.ptr(self.ws),
+                                   N.ptr(self.status), N.stream_handle()), "hc_ffn_stack")
+        return out
+
+    def forward(self, x: torch.Tensor, masks: Optional[torch.Tensor] = None, x_hist: Optional[torch.Tensor] = None,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """x: fp32 [H] on the device.  ``masks`` (int32 words [L, W]) forces
+        the fetch set of every layer instead of running the predictors."""
+        N.require_cuda(x)
+        x = x.to(torch.float32).contiguous().view(-1)
+        if masks is not None:
+            self.masks.copy_(masks)
+            return self.launch(x, True, x_hist, out)
+        self.first_mask(x)
+        return self.launch(x, False, x_hist, out)
+
+    __call__ = forward
+
+    def decode_host(self, x_host: torch.Tensor, y_host: torch.Tensor) -> torch.Tensor:
+        """Decode T tokens given in host memory: x_host [T, H] fp32 (pinned for
+        an asynchronous copy) -> y_host [T, H].  One host-to-device copy of the
+        inputs, T fused forwards, one device-to-host copy of the outputs, all
+        on the current stream; returns without synchronising."""
+        T = x_host.shape[0]
+        if getattr(self, "_io_in", None) is None or self._io_in.shape[0] < T:
+            self._io_in = torch.empty(T, HIDDEN_DIM, dtype=torch.float32, device=self.device)
+            self._io_out = torch.empty(T, HIDDEN_DIM, dtype=torch.float32, device=self.device)
+        xi, yo = self._io_in[:T], self._io_out[:T]
+        xi.copy_(x_host, non_blocking=True)
+        for t in range(T):
+            self.first_mask(xi[t])
+            self.launch(xi[t], False, None, yo[t])
+        y_host.copy_(yo, non_blocking=True)
+        return y_host
+
+    def check(self):
+        N.read_status(self.status, "hc_ffn_stack")
+
+    def active_counts(self) -> torch.Tensor:
+        """Active cold neurons per layer of the last forward (device)."""
+        m = (self.masks & self.fetch).to(torch.int64) & 0xFFFFFFFF
+        return torch.stack([torch.tensor([bin(int(v)).count("1") for v in row.tolist()]).sum() for row in m.cpu()])
+
+
+# ─── Reference-compatible pieces ─────────────────────────────────────────────
+def _gated_act(g, u, activation: str, act_on_both: bool):
+    act = F.relu if activation == "relu" else F.silu
+    return act(g) * act(u) if act_on_both else act(g) * u
+
+
+def sparse_ffn(x, activation, act_on_both, gate_hot, up_hot, down_hot, gate_cold, up_cold, down_cold):
+    """engine.py:173-209 for callers holding dense tensors (CUDA only).
+
+    The hot half runs in x's dtype and the cold half in fp32, cast back, as
+    the reference does.  The fused FP8/INT4 kernel path is :class:`FFNStack`
+    / :class:`SparseFFNLayer`, which never materialises dense cold weights."""
+    N.require_cuda(x)
+    results = []
+    if gate_hot is not None and gate_hot.shape[0] > 0:
+        g = F.linear(x, gate_hot)
+        u = F.linear(x, up_hot)
+        results.append(F.linear(_gated_act(g, u, activation, act_on_both), down_hot))
+    if gate_cold is not None and gate_cold.shape[0] > 0:
+        xf = x.float()
+        g = F.linear(xf, gate_cold)
+        u = F.linear(xf, up_cold)
+        results.append(F.linear(_gated_act(g, u, activation, act_on_both), down_cold).to(x.dtype))
+    if not results:
+        return torch.zeros_like(x)
+    return sum(results)
+
+
+class SparseFFNLayer(nn.Module):
+    """The reference's SparseFFNLayer (engine.py:212-312) on the fused kernel.
+
+    ``submit_cold_fetch`` returns the device mask words of the predicted set
+    (no host sync, no thread pool); ``forward`` runs RMSNorm + hot + cold +
+    residual in one launch per token row."""
+
+    _EID = 0
+
+    def __init__(self, layer_idx: int, hot_dir: str, cold_store: ColdWeightStore,
+                 predictor: Optional[PredictorRegistry], cfg: dict, device, executor=None,
+                 ffn_norm_weight: Optional[torch.Tensor] = None):
+        super().__init__()
+        self.layer_idx = layer_idx
+        self.cold_store = cold_store
+        self.predictor = predictor
+        self.device = torch.device(device)
+        self.executor = executor
+        self.activation = cfg.get("hidden_act", "silu")
+        self.act_on_both = cfg.get("act_on_both", False)
+        self.inter_dim = cfg["intermediate_dim"]
+        self.eps = cfg["rms_norm_eps"]
+        self.input_layernorm = nn.RMSNorm(cfg["hidden_dim"], eps=self.eps)
+        if ffn_norm_weight is not None:
+            self.input_layernorm.weight = nn.Parameter(ffn_norm_weight.to(self.device))
+        self.input_layernorm.to(self.device)
+        p = Path(hot_dir) / f"layer_{layer_idx:03d}_expert_{self._EID:03d}.pt"
+        if p.exists():
+            self.hot = HotNeurons.from_file(str(p), self.device)
+        else:
+            z8 = torch.zeros(0, HIDDEN_DIM, dtype=torch.float8_e4m3fn)
+            self.hot = HotNeurons(torch.zeros(0, dtype=torch.int64), z8, z8, z8.t(), None, self.device)
+        self._hot_id_set = set(self.hot.ids.tolist())
+        self._pred = predictor.get(layer_idx, self._EID) if predictor is not None else None
+        self._norm32 = self.input_layernorm.weight.detach().to(torch.float32).contiguous()
+        self._stack = FFNStack(cold_store, [self.hot], [self._norm32], [self._pred], self.activation,
+                               self.act_on_both, self.eps, layer_ids=[layer_idx], inter=self.inter_dim)
+
+    def _query(self, x_normed: torch.Tensor) -> torch.Tensor:
+        return x_normed[:, -1, :].mean(0, keepdim=True)          # engine.py:277
+
+    def _mask_words(self, x: torch.Tensor) -> torch.Tensor:
+        """Predicted-set words for input x [B, T, H] (not yet normalised)."""
+        if self._pred is None:
+            return self._stack._all_ones.view(1, -1).clone()
+        if x.shape[0] == 1:
+            row = x[0, -1:, :].to(torch.float32).contiguous()
+            return self._pred.predict_words(row, 0.5, norm_w=self._norm32, eps=self.eps)
+        with torch.no_grad():
+            q = self._query(self.input_layernorm(x.to(self._norm32.dtype)))
+        return self._pred.predict_words(q.to(torch.float32), 0.5)
+
+    def _cold_ids_for(self, x_normed: torch.Tensor) -> list[int]:
+        """engine.py:274-283: host list of the cold ids to fetch."""
+        if self._pred is not None:
+            mask = self.predictor.predict(self.layer_idx, self._EID, self._query(x_normed))
+            ids = mask[0].nonzero(as_tuple=True)[0].tolist()
+            return [i for i in ids if i not in self._hot_id_set]
+        return [i for i in range(self.inter_dim) if i not in self._hot_id_set]
+
+    def submit_cold_fetch(self, x: torch.Tensor):
+        """The lookahead prefetch (engine.py:285-290): device mask words."""
+        return self._mask_words(x)
+
+    def forward(self, x: torch.Tensor, prefetch_future=None) -> torch.Tensor:
+        B, T, H = x.shape
+        words = prefetch_future if prefetch_future is not None else self._mask_words(x)
+        self._stack.masks.copy_(words.view(1, -1))
+        rows = x.reshape(B * T, H).to(torch.float32).contiguous()
+        out = torch.empty_like(rows)
+        for r in range(rows.shape[0]):
+            self._stack.launch(rows[r], masks_given=True, out=out[r])
+        return out.reshape(B, T, H).to(x.dtype)

@@ -1,0 +1,228 @@
+/*
+ * hotcold.h -- C ABI of the B200 (sm_100a) hot/cold sparse-FFN library
+ * (libhotcold.so).
+ *
+ * The reference (Hot-Cold-Neural-Split-OpenInfer2) is pure Python; these entry
+ * points replace the Python/torch functions on its per-token FFN path.  Each
+ * declaration names the reference function it stands in for (file:line).
+ *
+ * Conventions
+ *  - Every pointer argument is a DEVICE pointer unless its comment says host.
+ *  - Functions are asynchronous on `stream` and return an HC_* status for
+ *    argument / launch errors.  Errors found by a kernel (an index out of
+ *    range, a bounded wait that expired) are OR-ed into the caller's device
+ *    word `status` (HC_ERR_* bits); read it after synchronising.
+ *  - Nothing allocates: scratch space is a caller-owned workspace whose size
+ *    comes from the matching *_workspace_bytes query and which must be zeroed
+ *    once after allocation (kernels leave it re-usable).
+ *  - Thread safety: calls are independent as long as they do not share a
+ *    workspace or a status word while in flight.
+ *  - Cold records are read in the reference's on-disk layout
+ *    (splitter.py:23-37): the image of cold_weights.bin is uploaded unchanged.
+ */
+#ifndef HOTCOLD_H
+#define HOTCOLD_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* hc_stream_t; /* == cudaStream_t */
+
+#if defined(__GNUC__)
+#define HC_API __attribute__((visibility("default")))
+#else
+#define HC_API
+#endif
+
+/* ---- status codes (return values and device status bits) ---------------- */
+#define HC_OK 0
+#define HC_ERR_ARG 1         /* bad argument, detected on the host            */
+#define HC_ERR_CUDA 2        /* a CUDA runtime call failed                    */
+#define HC_ERR_RANGE 4       /* device: an index pointed outside its table    */
+#define HC_ERR_TIMEOUT 8     /* device: a bounded wait expired                */
+#define HC_ERR_UNSUPPORTED 16 /* shape or mode this build does not handle    */
+
+/* ---- dtypes ------------------------------------------------------------- */
+#define HC_F32 0
+#define HC_BF16 1
+#define HC_F16 2
+
+/* ---- activations (engine.py:163-170) ------------------------------------ */
+#define HC_ACT_SILU 0
+#define HC_ACT_RELU 1
+
+/* Library identity / device checks.  hc_version returns HC_ABI_VERSION. */
+#define HC_ABI_VERSION 1
+HC_API int hc_version(void);
+HC_API const char* hc_status_string(int status);
+/* Number of SMs of the current device, or -1 when no CUDA device is usable. */
+HC_API int hc_device_sm_count(void);
+
+/* ======================================================================= */
+/* Cold store                                                              */
+/* ======================================================================= */
+
+/*
+ * hc_build_record_table -- replaces ColdWeightStore._section_offsets
+ * (splitter.py:332-352): scans each layer's section once and records, for
+ * every u16 neuron id, its record index (-1 when absent; a later duplicate
+ * wins, like the reference's dict).
+ *   cold_base        image of cold_weights.bin (device or mapped pinned host)
+ *   image_bytes      host: size of that image; records reaching past it are
+ *                    left out of the table and flag HC_ERR_RANGE
+ *   section_offsets  [n_layers] byte offset of each section header (device);
+ *                    must be a multiple of 16 (the reference page-aligns them)
+ *   n_records        [n_layers] n_cold of each section (device)
+ *   max_records      host: upper bound of n_records (grid size)
+ *   table            [n_layers][65536] int32 output (device)
+ *   status           device status word (may be NULL)
+ */
+HC_API int hc_build_record_table(const void* cold_base, int64_t image_bytes, const int64_t* section_offsets,
+                          const int32_t* n_records, int32_t n_layers, int32_t max_records,
+                          int32_t* table, int32_t* status, hc_stream_t stream);
+
+/*
+ * hc_map_ids -- the id handling of ColdWeightStore.read_neurons
+ * (splitter.py:365-372): maps requested neuron ids to record indices in
+ * request order, dropping ids that have no record.
+ *   ids [n] int64 requested ids; table [65536] of the layer;
+ *   rec_out [n] int32 record indices (first *count entries valid);
+ *   nid_out [n] int32 kept ids (may be NULL); count [1] int32 output.
+ * Single CTA; n <= 1<<20.
+ */
+HC_API int hc_map_ids(const int64_t* ids, int32_t n, const int32_t* table, int32_t* rec_out,
+               int32_t* nid_out, int32_t* count, hc_stream_t stream);
+
+/*
+ * hc_cold_gather_dequant -- replaces the per-neuron loop of
+ * ColdWeightStore.read_neurons + dequantize_int4 (splitter.py:354-403,
+ * :111-124).  For each layer j and each of K record indices, decodes the
+ * record's gate / up / down INT4 vectors with their fp16 group scales into
+ * neuron-major rows: out[j][k][0:4096] = q * s (exact in fp32; bf16 is the
+ * round-to-nearest-even of that fp32 value).
+ *   cold_base, image_bytes, section_offsets[n_layers], n_records[n_layers]:
+ *              as above (records reaching past image_bytes flag HC_ERR_RANGE)
+ *   rec_idx    [n_layers][K] int32; an index outside [0, n_records) sets
+ *              HC_ERR_RANGE and writes zeros for that row
+ *   count      optional [n_layers] int32 (NULL = K): rows k >= count[j] are
+ *              left untouched (lets the caller pass a device-side count)
+ *   out_dtype  HC_F32 or HC_BF16; gate/up/down_out [n_layers][K][4096]
+ */
+HC_API int hc_cold_gather_dequant(const void* cold_base, int64_t image_bytes, const int64_t* section_offsets,
+                           const int32_t* n_records, int32_t n_layers, const int32_t* rec_idx,
+                           int32_t K, const int32_t* count, int32_t out_dtype, void* gate_out,
+                           void* up_out, void* down_out, int32_t* status, hc_stream_t stream);
+
+/* ======================================================================= */
+/* Predictor                                                               */
+/* ======================================================================= */
+
+/*
+ * hc_predictor_workspace_bytes -- scratch for hc_predictor_forward.
+ */
+HC_API int64_t hc_predictor_workspace_bytes(int32_t batch, int32_t rank, int32_t inter);
+
+/*
+ * hc_predictor_forward -- replaces NeuronPredictor.forward / predict_mask
+ * (predictor.py:70-79), PredictorRegistry.predict (predictor.py:435-456) and
+ * the id selection of SparseFFNLayer._cold_ids_for (engine.py:274-283).
+ *   x        [batch][4096] fp32 predictor input
+ *   norm_w   optional [4096] fp32: when given, each row is first RMS-normalised
+ *            (x * rsqrt(mean(x^2) + eps) * norm_w), as SparseFFNLayer does
+ *            before querying the predictor (engine.py:289); NULL = x as is
+ *   w_down   [rank][4096] fp32   (nn.Linear weight of `down`)
+ *   w_up     [inter][rank] fp32  (nn.Linear weight of `up`), b_up [inter]
+ *   logit_threshold  mask bit = (logit >= logit_threshold); the host picks the
+ *            smallest fp32 logit whose torch.sigmoid reaches the probability
+ *            threshold, so the decision equals `sigmoid(logit) >= threshold`
+ *   mask_out [batch][ceil(inter/32)] uint32 bit masks (required)
+ *   probs_out / logits_out  optional [batch][inter] fp32 (NULL to skip)
+ *   fetch_bits optional [ceil(inter/32)] uint32: ids eligible for the cold
+ *            fetch (a record exists and the id is not hot); when given, row 0's
+ *            mask & fetch_bits is compacted in ascending id order into
+ *            ids_out [inter] int32 (+ rec_out via `table`, may be NULL) with
+ *            the number in count_out[0]
+ *   workspace  hc_predictor_workspace_bytes(batch, rank, inter) bytes, zeroed once
+ * Limits: rank <= 128, inter <= 65536, batch <= 64.
+ */
+HC_API int hc_predictor_forward(const float* x, int32_t batch, const float* norm_w, float eps,
+                                const float* w_down, const float* w_up,
+                         const float* b_up, int32_t rank, int32_t inter, float logit_threshold,
+                         uint32_t* mask_out, float* probs_out, float* logits_out,
+                         const uint32_t* fetch_bits, const int32_t* table, int32_t* ids_out,
+                         int32_t* rec_out, int32_t* count_out, void* workspace, int32_t* status,
+                         hc_stream_t stream);
+
+/* ======================================================================= */
+/* Fused sparse FFN (hot FP8 + cold INT4), one layer or a stack of layers  */
+/* ======================================================================= */
+
+/*
+ * Per-layer description consumed by hc_ffn_stack.  All pointers are device
+ * pointers.  Layout notes:
+ *  - hot: n_hot neurons, each 3 x 4096 e4m3 bytes in the order gate row, up
+ *    row, down column (the reference stores down as [4096][n_hot],
+ *    splitter.py:225; the host re-lays it out once at load time);
+ *    hot_scale [n_hot][3] fp32 or NULL (the reference's direct cast = 1.0)
+ *  - cold_records: first record of the layer's section inside the uploaded
+ *    cold_weights.bin image (16-byte aligned)
+ *  - fetch_bits [ceil(inter/32)]: 1 = cold id with a record and not hot
+ *  - pred_w_down_t [4096][rank] (transposed), pred_w_up [inter][rank],
+ *    pred_b_up [inter]: this layer's predictor, or all NULL
+ */
+typedef struct hc_layer_desc {
+  const uint8_t* hot;
+  const float* hot_scale;
+  const float* norm_w;
+  const uint8_t* cold_records;
+  const int32_t* table;
+  const uint32_t* fetch_bits;
+  const float* pred_w_down_t;
+  const float* pred_w_up;
+  const float* pred_b_up;
+  int32_t n_hot;
+  int32_t n_records;
+  int32_t inter;
+  int32_t rank;
+} hc_layer_desc;
+
+/* Grid size the stack kernel uses on the current device (1 CTA per SM). */
+HC_API int hc_ffn_stack_grid(void);
+HC_API int64_t hc_ffn_stack_workspace_bytes(int32_t grid, int32_t inter);
+
+/*
+ * hc_ffn_stack -- replaces, per layer, SparseFFNLayer.forward
+ * (engine.py:292-312: RMSNorm -> sparse_ffn -> residual) with sparse_ffn
+ * (engine.py:173-209: hot FP8 half + cold INT4 half, summed in-kernel), and
+ * the cross-layer predictor prefetch of DesdemonaEngine.forward
+ * (engine.py:421-438: layer l+1's fetch set comes from layer l's input).
+ *   layers     [n_layers] hc_layer_desc (device array); every layer has
+ *              `inter` neurons (inter % 4 == 0); a predictor rank must be a
+ *              multiple of 8 and <= 96 (else HC_ERR_UNSUPPORTED, no predictor)
+ *   x_in       [4096] fp32 input hidden state (batch 1)
+ *   masks      [n_layers][ceil(inter/32)] uint32 predicted-active bits: row 0
+ *              must be filled by the caller; row l+1 is written by the kernel
+ *              from layer l+1's predictor (all ones when that layer has no
+ *              predictor -- the reference's fetch-everything fallback,
+ *              engine.py:282-283) unless `masks_given` = 1, in which case
+ *              every row is an input.  The cold neurons a layer computes are
+ *              masks[l] & fetch_bits.
+ *   x_out      [4096] fp32 output; x_hist optional [n_layers][4096] fp32
+ *   eps        RMSNorm epsilon; act = HC_ACT_*; act_on_both = dReLU form
+ *   logit_threshold  as in hc_predictor_forward
+ *   grid       0 = hc_ffn_stack_grid(); tests may pass fewer CTAs
+ *   workspace  hc_ffn_stack_workspace_bytes(grid, inter), zeroed once
+ */
+HC_API int hc_ffn_stack(const hc_layer_desc* layers, int32_t n_layers, int32_t inter, const float* x_in,
+                 uint32_t* masks, int32_t masks_given, float* x_out, float* x_hist, float eps,
+                 int32_t act, int32_t act_on_both, float logit_threshold, int32_t grid,
+                 void* workspace, int32_t* status, hc_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HOTCOLD_H */

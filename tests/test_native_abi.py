@@ -1,0 +1,95 @@
+"""CPU checks of the C ABI and the host-side logic (no kernel launches)."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+import torch
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "hotcold.h")
+
+
+def _declared():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"^HC_API\s+[\w\s\*]+?\b(hc_\w+)\s*\(", src, flags=re.M)))
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    for n in ("hc_cold_gather_dequant", "hc_predictor_forward", "hc_ffn_stack", "hc_build_record_table"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    import hc_native as N
+    lib = ctypes.CDLL(N.LIB_PATH)
+    for n in _declared():
+        assert hasattr(lib, n), f"{n} declared in include/hotcold.h but not exported"
+    assert set(_declared()) == set(N.exported_symbols()), "ctypes signatures out of sync with the header"
+
+
+def test_version_and_status_strings():
+    import hc_native as N
+    assert N.lib.hc_version() == N.ABI_VERSION
+    assert N.status_string(0) == "ok"
+    assert "range" in N.status_string(N.HC_ERR_RANGE)
+    assert "wait" in N.status_string(N.HC_ERR_TIMEOUT)
+    assert N.lib.hc_predictor_workspace_bytes(1, 64, 14336) > 0
+    assert N.lib.hc_ffn_stack_workspace_bytes(148, 14336) > 148 * 4096 * 4
+    assert N.lib.hc_ffn_stack_workspace_bytes(0, 14336) == -1
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="CPU-only host check")
+def test_no_device_is_reported_not_faulted():
+    import hc_native as N
+    assert N.lib.hc_device_sm_count() == -1
+
+
+def test_argument_errors_are_reported_without_a_device():
+    """Host-side argument validation returns HC_ERR_ARG before any CUDA call."""
+    import hc_native as N
+    assert N.lib.hc_cold_gather_dequant(None, 0, None, None, 1, None, 4, None, 0, None, None, None, None,
+                                        None) == N.HC_ERR_ARG
+    assert N.lib.hc_predictor_forward(None, 1, None, 0.0, None, None, None, 64, 100, 0.0, None, None, None,
+                                      None, None, None, None, None, None, None, None) == N.HC_ERR_ARG
+    assert N.lib.hc_ffn_stack(None, 1, 64, None, None, 0, None, None, 1e-5, 0, 0, 0.0, 0, None, None,
+                              None) == N.HC_ERR_ARG
+    assert N.lib.hc_map_ids(None, -1, None, None, None, None, None) == N.HC_ERR_ARG
+
+
+def test_logit_threshold_reproduces_torch_sigmoid_decision():
+    from predictor import logit_threshold
+    for p in (0.5, 0.7, 0.3, 0.9, 0.01):
+        z = logit_threshold(p)
+        t = torch.tensor([z], dtype=torch.float32)
+        below = torch.nextafter(t, torch.tensor([-float("inf")]))
+        assert bool(torch.sigmoid(t)[0] >= p)
+        assert not bool(torch.sigmoid(below)[0] >= p)
+    assert logit_threshold(0.0) == float("-inf")
+    assert logit_threshold(1.5) == float("inf")
+    # a dense sweep around the 0.5 threshold agrees with torch exactly
+    z = logit_threshold(0.5)
+    grid = torch.linspace(-1e-6, 1e-6, 20001, dtype=torch.float32)
+    assert torch.equal(grid >= z, torch.sigmoid(grid) >= 0.5)
+
+
+def test_mask_word_packing_roundtrip():
+    from splitter import bits_to_words, words_to_bits
+    from oracle import hotcold_oracle as O
+    rng = np.random.default_rng(0)
+    for n in (1, 31, 32, 40, 14336, 14337):
+        m = rng.random(n) < 0.3
+        w = bits_to_words(m, n)
+        assert w.dtype == torch.int32 and w.numel() == (n + 31) // 32
+        assert np.array_equal(words_to_bits(w, n), m)
+        assert np.array_equal(O.mask_from_words(w.numpy(), n), m)
+        assert np.array_equal(O.words_from_mask(m), w.numpy())
+
+
+def test_layer_desc_layout_matches_c_struct():
+    import hc_native as N
+    # 9 pointers + 4 int32 = 88 bytes, pointer-aligned
+    assert ctypes.sizeof(N.LayerDesc) == 9 * 8 + 4 * 4
+    assert N.LayerDesc.n_hot.offset == 72
