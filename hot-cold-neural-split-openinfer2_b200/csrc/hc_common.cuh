@@ -101,6 +101,18 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// fire-and-forget L2 prefetch of [src, src + bytes) (16-B aligned, size % 16 == 0)
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void prefetch_l2_range(const void* src, size_t bytes) {
+  const char* p = static_cast<const char*>(src);
+  for (size_t off = 0; off < bytes; off += 32768) {
+    const size_t n = bytes - off < 32768 ? bytes - off : 32768;
+    prefetch_l2(p + off, static_cast<uint32_t>(n));
+  }
+}
+
 // named barrier among `nthreads` threads (id 0 is __syncthreads)
 __device__ __forceinline__ void named_bar(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
@@ -124,6 +136,43 @@ __device__ __forceinline__ void e4m3x4_to_f32(uint32_t w, float f[4]) {
 __device__ __forceinline__ void int4x8_to_f32(uint32_t w, float f[8]) {
 #pragma unroll
   for (int e = 0; e < 8; ++e) f[e] = static_cast<float>(static_cast<int32_t>(w << (28 - 4 * e)) >> 28);
+}
+
+// e4m3x2 (low byte -> low half) -> f16x2, exact
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t w16) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(static_cast<unsigned short>(w16 & 0xFFFFu)));
+  return r;
+}
+
+// y0 += lo(h2) * b, y1 += hi(h2) * b: f16 x f16 products (exact in fp32), fp32 accumulate
+__device__ __forceinline__ void fma2_f16_f32(float& y0, float& y1, uint32_t h2, unsigned short b) {
+  asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+      "fma.rn.f32.f16 %0, lo, %3, %0;\n\tfma.rn.f32.f16 %1, hi, %3, %1;\n\t}"
+      : "+f"(y0), "+f"(y1)
+      : "r"(h2), "h"(b));
+}
+
+// a += lo(w) * lo(x), b += hi(w) * hi(x): f16 x f16 products, fp32 accumulate
+__device__ __forceinline__ void fma2_f16f16_f32(float& a, float& b, uint32_t w, uint32_t x) {
+  asm("{\n\t.reg .f16 wl, wh, xl, xh;\n\tmov.b32 {wl, wh}, %2;\n\tmov.b32 {xl, xh}, %3;\n\t"
+      "fma.rn.f32.f16 %0, wl, xl, %0;\n\tfma.rn.f32.f16 %1, wh, xh, %1;\n\t}"
+      : "+f"(a), "+f"(b)
+      : "r"(w), "r"(x));
+}
+
+// warp-level tensor-core dot products (A rows 8..15 are zero: a1 = a3 = 0)
+__device__ __forceinline__ void mma_f16_m16n8k16(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_s8_m16n8k32(int (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
 }
 
 // bytes [2 .. 6) of the 8-byte pair (a, b): the 2-byte shift every record field has

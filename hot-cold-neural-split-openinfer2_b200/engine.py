@@ -108,6 +108,11 @@ class FFNStack:
                 rank=p.rank if p is not None else 0))
         self.desc_dev = N.layer_desc_array(descs, self.device)
         self.grid = int(grid) if grid else int(N.lib.hc_ffn_stack_grid())
+        if self.inter > 32768:
+            raise ValueError("the fused kernel handles intermediate_dim <= 32768")
+        max_rec = max(int(store.n_rec_host[li]) for li in self.layer_ids)
+        if (max_rec + self.grid - 1) // self.grid > 1024:
+            raise ValueError(f"grid {self.grid} is too small for {max_rec} cold records per layer (max 1024 per CTA)")
         self.ws = torch.zeros(int(N.lib.hc_ffn_stack_workspace_bytes(self.grid, self.inter)), dtype=torch.uint8,
                               device=self.device)
         self.masks = torch.zeros(self.L, self.words, dtype=torch.int32, device=self.device)
@@ -126,12 +131,33 @@ class FFNStack:
                              mask_out=self.masks[0:1])
 
     def launch(self, x: torch.Tensor, masks_given: bool = False, x_hist: Optional[torch.Tensor] = None,
-               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+               out: Optional[torch.Tensor] = None, trace: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """One hc_ffn_stack launch.  ``trace`` (int64 [L, grid, 16], device)
+        (zeroed) receives per-CTA phase timestamps and waits
+        (see include/hotcold.h)."""
         out = self.x_out if out is None else out
         N.check(N.lib.hc_ffn_stack(N.ptr(self.desc_dev), self.L, self.inter, N.ptr(x), N.ptr(self.masks),
                                    1 if masks_given else 0, N.ptr(out), N.ptr(x_hist), self.eps, self.act,
                                    1 if self.act_on_both else 0, self.thr, self.grid, N.ptr(self.ws),
-                                   N.ptr(self.status), N.stream_handle()), "hc_ffn_stack")
+                                   N.ptr(self.status), N.ptr(trace), N.stream_handle()), "hc_ffn_stack")
+        return out
+
+    def trace_summary(self, trace: torch.Tensor) -> dict:
+        """Mean / max over CTAs of each phase's duration (us) from a trace."""
+        t = trace.to(torch.float64).cpu() / 1000.0
+        names = ["norm", "hot", "wdown", "cold_list_wait", "cold", "barrier_a", "col_reduce", "wup", "barrier_b"]
+        out = {}
+        for i, n in enumerate(names):
+            d = t[:, :, i + 1] - t[:, :, i]
+            out[n] = (float(d.mean()), float(d.max()))
+        out["layer"] = (float((t[1:, :, 0] - t[:-1, :, 0]).mean()) if self.L > 1 else 0.0, 0.0)
+        out["issuer_hot"] = (float((t[:, :, 11] - t[:, :, 10]).mean()), float((t[:, :, 11] - t[:, :, 10]).max()))
+        out["issuer_wait_plan"] = (float((t[:, :, 13] - t[:, :, 12]).mean()), float((t[:, :, 13] - t[:, :, 12]).max()))
+        out["issuer_cold"] = (float((t[:, :, 14] - t[:, :, 13]).mean()), float((t[:, :, 14] - t[:, :, 13]).max()))
+        for k, i in (("cons_wait_hot", 15), ("cons_wait_cold", 16), ("issuer_wait_slot_hot", 18),
+                     ("issuer_wait_slot_cold", 19)):
+            out[k] = (float(t[:, :, i].mean()), float(t[:, :, i].max()))
+        out["plan_ready_after_start"] = (float((t[:, :, 20] - t[:, :, 0]).mean()), float((t[:, :, 20] - t[:, :, 0]).max()))
         return out
 
     def forward(self, x: torch.Tensor, masks: Optional[torch.Tensor] = None, x_hist: Optional[torch.Tensor] = None,

@@ -66,7 +66,7 @@ _SIGS = {
     "hc_ffn_stack_grid": (c_i32, []),
     "hc_ffn_stack_workspace_bytes": (c_i64, [c_i32, c_i32]),
     "hc_ffn_stack": (c_i32, [c_p, c_i32, c_i32, c_p, c_p, c_i32, c_p, c_p, c_f, c_i32, c_i32, c_f,
-                             c_i32, c_p, c_p, c_p]),
+                             c_i32, c_p, c_p, c_p, c_p]),
 }
 
 

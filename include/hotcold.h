@@ -200,8 +200,10 @@ HC_API int64_t hc_ffn_stack_workspace_bytes(int32_t grid, int32_t inter);
  * the cross-layer predictor prefetch of DesdemonaEngine.forward
  * (engine.py:421-438: layer l+1's fetch set comes from layer l's input).
  *   layers     [n_layers] hc_layer_desc (device array); every layer has
- *              `inter` neurons (inter % 4 == 0); a predictor rank must be a
- *              multiple of 8 and <= 96 (else HC_ERR_UNSUPPORTED, no predictor)
+ *              `inter` neurons (inter % 4 == 0, inter <= 32768); a predictor
+ *              rank must be a multiple of 8 and <= 96 (else HC_ERR_UNSUPPORTED,
+ *              no predictor); one CTA takes at most 1024 cold records per
+ *              layer, i.e. n_records <= 1024 * grid
  *   x_in       [4096] fp32 input hidden state (batch 1)
  *   masks      [n_layers][ceil(inter/32)] uint32 predicted-active bits: row 0
  *              must be filled by the caller; row l+1 is written by the kernel
@@ -215,11 +217,20 @@ HC_API int64_t hc_ffn_stack_workspace_bytes(int32_t grid, int32_t inter);
  *   logit_threshold  as in hc_predictor_forward
  *   grid       0 = hc_ffn_stack_grid(); tests may pass fewer CTAs
  *   workspace  hc_ffn_stack_workspace_bytes(grid, inter), zeroed once
+ *   trace      optional [n_layers][grid][24] uint64, zeroed by the caller:
+ *              %globaltimer stamps (ns) of each CTA's phase boundaries
+ *              (consumer events 0-9: layer start, norm done, hot done, W_down
+ *              done, cold list ready, cold done, barrier A passed, column
+ *              reduction done, W_up done, barrier B passed; issuer events
+ *              10-14: layer start, hot issued, W_down issued, cold list ready,
+ *              cold issued; 20: planner list ready) and accumulated waits in
+ *              ns (15/16: consumers on hot/cold slot fills, 18/19: issuer on
+ *              empty slots while issuing hot/cold); NULL = off
  */
 HC_API int hc_ffn_stack(const hc_layer_desc* layers, int32_t n_layers, int32_t inter, const float* x_in,
                  uint32_t* masks, int32_t masks_given, float* x_out, float* x_hist, float eps,
                  int32_t act, int32_t act_on_both, float logit_threshold, int32_t grid,
-                 void* workspace, int32_t* status, hc_stream_t stream);
+                 void* workspace, int32_t* status, uint64_t* trace, hc_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -55,7 +55,7 @@ def test_argument_errors_are_reported_without_a_device():
     assert N.lib.hc_predictor_forward(None, 1, None, 0.0, None, None, None, 64, 100, 0.0, None, None, None,
                                       None, None, None, None, None, None, None, None) == N.HC_ERR_ARG
     assert N.lib.hc_ffn_stack(None, 1, 64, None, None, 0, None, None, 1e-5, 0, 0, 0.0, 0, None, None,
-                              None) == N.HC_ERR_ARG
+                              None, None) == N.HC_ERR_ARG
     assert N.lib.hc_map_ids(None, -1, None, None, None, None, None) == N.HC_ERR_ARG
 
 
