@@ -16,6 +16,8 @@
 //      mask word; the last CTA compacts row 0 into the ordered id list.
 #include "hc_common.cuh"
 
+#include <mutex>
+
 namespace hc {
 
 constexpr int PRED_KCHUNK = 128;
@@ -236,4 +238,50 @@ extern "C" int hc_predictor_forward(const float* x, int32_t batch, const float* 
                                                       probs_out, logits_out, fetch_bits, table, ids_out, rec_out,
                                                       count_out, ws);
   return cudaGetLastError() == cudaSuccess ? HC_OK : HC_ERR_CUDA;
+}
+
+// --------------------------------------------------------------------------
+// Allocation-free variant.  Some callers cannot allocate device memory at
+// all: code that runs inside a fixed memory budget set up once at start (a
+// serving process whose allocator is frozen after warm-up, an embedded
+// runtime, a plugin host that owns every allocation and exposes none to its
+// plugins).  For them the predictor's scratch lives in this file-scope
+// device array instead of a caller workspace.  Every GPU that loads the
+// library holds it until the process exits.
+// --------------------------------------------------------------------------
+namespace hc {
+constexpr int STATIC_PRED_MAX_BR = 512;   // batch * rank the static scratch holds
+constexpr size_t STATIC_PRED_BYTES =
+    256 + sizeof(float) * ((size_t)(H / PRED_KCHUNK) * STATIC_PRED_MAX_BR + STATIC_PRED_MAX_BR);
+static __device__ __align__(256) unsigned char g_pred_scratch[STATIC_PRED_BYTES];
+
+constexpr int MAX_DEVICES = 64;
+static void* g_pred_scratch_addr[MAX_DEVICES] = {};
+static std::mutex g_pred_scratch_mu;
+}  // namespace hc
+
+extern "C" int hc_predictor_forward_static(const float* x, int32_t batch, const float* norm_w, float eps,
+                                           const float* w_down, const float* w_up, const float* b_up, int32_t rank,
+                                           int32_t inter, float logit_threshold, uint32_t* mask_out,
+                                           float* probs_out, float* logits_out, const uint32_t* fetch_bits,
+                                           const int32_t* table, int32_t* ids_out, int32_t* rec_out,
+                                           int32_t* count_out, int32_t* status, hc_stream_t stream) {
+  if (batch <= 0 || rank <= 0 || (int64_t)batch * rank > STATIC_PRED_MAX_BR) return HC_ERR_UNSUPPORTED;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) return HC_ERR_CUDA;
+  void* ws = nullptr;
+  {
+    // first call on this device (current device): resolve the array's device address once
+    std::lock_guard<std::mutex> lock(g_pred_scratch_mu);
+    ws = g_pred_scratch_addr[dev];
+    if (ws == nullptr) {
+      if (cudaGetSymbolAddress(&ws, g_pred_scratch) != cudaSuccess || ws == nullptr) return HC_ERR_CUDA;
+      g_pred_scratch_addr[dev] = ws;
+    }
+  }
+  // the array keeps the previous call's contents: restart the two completion counters at zero
+  if (cudaMemsetAsync(ws, 0, 256, reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess) return HC_ERR_CUDA;
+  return hc_predictor_forward(x, batch, norm_w, eps, w_down, w_up, b_up, rank, inter, logit_threshold, mask_out,
+                              probs_out, logits_out, fetch_bits, table, ids_out, rec_out, count_out, ws, status,
+                              stream);
 }

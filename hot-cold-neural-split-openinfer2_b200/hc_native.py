@@ -63,6 +63,8 @@ _SIGS = {
     "hc_predictor_workspace_bytes": (c_i64, [c_i32, c_i32, c_i32]),
     "hc_predictor_forward": (c_i32, [c_p, c_i32, c_p, c_f, c_p, c_p, c_p, c_i32, c_i32, c_f, c_p, c_p, c_p,
                                      c_p, c_p, c_p, c_p, c_p, c_p, c_p, c_p]),
+    "hc_predictor_forward_static": (c_i32, [c_p, c_i32, c_p, c_f, c_p, c_p, c_p, c_i32, c_i32, c_f, c_p, c_p, c_p,
+                                            c_p, c_p, c_p, c_p, c_p, c_p, c_p]),
     "hc_ffn_stack_grid": (c_i32, []),
     "hc_ffn_stack_workspace_bytes": (c_i64, [c_i32, c_i32]),
     "hc_ffn_stack": (c_i32, [c_p, c_i32, c_i32, c_p, c_p, c_i32, c_p, c_p, c_f, c_i32, c_i32, c_f,

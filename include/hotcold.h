@@ -156,6 +156,29 @@ HC_API int hc_predictor_forward(const float* x, int32_t batch, const float* norm
                          int32_t* rec_out, int32_t* count_out, void* workspace, int32_t* status,
                          hc_stream_t stream);
 
+/*
+ * hc_predictor_forward_static -- no counterpart in the reference.  The same
+ * computation and arguments as hc_predictor_forward, minus the workspace,
+ * for callers that cannot allocate device memory (a serving process whose
+ * allocator is frozen after start-up, an embedded runtime or a plugin host
+ * that owns every allocation).  The scratch is a file-scope device array of
+ * about 66 KB inside the library (held by every GPU that loads it until the
+ * process exits), so it supports batch * rank <= 512 and returns
+ * HC_ERR_UNSUPPORTED beyond that without launching anything.  The first call
+ * on a device looks up that array's address (cudaGetSymbolAddress) for the
+ * current device; make that first call before any stream capture.  Each call
+ * clears the array's counters on `stream` first; calls that overlap on the
+ * GPU share the array and race, so serialise them (one stream, or events).
+ * Nothing here calls cudaMalloc or cudaFree.
+ */
+HC_API int hc_predictor_forward_static(const float* x, int32_t batch, const float* norm_w, float eps,
+                                       const float* w_down, const float* w_up, const float* b_up,
+                                       int32_t rank, int32_t inter, float logit_threshold,
+                                       uint32_t* mask_out, float* probs_out, float* logits_out,
+                                       const uint32_t* fetch_bits, const int32_t* table, int32_t* ids_out,
+                                       int32_t* rec_out, int32_t* count_out, int32_t* status,
+                                       hc_stream_t stream);
+
 /* ======================================================================= */
 /* Fused sparse FFN (hot FP8 + cold INT4), one layer or a stack of layers  */
 /* ======================================================================= */
