@@ -110,9 +110,9 @@ class FFNStack:
         self.grid = int(grid) if grid else int(N.lib.hc_ffn_stack_grid())
         if self.inter > 32768:
             raise ValueError("the fused kernel handles intermediate_dim <= 32768")
-        max_rec = max(int(store.n_rec_host[li]) for li in self.layer_ids)
-        if (max_rec + self.grid - 1) // self.grid > 1024:
-            raise ValueError(f"grid {self.grid} is too small for {max_rec} cold records per layer (max 1024 per CTA)")
+        if (self.words + self.grid - 1) // self.grid * 32 > 1024:
+            raise ValueError(f"grid {self.grid} is too small for {self.inter} neurons per layer "
+                             "(one CTA owns at most 1024 neuron ids)")
         self.ws = torch.zeros(int(N.lib.hc_ffn_stack_workspace_bytes(self.grid, self.inter)), dtype=torch.uint8,
                               device=self.device)
         self.masks = torch.zeros(self.L, self.words, dtype=torch.int32, device=self.device)
@@ -132,7 +132,7 @@ class FFNStack:
 
     def launch(self, x: torch.Tensor, masks_given: bool = False, x_hist: Optional[torch.Tensor] = None,
                out: Optional[torch.Tensor] = None, trace: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """One hc_ffn_stack launch.  ``trace`` (int64 [L, grid, 16], device)
+        """One hc_ffn_stack launch.  ``trace`` (int64 [L, grid, 24], device)
         (zeroed) receives per-CTA phase timestamps and waits
         (see include/hotcold.h)."""
         out = self.x_out if out is None else out
@@ -145,7 +145,7 @@ class FFNStack:
     def trace_summary(self, trace: torch.Tensor) -> dict:
         """Mean / max over CTAs of each phase's duration (us) from a trace."""
         t = trace.to(torch.float64).cpu() / 1000.0
-        names = ["norm", "hot", "wdown", "cold_list_wait", "cold", "barrier_a", "col_reduce", "wup", "barrier_b"]
+        names = ["barrier_x", "norm", "own_mask", "hot", "wdown", "cold_list_wait", "cold", "y_add"]
         out = {}
         for i, n in enumerate(names):
             d = t[:, :, i + 1] - t[:, :, i]

@@ -225,8 +225,9 @@ HC_API int64_t hc_ffn_stack_workspace_bytes(int32_t grid, int32_t inter);
  *   layers     [n_layers] hc_layer_desc (device array); every layer has
  *              `inter` neurons (inter % 4 == 0, inter <= 32768); a predictor
  *              rank must be a multiple of 8 and <= 96 (else HC_ERR_UNSUPPORTED,
- *              no predictor); one CTA takes at most 1024 cold records per
- *              layer, i.e. n_records <= 1024 * grid
+ *              no predictor); CTA c owns the neuron ids of mask words
+ *              [c*W/grid, (c+1)*W/grid), W = ceil(inter/32), and at most 1024
+ *              of them, i.e. ceil(W/grid)*32 <= 1024 (else HC_ERR_UNSUPPORTED)
  *   x_in       [4096] fp32 input hidden state (batch 1)
  *   masks      [n_layers][ceil(inter/32)] uint32 predicted-active bits: row 0
  *              must be filled by the caller; row l+1 is written by the kernel
@@ -239,16 +240,20 @@ HC_API int64_t hc_ffn_stack_workspace_bytes(int32_t grid, int32_t inter);
  *   eps        RMSNorm epsilon; act = HC_ACT_*; act_on_both = dReLU form
  *   logit_threshold  as in hc_predictor_forward
  *   grid       0 = hc_ffn_stack_grid(); tests may pass fewer CTAs
- *   workspace  hc_ffn_stack_workspace_bytes(grid, inter), zeroed once
+ *   workspace  hc_ffn_stack_workspace_bytes(grid, inter), zeroed once; the
+ *              kernel leaves it zeroed again when it completes
  *   trace      optional [n_layers][grid][24] uint64, zeroed by the caller:
  *              %globaltimer stamps (ns) of each CTA's phase boundaries
- *              (consumer events 0-9: layer start, norm done, hot done, W_down
- *              done, cold list ready, cold done, barrier A passed, column
- *              reduction done, W_up done, barrier B passed; issuer events
- *              10-14: layer start, hot issued, W_down issued, cold list ready,
- *              cold issued; 20: planner list ready) and accumulated waits in
- *              ns (15/16: consumers on hot/cold slot fills, 18/19: issuer on
- *              empty slots while issuing hot/cold); NULL = off
+ *              (consumer events 0-8: layer start, grid barrier passed and x
+ *              updated, norm done, own mask words ready, hot done, W_down
+ *              done, cold list read, cold done, partial y added; issuer
+ *              events 10-14: layer start, hot issued, W_down issued, cold
+ *              list ready, cold issued; 20: planner list ready) and
+ *              accumulated waits in ns (15/16: consumers on hot/cold slot
+ *              fills, 18/19: issuer on empty slots while issuing hot/cold);
+ *              NULL = off
+ * The layer outputs are sums of per-CTA float partials added with atomics, so
+ * their last bits can differ between launches.
  */
 HC_API int hc_ffn_stack(const hc_layer_desc* layers, int32_t n_layers, int32_t inter, const float* x_in,
                  uint32_t* masks, int32_t masks_given, float* x_out, float* x_hist, float eps,

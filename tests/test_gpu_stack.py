@@ -136,34 +136,40 @@ def test_stack_full_geometry_two_layers(M):
 
 
 def test_stack_32_layers_properties(M):
-    """Full 32-layer stack: deterministic, finite, fetch counts consistent, and
-    the last layer matches the oracle."""
+    """Full 32-layer stack: finite, fetch counts consistent, layers 0, 15 and
+    31 match the oracle, and a rerun on the same fetch sets agrees."""
     engine, hc_synth, predictor, splitter = M
     syn = hc_synth.make_stack(n_layers=32, inter=14336, seed=16)
     st = syn.stack()
     x0 = torch.randn(4096, device="cuda")
     h1 = torch.empty(32, 4096, device="cuda")
     h2 = torch.empty(32, 4096, device="cuda")
-    a = st.forward(x0, x_hist=h1).clone()
-    m1 = st.masks.clone()
-    b = st.forward(x0, x_hist=h2).clone()
+    st.forward(x0, x_hist=h1)
     st.check()
-    assert torch.equal(a, b) and torch.equal(h1, h2) and torch.equal(m1, st.masks), "run-to-run bit identical"
+    m1 = st.masks.clone()
     assert torch.isfinite(h1).all()
     frac = float(st.active_counts().float().mean()) / 11469
     assert 0.3 < frac < 0.7, frac          # random predictor: ~half the cold set
-    # last layer against the oracle
-    l = 31
     inter = 14336
     host_img = syn.store.image.cpu().numpy().tobytes()
     ostore = O.ColdStoreOracle(host_img, syn.cold_index, {"hidden_dim": 4096})
-    mask = O.mask_from_words(st.masks[l].cpu().numpy(), inter) & O.mask_from_words(st.fetch[l].cpu().numpy(), inter)
-    hg, hu, hd = (t.double().cpu().numpy() for t in syn.hot[l].decoded())
-    xl = h1[l - 1].double().cpu().numpy()
-    ref = O.ffn_layer_from_records(xl, syn.norms[l].cpu().numpy(), syn.eps, "relu", True, (hg, hu, hd), ostore, l,
-                                   np.nonzero(mask)[0].tolist())
-    rel = np.linalg.norm((h1[l].double().cpu().numpy() - xl) - (ref - xl)) / np.linalg.norm(ref - xl)
-    assert rel <= TOL
+    for l in (0, 15, 31):
+        mask = O.mask_from_words(m1[l].cpu().numpy(), inter) & O.mask_from_words(st.fetch[l].cpu().numpy(), inter)
+        hg, hu, hd = (t.double().cpu().numpy() for t in syn.hot[l].decoded())
+        xl = (x0 if l == 0 else h1[l - 1]).double().cpu().numpy()
+        ref = O.ffn_layer_from_records(xl, syn.norms[l].cpu().numpy(), syn.eps, "relu", True, (hg, hu, hd), ostore,
+                                       l, np.nonzero(mask)[0].tolist())
+        rel = np.linalg.norm((h1[l].double().cpu().numpy() - xl) - (ref - xl)) / np.linalg.norm(ref - xl)
+        assert rel <= TOL, f"layer {l}: rel-L2 {rel:.3e}"
+    # Rerun on the same fetch sets.  The per-layer sums are float atomics, so
+    # the two runs differ in summation order; the f16 rounding of each layer's
+    # normalised input turns that into differences of ~1e-5 per layer.  (With
+    # the predictor in the loop, a logit on the threshold can flip and the
+    # random-weight stack amplifies it, so predicted runs are not compared.)
+    st.forward(x0, masks=m1, x_hist=h2)
+    st.check()
+    rel = ((h2 - h1).norm(dim=1) / h1.norm(dim=1)).max().item()
+    assert rel < 5e-3, f"rerun on the same fetch sets: rel-L2 {rel:.3e}"
 
 
 @pytest.mark.parametrize("tag,act,both", [("swiglu", "silu", False), ("drelu", "relu", True)])

@@ -37,7 +37,7 @@ def test_version_and_status_strings():
     assert "range" in N.status_string(N.HC_ERR_RANGE)
     assert "wait" in N.status_string(N.HC_ERR_TIMEOUT)
     assert N.lib.hc_predictor_workspace_bytes(1, 64, 14336) > 0
-    assert N.lib.hc_ffn_stack_workspace_bytes(148, 14336) > 148 * 4096 * 4
+    assert N.lib.hc_ffn_stack_workspace_bytes(148, 14336) >= 3 * 4096 * 4   # rotating layer accumulators
     assert N.lib.hc_ffn_stack_workspace_bytes(0, 14336) == -1
 
 
