@@ -9,70 +9,110 @@
 // prefetch does (engine.py:421-438).
 //
 // One persistent cooperative launch, one CTA per SM, one grid barrier per
-// layer.  CTA c owns a slice of the hot neurons, a contiguous neuron-id range
-// (for the predictor logits and the cold records in it) and a slice of the
-// next predictor's W_down rows.  Warp roles:
-//  * issuer warp: streams the CTA's units through a ring of 15 shared-memory
-//    slots with 1-D bulk copies (TMA engine) completing on mbarriers, and
-//    prefetches each layer's static weights into L2 one phase ahead;
+// layer.  CTA c owns a contiguous neuron-id range (its predictor logits and
+// the active cold records in it), a static slice of the first quarter of the
+// hot neurons and a slice of the next predictor's W_down rows; the other hot
+// neurons are claimed two at a time from a global counter, so CTAs with few
+// active cold records take more hot work.  Layer l+1's logits are computed at
+// the end of layer l, once a global counter shows every CTA has added its
+// W_down partials, so layer l+1's cold list is built, and its records are
+// streamed in, while the grid waits at the layer boundary.
+//
+// Roles:
+//  * issuer warp: streams the CTA's units (W_up tiles, hot neurons, W_down
+//    tiles, cold records) through a ring of shared-memory slots with 1-D bulk
+//    copies (TMA engine) completing on mbarriers, two slots per group, and
+//    prefetches the layer's static ranges into L2;
 //  * planner warp: turns the CTA's predicted-mask words into the ascending
-//    list of active cold records (ColdWeightStore's id -> record lookup) and
-//    prefetches those records into L2;
-//  * 16 consumer warps: thread t owns x[8t, 8t+8) (f16 pairs in registers)
-//    and y[8t, 8t+8); per group of neurons: partial gate/up dots, one CTA
-//    reduction, activation, down-projection into y.
-// Layer boundary: every CTA adds its partial y into a per-layer accumulator
-// with vector atomics (and the next predictor's z partials likewise), arrives
-// at the grid barrier, and after it reads x_{l+1} = x_l + y_l; the three
-// accumulators rotate and are cleared two layers ahead.  The float atomics
-// make the summation order, and so the last bits, vary between runs.
-// Every wait (slot, mbarrier, grid barrier) is bounded by a time limit; on
-// expiry the kernel ORs HC_ERR_TIMEOUT into the status word, drains its own
-// copies in flight and returns.
+//    list of its active cold records (ColdWeightStore's id -> record lookup)
+//    and prefetches them into L2;
+//  * 4 consumer subgroups of 128 threads: group g of a layer belongs to
+//    subgroup g % 4; thread u owns elements [32u, 32u+32) of every row and of
+//    its subgroup's partial y.  FP8 rows are dotted with RMSNorm(x) in f16
+//    (f16 x f16 products, fp32 sums); INT4 rows with RMSNorm(x) as 16-bit
+//    fixed point (two byte digits per element, dp4a, exact integer sums).
+// Layer boundary: the subgroups' partial y are summed in shared memory, added
+// to a per-layer global accumulator with vector atomics, and after the grid
+// barrier every CTA reads x_{l+1} = x_l + y_l.  The float atomics make the
+// summation order, and so the last bits, vary between runs.
+// Every wait on another agent (slot, mbarrier, grid barrier) is bounded by a
+// time limit; on expiry the kernel ORs HC_ERR_TIMEOUT into the status word,
+// waits (bounded) for its own copies in flight and returns.
+#include <algorithm>
+
 #include "hc_common.cuh"
 
 namespace hc {
 
-constexpr int CONS_THREADS = 512;       // 16 consumer warps, 8 elements of x / y per thread
+constexpr int CONS_THREADS = 512;
 constexpr int NWARPS = CONS_THREADS / 32;
-constexpr int EPT = H / CONS_THREADS;   // elements per consumer thread (8)
+constexpr int EPT = H / CONS_THREADS;   // element layout: x[8t, 8t+8) per consumer thread
+constexpr int NSG = 4;                  // consumer subgroups
+constexpr int SG_THREADS = CONS_THREADS / NSG;
+constexpr int SG_WARPS = SG_THREADS / 32;
+constexpr int SPT = H / SG_THREADS;     // 32 elements per subgroup thread
 constexpr int STACK_THREADS = CONS_THREADS + 64;   // + issuer warp + planner warp
-constexpr int SLOT_BYTES = 12800;       // one hot neuron (12288) or two cold records (2 x 6352)
-constexpr int NSLOTS = 15;
-constexpr int REC_SLOT_OFF = 6352;      // second cold record in a slot
-constexpr int NB = 8;                   // cold records per reduction round
-constexpr int NB_HOT = 4;               // hot neurons per reduction round
+constexpr int HALF_BYTES = 12800;       // one hot neuron (12288) or two cold records (2 x 6352)
+constexpr int ENTRY_BYTES = 2 * HALF_BYTES;   // one group: two halves
+constexpr int NE = 7;                   // ring entries
+constexpr int REC_SLOT_OFF = 6352;      // second cold record in a half
+constexpr int NB_HOT = 2;               // hot neurons per group (one per slot)
+constexpr int NB_COLD = 4;              // cold records per group (two per slot)
 constexpr int WD_ROWS = 32;             // W_down tile: 32 k-rows x rank
 constexpr int WU_ROWS = 32;             // W_up tile: 32 neurons x rank (+ bias) == one mask word
-constexpr int COLD_LIST = 1024;         // max cold records one CTA handles per layer
-constexpr int MAX_WORDS = 1024;         // mask words (inter <= 32768)
+constexpr int COLD_LIST = 1024;         // neuron ids one CTA owns (and so cold records per layer)
+constexpr int OWN_WORDS = COLD_LIST / 32;
 constexpr int HOT_BYTES = 3 * H;        // 12288
-constexpr int NACC = 3;                 // rotating y / z accumulators
+constexpr int NACC = 3;                 // rotating y / z / hot-claim accumulators
+constexpr int STATIC_HOT_DIV = 4;       // 1/4 of the hot neurons are split statically
+constexpr int WD_TILES = 4096 / 32;     // W_down tiles of a predictor (H / WD_ROWS)
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;   // 2 s
-static_assert(SLOT_BYTES % 16 == 0 && REC_SLOT_OFF % 16 == 0, "bulk copies need 16-byte aligned slots");
-static_assert(HOT_BYTES <= SLOT_BYTES && REC_SLOT_OFF + REC_COPY <= SLOT_BYTES, "slot too small");
-static_assert(32 * 96 * 4 + 32 * 4 <= SLOT_BYTES, "predictor tiles must fit a slot");
-static_assert(EPT == 8, "the decoders assume 8 elements per thread");
+static_assert(HALF_BYTES % 128 == 0 && REC_SLOT_OFF % 16 == 0, "halves must stay 16-byte aligned");
+static_assert(HOT_BYTES <= HALF_BYTES && REC_SLOT_OFF + REC_COPY <= HALF_BYTES, "half too small");
+static_assert(WU_ROWS * 96 * 4 + WU_ROWS * 4 <= HALF_BYTES, "predictor tiles must fit a half");
+static_assert(NE > NSG, "the subgroups' entries advance by NSG per group");
+static_assert(SPT == 32 && EPT == 8, "the decoders assume 32 elements per subgroup thread");
+
+enum : uint8_t { UNIT_PAD = 0, UNIT_HOT = 1, UNIT_COLD = 2, UNIT_WUP = 3, UNIT_WDOWN = 4 };
+
+// Written by the issuer before it arms an entry's mbarrier.
+struct SlotInfo {
+  uint32_t pos;      // ring position of this fill
+  int16_t layer;
+  uint8_t kind;      // UNIT_*
+  uint8_t n;         // units in the group (1..NB_*)
+  int32_t index;     // first hot neuron / tile of the group
+  int32_t pad;
+};
 
 struct StackSmem {
-  alignas(128) uint8_t ring[NSLOTS][SLOT_BYTES];
-  float xs[H];                      // predictor input RMSNorm_{l+1}(x_l) (rows of this CTA's W_down tiles)
-  float red[2][NWARPS][2 * NB];     // per-warp partial (gate, up) dots, double buffered
-  float z[128];                     // bottleneck of this layer's predictor
-  float zred[CONS_THREADS];
-  uint32_t own_words[MAX_WORDS];    // predicted mask words of this CTA's neuron-id range
+  __half xh[H];                     // RMSNorm_l(x) as f16 (hot neurons); with xq, a y stage later
+  uint4 xq[CONS_THREADS];           // the same as 16-bit fixed point, byte digits per 8 elements
+  float ystage[H];                  // subgroup partial y (element 32u+k at k*128+u); during the
+                                    // subgroup phase, subgroup s keeps the next predictor's z at s*128
+  int2 chunk[H / SPT];              // per 32 elements: (-8 * sum of the fixed-point values, bits of 2^-s)
+  float zred[NWARPS];
+  float red[NSG][2][SG_WARPS][2 * NB_COLD];
+  int32_t sgdec[NSG][2];            // per-subgroup decision of its poller
+  uint64_t tstat[8];                // trace counters of subgroup 0's poller
   int32_t plan_list[COLD_LIST];     // nids, then record indices, of this CTA's active cold records
+  uint32_t own_words[OWN_WORDS];    // predicted mask words of this CTA's neuron-id range
+  SlotInfo info[NE];
+  int32_t ngroups[4];               // groups issued per layer (l & 3)
+  int32_t sealed;                   // last layer whose groups are all issued
+  int32_t cons_layer;               // last layer the consumers started
   int32_t plan_n;
-  uint32_t ballot_word;
-  int32_t flag;                     // consumer-wide broadcast
-  int32_t abort;                    // sticky abort
-  uint32_t cons_k;                  // slots consumed (for the drain)
-  alignas(8) uint64_t full[NSLOTS];
-  alignas(8) uint64_t empty[NSLOTS];
-  alignas(8) uint64_t own_ready;    // consumers -> planner: own mask words of layer l written
-  alignas(8) uint64_t plan_full;    // planner -> issuer/consumers: cold list of layer l ready
-  alignas(8) uint64_t plan_empty;   // issuer + consumers -> planner: list consumed
+  int32_t abort;
+  int32_t wup_left;
+  int32_t flag;
+  int32_t last;
+  alignas(8) uint64_t full[NE];
+  alignas(8) uint64_t empty[NE];
+  alignas(8) uint64_t own_ready;    // consumers -> planner: own mask words of the next layer written
+  alignas(8) uint64_t plan_full;    // planner -> issuer: cold list of layer l ready
+  alignas(8) uint64_t plan_empty;   // issuer -> planner: list consumed
 };
+constexpr size_t RING_OFF = (sizeof(StackSmem) + 127) / 128 * 128;
 
 struct StackParams {
   const hc_layer_desc* layers;
@@ -90,361 +130,58 @@ struct StackParams {
   float thr;
   uint32_t* bar_count;
   uint32_t* exit_count;
+  uint32_t* hot_next;        // [NACC] hot-neuron claims per layer
+  uint32_t* zdone;           // [NACC] W_down tiles added into zacc per layer
   float* yacc;               // [NACC][H]   partial-y accumulators
   float* zacc;               // [NACC][128] predictor bottleneck accumulators
+  float* xbuf;               // [NACC][H]   x_l, written by CTA 0
   int32_t* status;
   uint64_t* trace;           // optional [n_layers][G][TRACE_EVENTS]
 };
 
-constexpr int TRACE_EVENTS = 24;
+constexpr int TRACE_EVENTS = 32;
 __device__ __forceinline__ void trace_ev(const StackParams& p, int l, int ev) {
   if (p.trace != nullptr) p.trace[((size_t)l * gridDim.x + blockIdx.x) * TRACE_EVENTS + ev] = globaltimer_ns();
 }
-__device__ __forceinline__ void trace_add(const StackParams& p, int l, int ev, uint64_t v) {
-  if (p.trace != nullptr) p.trace[((size_t)l * gridDim.x + blockIdx.x) * TRACE_EVENTS + ev] += v;
+__device__ __forceinline__ void trace_set(const StackParams& p, int l, int ev, uint64_t v) {
+  if (p.trace != nullptr) p.trace[((size_t)l * gridDim.x + blockIdx.x) * TRACE_EVENTS + ev] = v;
 }
 
+constexpr size_t WS_HOT_NEXT = 64;
+constexpr size_t WS_ZDONE = 96;
+constexpr size_t WS_EXIT = 128;
 constexpr size_t WS_YACC = 256;
 constexpr size_t WS_ZACC = WS_YACC + sizeof(float) * NACC * H;
-constexpr size_t WS_BYTES = WS_ZACC + sizeof(float) * NACC * 128;
+constexpr size_t WS_XBUF = WS_ZACC + sizeof(float) * NACC * 128;
+constexpr size_t WS_BYTES = WS_XBUF + sizeof(float) * NACC * H;
 
 __device__ __forceinline__ int64_t split_lo(int64_t n, int c, int G) { return n * c / G; }
-// predictor tiles must fit a slot and split evenly over 8 lanes
+// predictor tiles must fit a slot and split evenly over 4 threads per neuron
 __device__ __forceinline__ bool rank_ok(int r) { return r > 0 && r <= 96 && (r & 7) == 0; }
 
 __device__ __forceinline__ void red_add_v4(float* dst, float a, float b, float c, float d) {
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
 }
-
-// --------------------------------------------------------------------------
-// consumer helpers
-// --------------------------------------------------------------------------
-__device__ __forceinline__ float ld_half(const uint8_t* p) {
-  return __half2float(*reinterpret_cast<const __half*>(p));
-}
-__device__ __forceinline__ uint32_t ld_u32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
-__device__ __forceinline__ int slot_of(uint32_t k) { return (int)(k % NSLOTS); }
-__device__ __forceinline__ int slot_next(int s) { return s + 1 == NSLOTS ? 0 : s + 1; }
-
-// consumer-wide broadcast of a decision taken by consumer thread 0
-__device__ __forceinline__ bool cons_broadcast(StackSmem& sm, bool ok0) {
-  if (threadIdx.x == 0) sm.flag = ok0 ? 1 : 0;
-  named_bar(1, CONS_THREADS);
-  return sm.flag != 0;
-}
-
-// Wait (bounded, thread 0) for `n` consecutive ring fills starting at k, then
-// let every consumer thread observe the completed phases itself.
-__device__ __forceinline__ bool cons_acquire(StackSmem& sm, uint32_t k, int n) {
-  bool ok0 = true;
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < n && ok0; ++i) {
-      const uint32_t f = k + i;
-      ok0 = mbar_wait(&sm.full[f % NSLOTS], (f / NSLOTS) & 1u, WAIT_LIMIT_NS);
-    }
-    if (!ok0) sm.abort = 1;
-  }
-  const bool ok = cons_broadcast(sm, ok0);
-  if (ok) {
-    for (int i = 0; i < n; ++i) {
-      const uint32_t f = k + i;
-      while (!mbar_try_wait(&sm.full[f % NSLOTS], (f / NSLOTS) & 1u)) {
-      }
-    }
-  }
-  return ok;
-}
-// Every thread waits (bounded) for the group's fills itself; a thread whose
-// wait expires flags the abort, which all threads read right after the
-// group's barrier, so control flow stays uniform across named barriers.
-__device__ __forceinline__ void cons_wait_group(StackSmem& sm, uint32_t k, int n, uint64_t* waited) {
-  const uint64_t t0 = (waited != nullptr) ? globaltimer_ns() : 0;
-  int s = slot_of(k);
-  uint32_t par = (k / NSLOTS) & 1u;
-  for (int i = 0; i < n; ++i) {
-    if (!mbar_wait(&sm.full[s], par, WAIT_LIMIT_NS)) {
-      sm.abort = 1;
-      return;
-    }
-    s = slot_next(s);
-    if (s == 0) par ^= 1u;
-  }
-  if (waited != nullptr) *waited += globaltimer_ns() - t0;
-}
-__device__ __forceinline__ void cons_release(StackSmem& sm, uint32_t k, int n) {
-  __syncwarp();
-  if ((threadIdx.x & 31) == 0) {
-    int s = slot_of(k);
-    for (int i = 0; i < n; ++i) {
-      mbar_arrive(&sm.empty[s]);
-      s = slot_next(s);
-    }
-  }
-}
-
-// block reduction over the consumer threads (result in every thread)
-__device__ __forceinline__ float cons_sum(StackSmem& sm, float a) {
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-  const int warp = threadIdx.x >> 5;
-  named_bar(1, CONS_THREADS);
-  if ((threadIdx.x & 31) == 0) sm.zred[warp] = a;
-  named_bar(1, CONS_THREADS);
-  a = 0.0f;
-#pragma unroll
-  for (int w = 0; w < NWARPS; ++w) a += sm.zred[w];
-  return a;
-}
-
-// Thread t of the consumer group owns elements [8t, 8t+8) of x and y.  Its
-// x is kept in registers as f16 pairs in the orders the decoders produce:
-// xf8[i] = (x[2i], x[2i+1]) for FP8 rows; for an INT4 word xi4 = {(x0,x4),
-// (x1,x5), (x2,x6), (x3,x7)}, and xoff = 1032*(x0+x2+x4+x6) + 72*(x1+x3+x5+x7)
-// removes the decoding bias (see int4_pairs).
-struct XRegs {
-  uint32_t xf8[4];
-  uint32_t xi4[4];
-  float xoff;
-};
-
-// CTA reduction of 2*NBM per-thread partials (values: gate 0..NBM-1, then up
-// 0..NBM-1): a warp-level multi-value reduction, one barrier, then lanes
-// j < 2*NBM of every warp sum the NWARPS warp partials of value j.
-template <int NBM>
-__device__ __forceinline__ float group_reduce(StackSmem& sm, int buf, float (&v)[2 * NBM], bool& abort_seen) {
-  constexpr int V = 2 * NBM;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const float r = warp_reduce_multi<V>(v);
-  constexpr int SH = 5 - (V == 16 ? 4 : V == 8 ? 3 : V == 4 ? 2 : 1);
-  if ((lane & ((1 << SH) - 1)) == 0) sm.red[buf][warp][lane >> SH] = r;
-  named_bar(1, CONS_THREADS);
-  abort_seen = sm.abort != 0;      // sampled right after the barrier: identical in every thread
-  float s = 0.0f;
-  if (lane < V) {
-#pragma unroll
-    for (int w = 0; w < NWARPS; ++w) s += sm.red[buf][w][lane];
-  }
-  return s;
-}
-
-// 8 FP8 weights (one uint2) dotted with the thread's x: two fp32 chains
-__device__ __forceinline__ float dot8_fp8(uint2 w, const XRegs& x) {
-  float a = 0.0f, b = 0.0f;
-  fma2_f16f16_f32(a, b, e4m3x2_to_f16x2(w.x), x.xf8[0]);
-  fma2_f16f16_f32(a, b, e4m3x2_to_f16x2(w.x >> 16), x.xf8[1]);
-  fma2_f16f16_f32(a, b, e4m3x2_to_f16x2(w.y), x.xf8[2]);
-  fma2_f16f16_f32(a, b, e4m3x2_to_f16x2(w.y >> 16), x.xf8[3]);
-  return a + b;
-}
-
-// One packed INT4 word (8 signed nibbles, element i in bits 4i..4i+3) as four
-// f16 pairs with a bias, using one shift and four LOP3s (the sign flip is
-// folded into the LOP3 constant):
-//   h[0] = (1032+q0, 1032+q4)  h[1] = (1152+16q1, 1152+16q5)
-//   h[2] = (1032+q2, 1032+q6)  h[3] = (1152+16q3, 1152+16q7)
-__device__ __forceinline__ void int4_pairs(uint32_t w, uint32_t (&h)[4]) {
-  const uint32_t w8 = w >> 8;
-  h[0] = (w & 0x000F000Fu) ^ 0x64086408u;
-  h[1] = (w & 0x00F000F0u) ^ 0x64806480u;
-  h[2] = (w8 & 0x000F000Fu) ^ 0x64086408u;
-  h[3] = (w8 & 0x00F000F0u) ^ 0x64806480u;
-}
-// sum over the word of q_i * x_i (bias removed with x.xoff)
-__device__ __forceinline__ float dot8_int4(uint32_t w, const XRegs& x) {
-  uint32_t h[4];
-  int4_pairs(w, h);
-  float a0 = 0.0f, a1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
-  fma2_f16f16_f32(a0, a1, h[0], x.xi4[0]);
-  fma2_f16f16_f32(b0, b1, h[1], x.xi4[1]);
-  fma2_f16f16_f32(a0, a1, h[2], x.xi4[2]);
-  fma2_f16f16_f32(b0, b1, h[3], x.xi4[3]);
-  return fmaf(b0 + b1, 0.0625f, a0 + a1) - x.xoff;
-}
-// the thread's 8 INT4 elements of a record field: bytes [2 + 4t, 6 + 4t)
-__device__ __forceinline__ uint32_t ld_int4x8(const uint8_t* field4t) {
-  return shift2(ld_u32(field4t), ld_u32(field4t + 4));
-}
-
-// Hot group: nb (<= NB_HOT) FP8 neurons in ring fills ck .. ck+nb-1.
-__device__ __forceinline__ bool hot_group(StackSmem& sm, const StackParams& p, const float* hot_scale,
-                                          int64_t h_first, int nb, uint32_t ck, int buf, const XRegs& x,
-                                          float (&y)[EPT], uint64_t* waited) {
-  const int t = threadIdx.x, lane = t & 31;
-  float sg = 1.0f, su = 1.0f, sd = 1.0f;
-  if (hot_scale != nullptr && lane < nb) {
-    const float* s3 = hot_scale + (h_first + lane) * 3;
-    sg = __ldg(s3);
-    su = __ldg(s3 + 1);
-    sd = __ldg(s3 + 2);
-  }
-  const uint8_t* slot[NB_HOT];
-  {
-    int s = slot_of(ck);
-#pragma unroll
-    for (int j = 0; j < NB_HOT; ++j) {
-      slot[j] = sm.ring[s] + EPT * t;
-      s = slot_next(s);
-    }
-  }
-  cons_wait_group(sm, ck, nb, waited);
-  float v[2 * NB_HOT];
-#pragma unroll
-  for (int j = 0; j < NB_HOT; ++j) {
-    v[j] = 0.0f;
-    v[NB_HOT + j] = 0.0f;
-    if (j < nb) {
-      v[j] = dot8_fp8(*reinterpret_cast<const uint2*>(slot[j]), x);
-      v[NB_HOT + j] = dot8_fp8(*reinterpret_cast<const uint2*>(slot[j] + H), x);
-    }
-  }
-  bool abort_seen;
-  const float s = group_reduce<NB_HOT>(sm, buf, v, abort_seen);
-  if (abort_seen) return true;
-  const float uu = __shfl_down_sync(0xffffffffu, s, NB_HOT);   // lane j < nb: gate j, lane NB_HOT + j: up j
-  float a = 0.0f;
-  if (lane < nb) a = gated(s * sg, uu * su, p.relu, p.both) * sd;
-#pragma unroll
-  for (int n = 0; n < NB_HOT; ++n) {
-    const float an = __shfl_sync(0xffffffffu, a, n);
-    if (n < nb) {
-      const unsigned short a16 = __half_as_ushort(__float2half_rn(an));
-      const uint2 dw = *reinterpret_cast<const uint2*>(slot[n] + 2 * H);
-      fma2_f16_f32(y[0], y[1], e4m3x2_to_f16x2(dw.x), a16);
-      fma2_f16_f32(y[2], y[3], e4m3x2_to_f16x2(dw.x >> 16), a16);
-      fma2_f16_f32(y[4], y[5], e4m3x2_to_f16x2(dw.y), a16);
-      fma2_f16_f32(y[6], y[7], e4m3x2_to_f16x2(dw.y >> 16), a16);
-    }
-  }
-  cons_release(sm, ck, nb);
-  return false;
-}
-
-// Cold group: nb (<= NB) INT4 records, two per ring fill.
-__device__ __forceinline__ bool cold_group(StackSmem& sm, const StackParams& p, int nb, uint32_t ck, int buf,
-                                           const XRegs& x, float (&y)[EPT], uint64_t* waited) {
-  const int t = threadIdx.x, lane = t & 31;
-  const int gs = 2 * (t >> 4);   // byte offset of this thread's INT4 group scale
-  const int nslots = (nb + 1) >> 1;
-  const uint8_t* rec[NB];
-  {
-    int s = slot_of(ck);
-#pragma unroll
-    for (int j = 0; j < NB; j += 2) {
-      rec[j] = sm.ring[s];
-      rec[j + 1] = sm.ring[s] + REC_SLOT_OFF;
-      s = slot_next(s);
-    }
-  }
-  cons_wait_group(sm, ck, nslots, waited);
-  float v[2 * NB];
-#pragma unroll
-  for (int j = 0; j < NB; ++j) {
-    v[j] = 0.0f;
-    v[NB + j] = 0.0f;
-    if (j < nb) {
-      v[j] = dot8_int4(ld_int4x8(rec[j] + 4 * t), x) * ld_half(rec[j] + SCALE_OFF + gs);
-      v[NB + j] = dot8_int4(ld_int4x8(rec[j] + VEC_BYTES + 4 * t), x) * ld_half(rec[j] + SCALE_OFF + 2 * NGROUPS + gs);
-    }
-  }
-  bool abort_seen;
-  const float s = group_reduce<NB>(sm, buf, v, abort_seen);
-  if (abort_seen) return true;
-  const float uu = __shfl_down_sync(0xffffffffu, s, NB);
-  float a = 0.0f;
-  if (lane < nb) a = gated(s, uu, p.relu, p.both);
-  float csa = 0.0f, csb = 0.0f;   // sums of the f16 coefficients (the down rows carry a decoding bias)
-#pragma unroll
-  for (int n = 0; n < NB; ++n) {
-    const float an = __shfl_sync(0xffffffffu, a, n);
-    if (n < nb) {
-      const __half c16 = __float2half_rn(an * ld_half(rec[n] + SCALE_OFF + 4 * NGROUPS + gs));
-      const __half c16s = __hmul(c16, __float2half(0.0625f));    // exact unless subnormal; csb tracks it
-      csa += __half2float(c16);
-      csb += __half2float(c16s);
-      uint32_t h[4];
-      int4_pairs(ld_int4x8(rec[n] + 2 * VEC_BYTES + 4 * t), h);
-      const unsigned short cb = __half_as_ushort(c16), cs = __half_as_ushort(c16s);
-      fma2_f16_f32(y[0], y[4], h[0], cb);   // (1032 + q) * c
-      fma2_f16_f32(y[1], y[5], h[1], cs);   // (1152 + 16 q) * c / 16
-      fma2_f16_f32(y[2], y[6], h[2], cb);
-      fma2_f16_f32(y[3], y[7], h[3], cs);
-    }
-  }
-  // remove the decoding bias: 1032 * c for even elements, 1152 * (c / 16) for odd ones
-#pragma unroll
-  for (int j = 0; j < EPT; ++j) y[j] = (j & 1) ? fmaf(-1152.0f, csb, y[j]) : fmaf(-1032.0f, csa, y[j]);
-  cons_release(sm, ck, nslots);
-  return false;
-}
-
-// grid barrier: arrive (after this CTA's atomics) ...
-__device__ __forceinline__ void grid_arrive(const StackParams& p) {
-  named_bar(1, CONS_THREADS);
-  if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(p.bar_count, 1u);
-  }
-}
-// ... and wait (thread 0 spins, bounded; result broadcast)
-__device__ bool grid_wait(StackSmem& sm, const StackParams& p, uint32_t target) {
-  bool ok0 = true;
-  if (threadIdx.x == 0) {
-    if (ld_acquire_u32(p.bar_count) < target) {
-      const uint64_t t0 = globaltimer_ns();
-      uint32_t spins = 0;
-      while (ld_acquire_u32(p.bar_count) < target) {
-        if ((++spins & 255) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
-          ok0 = false;
-          break;
-        }
-        __nanosleep(32);
-      }
-    }
-    __threadfence();
-    if (!ok0) {
-      sm.abort = 1;
-      atomicOr(p.status, HC_ERR_TIMEOUT);
-    }
-  }
-  return cons_broadcast(sm, ok0);
+__device__ __forceinline__ int ld_vol(const int32_t* p) { return *reinterpret_cast<const volatile int32_t*>(p); }
+__device__ __forceinline__ uint32_t ld_vol_u(const uint32_t* p) {
+  return *reinterpret_cast<const volatile uint32_t*>(p);
 }
 
 // --------------------------------------------------------------------------
-// producer helpers
+// per-layer work split of CTA c (shared by all roles)
 // --------------------------------------------------------------------------
-struct Producer {
-  uint32_t k = 0;       // fills issued
-  uint64_t pol = 0;
-  bool ok = true;
-};
-
-// issuer lane 0: take the next slot (bounded wait for it to be empty)
-__device__ __forceinline__ uint8_t* prod_slot(StackSmem& sm, Producer& pr, uint32_t bytes, uint64_t* waited) {
-  const uint32_t s = pr.k % NSLOTS;
-  const uint32_t round = pr.k / NSLOTS;
-  if (round > 0) {
-    const uint64_t t0 = (waited != nullptr) ? globaltimer_ns() : 0;
-    if (!mbar_wait(&sm.empty[s], (round - 1) & 1u, WAIT_LIMIT_NS)) {
-      pr.ok = false;
-      return nullptr;
-    }
-    if (waited != nullptr) *waited += globaltimer_ns() - t0;
-  }
-  mbar_arrive_expect_tx(&sm.full[s], bytes);
-  return sm.ring[s];
-}
-
-// per-layer work split of CTA c (shared by all three roles)
 struct Split {
-  int64_t h0, h1;       // hot neurons
+  int64_t h0, h1;       // static hot neurons
+  int64_t n_static;     // hot neurons [n_static, n_hot) are claimed dynamically
   int u0, u1;           // own W_up tiles == own mask words (neuron ids [32 u0, 32 u1))
   int d0, d1;           // W_down tiles of the next layer's predictor
 };
 __device__ __forceinline__ Split make_split(const StackParams& p, const hc_layer_desc& d, bool pred_next, int c,
                                             int G) {
   Split s;
-  s.h0 = split_lo(d.n_hot, c, G);
-  s.h1 = split_lo(d.n_hot, c + 1, G);
+  s.n_static = d.n_hot / STATIC_HOT_DIV;
+  s.h0 = split_lo(s.n_static, c, G);
+  s.h1 = split_lo(s.n_static, c + 1, G);
   s.u0 = (int)split_lo(p.words, c, G);
   s.u1 = (int)split_lo(p.words, c + 1, G);
   const int nd = H / WD_ROWS;
@@ -463,106 +200,556 @@ __device__ __forceinline__ bool next_pred(const StackParams& p, int l) {
 }
 
 // --------------------------------------------------------------------------
+// consumer helpers
+// --------------------------------------------------------------------------
+__device__ __forceinline__ float ld_half(const uint8_t* p) {
+  return __half2float(*reinterpret_cast<const __half*>(p));
+}
+__device__ __forceinline__ bool cons_broadcast(StackSmem& sm, bool ok0) {
+  if (threadIdx.x == 0) sm.flag = ok0 ? 1 : 0;
+  named_bar(1, CONS_THREADS);
+  return sm.flag != 0;
+}
+// sum over the 512 consumer threads (result in every thread)
+__device__ __forceinline__ float cons_sum(StackSmem& sm, float a) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+  named_bar(1, CONS_THREADS);
+  if ((threadIdx.x & 31) == 0) sm.zred[threadIdx.x >> 5] = a;
+  named_bar(1, CONS_THREADS);
+  a = 0.0f;
+#pragma unroll
+  for (int w = 0; w < NWARPS; ++w) a += sm.zred[w];
+  return a;
+}
+
+// One thread polls ring position q (entry e, phase parity par).  Returns 1
+// when it holds a fill of layer l, 0 when layer l's stream ended before it
+// (the fill belongs to the next layer, or the issuer sealed layer l with
+// fewer groups), -1 when the wait limit passed.  A fill counts once the
+// entry's info names q: the issuer writes it only after the entry's previous
+// fill was consumed, so the mbarrier parity test that follows is exact.
+__device__ __forceinline__ int poll_pos(StackSmem& sm, uint32_t q, int e, uint32_t par, int l, int gi,
+                                        uint64_t* waited) {
+  if (mbar_test_wait(&sm.full[e], par) && ld_vol_u(&sm.info[e].pos) == q && mbar_test_wait(&sm.full[e], par))
+    return (sm.info[e].layer == l) ? 1 : 0;
+  const uint64_t c0 = (waited != nullptr) ? (uint64_t)clock64() : 0;
+  const uint64_t t0 = globaltimer_ns();
+  int r = -1;
+  for (uint32_t i = 0;; ++i) {
+    // suspends until the phase completes or ~200 ns pass
+    if (mbar_try_wait_hint(&sm.full[e], par, 200) && ld_vol_u(&sm.info[e].pos) == q &&
+        mbar_test_wait(&sm.full[e], par)) {
+      r = (sm.info[e].layer == l) ? 1 : 0;
+      break;
+    }
+    if (ld_vol(&sm.sealed) >= l) {
+      __threadfence_block();
+      if (gi >= ld_vol(&sm.ngroups[l & 3])) {
+        r = 0;
+        break;
+      }
+    }
+    if ((i & 15) == 15 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) break;
+  }
+  if (waited != nullptr) *waited += (uint64_t)clock64() - c0;
+  return r;
+}
+// every thread observes the (already completed) fill itself
+__device__ __forceinline__ void observe_pos(StackSmem& sm, int e, uint32_t par) {
+  while (!mbar_test_wait(&sm.full[e], par)) {
+  }
+}
+__device__ __forceinline__ void sg_release(StackSmem& sm, int e) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(&sm.empty[e]);
+}
+
+// Subgroup reduction of V per-thread partials: warp-level multi-value
+// reduction, one subgroup barrier, then lanes j < V of every warp sum the
+// SG_WARPS warp partials of value j.
+template <int V>
+__device__ __forceinline__ float sg_reduce(StackSmem& sm, int sg, int buf, float (&v)[V]) {
+  const int lane = threadIdx.x & 31, w = (threadIdx.x >> 5) & (SG_WARPS - 1);
+  const float r = warp_reduce_multi<V>(v);
+  constexpr int SH = 5 - (V == 16 ? 4 : V == 8 ? 3 : V == 4 ? 2 : 1);
+  if ((lane & ((1 << SH) - 1)) == 0) sm.red[sg][buf][w][lane >> SH] = r;
+  named_bar(2 + sg, SG_THREADS);
+  float s = 0.0f;
+  if (lane < V) {
+#pragma unroll
+    for (int k = 0; k < SG_WARPS; ++k) s += sm.red[sg][buf][k][lane];
+  }
+  return s;
+}
+
+// Subgroup-thread copy of the layer's normalised input as fixed point: for
+// word j (elements 8j..8j+7 of the thread's 32) d[4j..4j+3] = high digits of
+// the even / odd elements (signed bytes), low digits of the even / odd
+// elements (unsigned bytes); x = (256 * high + low) * 2^-s.
+struct XFix {
+  uint32_t d[16];
+  int corr;      // -8 * sum of the 32 fixed-point values (removes the +8 nibble bias)
+  float scale;   // 2^-s
+};
+
+// The thread's 32 INT4 elements of a record field (bytes [2 + 16u, 18 + 16u)
+// of the field, which starts 2 bytes past a 16-byte boundary) as 4 words.
+__device__ __forceinline__ void int4_words(const uint8_t* aligned, uint32_t (&w)[4]) {
+  const uint4 a = *reinterpret_cast<const uint4*>(aligned);
+  uint32_t e = __shfl_down_sync(0xffffffffu, a.x, 1);      // lane i+1 holds bytes [16, 20) of lane i
+  if ((threadIdx.x & 31) == 31) e = *reinterpret_cast<const uint32_t*>(aligned + 16);
+  w[0] = shift2(a.x, a.y);
+  w[1] = shift2(a.y, a.z);
+  w[2] = shift2(a.z, a.w);
+  w[3] = shift2(a.w, e);
+}
+
+// INT4 field (32 elements) dotted with x: exact integer sum, one float scale
+__device__ __forceinline__ float dot32_int4(const uint8_t* aligned, const XFix& xf) {
+  uint32_t w[4];
+  int4_words(aligned, w);
+  int acc_h = 0;
+  uint32_t acc_l = (uint32_t)xf.corr;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t lo = (w[j] & 0x0F0F0F0Fu) ^ 0x08080808u;          // elements 0,2,4,6 as q + 8
+    const uint32_t hi = ((w[j] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;   // elements 1,3,5,7 as q + 8
+    acc_h = dp4a_us(lo, xf.d[4 * j + 0], acc_h);
+    acc_h = dp4a_us(hi, xf.d[4 * j + 1], acc_h);
+    acc_l = dp4a_uu(lo, xf.d[4 * j + 2], acc_l);
+    acc_l = dp4a_uu(hi, xf.d[4 * j + 3], acc_l);
+  }
+  return (float)(int)((uint32_t)acc_h * 256u + acc_l) * xf.scale;
+}
+
+// One packed INT4 word (8 signed nibbles, element i in bits 4i..4i+3) as four
+// f16 pairs with a bias, using one shift and four LOP3s (the sign flip is
+// folded into the LOP3 constant):
+//   h[0] = (1032+q0, 1032+q4)  h[1] = (1152+16q1, 1152+16q5)
+//   h[2] = (1032+q2, 1032+q6)  h[3] = (1152+16q3, 1152+16q7)
+__device__ __forceinline__ void int4_pairs(uint32_t w, uint32_t (&h)[4]) {
+  const uint32_t w8 = w >> 8;
+  h[0] = (w & 0x000F000Fu) ^ 0x64086408u;
+  h[1] = (w & 0x00F000F0u) ^ 0x64806480u;
+  h[2] = (w8 & 0x000F000Fu) ^ 0x64086408u;
+  h[3] = (w8 & 0x00F000F0u) ^ 0x64806480u;
+}
+
+// y += c * q over the thread's 32 elements of an INT4 down row (biased: the
+// caller removes 1032 * c from even and 1152 * c/16 from odd elements)
+__device__ __forceinline__ void axpy32_int4(const uint8_t* aligned, unsigned short cb, unsigned short cs,
+                                            float (&y)[SPT]) {
+  uint32_t w[4];
+  int4_words(aligned, w);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t h[4];
+    int4_pairs(w[j], h);
+    fma2_f16_f32(y[8 * j + 0], y[8 * j + 4], h[0], cb);
+    fma2_f16_f32(y[8 * j + 1], y[8 * j + 5], h[1], cs);
+    fma2_f16_f32(y[8 * j + 2], y[8 * j + 6], h[2], cb);
+    fma2_f16_f32(y[8 * j + 3], y[8 * j + 7], h[3], cs);
+  }
+}
+
+// 32 FP8 weights dotted with 32 f16 x (pairs in xp): two fp32 chains
+__device__ __forceinline__ float dot32_fp8(const uint8_t* row, const uint32_t (&xp)[16]) {
+  const uint4 a = *reinterpret_cast<const uint4*>(row);
+  const uint4 b = *reinterpret_cast<const uint4*>(row + 16);
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    fma2_f16f16_f32(s0, s1, e4m3x2_to_f16x2(w[i]), xp[2 * i]);
+    fma2_f16f16_f32(s0, s1, e4m3x2_to_f16x2(w[i] >> 16), xp[2 * i + 1]);
+  }
+  return s0 + s1;
+}
+__device__ __forceinline__ void axpy32_fp8(const uint8_t* row, unsigned short a16, float (&y)[SPT]) {
+  const uint4 a = *reinterpret_cast<const uint4*>(row);
+  const uint4 b = *reinterpret_cast<const uint4*>(row + 16);
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    fma2_f16_f32(y[4 * i + 0], y[4 * i + 1], e4m3x2_to_f16x2(w[i]), a16);
+    fma2_f16_f32(y[4 * i + 2], y[4 * i + 3], e4m3x2_to_f16x2(w[i] >> 16), a16);
+  }
+}
+
+// Hot group: n (<= NB_HOT) FP8 neurons, one per slot.
+__device__ __forceinline__ void sg_hot(StackSmem& sm, const StackParams& p, const float* hot_scale,
+                                       const uint8_t* slot0, const uint8_t* slot1, int n, int64_t i0, int sg, int buf,
+                                       float (&y)[SPT]) {
+  const int u = threadIdx.x & (SG_THREADS - 1), lane = threadIdx.x & 31;
+  uint32_t xp[16];
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(sm.xh + SPT * u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 v = src[i];
+      xp[4 * i] = v.x; xp[4 * i + 1] = v.y; xp[4 * i + 2] = v.z; xp[4 * i + 3] = v.w;
+    }
+  }
+  float v[2 * NB_HOT];
+  v[0] = dot32_fp8(slot0 + SPT * u, xp);
+  v[NB_HOT] = dot32_fp8(slot0 + H + SPT * u, xp);
+  v[1] = 0.0f;
+  v[NB_HOT + 1] = 0.0f;
+  if (n > 1) {
+    v[1] = dot32_fp8(slot1 + SPT * u, xp);
+    v[NB_HOT + 1] = dot32_fp8(slot1 + H + SPT * u, xp);
+  }
+  const float s = sg_reduce<2 * NB_HOT>(sm, sg, buf, v);
+  const float uu = __shfl_down_sync(0xffffffffu, s, NB_HOT);   // lane j < n: gate j, lane NB_HOT + j: up j
+  float a = 0.0f;
+  if (lane < n) {
+    float sgs = 1.0f, sus = 1.0f, sds = 1.0f;
+    if (hot_scale != nullptr) {
+      const float* s3 = hot_scale + (i0 + lane) * 3;
+      sgs = __ldg(s3);
+      sus = __ldg(s3 + 1);
+      sds = __ldg(s3 + 2);
+    }
+    a = gated(s * sgs, uu * sus, p.relu, p.both) * sds;
+  }
+  const float a0 = __shfl_sync(0xffffffffu, a, 0), a1 = __shfl_sync(0xffffffffu, a, 1);
+  axpy32_fp8(slot0 + 2 * H + SPT * u, __half_as_ushort(__float2half_rn(a0)), y);
+  if (n > 1) axpy32_fp8(slot1 + 2 * H + SPT * u, __half_as_ushort(__float2half_rn(a1)), y);
+}
+
+// Cold group: n (<= NB_COLD) INT4 records, two per slot.
+__device__ __forceinline__ void sg_cold(StackSmem& sm, const StackParams& p, const uint8_t* slot0,
+                                        const uint8_t* slot1, int n, int sg, int buf, float (&y)[SPT]) {
+  const int u = threadIdx.x & (SG_THREADS - 1), lane = threadIdx.x & 31;
+  XFix xf;
+  {
+    const uint4* src = sm.xq + 4 * u;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 v = src[j];
+      xf.d[4 * j] = v.x; xf.d[4 * j + 1] = v.y; xf.d[4 * j + 2] = v.z; xf.d[4 * j + 3] = v.w;
+    }
+    const int2 ch = sm.chunk[u];
+    xf.corr = ch.x;
+    xf.scale = __int_as_float(ch.y);
+  }
+  const int gs = 2 * (u >> 2);                 // byte offset of this thread's INT4 group scale
+  const uint8_t* rec[NB_COLD] = {slot0, slot0 + REC_SLOT_OFF, slot1, slot1 + REC_SLOT_OFF};
+  float v[2 * NB_COLD];
+#pragma unroll
+  for (int j = 0; j < NB_COLD; ++j) {
+    v[j] = 0.0f;
+    v[NB_COLD + j] = 0.0f;
+    if (j < n) {
+      v[j] = dot32_int4(rec[j] + 16 * u, xf) * ld_half(rec[j] + SCALE_OFF + gs);
+      v[NB_COLD + j] = dot32_int4(rec[j] + VEC_BYTES + 16 * u, xf) * ld_half(rec[j] + SCALE_OFF + 2 * NGROUPS + gs);
+    }
+  }
+  const float s = sg_reduce<2 * NB_COLD>(sm, sg, buf, v);
+  const float uu = __shfl_down_sync(0xffffffffu, s, NB_COLD);
+  float a = 0.0f;
+  if (lane < n) a = gated(s, uu, p.relu, p.both);
+  float csa = 0.0f, csb = 0.0f;   // sums of the f16 coefficients (the decoded rows carry a bias)
+#pragma unroll
+  for (int j = 0; j < NB_COLD; ++j) {
+    const float aj = __shfl_sync(0xffffffffu, a, j);
+    if (j < n) {
+      const __half c16 = __float2half_rn(aj * ld_half(rec[j] + SCALE_OFF + 4 * NGROUPS + gs));
+      const __half c16s = __hmul(c16, __float2half(0.0625f));    // exact unless subnormal; csb tracks it
+      csa += __half2float(c16);
+      csb += __half2float(c16s);
+      axpy32_int4(rec[j] + 2 * VEC_BYTES + 16 * u, __half_as_ushort(c16), __half_as_ushort(c16s), y);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < SPT; ++k) y[k] = (k & 1) ? fmaf(-1152.0f, csb, y[k]) : fmaf(-1032.0f, csa, y[k]);
+}
+
+// W_up group: n (<= 2) tiles of layer ln's predictor -> own mask words of layer ln.
+// Its bottleneck z is complete once all WD_TILES W_down tiles were added.
+__device__ __forceinline__ void sg_wup(StackSmem& sm, const StackParams& p, int rank, const uint8_t* slot0,
+                                       const uint8_t* slot1, int n, int tile0, int u0, int ln, int sg) {
+  const int u = threadIdx.x & (SG_THREADS - 1), lane = threadIdx.x & 31, w = u >> 5;
+  float* z = sm.ystage + sg * 128;
+  if (u == 0) {
+    const uint32_t* cnt = p.zdone + ln % NACC;
+    if (ld_acquire_u32(cnt) < (uint32_t)WD_TILES) {
+      const uint64_t t0 = globaltimer_ns();
+      uint32_t i = 0;
+      while (ld_acquire_u32(cnt) < (uint32_t)WD_TILES) {
+        if ((++i & 63) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+          sm.abort = 1;
+          atomicOr(p.status, HC_ERR_TIMEOUT);
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    __threadfence();
+  }
+  named_bar(2 + sg, SG_THREADS);
+  if (u < rank) z[u] = __ldcg(p.zacc + (size_t)(ln % NACC) * 128 + u);
+  named_bar(2 + sg, SG_THREADS);
+  const int per = rank >> 2;                    // 4 threads per neuron
+  const int j = u >> 2, part = u & 3;
+  for (int k = 0; k < n; ++k) {
+    const int tile = tile0 + k;
+    const float* t = reinterpret_cast<const float*>(k == 0 ? slot0 : slot1);
+    const int rows = min(WU_ROWS, p.inter - tile * WU_ROWS);
+    float acc = 0.0f;
+    if (j < rows) {
+      const float2* wr = reinterpret_cast<const float2*>(t + j * rank + part * per);
+      const float2* zr = reinterpret_cast<const float2*>(z + part * per);
+      const int half = per >> 1;
+      int ii = j % half;                        // rows of a warp start at different banks
+      for (int i = 0; i < half; ++i) {
+        const float2 a = wr[ii], b = zr[ii];
+        acc = fmaf(a.x, b.x, acc);
+        acc = fmaf(a.y, b.y, acc);
+        ii = (ii + 1 == half) ? 0 : ii + 1;
+      }
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    const float lg = acc + ((j < rows) ? t[WU_ROWS * rank + j] : 0.0f);
+    const bool on = (j < rows) && (lg >= p.thr);
+    const unsigned b = __ballot_sync(0xffffffffu, on && part == 0);
+    if (lane == 0) {
+      uint32_t byte = 0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) byte |= ((b >> (4 * q)) & 1u) << q;
+      reinterpret_cast<uint8_t*>(sm.own_words)[4 * (tile - u0) + w] = (uint8_t)byte;
+    }
+  }
+  named_bar(2 + sg, SG_THREADS);
+  if (u == 0) {
+    const uint32_t w0 = sm.own_words[tile0 - u0];
+    const uint32_t w1 = (n > 1) ? sm.own_words[tile0 + 1 - u0] : 0u;
+    __threadfence_block();
+    if (atomicSub(&sm.wup_left, n) == n) {
+      mbar_arrive(&sm.own_ready);
+      trace_ev(p, ln, 21);
+    }
+    uint32_t* mrow = p.masks + (size_t)ln * p.words;
+    mrow[tile0] = w0;
+    if (n > 1) mrow[tile0 + 1] = w1;
+  }
+}
+
+// W_down group: n (<= 2) tiles of layer l+1's predictor -> z partials, then
+// the tiles are counted in zdone (after the partials are visible).
+__device__ __forceinline__ void sg_wdown(StackSmem& sm, const StackParams& p, const float* xs,
+                                         const uint8_t* slot0, const uint8_t* slot1, int n, int tile0, int d0,
+                                         int rank_n, int l, int sg) {
+  const int u = threadIdx.x & (SG_THREADS - 1);
+  const int parts = SG_THREADS / rank_n, r = u % rank_n, part = u / rank_n;
+  if (part < parts) {
+    float acc = 0.0f;
+    for (int k = 0; k < n; ++k) {
+      const float* t = reinterpret_cast<const float*>(k == 0 ? slot0 : slot1);
+      const float* xr = xs + (tile0 + k - d0) * WD_ROWS;
+      for (int row = part; row < WD_ROWS; row += parts) acc = fmaf(t[row * rank_n + r], xr[row], acc);
+    }
+    atomicAdd(p.zacc + (size_t)((l + 1) % NACC) * 128 + r, acc);
+  }
+  named_bar(2 + sg, SG_THREADS);
+  if (u == 0) {
+    __threadfence();
+    atomicAdd(p.zdone + (l + 1) % NACC, (uint32_t)n);
+  }
+}
+
+// grid barrier: arrive (after this CTA's atomics) ...
+__device__ __forceinline__ void grid_arrive(const StackParams& p) {
+  named_bar(1, CONS_THREADS);
+  if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar_count) : "memory");
+}
+// ... and wait (thread 0 spins, bounded; result broadcast)
+__device__ bool grid_wait(StackSmem& sm, const StackParams& p, uint32_t target) {
+  bool ok0 = true;
+  if (threadIdx.x == 0) {
+    if (ld_acquire_u32(p.bar_count) < target) {
+      const uint64_t t0 = globaltimer_ns();
+      uint32_t spins = 0;
+      while (ld_acquire_u32(p.bar_count) < target) {
+        if ((++spins & 255) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+          ok0 = false;
+          break;
+        }
+        __nanosleep(32);
+      }
+    }
+    __threadfence();
+    if (!ok0 || ld_vol(&sm.abort) != 0) {
+      ok0 = false;
+      sm.abort = 1;
+      atomicOr(p.status, HC_ERR_TIMEOUT);
+    }
+  }
+  return cons_broadcast(sm, ok0);
+}
+
+// --------------------------------------------------------------------------
+// issuer helpers
+// --------------------------------------------------------------------------
+struct Producer {
+  uint32_t k = 0;       // ring positions issued
+  uint64_t pol = 0;
+  bool ok = true;
+};
+
+// Take the next ring position (bounded wait for its entry to be empty), write
+// its info, arm its mbarrier with the group's bytes and start the copies.
+struct Copy {
+  const void* src;
+  uint32_t bytes;
+  uint32_t off;      // destination offset in the entry
+};
+template <int NCP>
+__device__ __forceinline__ void issue_entry(StackSmem& sm, uint8_t* ring, Producer& pr, int l, uint8_t kind, int n,
+                                            int64_t index, const Copy (&cp)[NCP], uint64_t* waited) {
+  const uint32_t q = pr.k;
+  const int e = (int)(q % (uint32_t)NE);
+  const uint32_t round = q / (uint32_t)NE;
+  if (round > 0) {
+    const uint64_t t0 = (waited != nullptr) ? globaltimer_ns() : 0;
+    if (!mbar_wait(&sm.empty[e], (round - 1) & 1u, WAIT_LIMIT_NS)) {
+      pr.ok = false;
+      return;
+    }
+    if (waited != nullptr) *waited += globaltimer_ns() - t0;
+  }
+  SlotInfo& inf = sm.info[e];
+  inf.layer = (int16_t)l;
+  inf.kind = kind;
+  inf.n = (uint8_t)n;
+  inf.index = (int32_t)index;
+  *reinterpret_cast<volatile uint32_t*>(&inf.pos) = q;
+  uint8_t* dst = ring + (size_t)e * ENTRY_BYTES;
+  uint32_t total = 0;
+#pragma unroll
+  for (int i = 0; i < NCP; ++i) total += cp[i].bytes;
+  mbar_arrive_expect_tx(&sm.full[e], total);
+#pragma unroll
+  for (int i = 0; i < NCP; ++i)
+    if (cp[i].bytes) bulk_g2s(dst + cp[i].off, cp[i].src, cp[i].bytes, &sm.full[e], pr.pol);
+  ++pr.k;
+}
+
+// --------------------------------------------------------------------------
 // the kernel
 // --------------------------------------------------------------------------
 __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   StackSmem& sm = *reinterpret_cast<StackSmem*>(smem_raw);
+  uint8_t* ring = smem_raw + RING_OFF;
+  float* xs = reinterpret_cast<float*>(ring + (size_t)NE * ENTRY_BYTES);
   const int tid = threadIdx.x;
   const int G = gridDim.x;
   const int c = blockIdx.x;
 
   if (tid == 0) {
-    for (int s = 0; s < NSLOTS; ++s) {
-      mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], NWARPS);
+    for (int e = 0; e < NE; ++e) {
+      mbar_init(&sm.full[e], 1);
+      mbar_init(&sm.empty[e], SG_WARPS);
+      sm.info[e].pos = 0xFFFFFFFFu;
     }
     mbar_init(&sm.own_ready, 1);
     mbar_init(&sm.plan_full, 1);
-    mbar_init(&sm.plan_empty, 2);
+    mbar_init(&sm.plan_empty, 1);
     sm.abort = 0;
     sm.flag = 1;
-    sm.cons_k = 0;
-    sm.ballot_word = 0;
+    sm.sealed = -1;
+    sm.cons_layer = -1;
     mbar_fence_init();
   }
   __syncthreads();
 
   if (tid >= CONS_THREADS + 32) {
     // ============================ planner warp =============================
-    // Per layer: wait for the CTA's own mask words, then list the active cold
-    // ids of its neuron range in ascending order, resolve them to record
-    // indices (batched table loads) and prefetch the records into L2.
+    // Per layer: take the CTA's own mask words (from the consumers' W_up
+    // groups at the end of the previous layer, from `masks` when given or for
+    // layer 0, or all ones without a predictor), list the active cold ids of
+    // its neuron range in ascending order, resolve them to record indices and
+    // prefetch the records into L2.
     const int lane = tid & 31;
     bool ok = true;
+    // The static part of a layer's lookup (fetch_bits word and table entries
+    // of the own id range) is loaded while the previous layer runs, so only
+    // shared-memory work remains once the own mask words arrive.
+    uint32_t fetch = 0;
+    auto preload = [&](int l) {
+      const hc_layer_desc& d = p.layers[l];
+      const int u0 = (int)split_lo(p.words, c, G), u1 = (int)split_lo(p.words, c + 1, G);
+      fetch = (lane < u1 - u0) ? __ldg(d.fetch_bits + u0 + lane) : 0u;
+      const int id0 = u0 * 32, nid = min(u1 * 32, p.inter) - id0;
+      for (int i = lane; i < nid; i += 32) sm.plan_list[i] = __ldg(d.table + id0 + i);
+      __syncwarp();
+    };
+    preload(0);
+    uint32_t ready_phase = 0;
     for (int l = 0; l < p.n_layers && ok; ++l) {
-      const hc_layer_desc d = p.layers[l];
-      const Split sp = make_split(p, d, false, c, G);
+      const hc_layer_desc& dl = p.layers[l];
+      const uint8_t* cold_records = dl.cold_records;
+      const int n_records = dl.n_records;
+      const int u0 = (int)split_lo(p.words, c, G), nw = (int)split_lo(p.words, c + 1, G) - u0;
       if (l > 0) {
+        // the issuer is done with the previous list once it issued that layer's cold records
         if (lane == 0) ok = mbar_wait(&sm.plan_empty, (uint32_t)(l - 1) & 1u, WAIT_LIMIT_NS);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
+        preload(l);
       }
-      if (lane == 0) ok = mbar_wait(&sm.own_ready, (uint32_t)l & 1u, WAIT_LIMIT_NS);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      const int nw = sp.u1 - sp.u0;
-      // lane-contiguous word chunks; counts, prefix
-      const int wpl = (nw + 31) / 32;
-      const int wb = lane * wpl, we = min(nw, wb + wpl);
-      int mycnt = 0;
-      for (int w = wb; w < we; ++w) {
-        const uint32_t m = sm.own_words[w] & __ldg(d.fetch_bits + sp.u0 + w);
-        sm.own_words[w] = m;
-        mycnt += __popc(m);
-      }
-      int incl = mycnt;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int u = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += u;
-      }
-      int cnt = __shfl_sync(0xffffffffu, incl, 31);
-      if (cnt > COLD_LIST) {
-        if (lane == 0) atomicOr(p.status, HC_ERR_UNSUPPORTED);
-        cnt = COLD_LIST;
-      }
-      int rank = incl - mycnt;
-      for (int w = wb; w < we && rank < cnt; ++w) {
-        uint32_t m = sm.own_words[w];
-        while (m && rank < cnt) {
-          const int bit = __ffs(m) - 1;
-          m &= m - 1;
-          sm.plan_list[rank++] = (sp.u0 + w) * 32 + bit;
+      uint32_t own = 0;
+      uint32_t* mrow = p.masks + (size_t)l * p.words;
+      if (layer_logits(p, dl, l)) {
+        if (nw > 0) {
+          if (lane == 0) ok = mbar_wait(&sm.own_ready, ready_phase & 1u, WAIT_LIMIT_NS);
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) break;
+          ++ready_phase;
+          if (lane < nw) own = sm.own_words[lane];
         }
+      } else if (l == 0 || p.masks_given) {
+        if (lane < nw) own = __ldcg(mrow + u0 + lane);
+      } else if (lane < nw) {
+        // no predictor: fetch every cold neuron (engine.py:282-283)
+        const int valid = min(32, p.inter - 32 * (u0 + lane));
+        own = valid >= 32 ? 0xffffffffu : ((1u << valid) - 1u);
+        mrow[u0 + lane] = own;
       }
-      __syncwarp();
-      for (int i0 = 0; i0 < cnt; i0 += 32 * 4) {
-        int r[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int i = i0 + k * 32 + lane;
-          r[k] = (i < cnt) ? __ldg(d.table + sm.plan_list[i]) : 0;
-        }
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int i = i0 + k * 32 + lane;
-          if (i < cnt) {
-            if (r[k] < 0 || r[k] >= d.n_records) {
-              atomicOr(p.status, HC_ERR_RANGE);
-              r[k] = 0;
-            }
-            sm.plan_list[i] = r[k];
-            prefetch_l2(d.cold_records + (size_t)r[k] * REC_BYTES, REC_COPY);
+      if (lane == 0) trace_ev(p, l, 22);
+      // active words (nw <= OWN_WORDS = 32: one per lane), then in-place
+      // compaction word by word: word w's entries are read (one per lane)
+      // before its writes, which land below 32 (w + 1)
+      const uint32_t mw = own & fetch;
+      int cnt = 0;
+      for (int w = 0; w < nw; ++w) {
+        const uint32_t m = __shfl_sync(0xffffffffu, mw, w);
+        if (m == 0) continue;
+        const bool on = (m >> lane) & 1u;
+        int r = on ? sm.plan_list[w * 32 + lane] : 0;
+        __syncwarp();
+        if (on) {
+          if (r < 0 || r >= n_records) {
+            atomicOr(p.status, HC_ERR_RANGE);
+            r = 0;
           }
+          sm.plan_list[cnt + __popc(m & ((1u << lane) - 1u))] = r;
         }
+        cnt += __popc(m);
+        __syncwarp();
       }
-      if (lane == 0) sm.plan_n = cnt;
-      __syncwarp();
       if (lane == 0) {
+        sm.plan_n = cnt;
         mbar_arrive(&sm.plan_full);
         trace_ev(p, l, 20);
+        trace_set(p, l, 17, (uint64_t)cnt);
       }
+      // records the issuer cannot take yet (ring full) come from L2 when it can
+      for (int i = lane; i < cnt; i += 32)
+        prefetch_l2(cold_records + (size_t)sm.plan_list[i] * REC_BYTES, REC_COPY);
     }
     if (lane == 0 && !ok) {
       sm.abort = 1;
@@ -572,23 +759,44 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
     __syncthreads();
   } else if (tid >= CONS_THREADS) {
     // ============================ issuer warp ==============================
-    // Lane 0 streams the CTA's units in the consumers' order: this layer's own
-    // W_up tiles, hot neurons, the next predictor's W_down tiles, the
-    // planner's cold records.  At each layer start it prefetches the layer's
-    // static ranges into L2 so HBM keeps streaming across the grid barrier.
+    // Lane 0 streams the CTA's groups of layer l in order: the next
+    // predictor's W_down tiles, the planner's cold records, the next
+    // predictor's own W_up tiles, the static hot neurons, then hot neurons
+    // claimed from the layer's global counter until none are left; then it
+    // seals the layer.
     const int lane = tid & 31;
     Producer pr;
     if (lane == 0) {
       pr.pol = l2_evict_first_policy();
       for (int l = 0; l < p.n_layers && pr.ok; ++l) {
+        // stay at most two layers ahead of the consumers (ngroups is indexed l & 3)
+        {
+          const uint64_t t0 = globaltimer_ns();
+          uint32_t i = 0;
+          while (ld_vol(&sm.cons_layer) < l - 2) {
+            if ((++i & 63) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+              pr.ok = false;
+              break;
+            }
+          }
+          if (!pr.ok) break;
+        }
         const hc_layer_desc d = p.layers[l];
         const bool pred_next = next_pred(p, l);
-        const bool logits = layer_logits(p, d, l);
         const Split sp = make_split(p, d, pred_next, c, G);
         const hc_layer_desc* dn = pred_next ? &p.layers[l + 1] : nullptr;
         const int rank_n = pred_next ? dn->rank : 0;
+        uint64_t iw = 0;
+        uint64_t* iwp = p.trace ? &iw : nullptr;
+        int ng = 0;
         trace_ev(p, l, 10);
+        // L2 prefetch: static hot slice, a 1/G share of the dynamic hot range, next predictor tiles
         if (sp.h1 > sp.h0) prefetch_l2_range(d.hot + sp.h0 * HOT_BYTES, (size_t)(sp.h1 - sp.h0) * HOT_BYTES);
+        {
+          const int64_t nd = d.n_hot - sp.n_static;
+          const int64_t a = sp.n_static + split_lo(nd, c, G), b = sp.n_static + split_lo(nd, c + 1, G);
+          if (b > a) prefetch_l2_range(d.hot + a * HOT_BYTES, (size_t)(b - a) * HOT_BYTES);
+        }
         if (sp.d1 > sp.d0)
           prefetch_l2_range(dn->pred_w_down_t + (size_t)sp.d0 * WD_ROWS * rank_n,
                             (size_t)(sp.d1 - sp.d0) * WD_ROWS * rank_n * 4);
@@ -596,60 +804,109 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
           const int rows = min(sp.u1 * WU_ROWS, p.inter) - sp.u0 * WU_ROWS;
           prefetch_l2_range(dn->pred_w_up + (size_t)sp.u0 * WU_ROWS * rank_n, (size_t)rows * rank_n * 4);
         }
-        uint64_t iw_hot = 0, iw_cold = 0;
-        // own W_up tiles of this layer's predictor (consumed first)
-        if (logits) {
-          for (int u = sp.u0; u < sp.u1 && pr.ok; ++u) {
-            const int rows = min(WU_ROWS, p.inter - u * WU_ROWS);
-            const uint32_t wbytes = rows * d.rank * 4, bbytes = rows * 4;
-            uint8_t* dst = prod_slot(sm, pr, wbytes + bbytes, nullptr);
-            if (!dst) break;
-            uint64_t* bar = &sm.full[pr.k % NSLOTS];
-            bulk_g2s(dst, d.pred_w_up + (size_t)u * WU_ROWS * d.rank, wbytes, bar, pr.pol);
-            bulk_g2s(dst + WU_ROWS * d.rank * 4, d.pred_b_up + (size_t)u * WU_ROWS, bbytes, bar, pr.pol);
-            ++pr.k;
-          }
-        }
-        // hot neurons
-        for (int64_t i = sp.h0; i < sp.h1 && pr.ok; ++i) {
-          uint8_t* dst = prod_slot(sm, pr, HOT_BYTES, p.trace ? &iw_hot : nullptr);
-          if (!dst) break;
-          bulk_g2s(dst, d.hot + i * HOT_BYTES, HOT_BYTES, &sm.full[pr.k % NSLOTS], pr.pol);
-          ++pr.k;
-        }
-        trace_ev(p, l, 11);
-        // W_down tiles of the next layer's predictor
-        for (int u = sp.d0; u < sp.d1 && pr.ok; ++u) {
+        // W_down tiles of the next layer's predictor, two per group (first: every
+        // CTA's W_up groups wait for all of them)
+        for (int u = sp.d0; u < sp.d1 && pr.ok; u += 2) {
+          const int n = min(2, sp.d1 - u);
           const uint32_t bytes = WD_ROWS * rank_n * 4;
-          uint8_t* dst = prod_slot(sm, pr, bytes, nullptr);
-          if (!dst) break;
-          bulk_g2s(dst, dn->pred_w_down_t + (size_t)u * WD_ROWS * rank_n, bytes, &sm.full[pr.k % NSLOTS], pr.pol);
-          ++pr.k;
+          Copy cp[2];
+#pragma unroll
+          for (int k = 0; k < 2; ++k)
+            cp[k] = {k < n ? dn->pred_w_down_t + (size_t)(u + k) * WD_ROWS * rank_n : nullptr, k < n ? bytes : 0u,
+                     (uint32_t)(k * HALF_BYTES)};
+          issue_entry(sm, ring, pr, l, UNIT_WDOWN, n, u, cp, iwp);
+          ++ng;
         }
         if (!pr.ok) break;
-        trace_ev(p, l, 12);
-        // the planner's cold records, two per slot
+        // the planner's cold records of this layer, four per group
         if (!mbar_wait(&sm.plan_full, (uint32_t)l & 1u, WAIT_LIMIT_NS)) {
           pr.ok = false;
           break;
         }
-        trace_ev(p, l, 13);
+        trace_ev(p, l, 11);
         const int cnt = sm.plan_n;
-        for (int j = 0; j < cnt && pr.ok; j += 2) {
-          const int two = (j + 1 < cnt) ? 2 : 1;
-          uint8_t* dst = prod_slot(sm, pr, two * REC_COPY, p.trace ? &iw_cold : nullptr);
-          if (!dst) break;
-          uint64_t* bar = &sm.full[pr.k % NSLOTS];
-          bulk_g2s(dst, d.cold_records + (size_t)sm.plan_list[j] * REC_BYTES, REC_COPY, bar, pr.pol);
-          if (two == 2)
-            bulk_g2s(dst + REC_SLOT_OFF, d.cold_records + (size_t)sm.plan_list[j + 1] * REC_BYTES, REC_COPY, bar,
-                     pr.pol);
-          ++pr.k;
+        for (int j = 0; j < cnt && pr.ok; j += NB_COLD) {
+          const int n = min(NB_COLD, cnt - j);
+          Copy cp[NB_COLD];
+#pragma unroll
+          for (int k = 0; k < NB_COLD; ++k)
+            cp[k] = {k < n ? d.cold_records + (size_t)sm.plan_list[j + k] * REC_BYTES : nullptr,
+                     k < n ? (uint32_t)REC_COPY : 0u, (uint32_t)((k >> 1) * HALF_BYTES + (k & 1) * REC_SLOT_OFF)};
+          issue_entry(sm, ring, pr, l, UNIT_COLD, n, j, cp, iwp);
+          ++ng;
         }
+        if (!pr.ok) break;
         mbar_arrive(&sm.plan_empty);
+        trace_ev(p, l, 12);
+        // own W_up tiles of the next layer's predictor, two per group: its mask
+        // words, and so its cold list, are ready before the next layer starts
+        if (pred_next) {
+          for (int u = sp.u0; u < sp.u1 && pr.ok; u += 2) {
+            const int n = min(2, sp.u1 - u);
+            Copy cp[4];
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+              const int rows = k < n ? min(WU_ROWS, p.inter - (u + k) * WU_ROWS) : 0;
+              cp[2 * k] = {k < n ? dn->pred_w_up + (size_t)(u + k) * WU_ROWS * rank_n : nullptr,
+                           (uint32_t)(rows * rank_n * 4), (uint32_t)(k * HALF_BYTES)};
+              cp[2 * k + 1] = {k < n ? dn->pred_b_up + (size_t)(u + k) * WU_ROWS : nullptr, (uint32_t)(rows * 4),
+                               (uint32_t)(k * HALF_BYTES + WU_ROWS * rank_n * 4)};
+            }
+            issue_entry(sm, ring, pr, l, UNIT_WUP, n, u, cp, iwp);
+            ++ng;
+          }
+        }
+        // static hot neurons, two per group
+        for (int64_t i = sp.h0; i < sp.h1 && pr.ok; i += NB_HOT) {
+          const int n = (int)min((int64_t)NB_HOT, sp.h1 - i);
+          Copy cp[2];
+#pragma unroll
+          for (int k = 0; k < 2; ++k)
+            cp[k] = {k < n ? d.hot + (i + k) * HOT_BYTES : nullptr, k < n ? (uint32_t)HOT_BYTES : 0u,
+                     (uint32_t)(k * HALF_BYTES)};
+          issue_entry(sm, ring, pr, l, UNIT_HOT, n, i, cp, iwp);
+          ++ng;
+        }
+        trace_ev(p, l, 13);
+        // Dynamic hot neurons, two per claim until the layer's counter passes
+        // n_hot; the next claim is taken before the current one is issued.  The
+        // counter was cleared in layer l-2, which this CTA's consumers passed
+        // once they started layer l-1.
+        {
+          const uint64_t t0 = globaltimer_ns();
+          uint32_t i = 0;
+          while (ld_vol(&sm.cons_layer) < l - 1) {
+            if ((++i & 63) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+              pr.ok = false;
+              break;
+            }
+          }
+          if (!pr.ok) break;
+          __threadfence();
+        }
+        uint64_t claimed = 0;
+        int64_t next = sp.n_static + (int64_t)atomicAdd(p.hot_next + l % NACC, (uint32_t)NB_HOT);
+        while (pr.ok && next < d.n_hot) {
+          const int64_t i = next;
+          next = sp.n_static + (int64_t)atomicAdd(p.hot_next + l % NACC, (uint32_t)NB_HOT);
+          const int n = (int)min((int64_t)NB_HOT, d.n_hot - i);
+          Copy cp[2];
+#pragma unroll
+          for (int k = 0; k < 2; ++k)
+            cp[k] = {k < n ? d.hot + (i + k) * HOT_BYTES : nullptr, k < n ? (uint32_t)HOT_BYTES : 0u,
+                     (uint32_t)(k * HALF_BYTES)};
+          issue_entry(sm, ring, pr, l, UNIT_HOT, n, i, cp, iwp);
+          ++ng;
+          claimed += n;
+        }
+        if (!pr.ok) break;
+        sm.ngroups[l & 3] = ng;
+        __threadfence_block();
+        *reinterpret_cast<volatile int32_t*>(&sm.sealed) = l;
         trace_ev(p, l, 14);
-        trace_add(p, l, 18, iw_hot);
-        trace_add(p, l, 19, iw_cold);
+        trace_set(p, l, 15, claimed);
+        trace_set(p, l, 18, iw);
+        trace_set(p, l, 19, (uint64_t)ng);
       }
       if (!pr.ok) {
         sm.abort = 1;
@@ -658,63 +915,73 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
     }
     __syncwarp();
     __syncthreads();
-    // drain: every issued copy must have landed before the CTA exits
+    // drain: every issued copy must have landed before the CTA exits (the
+    // last fill of each slot; earlier ones completed before it was issued)
     if (lane == 0) {
-      for (uint32_t f = sm.cons_k; f < pr.k; ++f)
-        if (!mbar_wait(&sm.full[f % NSLOTS], (f / NSLOTS) & 1u, WAIT_LIMIT_NS)) {
+      const uint32_t first = pr.k > (uint32_t)NE ? pr.k - (uint32_t)NE : 0u;
+      for (uint32_t q = first; q < pr.k; ++q)
+        if (!mbar_wait(&sm.full[q % (uint32_t)NE], (q / (uint32_t)NE) & 1u, WAIT_LIMIT_NS)) {
           atomicOr(p.status, HC_ERR_TIMEOUT);
           break;
         }
     }
   } else {
-    // ============================ consumer warps ===========================
-    const int t = tid, lane = t & 31;
-    uint32_t ck = 0;
-    int gbuf = 0;
+    // ============================ consumer threads =========================
+    const int t = tid;
+    const int sg = t / SG_THREADS, u = t & (SG_THREADS - 1);
+    uint32_t base = 0;       // ring position of the layer's first group
+    int rbuf = 0, dbuf = 0;
     bool ok = true;
-    float x[EPT];
-    {
-      const float4* src = reinterpret_cast<const float4*>(p.x_in + EPT * t);
-      const float4 q0 = __ldg(src), q1 = __ldg(src + 1);
-      x[0] = q0.x; x[1] = q0.y; x[2] = q0.z; x[3] = q0.w; x[4] = q1.x; x[5] = q1.y; x[6] = q1.z; x[7] = q1.w;
-    }
     for (int l = 0; l < p.n_layers && ok; ++l) {
       const hc_layer_desc d = p.layers[l];
       const bool pred_next = next_pred(p, l);
-      const bool logits = layer_logits(p, d, l);
       if (t == 0 && c == 0 && !p.masks_given && d.pred_w_up != nullptr && !rank_ok(d.rank))
         atomicOr(p.status, HC_ERR_UNSUPPORTED);
       const Split sp = make_split(p, d, pred_next, c, G);
       const hc_layer_desc* dn = pred_next ? &p.layers[l + 1] : nullptr;
       const int rank_n = pred_next ? dn->rank : 0;
-      if (t == 0) trace_ev(p, l, 0);
-      uint64_t w_hot = 0, w_cold = 0;
 
       // ---- layer boundary: x_l = x_{l-1} + y_{l-1} once every CTA has added its part
-      if (l > 0) {
+      float x[EPT];
+      if (l == 0) {
+        const float4* src = reinterpret_cast<const float4*>(p.x_in + EPT * t);
+        const float4 q0 = __ldg(src), q1 = __ldg(src + 1);
+        x[0] = q0.x; x[1] = q0.y; x[2] = q0.z; x[3] = q0.w; x[4] = q1.x; x[5] = q1.y; x[6] = q1.z; x[7] = q1.w;
+      } else {
         ok = grid_wait(sm, p, (uint32_t)l * G);
         if (!ok) break;
+        const float4* xv = reinterpret_cast<const float4*>(p.xbuf + (size_t)((l - 1) % NACC) * H + EPT * t);
         const float4* yv = reinterpret_cast<const float4*>(p.yacc + (size_t)((l - 1) % NACC) * H + EPT * t);
-        const float4 a = __ldcg(yv), b = __ldcg(yv + 1);
-        x[0] += a.x; x[1] += a.y; x[2] += a.z; x[3] += a.w; x[4] += b.x; x[5] += b.y; x[6] += b.z; x[7] += b.w;
+        const float4 xa = __ldcg(xv), xb = __ldcg(xv + 1), a = __ldcg(yv), b = __ldcg(yv + 1);
+        x[0] = xa.x + a.x; x[1] = xa.y + a.y; x[2] = xa.z + a.z; x[3] = xa.w + a.w;
+        x[4] = xb.x + b.x; x[5] = xb.y + b.y; x[6] = xb.z + b.z; x[7] = xb.w + b.w;
         if (p.x_hist && c == 0) {
           float4* h = reinterpret_cast<float4*>(p.x_hist + (size_t)(l - 1) * H + EPT * t);
           h[0] = make_float4(x[0], x[1], x[2], x[3]);
           h[1] = make_float4(x[4], x[5], x[6], x[7]);
         }
       }
-      // clear the accumulators layer l+1 adds into (last read before the barrier just passed)
+      if (c == 0) {
+        // x_l for every CTA at layer l+1 (x_{l-3}'s readers all passed the barrier above)
+        float4* xo = reinterpret_cast<float4*>(p.xbuf + (size_t)(l % NACC) * H + EPT * t);
+        xo[0] = make_float4(x[0], x[1], x[2], x[3]);
+        xo[1] = make_float4(x[4], x[5], x[6], x[7]);
+      }
+      if (t == 0) trace_ev(p, l, 0);
+      // Clear accumulators ahead of use (their previous users finished before the
+      // barrier above): y of layer l+1 is added after barrier l+1; z of layer
+      // l+2 and its tile count during layer l+1; the hot-neuron counter of layer
+      // l+2 once the claiming CTA's consumers started layer l+1.
       {
         float* yz = p.yacc + (size_t)((l + 1) % NACC) * H;
         for (int i = (int)split_lo(H / 4, c, G) + t; i < (int)split_lo(H / 4, c + 1, G); i += CONS_THREADS)
           reinterpret_cast<float4*>(yz)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (c == 0 && t < 128) p.zacc[(size_t)((l + 2) % NACC) * 128 + t] = 0.0f;
+        if (c == 0 && t == 0) p.hot_next[(l + 2) % NACC] = 0u;
+        if (c == 0 && t == 1) p.zdone[(l + 2) % NACC] = 0u;
       }
-      if (t == 0) trace_ev(p, l, 1);
 
-      // ---- RMSNorm (engine.py:295; torch.nn.RMSNorm); x as f16 pairs in registers
-      float y[EPT];
-      XRegs xr;
+      // ---- RMSNorm (engine.py:295; torch.nn.RMSNorm) -> f16 and fixed-point copies
       {
         float nw[EPT];
         if (d.norm_w) {
@@ -730,169 +997,178 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         for (int i = 0; i < EPT; ++i) ss = fmaf(x[i], x[i], ss);
         ss = cons_sum(sm, ss);
         const float rstd = rsqrtf(ss / (float)H + p.eps);
-        __half xh[EPT];
-        float xe = 0.0f, xo = 0.0f;
+        float xn[EPT];
+        float am = 0.0f;
 #pragma unroll
         for (int i = 0; i < EPT; ++i) {
-          xh[i] = __float2half_rn(x[i] * rstd * nw[i]);
-          if (i & 1) xo += __half2float(xh[i]);
-          else xe += __half2float(xh[i]);
+          xn[i] = x[i] * rstd * nw[i];
+          am = fmaxf(am, fabsf(xn[i]));
         }
-        xr.xoff = 1032.0f * xe + 72.0f * xo;
-        auto pk = [](__half lo, __half hi) {
-          return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
-        };
-        xr.xf8[0] = pk(xh[0], xh[1]); xr.xf8[1] = pk(xh[2], xh[3]);
-        xr.xf8[2] = pk(xh[4], xh[5]); xr.xf8[3] = pk(xh[6], xh[7]);
-        xr.xi4[0] = pk(xh[0], xh[4]); xr.xi4[1] = pk(xh[1], xh[5]);
-        xr.xi4[2] = pk(xh[2], xh[6]); xr.xi4[3] = pk(xh[3], xh[7]);
+        {
+          __half2 h2[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) h2[i] = __floats2half2_rn(xn[2 * i], xn[2 * i + 1]);
+          *reinterpret_cast<uint4*>(sm.xh + EPT * t) = *reinterpret_cast<const uint4*>(h2);
+        }
+        // 16-bit fixed point per 32 elements (4 threads): |x| * 2^s < 2^15
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+        int sh = 14 - (((__float_as_int(am) >> 23) & 255) - 127);
+        sh = max(-126, min(126, sh));
+        const float sc = __int_as_float((127 + sh) << 23), isc = __int_as_float((127 - sh) << 23);
+        int xi[EPT];
+        int sum = 0;
+#pragma unroll
+        for (int i = 0; i < EPT; ++i) {
+          xi[i] = max(-32768, min(32767, __float2int_rn(xn[i] * sc)));
+          sum += xi[i];
+        }
+        auto hb = [](int v) { return (uint32_t)((v >> 8) & 0xFF); };
+        auto lb = [](int v) { return (uint32_t)(v & 0xFF); };
+        uint4 dq;
+        dq.x = hb(xi[0]) | (hb(xi[2]) << 8) | (hb(xi[4]) << 16) | (hb(xi[6]) << 24);
+        dq.y = hb(xi[1]) | (hb(xi[3]) << 8) | (hb(xi[5]) << 16) | (hb(xi[7]) << 24);
+        dq.z = lb(xi[0]) | (lb(xi[2]) << 8) | (lb(xi[4]) << 16) | (lb(xi[6]) << 24);
+        dq.w = lb(xi[1]) | (lb(xi[3]) << 8) | (lb(xi[5]) << 16) | (lb(xi[7]) << 24);
+        sm.xq[t] = dq;
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        if ((t & 3) == 0) sm.chunk[t >> 2] = make_int2(-8 * sum, __float_as_int(isc));
         if (pred_next) {
-          // only the rows of this CTA's W_down tiles are read
+          // the rows of this CTA's W_down tiles of the next predictor: RMSNorm_{l+1}(x_l)
           const int r0 = sp.d0 * WD_ROWS, r1 = sp.d1 * WD_ROWS;
-          if (EPT * t + EPT > r0 && EPT * t < r1) {
+          if (EPT * t >= r0 && EPT * t < r1) {
 #pragma unroll
             for (int i = 0; i < EPT; ++i) {
               const float w = dn->norm_w ? __ldg(dn->norm_w + EPT * t + i) : 1.0f;
-              sm.xs[EPT * t + i] = x[i] * rstd * w;
+              xs[EPT * t + i - r0] = x[i] * rstd * w;
             }
           }
         }
-#pragma unroll
-        for (int i = 0; i < EPT; ++i) y[i] = 0.0f;
       }
-      if (t == 0) trace_ev(p, l, 2);
-
-      // ---- own mask words of layer l (predictor logits of the own id range)
-      {
-        const int nw = sp.u1 - sp.u0;
-        uint32_t* mrow = p.masks + (size_t)l * p.words;
-        if (!logits) {
-          for (int w = t; w < nw; w += CONS_THREADS) {
-            uint32_t m;
-            if (l == 0 || p.masks_given) {
-              m = __ldcg(mrow + sp.u0 + w);
-            } else {
-              // no predictor: fetch every cold neuron (engine.py:282-283)
-              const int valid = min(32, p.inter - 32 * (sp.u0 + w));
-              m = valid >= 32 ? 0xffffffffu : ((1u << valid) - 1u);
-              mrow[sp.u0 + w] = m;
-            }
-            sm.own_words[w] = m;
-          }
-        } else if (nw > 0) {
-          // z of this layer (complete: summed into zacc by all CTAs before the barrier)
-          if (t < d.rank) sm.z[t] = __ldcg(p.zacc + (size_t)(l % NACC) * 128 + t);
-          named_bar(1, CONS_THREADS);
-          const int per = d.rank / 8;
-          for (int u = sp.u0; u < sp.u1 && ok; ++u) {
-            ok = cons_acquire(sm, ck, 1);
-            if (!ok) break;
-            const float* tile = reinterpret_cast<const float*>(sm.ring[slot_of(ck)]);
-            const int rows = min(WU_ROWS, p.inter - u * WU_ROWS);
-            const int j = (t < 256) ? (t >> 3) : WU_ROWS, part = t & 7;   // 256 threads: 32 neurons x 8
-            float acc = 0.0f;
-            if (j < rows)
-              for (int i = 0; i < per; ++i) acc = fmaf(tile[j * d.rank + part * per + i], sm.z[part * per + i], acc);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 4);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-            const float lg = acc + ((j < rows) ? tile[WU_ROWS * d.rank + j] : 0.0f);
-            const bool on = (j < rows) && (lg >= p.thr);
-            const unsigned b = __ballot_sync(0xffffffffu, on && part == 0);
-            if (lane == 0 && t < 256) {
-              const uint32_t nib = ((b >> 0) & 1u) | (((b >> 8) & 1u) << 1) | (((b >> 16) & 1u) << 2) |
-                                   (((b >> 24) & 1u) << 3);
-              atomicOr(&sm.ballot_word, nib << (4 * (t >> 5)));
-            }
-            named_bar(1, CONS_THREADS);
-            if (t == 0) {
-              sm.own_words[u - sp.u0] = sm.ballot_word;
-              mrow[u] = sm.ballot_word;
-              sm.ballot_word = 0;
-            }
-            cons_release(sm, ck, 1);
-            ck += 1;
-          }
-        }
-        named_bar(1, CONS_THREADS);
-        if (t == 0) mbar_arrive(&sm.own_ready);
-      }
-      if (!ok) break;
-      if (t == 0) trace_ev(p, l, 3);
-
-      // ---- hot neurons, groups of NB_HOT
-      for (int64_t i = sp.h0; i < sp.h1; i += NB_HOT) {
-        const int nb = (int)(sp.h1 - i < NB_HOT ? sp.h1 - i : NB_HOT);
-        if (hot_group(sm, p, d.hot_scale, i, nb, ck, gbuf, xr, y, (t == 0 && p.trace) ? &w_hot : nullptr)) {
-          ok = false;
-          break;
-        }
-        ck += nb;
-        gbuf ^= 1;
-      }
-      if (!ok) break;
-      if (t == 0) trace_ev(p, l, 4);
-
-      // ---- W_down tiles of predictor l+1 -> z partials added into zacc
-      for (int u = sp.d0; u < sp.d1 && ok; ++u) {
-        ok = cons_acquire(sm, ck, 1);
-        if (!ok) break;
-        const float* tile = reinterpret_cast<const float*>(sm.ring[slot_of(ck)]);
-        const int parts = CONS_THREADS / rank_n;
-        float acc = 0.0f;
-        const int r = t % rank_n, part = t / rank_n;
-        if (part < parts)
-          for (int row = part; row < WD_ROWS; row += parts)
-            acc = fmaf(tile[row * rank_n + r], sm.xs[u * WD_ROWS + row], acc);
-        sm.zred[t] = acc;
-        named_bar(1, CONS_THREADS);
-        if (t < rank_n) {
-          float s = 0.0f;
-          for (int q = 0; q < parts; ++q) s += sm.zred[q * rank_n + t];
-          atomicAdd(p.zacc + (size_t)((l + 1) % NACC) * 128 + t, s);
-        }
-        named_bar(1, CONS_THREADS);
-        cons_release(sm, ck, 1);
-        ck += 1;
-      }
-      if (!ok) break;
-      if (t == 0) trace_ev(p, l, 5);
-
-      // ---- cold records: the planner's list of this CTA's active cold neurons
-      {
-        bool ok0 = true;
-        if (t == 0) ok0 = mbar_wait(&sm.plan_full, (uint32_t)l & 1u, WAIT_LIMIT_NS);
-        ok = cons_broadcast(sm, ok0);
-        if (!ok) break;
-        while (!mbar_try_wait(&sm.plan_full, (uint32_t)l & 1u)) {
-        }
-        const int cnt = sm.plan_n;
-        named_bar(1, CONS_THREADS);
-        if (t == 0) {
-          mbar_arrive(&sm.plan_empty);
-          trace_ev(p, l, 6);
-        }
-        for (int i = 0; i < cnt; i += NB) {
-          const int nb = cnt - i < NB ? cnt - i : NB;
-          if (cold_group(sm, p, nb, ck, gbuf, xr, y, (t == 0 && p.trace) ? &w_cold : nullptr)) {
-            ok = false;
-            break;
-          }
-          ck += (nb + 1) >> 1;
-          gbuf ^= 1;
-        }
-      }
-      if (!ok) break;
       if (t == 0) {
-        trace_ev(p, l, 7);
-        trace_add(p, l, 15, w_hot);
-        trace_add(p, l, 16, w_cold);
+        // W_up tiles of the next layer's predictor this CTA turns into mask words
+        sm.wup_left = pred_next ? sp.u1 - sp.u0 : 0;
+        *reinterpret_cast<volatile int32_t*>(&sm.cons_layer) = l;
       }
-      // ---- add this CTA's partial y, arrive at the layer's grid barrier
+      named_bar(1, CONS_THREADS);
+      if (t == 0) trace_ev(p, l, 1);
+
+      // ---- subgroup phase: groups g = sg, sg + 4, ... of the layer's stream
+      float y[SPT];
+#pragma unroll
+      for (int k = 0; k < SPT; ++k) y[k] = 0.0f;
+      // trace counters (subgroup 0's poller, SM cycles): 0 fill waits, 1 cold,
+      // 2 hot, 3 predictor groups, 4 group barrier, 5 observe, 6 release, 7 start
+      const bool tr = p.trace != nullptr && t == 0;
+      if (tr) {
+        for (int k = 0; k < 7; ++k) sm.tstat[k] = 0;
+        sm.tstat[7] = (uint64_t)clock64();
+      }
+      // this subgroup's groups sit at ring positions base + sg, base + sg + 4, ...
+      uint32_t q = base + (uint32_t)sg;
+      int e = (int)(q % (uint32_t)NE);
+      uint32_t par = (q / (uint32_t)NE) & 1u;
+      for (int gi = sg;; gi += NSG) {
+        uint64_t tb = 0;
+        // one poller per subgroup decides; the decision reaches all 128 threads through the barrier
+        if (u == 0) {
+          int r = poll_pos(sm, q, e, par, l, gi, tr ? &sm.tstat[0] : nullptr);
+          if (ld_vol(&sm.abort) != 0) r = -1;
+          if (r < 0) sm.abort = 1;
+          sm.sgdec[sg][dbuf] = r;
+          if (tr) tb = (uint64_t)clock64();
+        }
+        named_bar(2 + sg, SG_THREADS);
+        if (tr) {
+          const uint64_t now = (uint64_t)clock64();
+          sm.tstat[4] += now - tb;
+          tb = now;
+        }
+        const int r = sm.sgdec[sg][dbuf];
+        dbuf ^= 1;
+        if (r <= 0) break;
+        observe_pos(sm, e, par);
+        const SlotInfo inf = sm.info[e];
+        const uint8_t* s0 = ring + (size_t)e * ENTRY_BYTES;
+        const uint8_t* s1 = s0 + HALF_BYTES;
+        const uint64_t tg0 = tr ? (uint64_t)clock64() : 0;
+        if (tr) sm.tstat[5] += tg0 - tb;
+        if (inf.kind == UNIT_COLD) {
+          sg_cold(sm, p, s0, s1, inf.n, sg, rbuf, y);
+          rbuf ^= 1;
+        } else if (inf.kind == UNIT_HOT) {
+          sg_hot(sm, p, d.hot_scale, s0, s1, inf.n, inf.index, sg, rbuf, y);
+          rbuf ^= 1;
+        } else if (inf.kind == UNIT_WUP) {
+          sg_wup(sm, p, rank_n, s0, s1, inf.n, inf.index, sp.u0, l + 1, sg);
+        } else if (inf.kind == UNIT_WDOWN) {
+          sg_wdown(sm, p, xs, s0, s1, inf.n, inf.index, sp.d0, rank_n, l, sg);
+        }
+        uint64_t tg1 = 0;
+        if (tr) {
+          tg1 = (uint64_t)clock64();
+          sm.tstat[inf.kind == UNIT_COLD ? 1 : inf.kind == UNIT_HOT ? 2 : 3] += tg1 - tg0;
+        }
+        sg_release(sm, e);
+        if (tr) sm.tstat[6] += (uint64_t)clock64() - tg1;
+        q += NSG;
+        e += NSG;
+        if (e >= NE) {
+          e -= NE;
+          par ^= 1u;
+        }
+      }
+      if (p.trace != nullptr && u == 0) trace_ev(p, l, 4 + sg);
+      if (tr) {
+        trace_set(p, l, 16, sm.tstat[0]);
+        trace_set(p, l, 2, sm.tstat[1]);
+        trace_set(p, l, 3, sm.tstat[2]);
+        trace_set(p, l, 23, sm.tstat[3]);
+        trace_set(p, l, 24, sm.tstat[4]);
+        trace_set(p, l, 25, sm.tstat[5]);
+        trace_set(p, l, 26, sm.tstat[6]);
+        trace_set(p, l, 27, (uint64_t)clock64() - sm.tstat[7]);
+      }
+      // ---- all subgroups done: one abort decision for everyone, then sum the
+      // partial y (fixed tree in shared memory) and add it to the layer's accumulator
+      if (t == 0) sm.flag = ld_vol(&sm.abort) ? 0 : 1;
+      named_bar(1, CONS_THREADS);
+      if (sm.flag == 0) {
+        ok = false;
+        break;
+      }
+      base += (uint32_t)ld_vol(&sm.ngroups[l & 3]);
       {
+        float* bufA = sm.ystage;
+        float* bufB = reinterpret_cast<float*>(sm.xh);     // xh + xq: 16 KB, dead until the next layer
+        if (sg >= 2) {
+          float* dst = sg == 2 ? bufA : bufB;
+#pragma unroll
+          for (int k = 0; k < SPT; ++k) dst[k * SG_THREADS + u] = y[k];
+        }
+        named_bar(1, CONS_THREADS);
+        if (sg < 2) {
+          const float* src = sg == 0 ? bufA : bufB;
+#pragma unroll
+          for (int k = 0; k < SPT; ++k) y[k] += src[k * SG_THREADS + u];
+        }
+        named_bar(1, CONS_THREADS);
+        if (sg < 2) {
+          float* dst = sg == 0 ? bufA : bufB;
+#pragma unroll
+          for (int k = 0; k < SPT; ++k) dst[k * SG_THREADS + u] = y[k];
+        }
+        named_bar(1, CONS_THREADS);
+        // element layout: thread t adds elements [8t, 8t+8) (element 32u+k sits at k*128+u)
+        float e[EPT];
+        const int eu = t >> 2, ek = EPT * (t & 3);
+#pragma unroll
+        for (int i = 0; i < EPT; ++i) e[i] = bufA[(ek + i) * SG_THREADS + eu] + bufB[(ek + i) * SG_THREADS + eu];
         float* ya = p.yacc + (size_t)(l % NACC) * H + EPT * t;
-        red_add_v4(ya, y[0], y[1], y[2], y[3]);
-        red_add_v4(ya + 4, y[4], y[5], y[6], y[7]);
+        red_add_v4(ya, e[0], e[1], e[2], e[3]);
+        red_add_v4(ya + 4, e[4], e[5], e[6], e[7]);
+        if (t == 0) trace_ev(p, l, 9);
       }
       grid_arrive(p);
       if (t == 0) trace_ev(p, l, 8);
@@ -902,10 +1178,11 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
       const int L = p.n_layers;
       ok = grid_wait(sm, p, (uint32_t)L * G);
       if (ok && c == 0) {
+        const float4* xv = reinterpret_cast<const float4*>(p.xbuf + (size_t)((L - 1) % NACC) * H + EPT * t);
         const float4* yv = reinterpret_cast<const float4*>(p.yacc + (size_t)((L - 1) % NACC) * H + EPT * t);
-        const float4 a = __ldcg(yv), b = __ldcg(yv + 1);
-        const float4 o0 = make_float4(x[0] + a.x, x[1] + a.y, x[2] + a.z, x[3] + a.w);
-        const float4 o1 = make_float4(x[4] + b.x, x[5] + b.y, x[6] + b.z, x[7] + b.w);
+        const float4 xa = __ldcg(xv), xb = __ldcg(xv + 1), a = __ldcg(yv), b = __ldcg(yv + 1);
+        const float4 o0 = make_float4(xa.x + a.x, xa.y + a.y, xa.z + a.z, xa.w + a.w);
+        const float4 o1 = make_float4(xb.x + b.x, xb.y + b.y, xb.z + b.z, xb.w + b.w);
         float4* out = reinterpret_cast<float4*>(p.x_out + EPT * t);
         out[0] = o0;
         out[1] = o1;
@@ -916,26 +1193,24 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         }
       }
     }
-    if (t == 0) {
-      sm.cons_k = ck;
-      if (!ok) atomicOr(p.status, HC_ERR_TIMEOUT);
-    }
+    if (t == 0 && !ok) atomicOr(p.status, HC_ERR_TIMEOUT);
     __syncthreads();
   }
 
   // Once every CTA is past its last read: reset the barrier counters and clear
   // the accumulators, so the next launch starts from a clean workspace.
-  __shared__ int s_last;
   if (tid == 0) {
     __threadfence();
-    s_last = atomicAdd(p.exit_count, 1u) == (uint32_t)G - 1;
+    sm.last = atomicAdd(p.exit_count, 1u) == (uint32_t)G - 1;
   }
   __syncthreads();
-  if (s_last) {
+  if (sm.last) {
     __threadfence();
     for (int i = tid; i < NACC * H / 4; i += STACK_THREADS)
       reinterpret_cast<float4*>(p.yacc)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int i = tid; i < NACC * 128; i += STACK_THREADS) p.zacc[i] = 0.0f;
+    if (tid < NACC) p.hot_next[tid] = 0u;
+    if (tid < NACC) p.zdone[tid] = 0u;
     if (tid == 0) {
       *p.bar_count = 0;
       *p.exit_count = 0;
@@ -965,8 +1240,9 @@ extern "C" int hc_ffn_stack(const hc_layer_desc* layers, int32_t n_layers, int32
                             uint32_t* masks, int32_t masks_given, float* x_out, float* x_hist, float eps,
                             int32_t act, int32_t act_on_both, float logit_threshold, int32_t grid, void* workspace,
                             int32_t* status, uint64_t* trace, hc_stream_t stream) {
-  if (!layers || n_layers <= 0 || !x_in || !masks || !x_out || !workspace || !status) return HC_ERR_ARG;
-  if (inter <= 0 || inter > 32 * MAX_WORDS || (inter & 3) != 0 || (act != HC_ACT_SILU && act != HC_ACT_RELU))
+  if (!layers || n_layers <= 0 || n_layers > 32767 || !x_in || !masks || !x_out || !workspace || !status)
+    return HC_ERR_ARG;
+  if (inter <= 0 || inter > 32768 || (inter & 3) != 0 || (act != HC_ACT_SILU && act != HC_ACT_RELU))
     return HC_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(x_in) & 15) || (reinterpret_cast<uintptr_t>(x_out) & 15) ||
       (reinterpret_cast<uintptr_t>(workspace) & 15) || (x_hist && (reinterpret_cast<uintptr_t>(x_hist) & 15)))
@@ -974,14 +1250,18 @@ extern "C" int hc_ffn_stack(const hc_layer_desc* layers, int32_t n_layers, int32
   int G = grid > 0 ? grid : hc_ffn_stack_grid();
   if (G <= 0) return HC_ERR_CUDA;
   const int words = (inter + 31) / 32;
-  if ((int64_t)((words + G - 1) / G) * 32 > COLD_LIST) return HC_ERR_UNSUPPORTED;   // own range too wide
-  static bool attr_set = false;
-  const int smem = (int)sizeof(StackSmem);
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(ffn_stack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-      return HC_ERR_CUDA;
-    attr_set = true;
-  }
+  if ((words + G - 1) / G > OWN_WORDS) return HC_ERR_UNSUPPORTED;   // own neuron-id range too wide
+  int dev = 0, smem_max = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+    return HC_ERR_CUDA;
+  const int wd_tiles = (H / WD_ROWS + G - 1) / G;
+  const size_t xs_bytes = (size_t)wd_tiles * WD_ROWS * sizeof(float);
+  const size_t smem_need = RING_OFF + (size_t)NE * ENTRY_BYTES + xs_bytes;
+  if ((long)smem_need > (long)smem_max) return HC_ERR_UNSUPPORTED;
+  const int smem = (int)smem_need;
+  if (cudaFuncSetAttribute(ffn_stack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return HC_ERR_CUDA;
   StackParams p;
   p.layers = layers;
   p.n_layers = n_layers;
@@ -998,9 +1278,12 @@ extern "C" int hc_ffn_stack(const hc_layer_desc* layers, int32_t n_layers, int32
   p.thr = logit_threshold;
   char* ws = static_cast<char*>(workspace);
   p.bar_count = reinterpret_cast<uint32_t*>(ws);
-  p.exit_count = reinterpret_cast<uint32_t*>(ws + 128);
+  p.hot_next = reinterpret_cast<uint32_t*>(ws + WS_HOT_NEXT);
+  p.zdone = reinterpret_cast<uint32_t*>(ws + WS_ZDONE);
+  p.exit_count = reinterpret_cast<uint32_t*>(ws + WS_EXIT);
   p.yacc = reinterpret_cast<float*>(ws + WS_YACC);
   p.zacc = reinterpret_cast<float*>(ws + WS_ZACC);
+  p.xbuf = reinterpret_cast<float*>(ws + WS_XBUF);
   p.status = status;
   p.trace = trace;
   void* args[] = {&p};

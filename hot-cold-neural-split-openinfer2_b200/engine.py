@@ -132,7 +132,7 @@ class FFNStack:
 
     def launch(self, x: torch.Tensor, masks_given: bool = False, x_hist: Optional[torch.Tensor] = None,
                out: Optional[torch.Tensor] = None, trace: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """One hc_ffn_stack launch.  ``trace`` (int64 [L, grid, 24], device)
+        """One hc_ffn_stack launch.  ``trace`` (int64 [L, grid, 32], device)
         (zeroed) receives per-CTA phase timestamps and waits
         (see include/hotcold.h)."""
         out = self.x_out if out is None else out
@@ -142,22 +142,46 @@ class FFNStack:
                                    N.ptr(self.status), N.ptr(trace), N.stream_handle()), "hc_ffn_stack")
         return out
 
-    def trace_summary(self, trace: torch.Tensor) -> dict:
-        """Mean / max over CTAs of each phase's duration (us) from a trace."""
-        t = trace.to(torch.float64).cpu() / 1000.0
-        names = ["barrier_x", "norm", "own_mask", "hot", "wdown", "cold_list_wait", "cold", "y_add"]
+    def trace_summary(self, trace: torch.Tensor, clock_ghz: float = 1.965) -> dict:
+        """Mean / max over CTAs of each phase (us, or counts) from a trace;
+        the subgroup-0 loop counters are SM cycles, converted at ``clock_ghz``."""
+        t = trace.to(torch.float64).cpu()
+        us = t / 1000.0
         out = {}
-        for i, n in enumerate(names):
-            d = t[:, :, i + 1] - t[:, :, i]
-            out[n] = (float(d.mean()), float(d.max()))
-        out["layer"] = (float((t[1:, :, 0] - t[:-1, :, 0]).mean()) if self.L > 1 else 0.0, 0.0)
-        out["issuer_hot"] = (float((t[:, :, 11] - t[:, :, 10]).mean()), float((t[:, :, 11] - t[:, :, 10]).max()))
-        out["issuer_wait_plan"] = (float((t[:, :, 13] - t[:, :, 12]).mean()), float((t[:, :, 13] - t[:, :, 12]).max()))
-        out["issuer_cold"] = (float((t[:, :, 14] - t[:, :, 13]).mean()), float((t[:, :, 14] - t[:, :, 13]).max()))
-        for k, i in (("cons_wait_hot", 15), ("cons_wait_cold", 16), ("issuer_wait_slot_hot", 18),
-                     ("issuer_wait_slot_cold", 19)):
-            out[k] = (float(t[:, :, i].mean()), float(t[:, :, i].max()))
-        out["plan_ready_after_start"] = (float((t[:, :, 20] - t[:, :, 0]).mean()), float((t[:, :, 20] - t[:, :, 0]).max()))
+
+        def put(name, d):
+            out[name] = (float(d.mean()), float(d.max()))
+
+        sg_done = us[:, :, 4:8]
+        put("phase0", us[:, :, 1] - us[:, :, 0])
+        for k in range(4):
+            put(f"subgroup{k}", us[:, :, 4 + k] - us[:, :, 1])
+        put("subgroup_spread", sg_done.max(dim=2).values - sg_done.min(dim=2).values)
+        put("y_sum", us[:, :, 9] - sg_done.max(dim=2).values)
+        put("arrive", us[:, :, 8] - us[:, :, 9])
+        if self.L > 1:
+            put("barrier_wait", us[1:, :, 0] - us[:-1, :, 8])
+            put("layer", us[1:, :, 0] - us[:-1, :, 0])
+        put("issue_wdown_plan_wait", us[:, :, 11] - us[:, :, 10])
+        put("issue_cold", us[:, :, 12] - us[:, :, 11])
+        put("issue_static_hot", us[:, :, 13] - us[:, :, 12])
+        put("issue_dynamic_hot_wup", us[:, :, 14] - us[:, :, 13])
+        put("own_words_after_start", us[:, :, 21] - us[:, :, 0])
+        put("planner_wake_after_start", us[:, :, 22] - us[:, :, 0])
+        put("plan_ready_after_start", us[:, :, 20] - us[:, :, 0])
+        cyc = t / (1000.0 * clock_ghz)          # subgroup-0 counters are SM cycles
+        put("sg0_poll_wait", cyc[:, :, 16])
+        put("sg0_cold_groups", cyc[:, :, 2])
+        put("sg0_hot_groups", cyc[:, :, 3])
+        put("sg0_other_groups", cyc[:, :, 23])
+        put("sg0_group_barrier", cyc[:, :, 24])
+        put("sg0_observe", cyc[:, :, 25])
+        put("sg0_release", cyc[:, :, 26])
+        put("sg0_total", cyc[:, :, 27])
+        put("issuer_slot_wait", us[:, :, 18])
+        put("dynamic_hot_claimed[n]", t[:, :, 15])
+        put("cold_records[n]", t[:, :, 17])
+        put("groups[n]", t[:, :, 19])
         return out
 
     def forward(self, x: torch.Tensor, masks: Optional[torch.Tensor] = None, x_hist: Optional[torch.Tensor] = None,

@@ -36,7 +36,7 @@ def main():
     if args.what == "stack":
         st = syn.stack(grid=args.grid)
         x = torch.randn(args.tokens, 4096, device="cuda")
-        trace = torch.zeros(args.layers, st.grid, 24, dtype=torch.int64, device="cuda") if args.trace else None
+        trace = torch.zeros(args.layers, st.grid, 32, dtype=torch.int64, device="cuda") if args.trace else None
         for t in range(args.tokens):
             if trace is not None:
                 trace.zero_()          # keep the last token's stamps and waits

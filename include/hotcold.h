@@ -242,15 +242,20 @@ HC_API int64_t hc_ffn_stack_workspace_bytes(int32_t grid, int32_t inter);
  *   grid       0 = hc_ffn_stack_grid(); tests may pass fewer CTAs
  *   workspace  hc_ffn_stack_workspace_bytes(grid, inter), zeroed once; the
  *              kernel leaves it zeroed again when it completes
- *   trace      optional [n_layers][grid][24] uint64, zeroed by the caller:
- *              %globaltimer stamps (ns) of each CTA's phase boundaries
- *              (consumer events 0-8: layer start, grid barrier passed and x
- *              updated, norm done, own mask words ready, hot done, W_down
- *              done, cold list read, cold done, partial y added; issuer
- *              events 10-14: layer start, hot issued, W_down issued, cold
- *              list ready, cold issued; 20: planner list ready) and
- *              accumulated waits in ns (15/16: consumers on hot/cold slot
- *              fills, 18/19: issuer on empty slots while issuing hot/cold);
+ *   trace      optional [n_layers][grid][32] uint64, zeroed by the caller:
+ *              %globaltimer stamps (ns) per CTA and layer -- 0: layer start
+ *              (grid barrier passed), 1: normalised input ready, 4-7:
+ *              consumer subgroup 0-3 done, 9: partial y added, 8: grid
+ *              barrier arrival; issuer 10: layer start, 11: cold list
+ *              received, 12: cold issued, 13: static hot issued, 14: layer
+ *              sealed; 21: own mask words ready (stamped at the end of the
+ *              previous layer), 22: planner took them, 20: cold list ready --
+ *              plus 15: hot neurons claimed dynamically, 16: ns subgroup 0
+ *              waited for fills, 17: active cold records, 18: ns the issuer
+ *              waited for empty slots, 19: groups issued; SM cycles of
+ *              subgroup 0's poller: 16 waiting for fills, 2/3/23 on cold /
+ *              hot / predictor groups, 24/25/26 in its group barrier / seeing
+ *              the fills / releasing, 27 in total;
  *              NULL = off
  * The layer outputs are sums of per-CTA float partials added with atomics, so
  * their last bits can differ between launches.
