@@ -19,13 +19,15 @@
 // streamed in, while the grid waits at the layer boundary.
 //
 // Roles:
-//  * issuer warp: streams the CTA's units (W_up tiles, hot neurons, W_down
-//    tiles, cold records) through a ring of shared-memory slots with 1-D bulk
-//    copies (TMA engine) completing on mbarriers, two slots per group, and
-//    prefetches the layer's static ranges into L2;
-//  * planner warp: turns the CTA's predicted-mask words into the ascending
-//    list of its active cold records (ColdWeightStore's id -> record lookup)
-//    and prefetches them into L2;
+//  * issuer warp: streams the CTA's groups (cold records, hot neurons)
+//    through a ring of shared-memory entries with 1-D bulk copies (TMA
+//    engine) completing on mbarriers, and prefetches the layer's static
+//    ranges into L2;
+//  * planner warp: runs the next layer's predictor for the CTA's share (its
+//    W_down rows, then, once every CTA's share is in, the logits of its
+//    neuron-id range), and turns the mask words into the ascending list of
+//    its active cold records (ColdWeightStore's id -> record lookup), which
+//    it prefetches into L2;
 //  * 4 consumer subgroups of 128 threads: group g of a layer belongs to
 //    subgroup g % 4; thread u owns elements [32u, 32u+32) of every row and of
 //    its subgroup's partial y.  FP8 rows are dotted with RMSNorm(x) in f16
@@ -64,6 +66,7 @@ constexpr int COLD_LIST = 1024;         // neuron ids one CTA owns (and so cold 
 constexpr int OWN_WORDS = COLD_LIST / 32;
 constexpr int HOT_BYTES = 3 * H;        // 12288
 constexpr int NACC = 3;                 // rotating y / z / hot-claim accumulators
+constexpr int YCOPIES = 1;              // CTA c adds its partial y into copy c % YCOPIES
 constexpr int STATIC_HOT_DIV = 4;       // 1/4 of the hot neurons are split statically
 constexpr int WD_TILES = 4096 / 32;     // W_down tiles of a predictor (H / WD_ROWS)
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;   // 2 s
@@ -73,7 +76,7 @@ static_assert(WU_ROWS * 96 * 4 + WU_ROWS * 4 <= HALF_BYTES, "predictor tiles mus
 static_assert(NE > NSG, "the subgroups' entries advance by NSG per group");
 static_assert(SPT == 32 && EPT == 8, "the decoders assume 32 elements per subgroup thread");
 
-enum : uint8_t { UNIT_PAD = 0, UNIT_HOT = 1, UNIT_COLD = 2, UNIT_WUP = 3, UNIT_WDOWN = 4 };
+enum : uint8_t { UNIT_HOT = 1, UNIT_COLD = 2 };
 
 // Written by the issuer before it arms an entry's mbarrier.
 struct SlotInfo {
@@ -86,10 +89,12 @@ struct SlotInfo {
 };
 
 struct StackSmem {
+  alignas(128) uint8_t pbuf[HALF_BYTES];   // planner: one predictor tile (W_down or W_up + bias)
   __half xh[H];                     // RMSNorm_l(x) as f16 (hot neurons); with xq, a y stage later
   uint4 xq[CONS_THREADS];           // the same as 16-bit fixed point, byte digits per 8 elements
-  float ystage[H];                  // subgroup partial y (element 32u+k at k*128+u); during the
-                                    // subgroup phase, subgroup s keeps the next predictor's z at s*128
+  float ystage[H];                  // subgroup partial y (element 32u+k at k*128+u); earlier in the
+                                    // layer, the planner's W_down rows RMSNorm_{l+1}(x_l)
+  float z[128];                     // planner: bottleneck of the next layer's predictor
   int2 chunk[H / SPT];              // per 32 elements: (-8 * sum of the fixed-point values, bits of 2^-s)
   float zred[NWARPS];
   float red[NSG][2][SG_WARPS][2 * NB_COLD];
@@ -103,12 +108,13 @@ struct StackSmem {
   int32_t cons_layer;               // last layer the consumers started
   int32_t plan_n;
   int32_t abort;
-  int32_t wup_left;
   int32_t flag;
   int32_t last;
   alignas(8) uint64_t full[NE];
   alignas(8) uint64_t empty[NE];
-  alignas(8) uint64_t own_ready;    // consumers -> planner: own mask words of the next layer written
+  alignas(8) uint64_t phase0_done;  // consumers -> planner: normalised input (and W_down rows) ready
+  alignas(8) uint64_t pbar;         // planner's own tile copies
+  alignas(8) uint64_t wdown_done;   // planner -> consumers: done with the W_down rows in ystage
   alignas(8) uint64_t plan_full;    // planner -> issuer: cold list of layer l ready
   alignas(8) uint64_t plan_empty;   // issuer -> planner: list consumed
 };
@@ -132,7 +138,7 @@ struct StackParams {
   uint32_t* exit_count;
   uint32_t* hot_next;        // [NACC] hot-neuron claims per layer
   uint32_t* zdone;           // [NACC] W_down tiles added into zacc per layer
-  float* yacc;               // [NACC][H]   partial-y accumulators
+  float* yacc;               // [NACC][YCOPIES][H] partial-y accumulators
   float* zacc;               // [NACC][128] predictor bottleneck accumulators
   float* xbuf;               // [NACC][H]   x_l, written by CTA 0
   int32_t* status;
@@ -151,13 +157,46 @@ constexpr size_t WS_HOT_NEXT = 64;
 constexpr size_t WS_ZDONE = 96;
 constexpr size_t WS_EXIT = 128;
 constexpr size_t WS_YACC = 256;
-constexpr size_t WS_ZACC = WS_YACC + sizeof(float) * NACC * H;
+constexpr size_t WS_ZACC = WS_YACC + sizeof(float) * NACC * YCOPIES * H;
 constexpr size_t WS_XBUF = WS_ZACC + sizeof(float) * NACC * 128;
 constexpr size_t WS_BYTES = WS_XBUF + sizeof(float) * NACC * H;
 
 __device__ __forceinline__ int64_t split_lo(int64_t n, int c, int G) { return n * c / G; }
 // predictor tiles must fit a slot and split evenly over 4 threads per neuron
 __device__ __forceinline__ bool rank_ok(int r) { return r > 0 && r <= 96 && (r & 7) == 0; }
+
+// x_l[8t, 8t+8) = x_{l-1} + sum of the YCOPIES partial-y copies of layer l-1
+__device__ __forceinline__ void load_x(const StackParams& p, int lm1, int t, float (&x)[8]) {
+  const float4* xv = reinterpret_cast<const float4*>(p.xbuf + (size_t)(lm1 % NACC) * H + 8 * t);
+  float4 a = __ldcg(xv), b = __ldcg(xv + 1);
+  float4 ya[YCOPIES], yb[YCOPIES];
+#pragma unroll
+  for (int k = 0; k < YCOPIES; ++k) {
+    const float4* yv = reinterpret_cast<const float4*>(p.yacc + ((size_t)(lm1 % NACC) * YCOPIES + k) * H + 8 * t);
+    ya[k] = __ldcg(yv);
+    yb[k] = __ldcg(yv + 1);
+  }
+#pragma unroll
+  for (int k = 0; k < YCOPIES; ++k) {
+    a.x += ya[k].x; a.y += ya[k].y; a.z += ya[k].z; a.w += ya[k].w;
+    b.x += yb[k].x; b.y += yb[k].y; b.z += yb[k].z; b.w += yb[k].w;
+  }
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+
+// generic-proxy shared-memory writes -> visible to the bulk-copy (async) proxy
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// dst[i] += src[i] (fp32), bytes % 16 == 0, both 16-byte aligned, done by the L2
+__device__ __forceinline__ void bulk_reduce_add_f32(float* dst, const float* src, uint32_t bytes) {
+  asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(dst),
+               "r"(smem_u32(src)), "r"(bytes)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// wait until this thread's bulk groups completed (their writes performed)
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void red_add_v4(float* dst, float a, float b, float c, float d) {
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
@@ -226,20 +265,20 @@ __device__ __forceinline__ float cons_sum(StackSmem& sm, float a) {
 // One thread polls ring position q (entry e, phase parity par).  Returns 1
 // when it holds a fill of layer l, 0 when layer l's stream ended before it
 // (the fill belongs to the next layer, or the issuer sealed layer l with
-// fewer groups), -1 when the wait limit passed.  A fill counts once the
-// entry's info names q: the issuer writes it only after the entry's previous
-// fill was consumed, so the mbarrier parity test that follows is exact.
+// fewer groups), -1 when the wait limit passed.  Position q is looked at once
+// the entry's info names it: the issuer writes that only after the entry's
+// previous fill was consumed, so the mbarrier parity test is then exact.  The
+// poller's observation of the completed phase reaches the rest of its
+// subgroup through the subgroup barrier that follows.
 __device__ __forceinline__ int poll_pos(StackSmem& sm, uint32_t q, int e, uint32_t par, int l, int gi,
                                         uint64_t* waited) {
-  if (mbar_test_wait(&sm.full[e], par) && ld_vol_u(&sm.info[e].pos) == q && mbar_test_wait(&sm.full[e], par))
-    return (sm.info[e].layer == l) ? 1 : 0;
+  if (ld_vol_u(&sm.info[e].pos) == q && mbar_test_wait(&sm.full[e], par)) return (sm.info[e].layer == l) ? 1 : 0;
   const uint64_t c0 = (waited != nullptr) ? (uint64_t)clock64() : 0;
   const uint64_t t0 = globaltimer_ns();
   int r = -1;
   for (uint32_t i = 0;; ++i) {
     // suspends until the phase completes or ~200 ns pass
-    if (mbar_try_wait_hint(&sm.full[e], par, 200) && ld_vol_u(&sm.info[e].pos) == q &&
-        mbar_test_wait(&sm.full[e], par)) {
+    if (ld_vol_u(&sm.info[e].pos) == q && mbar_try_wait_hint(&sm.full[e], par, 200)) {
       r = (sm.info[e].layer == l) ? 1 : 0;
       break;
     }
@@ -254,11 +293,6 @@ __device__ __forceinline__ int poll_pos(StackSmem& sm, uint32_t q, int e, uint32
   }
   if (waited != nullptr) *waited += (uint64_t)clock64() - c0;
   return r;
-}
-// every thread observes the (already completed) fill itself
-__device__ __forceinline__ void observe_pos(StackSmem& sm, int e, uint32_t par) {
-  while (!mbar_test_wait(&sm.full[e], par)) {
-  }
 }
 __device__ __forceinline__ void sg_release(StackSmem& sm, int e) {
   __syncwarp();
@@ -466,100 +500,6 @@ __device__ __forceinline__ void sg_cold(StackSmem& sm, const StackParams& p, con
   for (int k = 0; k < SPT; ++k) y[k] = (k & 1) ? fmaf(-1152.0f, csb, y[k]) : fmaf(-1032.0f, csa, y[k]);
 }
 
-// W_up group: n (<= 2) tiles of layer ln's predictor -> own mask words of layer ln.
-// Its bottleneck z is complete once all WD_TILES W_down tiles were added.
-__device__ __forceinline__ void sg_wup(StackSmem& sm, const StackParams& p, int rank, const uint8_t* slot0,
-                                       const uint8_t* slot1, int n, int tile0, int u0, int ln, int sg) {
-  const int u = threadIdx.x & (SG_THREADS - 1), lane = threadIdx.x & 31, w = u >> 5;
-  float* z = sm.ystage + sg * 128;
-  if (u == 0) {
-    const uint32_t* cnt = p.zdone + ln % NACC;
-    if (ld_acquire_u32(cnt) < (uint32_t)WD_TILES) {
-      const uint64_t t0 = globaltimer_ns();
-      uint32_t i = 0;
-      while (ld_acquire_u32(cnt) < (uint32_t)WD_TILES) {
-        if ((++i & 63) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
-          sm.abort = 1;
-          atomicOr(p.status, HC_ERR_TIMEOUT);
-          break;
-        }
-        __nanosleep(64);
-      }
-    }
-    __threadfence();
-  }
-  named_bar(2 + sg, SG_THREADS);
-  if (u < rank) z[u] = __ldcg(p.zacc + (size_t)(ln % NACC) * 128 + u);
-  named_bar(2 + sg, SG_THREADS);
-  const int per = rank >> 2;                    // 4 threads per neuron
-  const int j = u >> 2, part = u & 3;
-  for (int k = 0; k < n; ++k) {
-    const int tile = tile0 + k;
-    const float* t = reinterpret_cast<const float*>(k == 0 ? slot0 : slot1);
-    const int rows = min(WU_ROWS, p.inter - tile * WU_ROWS);
-    float acc = 0.0f;
-    if (j < rows) {
-      const float2* wr = reinterpret_cast<const float2*>(t + j * rank + part * per);
-      const float2* zr = reinterpret_cast<const float2*>(z + part * per);
-      const int half = per >> 1;
-      int ii = j % half;                        // rows of a warp start at different banks
-      for (int i = 0; i < half; ++i) {
-        const float2 a = wr[ii], b = zr[ii];
-        acc = fmaf(a.x, b.x, acc);
-        acc = fmaf(a.y, b.y, acc);
-        ii = (ii + 1 == half) ? 0 : ii + 1;
-      }
-    }
-    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-    const float lg = acc + ((j < rows) ? t[WU_ROWS * rank + j] : 0.0f);
-    const bool on = (j < rows) && (lg >= p.thr);
-    const unsigned b = __ballot_sync(0xffffffffu, on && part == 0);
-    if (lane == 0) {
-      uint32_t byte = 0;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) byte |= ((b >> (4 * q)) & 1u) << q;
-      reinterpret_cast<uint8_t*>(sm.own_words)[4 * (tile - u0) + w] = (uint8_t)byte;
-    }
-  }
-  named_bar(2 + sg, SG_THREADS);
-  if (u == 0) {
-    const uint32_t w0 = sm.own_words[tile0 - u0];
-    const uint32_t w1 = (n > 1) ? sm.own_words[tile0 + 1 - u0] : 0u;
-    __threadfence_block();
-    if (atomicSub(&sm.wup_left, n) == n) {
-      mbar_arrive(&sm.own_ready);
-      trace_ev(p, ln, 21);
-    }
-    uint32_t* mrow = p.masks + (size_t)ln * p.words;
-    mrow[tile0] = w0;
-    if (n > 1) mrow[tile0 + 1] = w1;
-  }
-}
-
-// W_down group: n (<= 2) tiles of layer l+1's predictor -> z partials, then
-// the tiles are counted in zdone (after the partials are visible).
-__device__ __forceinline__ void sg_wdown(StackSmem& sm, const StackParams& p, const float* xs,
-                                         const uint8_t* slot0, const uint8_t* slot1, int n, int tile0, int d0,
-                                         int rank_n, int l, int sg) {
-  const int u = threadIdx.x & (SG_THREADS - 1);
-  const int parts = SG_THREADS / rank_n, r = u % rank_n, part = u / rank_n;
-  if (part < parts) {
-    float acc = 0.0f;
-    for (int k = 0; k < n; ++k) {
-      const float* t = reinterpret_cast<const float*>(k == 0 ? slot0 : slot1);
-      const float* xr = xs + (tile0 + k - d0) * WD_ROWS;
-      for (int row = part; row < WD_ROWS; row += parts) acc = fmaf(t[row * rank_n + r], xr[row], acc);
-    }
-    atomicAdd(p.zacc + (size_t)((l + 1) % NACC) * 128 + r, acc);
-  }
-  named_bar(2 + sg, SG_THREADS);
-  if (u == 0) {
-    __threadfence();
-    atomicAdd(p.zdone + (l + 1) % NACC, (uint32_t)n);
-  }
-}
-
 // grid barrier: arrive (after this CTA's atomics) ...
 __device__ __forceinline__ void grid_arrive(const StackParams& p) {
   named_bar(1, CONS_THREADS);
@@ -644,7 +584,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
   extern __shared__ __align__(128) uint8_t smem_raw[];
   StackSmem& sm = *reinterpret_cast<StackSmem*>(smem_raw);
   uint8_t* ring = smem_raw + RING_OFF;
-  float* xs = reinterpret_cast<float*>(ring + (size_t)NE * ENTRY_BYTES);
+  float* xs = sm.ystage;
   const int tid = threadIdx.x;
   const int G = gridDim.x;
   const int c = blockIdx.x;
@@ -655,7 +595,9 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
       mbar_init(&sm.empty[e], SG_WARPS);
       sm.info[e].pos = 0xFFFFFFFFu;
     }
-    mbar_init(&sm.own_ready, 1);
+    mbar_init(&sm.phase0_done, 1);
+    mbar_init(&sm.pbar, 1);
+    mbar_init(&sm.wdown_done, 1);
     mbar_init(&sm.plan_full, 1);
     mbar_init(&sm.plan_empty, 1);
     sm.abort = 0;
@@ -668,61 +610,43 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
 
   if (tid >= CONS_THREADS + 32) {
     // ============================ planner warp =============================
-    // Per layer: take the CTA's own mask words (from the consumers' W_up
-    // groups at the end of the previous layer, from `masks` when given or for
-    // layer 0, or all ones without a predictor), list the active cold ids of
-    // its neuron range in ascending order, resolve them to record indices and
-    // prefetch the records into L2.
+    // List of layer 0 from `masks`; then per layer l: the CTA's W_down rows of
+    // layer l+1's predictor (once the consumers normalised x_l), and, once
+    // every CTA's rows are in, the logits of its neuron-id range -> its mask
+    // words of layer l+1 (or `masks` when given, or all ones without a
+    // predictor) -> the ascending list of its active cold records.
     const int lane = tid & 31;
     bool ok = true;
+    const int u0 = (int)split_lo(p.words, c, G), nw = (int)split_lo(p.words, c + 1, G) - u0;
+    uint32_t pphase = 0, p0phase = 0;
+    // one tile into pbuf with the planner's own bulk copy (bounded wait)
+    auto load_tile = [&](const void* a, uint32_t abytes, const void* b, uint32_t bbytes, uint32_t boff) -> bool {
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&sm.pbar, abytes + bbytes);
+        bulk_g2s(sm.pbuf, a, abytes, &sm.pbar, 0ull);
+        if (bbytes) bulk_g2s(sm.pbuf + boff, b, bbytes, &sm.pbar, 0ull);
+      }
+      const bool done = mbar_wait(&sm.pbar, pphase & 1u, WAIT_LIMIT_NS);
+      ++pphase;
+      return __all_sync(0xffffffffu, done);
+    };
     // The static part of a layer's lookup (fetch_bits word and table entries
-    // of the own id range) is loaded while the previous layer runs, so only
-    // shared-memory work remains once the own mask words arrive.
+    // of the own id range) is loaded early, so only shared-memory work
+    // remains once the own mask words are known.
     uint32_t fetch = 0;
     auto preload = [&](int l) {
       const hc_layer_desc& d = p.layers[l];
-      const int u0 = (int)split_lo(p.words, c, G), u1 = (int)split_lo(p.words, c + 1, G);
-      fetch = (lane < u1 - u0) ? __ldg(d.fetch_bits + u0 + lane) : 0u;
-      const int id0 = u0 * 32, nid = min(u1 * 32, p.inter) - id0;
+      fetch = (lane < nw) ? __ldg(d.fetch_bits + u0 + lane) : 0u;
+      const int id0 = u0 * 32, nid = min((u0 + nw) * 32, p.inter) - id0;
       for (int i = lane; i < nid; i += 32) sm.plan_list[i] = __ldg(d.table + id0 + i);
       __syncwarp();
     };
-    preload(0);
-    uint32_t ready_phase = 0;
-    for (int l = 0; l < p.n_layers && ok; ++l) {
+    // own words (one per lane) & fetch bits -> ascending record list of layer l
+    auto build = [&](int l, uint32_t own) {
       const hc_layer_desc& dl = p.layers[l];
-      const uint8_t* cold_records = dl.cold_records;
       const int n_records = dl.n_records;
-      const int u0 = (int)split_lo(p.words, c, G), nw = (int)split_lo(p.words, c + 1, G) - u0;
-      if (l > 0) {
-        // the issuer is done with the previous list once it issued that layer's cold records
-        if (lane == 0) ok = mbar_wait(&sm.plan_empty, (uint32_t)(l - 1) & 1u, WAIT_LIMIT_NS);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
-        preload(l);
-      }
-      uint32_t own = 0;
-      uint32_t* mrow = p.masks + (size_t)l * p.words;
-      if (layer_logits(p, dl, l)) {
-        if (nw > 0) {
-          if (lane == 0) ok = mbar_wait(&sm.own_ready, ready_phase & 1u, WAIT_LIMIT_NS);
-          ok = __shfl_sync(0xffffffffu, ok, 0);
-          if (!ok) break;
-          ++ready_phase;
-          if (lane < nw) own = sm.own_words[lane];
-        }
-      } else if (l == 0 || p.masks_given) {
-        if (lane < nw) own = __ldcg(mrow + u0 + lane);
-      } else if (lane < nw) {
-        // no predictor: fetch every cold neuron (engine.py:282-283)
-        const int valid = min(32, p.inter - 32 * (u0 + lane));
-        own = valid >= 32 ? 0xffffffffu : ((1u << valid) - 1u);
-        mrow[u0 + lane] = own;
-      }
-      if (lane == 0) trace_ev(p, l, 22);
-      // active words (nw <= OWN_WORDS = 32: one per lane), then in-place
-      // compaction word by word: word w's entries are read (one per lane)
-      // before its writes, which land below 32 (w + 1)
+      // in-place compaction word by word: word w's entries are read (one per
+      // lane) before its writes, which land below 32 (w + 1)
       const uint32_t mw = own & fetch;
       int cnt = 0;
       for (int w = 0; w < nw; ++w) {
@@ -749,7 +673,115 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
       }
       // records the issuer cannot take yet (ring full) come from L2 when it can
       for (int i = lane; i < cnt; i += 32)
-        prefetch_l2(cold_records + (size_t)sm.plan_list[i] * REC_BYTES, REC_COPY);
+        prefetch_l2(dl.cold_records + (size_t)sm.plan_list[i] * REC_BYTES, REC_COPY);
+    };
+    // mask words of layer l without its predictor: given, or all ones
+    auto words_without_predictor = [&](int l) -> uint32_t {
+      uint32_t* mrow = p.masks + (size_t)l * p.words;
+      if (lane >= nw) return 0u;
+      if (l == 0 || p.masks_given) return __ldcg(mrow + u0 + lane);
+      // no predictor: fetch every cold neuron (engine.py:282-283)
+      const int valid = min(32, p.inter - 32 * (u0 + lane));
+      const uint32_t m = valid >= 32 ? 0xffffffffu : ((1u << valid) - 1u);
+      mrow[u0 + lane] = m;
+      return m;
+    };
+    preload(0);
+    build(0, words_without_predictor(0));
+    for (int l = 0; l + 1 < p.n_layers && ok; ++l) {
+      const bool pred_next = next_pred(p, l);
+      const hc_layer_desc& dn = p.layers[l + 1];
+      const int rank = pred_next ? dn.rank : 0;
+      uint32_t own = 0;
+      if (pred_next) {
+        // ---- W_down rows [d0, d1) of layer l+1's predictor on RMSNorm_{l+1}(x_l)
+        const int nd = H / WD_ROWS;
+        const int d0 = (int)split_lo(nd, c, G), d1 = (int)split_lo(nd, c + 1, G);
+        // (one phase per layer with a next predictor, like wdown_done)
+        if (lane == 0) ok = mbar_wait(&sm.phase0_done, p0phase & 1u, WAIT_LIMIT_NS);
+        ++p0phase;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        for (int tile = d0; tile < d1 && ok; ++tile) {
+          ok = load_tile(dn.pred_w_down_t + (size_t)tile * WD_ROWS * rank, WD_ROWS * rank * 4, nullptr, 0, 0);
+          if (!ok) break;
+          const float* t = reinterpret_cast<const float*>(sm.pbuf);
+          const float* xr = xs + (tile - d0) * WD_ROWS;
+          for (int r = lane; r < rank; r += 32) {
+            float acc = 0.0f;
+#pragma unroll 8
+            for (int row = 0; row < WD_ROWS; ++row) acc = fmaf(t[row * rank + r], xr[row], acc);
+            atomicAdd(p.zacc + (size_t)((l + 1) % NACC) * 128 + r, acc);
+          }
+          __syncwarp();      // pbuf is reused by the next copy
+        }
+        if (!ok) break;
+        if (lane == 0) {
+          mbar_arrive(&sm.wdown_done);       // ystage is the consumers' again
+          if (d1 > d0) {
+            __threadfence();
+            atomicAdd(p.zdone + (l + 1) % NACC, (uint32_t)(d1 - d0));
+          }
+        }
+        // ---- the issuer is done with list l; start on list l+1
+        if (lane == 0) ok = mbar_wait(&sm.plan_empty, (uint32_t)l & 1u, WAIT_LIMIT_NS);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        preload(l + 1);
+        if (nw > 0) {
+          // ---- z of layer l+1 is complete once all W_down tiles were added
+          if (lane == 0) {
+            const uint32_t* cnt = p.zdone + (l + 1) % NACC;
+            const uint64_t t0 = globaltimer_ns();
+            uint32_t i = 0;
+            while (ld_acquire_u32(cnt) < (uint32_t)WD_TILES) {
+              if ((++i & 63) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+                ok = false;
+                break;
+              }
+              __nanosleep(100);
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) break;
+          __syncwarp();      // lane 0's acquire orders every lane's reads of z below
+          for (int i = lane; i < rank; i += 32) sm.z[i] = __ldcg(p.zacc + (size_t)((l + 1) % NACC) * 128 + i);
+          __syncwarp();
+          // ---- own logits: one W_up tile (32 neurons == one mask word) at a time
+          for (int w = 0; w < nw && ok; ++w) {
+            const int tile = u0 + w;
+            const int rows = min(WU_ROWS, p.inter - tile * WU_ROWS);
+            ok = load_tile(dn.pred_w_up + (size_t)tile * WU_ROWS * rank, rows * rank * 4,
+                           dn.pred_b_up + (size_t)tile * WU_ROWS, rows * 4, WU_ROWS * rank * 4);
+            if (!ok) break;
+            const float* t = reinterpret_cast<const float*>(sm.pbuf);
+            float acc = 0.0f;
+            if (lane < rows) {
+              // lane = neuron; the rotated start keeps the 32 rows on distinct banks
+              const float* row = t + lane * rank;
+              int k = lane % rank;
+              for (int i = 0; i < rank; ++i) {
+                acc = fmaf(row[k], sm.z[k], acc);
+                k = (k + 1 == rank) ? 0 : k + 1;
+              }
+              acc += t[WU_ROWS * rank + lane];
+            }
+            const uint32_t word = __ballot_sync(0xffffffffu, lane < rows && acc >= p.thr);
+            if (lane == w) own = word;
+            __syncwarp();
+          }
+          if (!ok) break;
+          if (lane < nw) p.masks[(size_t)(l + 1) * p.words + u0 + lane] = own;
+          if (lane == 0) trace_ev(p, l + 1, 21);
+        }
+      } else {
+        if (lane == 0) ok = mbar_wait(&sm.plan_empty, (uint32_t)l & 1u, WAIT_LIMIT_NS);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        preload(l + 1);
+        own = words_without_predictor(l + 1);
+      }
+      build(l + 1, own);
     }
     if (lane == 0 && !ok) {
       sm.abort = 1;
@@ -759,11 +791,9 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
     __syncthreads();
   } else if (tid >= CONS_THREADS) {
     // ============================ issuer warp ==============================
-    // Lane 0 streams the CTA's groups of layer l in order: the next
-    // predictor's W_down tiles, the planner's cold records, the next
-    // predictor's own W_up tiles, the static hot neurons, then hot neurons
-    // claimed from the layer's global counter until none are left; then it
-    // seals the layer.
+    // Lane 0 streams the CTA's groups of layer l in order: the planner's cold
+    // records, the static hot neurons, then hot neurons claimed from the
+    // layer's global counter until none are left; then it seals the layer.
     const int lane = tid & 31;
     Producer pr;
     if (lane == 0) {
@@ -804,20 +834,6 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
           const int rows = min(sp.u1 * WU_ROWS, p.inter) - sp.u0 * WU_ROWS;
           prefetch_l2_range(dn->pred_w_up + (size_t)sp.u0 * WU_ROWS * rank_n, (size_t)rows * rank_n * 4);
         }
-        // W_down tiles of the next layer's predictor, two per group (first: every
-        // CTA's W_up groups wait for all of them)
-        for (int u = sp.d0; u < sp.d1 && pr.ok; u += 2) {
-          const int n = min(2, sp.d1 - u);
-          const uint32_t bytes = WD_ROWS * rank_n * 4;
-          Copy cp[2];
-#pragma unroll
-          for (int k = 0; k < 2; ++k)
-            cp[k] = {k < n ? dn->pred_w_down_t + (size_t)(u + k) * WD_ROWS * rank_n : nullptr, k < n ? bytes : 0u,
-                     (uint32_t)(k * HALF_BYTES)};
-          issue_entry(sm, ring, pr, l, UNIT_WDOWN, n, u, cp, iwp);
-          ++ng;
-        }
-        if (!pr.ok) break;
         // the planner's cold records of this layer, four per group
         if (!mbar_wait(&sm.plan_full, (uint32_t)l & 1u, WAIT_LIMIT_NS)) {
           pr.ok = false;
@@ -838,24 +854,6 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         if (!pr.ok) break;
         mbar_arrive(&sm.plan_empty);
         trace_ev(p, l, 12);
-        // own W_up tiles of the next layer's predictor, two per group: its mask
-        // words, and so its cold list, are ready before the next layer starts
-        if (pred_next) {
-          for (int u = sp.u0; u < sp.u1 && pr.ok; u += 2) {
-            const int n = min(2, sp.u1 - u);
-            Copy cp[4];
-#pragma unroll
-            for (int k = 0; k < 2; ++k) {
-              const int rows = k < n ? min(WU_ROWS, p.inter - (u + k) * WU_ROWS) : 0;
-              cp[2 * k] = {k < n ? dn->pred_w_up + (size_t)(u + k) * WU_ROWS * rank_n : nullptr,
-                           (uint32_t)(rows * rank_n * 4), (uint32_t)(k * HALF_BYTES)};
-              cp[2 * k + 1] = {k < n ? dn->pred_b_up + (size_t)(u + k) * WU_ROWS : nullptr, (uint32_t)(rows * 4),
-                               (uint32_t)(k * HALF_BYTES + WU_ROWS * rank_n * 4)};
-            }
-            issue_entry(sm, ring, pr, l, UNIT_WUP, n, u, cp, iwp);
-            ++ng;
-          }
-        }
         // static hot neurons, two per group
         for (int64_t i = sp.h0; i < sp.h1 && pr.ok; i += NB_HOT) {
           const int n = (int)min((int64_t)NB_HOT, sp.h1 - i);
@@ -930,6 +928,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
     const int t = tid;
     const int sg = t / SG_THREADS, u = t & (SG_THREADS - 1);
     uint32_t base = 0;       // ring position of the layer's first group
+    uint32_t wd_phase = 0;   // layers with a next predictor so far (wdown_done phases)
     int rbuf = 0, dbuf = 0;
     bool ok = true;
     for (int l = 0; l < p.n_layers && ok; ++l) {
@@ -939,7 +938,6 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         atomicOr(p.status, HC_ERR_UNSUPPORTED);
       const Split sp = make_split(p, d, pred_next, c, G);
       const hc_layer_desc* dn = pred_next ? &p.layers[l + 1] : nullptr;
-      const int rank_n = pred_next ? dn->rank : 0;
 
       // ---- layer boundary: x_l = x_{l-1} + y_{l-1} once every CTA has added its part
       float x[EPT];
@@ -950,11 +948,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
       } else {
         ok = grid_wait(sm, p, (uint32_t)l * G);
         if (!ok) break;
-        const float4* xv = reinterpret_cast<const float4*>(p.xbuf + (size_t)((l - 1) % NACC) * H + EPT * t);
-        const float4* yv = reinterpret_cast<const float4*>(p.yacc + (size_t)((l - 1) % NACC) * H + EPT * t);
-        const float4 xa = __ldcg(xv), xb = __ldcg(xv + 1), a = __ldcg(yv), b = __ldcg(yv + 1);
-        x[0] = xa.x + a.x; x[1] = xa.y + a.y; x[2] = xa.z + a.z; x[3] = xa.w + a.w;
-        x[4] = xb.x + b.x; x[5] = xb.y + b.y; x[6] = xb.z + b.z; x[7] = xb.w + b.w;
+        load_x(p, l - 1, t, x);
         if (p.x_hist && c == 0) {
           float4* h = reinterpret_cast<float4*>(p.x_hist + (size_t)(l - 1) * H + EPT * t);
           h[0] = make_float4(x[0], x[1], x[2], x[3]);
@@ -973,8 +967,9 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
       // l+2 and its tile count during layer l+1; the hot-neuron counter of layer
       // l+2 once the claiming CTA's consumers started layer l+1.
       {
-        float* yz = p.yacc + (size_t)((l + 1) % NACC) * H;
-        for (int i = (int)split_lo(H / 4, c, G) + t; i < (int)split_lo(H / 4, c + 1, G); i += CONS_THREADS)
+        float* yz = p.yacc + (size_t)((l + 1) % NACC) * YCOPIES * H;
+        constexpr int NV = YCOPIES * H / 4;
+        for (int i = (int)split_lo(NV, c, G) + t; i < (int)split_lo(NV, c + 1, G); i += CONS_THREADS)
           reinterpret_cast<float4*>(yz)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (c == 0 && t < 128) p.zacc[(size_t)((l + 2) % NACC) * 128 + t] = 0.0f;
         if (c == 0 && t == 0) p.hot_next[(l + 2) % NACC] = 0u;
@@ -1046,20 +1041,19 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
           }
         }
       }
-      if (t == 0) {
-        // W_up tiles of the next layer's predictor this CTA turns into mask words
-        sm.wup_left = pred_next ? sp.u1 - sp.u0 : 0;
-        *reinterpret_cast<volatile int32_t*>(&sm.cons_layer) = l;
-      }
+      if (t == 0) *reinterpret_cast<volatile int32_t*>(&sm.cons_layer) = l;
       named_bar(1, CONS_THREADS);
-      if (t == 0) trace_ev(p, l, 1);
+      if (t == 0) {
+        if (pred_next) mbar_arrive(&sm.phase0_done);     // the planner's W_down rows (xs) are written
+        trace_ev(p, l, 1);
+      }
 
       // ---- subgroup phase: groups g = sg, sg + 4, ... of the layer's stream
       float y[SPT];
 #pragma unroll
       for (int k = 0; k < SPT; ++k) y[k] = 0.0f;
       // trace counters (subgroup 0's poller, SM cycles): 0 fill waits, 1 cold,
-      // 2 hot, 3 predictor groups, 4 group barrier, 5 observe, 6 release, 7 start
+      // 2 hot, 4 group barrier, 5 group setup, 6 release, 7 start
       const bool tr = p.trace != nullptr && t == 0;
       if (tr) {
         for (int k = 0; k < 7; ++k) sm.tstat[k] = 0;
@@ -1088,7 +1082,6 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         const int r = sm.sgdec[sg][dbuf];
         dbuf ^= 1;
         if (r <= 0) break;
-        observe_pos(sm, e, par);
         const SlotInfo inf = sm.info[e];
         const uint8_t* s0 = ring + (size_t)e * ENTRY_BYTES;
         const uint8_t* s1 = s0 + HALF_BYTES;
@@ -1097,18 +1090,14 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         if (inf.kind == UNIT_COLD) {
           sg_cold(sm, p, s0, s1, inf.n, sg, rbuf, y);
           rbuf ^= 1;
-        } else if (inf.kind == UNIT_HOT) {
+        } else {
           sg_hot(sm, p, d.hot_scale, s0, s1, inf.n, inf.index, sg, rbuf, y);
           rbuf ^= 1;
-        } else if (inf.kind == UNIT_WUP) {
-          sg_wup(sm, p, rank_n, s0, s1, inf.n, inf.index, sp.u0, l + 1, sg);
-        } else if (inf.kind == UNIT_WDOWN) {
-          sg_wdown(sm, p, xs, s0, s1, inf.n, inf.index, sp.d0, rank_n, l, sg);
         }
         uint64_t tg1 = 0;
         if (tr) {
           tg1 = (uint64_t)clock64();
-          sm.tstat[inf.kind == UNIT_COLD ? 1 : inf.kind == UNIT_HOT ? 2 : 3] += tg1 - tg0;
+          sm.tstat[inf.kind == UNIT_COLD ? 1 : 2] += tg1 - tg0;
         }
         sg_release(sm, e);
         if (tr) sm.tstat[6] += (uint64_t)clock64() - tg1;
@@ -1132,7 +1121,16 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
       }
       // ---- all subgroups done: one abort decision for everyone, then sum the
       // partial y (fixed tree in shared memory) and add it to the layer's accumulator
-      if (t == 0) sm.flag = ld_vol(&sm.abort) ? 0 : 1;
+      if (t == 0) {
+        bool okw = true;
+        if (pred_next) okw = mbar_wait(&sm.wdown_done, wd_phase & 1u, WAIT_LIMIT_NS);
+        if (!okw) {
+          sm.abort = 1;
+          atomicOr(p.status, HC_ERR_TIMEOUT);
+        }
+        sm.flag = ld_vol(&sm.abort) ? 0 : 1;
+      }
+      if (pred_next) ++wd_phase;
       named_bar(1, CONS_THREADS);
       if (sm.flag == 0) {
         ok = false;
@@ -1160,29 +1158,41 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
           for (int k = 0; k < SPT; ++k) dst[k * SG_THREADS + u] = y[k];
         }
         named_bar(1, CONS_THREADS);
-        // element layout: thread t adds elements [8t, 8t+8) (element 32u+k sits at k*128+u)
+        // element layout: thread t sums elements [8t, 8t+8) (element 32u+k sits at
+        // k*128+u) and stores them in element order for one bulk reduction
         float e[EPT];
         const int eu = t >> 2, ek = EPT * (t & 3);
 #pragma unroll
         for (int i = 0; i < EPT; ++i) e[i] = bufA[(ek + i) * SG_THREADS + eu] + bufB[(ek + i) * SG_THREADS + eu];
-        float* ya = p.yacc + (size_t)(l % NACC) * H + EPT * t;
-        red_add_v4(ya, e[0], e[1], e[2], e[3]);
-        red_add_v4(ya + 4, e[4], e[5], e[6], e[7]);
-        if (t == 0) trace_ev(p, l, 9);
+        named_bar(1, CONS_THREADS);
+        float4* yo = reinterpret_cast<float4*>(bufA + EPT * t);
+        yo[0] = make_float4(e[0], e[1], e[2], e[3]);
+        yo[1] = make_float4(e[4], e[5], e[6], e[7]);
+        fence_proxy_async_smem();
+        named_bar(1, CONS_THREADS);
+        if (t == 0) {
+          trace_ev(p, l, 9);
+          // y_l += this CTA's partial: the L2 adds 16 KB in one bulk operation
+          bulk_reduce_add_f32(p.yacc + ((size_t)(l % NACC) * YCOPIES + c % YCOPIES) * H, bufA, H * sizeof(float));
+          bulk_wait_all();
+          trace_ev(p, l, 28);
+          // then the grid-barrier arrival, ordered after the reduction's writes
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          trace_ev(p, l, 29);
+          asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar_count) : "memory");
+          trace_ev(p, l, 8);
+        }
       }
-      grid_arrive(p);
-      if (t == 0) trace_ev(p, l, 8);
     }
     // ---- output: x_L = x_{L-1} + y_{L-1}
     if (ok) {
       const int L = p.n_layers;
       ok = grid_wait(sm, p, (uint32_t)L * G);
       if (ok && c == 0) {
-        const float4* xv = reinterpret_cast<const float4*>(p.xbuf + (size_t)((L - 1) % NACC) * H + EPT * t);
-        const float4* yv = reinterpret_cast<const float4*>(p.yacc + (size_t)((L - 1) % NACC) * H + EPT * t);
-        const float4 xa = __ldcg(xv), xb = __ldcg(xv + 1), a = __ldcg(yv), b = __ldcg(yv + 1);
-        const float4 o0 = make_float4(xa.x + a.x, xa.y + a.y, xa.z + a.z, xa.w + a.w);
-        const float4 o1 = make_float4(xb.x + b.x, xb.y + b.y, xb.z + b.z, xb.w + b.w);
+        float xo[EPT];
+        load_x(p, L - 1, t, xo);
+        const float4 o0 = make_float4(xo[0], xo[1], xo[2], xo[3]);
+        const float4 o1 = make_float4(xo[4], xo[5], xo[6], xo[7]);
         float4* out = reinterpret_cast<float4*>(p.x_out + EPT * t);
         out[0] = o0;
         out[1] = o1;
@@ -1206,7 +1216,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
   __syncthreads();
   if (sm.last) {
     __threadfence();
-    for (int i = tid; i < NACC * H / 4; i += STACK_THREADS)
+    for (int i = tid; i < NACC * YCOPIES * H / 4; i += STACK_THREADS)
       reinterpret_cast<float4*>(p.yacc)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int i = tid; i < NACC * 128; i += STACK_THREADS) p.zacc[i] = 0.0f;
     if (tid < NACC) p.hot_next[tid] = 0u;
@@ -1255,9 +1265,7 @@ extern "C" int hc_ffn_stack(const hc_layer_desc* layers, int32_t n_layers, int32
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
     return HC_ERR_CUDA;
-  const int wd_tiles = (H / WD_ROWS + G - 1) / G;
-  const size_t xs_bytes = (size_t)wd_tiles * WD_ROWS * sizeof(float);
-  const size_t smem_need = RING_OFF + (size_t)NE * ENTRY_BYTES + xs_bytes;
+  const size_t smem_need = RING_OFF + (size_t)NE * ENTRY_BYTES;
   if ((long)smem_need > (long)smem_max) return HC_ERR_UNSUPPORTED;
   const int smem = (int)smem_need;
   if (cudaFuncSetAttribute(ffn_stack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)

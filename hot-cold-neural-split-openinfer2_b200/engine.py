@@ -159,6 +159,9 @@ class FFNStack:
         put("subgroup_spread", sg_done.max(dim=2).values - sg_done.min(dim=2).values)
         put("y_sum", us[:, :, 9] - sg_done.max(dim=2).values)
         put("arrive", us[:, :, 8] - us[:, :, 9])
+        put("arrive.bulk_reduce", us[:, :, 28] - us[:, :, 9])
+        put("arrive.proxy_fence", us[:, :, 29] - us[:, :, 28])
+        put("arrive.release", us[:, :, 8] - us[:, :, 29])
         if self.L > 1:
             put("barrier_wait", us[1:, :, 0] - us[:-1, :, 8])
             put("layer", us[1:, :, 0] - us[:-1, :, 0])
