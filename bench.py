@@ -308,7 +308,8 @@ def run_gpu(args):
         cpu = cpu_reference(4, 0, layers_per_step=2, budget_s=25.0)
         line = {"metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+                "scaling": "weak", "vs_baseline": None, "dtype": "e4m3/int4 weights, fp32 accumulate",
+                "data": "synthetic",
                 "config": {"workload": WORKLOAD, "layers": LAYERS, "hidden": H, "inter": INTER, "hot": N_HOT,
                            "rank": RANK, "batch": 1, "tokens_per_step": TOKENS,
                            "cold_fetched_per_token": round(mean_fetched, 1),
