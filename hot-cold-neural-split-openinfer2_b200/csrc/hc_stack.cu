@@ -67,7 +67,8 @@ constexpr int OWN_WORDS = COLD_LIST / 32;
 constexpr int HOT_BYTES = 3 * H;        // 12288
 constexpr int NACC = 3;                 // rotating y / z / hot-claim accumulators
 constexpr int YCOPIES = 1;              // CTA c adds its partial y into copy c % YCOPIES
-constexpr int STATIC_HOT_DIV = 4;       // 1/4 of the hot neurons are split statically
+constexpr int COLD_CLAIM = 8;           // cold records taken from the layer's pool per claim
+constexpr int POOL_CAP = 32768;         // cold-pool entries per layer (>= inter)
 constexpr int WD_TILES = 4096 / 32;     // W_down tiles of a predictor (H / WD_ROWS)
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;   // 2 s
 static_assert(HALF_BYTES % 128 == 0 && REC_SLOT_OFF % 16 == 0, "halves must stay 16-byte aligned");
@@ -106,7 +107,6 @@ struct StackSmem {
   int32_t ngroups[4];               // groups issued per layer (l & 3)
   int32_t sealed;                   // last layer whose groups are all issued
   int32_t cons_layer;               // last layer the consumers started
-  int32_t plan_n;
   int32_t abort;
   int32_t flag;
   int32_t last;
@@ -115,8 +115,6 @@ struct StackSmem {
   alignas(8) uint64_t phase0_done;  // consumers -> planner: normalised input (and W_down rows) ready
   alignas(8) uint64_t pbar;         // planner's own tile copies
   alignas(8) uint64_t wdown_done;   // planner -> consumers: done with the W_down rows in ystage
-  alignas(8) uint64_t plan_full;    // planner -> issuer: cold list of layer l ready
-  alignas(8) uint64_t plan_empty;   // issuer -> planner: list consumed
 };
 constexpr size_t RING_OFF = (sizeof(StackSmem) + 127) / 128 * 128;
 
@@ -138,6 +136,10 @@ struct StackParams {
   uint32_t* exit_count;
   uint32_t* hot_next;        // [NACC] hot-neuron claims per layer
   uint32_t* zdone;           // [NACC] W_down tiles added into zacc per layer
+  uint32_t* gfill;           // [NACC] cold-pool entries reserved per layer
+  uint32_t* gclaim;          // [NACC] cold-pool entries claimed per layer
+  uint32_t* gdone;           // [NACC] CTAs that published their cold list per layer
+  int32_t* gpool;            // [NACC][POOL_CAP] cold record indices of the layer, all CTAs
   float* yacc;               // [NACC][YCOPIES][H] partial-y accumulators
   float* zacc;               // [NACC][128] predictor bottleneck accumulators
   float* xbuf;               // [NACC][H]   x_l, written by CTA 0
@@ -153,13 +155,17 @@ __device__ __forceinline__ void trace_set(const StackParams& p, int l, int ev, u
   if (p.trace != nullptr) p.trace[((size_t)l * gridDim.x + blockIdx.x) * TRACE_EVENTS + ev] = v;
 }
 
-constexpr size_t WS_HOT_NEXT = 64;
-constexpr size_t WS_ZDONE = 96;
-constexpr size_t WS_EXIT = 128;
+constexpr size_t WS_EXIT = 16;
+constexpr size_t WS_HOT_NEXT = 32;
+constexpr size_t WS_ZDONE = 48;
+constexpr size_t WS_GFILL = 64;
+constexpr size_t WS_GCLAIM = 80;
+constexpr size_t WS_GDONE = 96;
 constexpr size_t WS_YACC = 256;
 constexpr size_t WS_ZACC = WS_YACC + sizeof(float) * NACC * YCOPIES * H;
 constexpr size_t WS_XBUF = WS_ZACC + sizeof(float) * NACC * 128;
-constexpr size_t WS_BYTES = WS_XBUF + sizeof(float) * NACC * H;
+constexpr size_t WS_POOL = WS_XBUF + sizeof(float) * NACC * H;
+constexpr size_t WS_BYTES = WS_POOL + sizeof(int32_t) * NACC * POOL_CAP;
 
 __device__ __forceinline__ int64_t split_lo(int64_t n, int c, int G) { return n * c / G; }
 // predictor tiles must fit a slot and split evenly over 4 threads per neuron
@@ -218,7 +224,7 @@ struct Split {
 __device__ __forceinline__ Split make_split(const StackParams& p, const hc_layer_desc& d, bool pred_next, int c,
                                             int G) {
   Split s;
-  s.n_static = d.n_hot / STATIC_HOT_DIV;
+  s.n_static = 0;
   s.h0 = split_lo(s.n_static, c, G);
   s.h1 = split_lo(s.n_static, c + 1, G);
   s.u0 = (int)split_lo(p.words, c, G);
@@ -598,8 +604,6 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
     mbar_init(&sm.phase0_done, 1);
     mbar_init(&sm.pbar, 1);
     mbar_init(&sm.wdown_done, 1);
-    mbar_init(&sm.plan_full, 1);
-    mbar_init(&sm.plan_empty, 1);
     sm.abort = 0;
     sm.flag = 1;
     sm.sealed = -1;
@@ -665,15 +669,38 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         cnt += __popc(m);
         __syncwarp();
       }
-      if (lane == 0) {
-        sm.plan_n = cnt;
-        mbar_arrive(&sm.plan_full);
+      // Publish into the layer's pool, which every CTA's issuer takes from.  The
+      // pool's counters were cleared in layer l-2, before this CTA's consumers
+      // started layer l-1.
+      if (lane == 0 && l > 0) {
+        const uint64_t t0 = globaltimer_ns();
+        uint32_t i = 0;
+        while (ld_vol(&sm.cons_layer) < l - 1) {
+          if ((++i & 63) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+            ok = false;
+            break;
+          }
+        }
+        __threadfence();
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      uint32_t base = 0;
+      if (lane == 0 && ok) base = atomicAdd(p.gfill + l % NACC, (uint32_t)cnt);
+      base = __shfl_sync(0xffffffffu, base, 0);
+      int32_t* pool = p.gpool + (size_t)(l % NACC) * POOL_CAP;
+      if (ok)
+        for (int i = lane; i < cnt; i += 32) pool[base + i] = sm.plan_list[i];
+      __syncwarp();
+      if (lane == 0 && ok) {
+        __threadfence();
+        atomicAdd(p.gdone + l % NACC, 1u);
         trace_ev(p, l, 20);
         trace_set(p, l, 17, (uint64_t)cnt);
       }
-      // records the issuer cannot take yet (ring full) come from L2 when it can
-      for (int i = lane; i < cnt; i += 32)
-        prefetch_l2(dl.cold_records + (size_t)sm.plan_list[i] * REC_BYTES, REC_COPY);
+      // the records come from L2 for whichever CTA takes them
+      if (ok)
+        for (int i = lane; i < cnt; i += 32)
+          prefetch_l2(dl.cold_records + (size_t)sm.plan_list[i] * REC_BYTES, REC_COPY);
     };
     // mask words of layer l without its predictor: given, or all ones
     auto words_without_predictor = [&](int l) -> uint32_t {
@@ -723,10 +750,6 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
             atomicAdd(p.zdone + (l + 1) % NACC, (uint32_t)(d1 - d0));
           }
         }
-        // ---- the issuer is done with list l; start on list l+1
-        if (lane == 0) ok = mbar_wait(&sm.plan_empty, (uint32_t)l & 1u, WAIT_LIMIT_NS);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
         preload(l + 1);
         if (nw > 0) {
           // ---- z of layer l+1 is complete once all W_down tiles were added
@@ -775,13 +798,11 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
           if (lane == 0) trace_ev(p, l + 1, 21);
         }
       } else {
-        if (lane == 0) ok = mbar_wait(&sm.plan_empty, (uint32_t)l & 1u, WAIT_LIMIT_NS);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
         preload(l + 1);
         own = words_without_predictor(l + 1);
       }
       build(l + 1, own);
+      if (!ok) break;
     }
     if (lane == 0 && !ok) {
       sm.abort = 1;
@@ -791,9 +812,10 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
     __syncthreads();
   } else if (tid >= CONS_THREADS) {
     // ============================ issuer warp ==============================
-    // Lane 0 streams the CTA's groups of layer l in order: the planner's cold
-    // records, the static hot neurons, then hot neurons claimed from the
-    // layer's global counter until none are left; then it seals the layer.
+    // Lane 0 streams the CTA's groups of layer l in order: cold records taken
+    // from the layer's pool (all CTAs' lists) until it is empty, then hot
+    // neurons claimed from the layer's counter until none are left; then it
+    // seals the layer.
     const int lane = tid & 31;
     Producer pr;
     if (lane == 0) {
@@ -834,42 +856,8 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
           const int rows = min(sp.u1 * WU_ROWS, p.inter) - sp.u0 * WU_ROWS;
           prefetch_l2_range(dn->pred_w_up + (size_t)sp.u0 * WU_ROWS * rank_n, (size_t)rows * rank_n * 4);
         }
-        // the planner's cold records of this layer, four per group
-        if (!mbar_wait(&sm.plan_full, (uint32_t)l & 1u, WAIT_LIMIT_NS)) {
-          pr.ok = false;
-          break;
-        }
-        trace_ev(p, l, 11);
-        const int cnt = sm.plan_n;
-        for (int j = 0; j < cnt && pr.ok; j += NB_COLD) {
-          const int n = min(NB_COLD, cnt - j);
-          Copy cp[NB_COLD];
-#pragma unroll
-          for (int k = 0; k < NB_COLD; ++k)
-            cp[k] = {k < n ? d.cold_records + (size_t)sm.plan_list[j + k] * REC_BYTES : nullptr,
-                     k < n ? (uint32_t)REC_COPY : 0u, (uint32_t)((k >> 1) * HALF_BYTES + (k & 1) * REC_SLOT_OFF)};
-          issue_entry(sm, ring, pr, l, UNIT_COLD, n, j, cp, iwp);
-          ++ng;
-        }
-        if (!pr.ok) break;
-        mbar_arrive(&sm.plan_empty);
-        trace_ev(p, l, 12);
-        // static hot neurons, two per group
-        for (int64_t i = sp.h0; i < sp.h1 && pr.ok; i += NB_HOT) {
-          const int n = (int)min((int64_t)NB_HOT, sp.h1 - i);
-          Copy cp[2];
-#pragma unroll
-          for (int k = 0; k < 2; ++k)
-            cp[k] = {k < n ? d.hot + (i + k) * HOT_BYTES : nullptr, k < n ? (uint32_t)HOT_BYTES : 0u,
-                     (uint32_t)(k * HALF_BYTES)};
-          issue_entry(sm, ring, pr, l, UNIT_HOT, n, i, cp, iwp);
-          ++ng;
-        }
-        trace_ev(p, l, 13);
-        // Dynamic hot neurons, two per claim until the layer's counter passes
-        // n_hot; the next claim is taken before the current one is issued.  The
-        // counter was cleared in layer l-2, which this CTA's consumers passed
-        // once they started layer l-1.
+        // The layer's counters (cold pool, hot neurons) were cleared in layer
+        // l-2, which this CTA's consumers passed once they started layer l-1.
         {
           const uint64_t t0 = globaltimer_ns();
           uint32_t i = 0;
@@ -882,6 +870,54 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
           if (!pr.ok) break;
           __threadfence();
         }
+        // Cold records from the layer's pool, COLD_CLAIM per claim (the next
+        // claim is taken before the current one is issued), once every CTA has
+        // published its list.
+        {
+          const uint64_t t0 = globaltimer_ns();
+          uint32_t i = 0;
+          while (ld_acquire_u32(p.gdone + l % NACC) < (uint32_t)G) {
+            if ((++i & 63) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+              pr.ok = false;
+              break;
+            }
+            __nanosleep(64);
+          }
+          if (!pr.ok) break;
+        }
+        trace_ev(p, l, 11);
+        uint64_t cold_taken = 0;
+        {
+          const uint32_t total = __ldcg(p.gfill + l % NACC);
+          const int32_t* pool = p.gpool + (size_t)(l % NACC) * POOL_CAP;
+          uint32_t i = atomicAdd(p.gclaim + l % NACC, (uint32_t)COLD_CLAIM);
+          while (pr.ok && i < total) {
+            const uint32_t inext = atomicAdd(p.gclaim + l % NACC, (uint32_t)COLD_CLAIM);
+            const int n = (int)min((uint32_t)COLD_CLAIM, total - i);
+            int rec[COLD_CLAIM];
+#pragma unroll
+            for (int k = 0; k < COLD_CLAIM; ++k) rec[k] = (k < n) ? __ldcg(pool + i + k) : 0;
+#pragma unroll
+            for (int j = 0; j < COLD_CLAIM; j += NB_COLD) {
+              if (j >= n || !pr.ok) break;
+              const int m = min(NB_COLD, n - j);
+              Copy cp[NB_COLD];
+#pragma unroll
+              for (int k = 0; k < NB_COLD; ++k)
+                cp[k] = {k < m ? d.cold_records + (size_t)rec[j + k] * REC_BYTES : nullptr,
+                         k < m ? (uint32_t)REC_COPY : 0u,
+                         (uint32_t)((k >> 1) * HALF_BYTES + (k & 1) * REC_SLOT_OFF)};
+              issue_entry(sm, ring, pr, l, UNIT_COLD, m, (int64_t)(i + j), cp, iwp);
+              ++ng;
+            }
+            cold_taken += n;
+            i = inext;
+          }
+        }
+        if (!pr.ok) break;
+        trace_ev(p, l, 12);
+        trace_ev(p, l, 13);
+        // Hot neurons, two per claim until the layer's counter passes n_hot.
         uint64_t claimed = 0;
         int64_t next = sp.n_static + (int64_t)atomicAdd(p.hot_next + l % NACC, (uint32_t)NB_HOT);
         while (pr.ok && next < d.n_hot) {
@@ -903,6 +939,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         *reinterpret_cast<volatile int32_t*>(&sm.sealed) = l;
         trace_ev(p, l, 14);
         trace_set(p, l, 15, claimed);
+        trace_set(p, l, 30, cold_taken);
         trace_set(p, l, 18, iw);
         trace_set(p, l, 19, (uint64_t)ng);
       }
@@ -964,8 +1001,9 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
       if (t == 0) trace_ev(p, l, 0);
       // Clear accumulators ahead of use (their previous users finished before the
       // barrier above): y of layer l+1 is added after barrier l+1; z of layer
-      // l+2 and its tile count during layer l+1; the hot-neuron counter of layer
-      // l+2 once the claiming CTA's consumers started layer l+1.
+      // l+2 and its tile count during layer l+1; the cold pool of layer l+2 is
+      // filled, and its hot and cold counters claimed, only once the CTA doing
+      // it has started layer l+1.
       {
         float* yz = p.yacc + (size_t)((l + 1) % NACC) * YCOPIES * H;
         constexpr int NV = YCOPIES * H / 4;
@@ -974,6 +1012,9 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         if (c == 0 && t < 128) p.zacc[(size_t)((l + 2) % NACC) * 128 + t] = 0.0f;
         if (c == 0 && t == 0) p.hot_next[(l + 2) % NACC] = 0u;
         if (c == 0 && t == 1) p.zdone[(l + 2) % NACC] = 0u;
+        if (c == 0 && t == 2) p.gfill[(l + 2) % NACC] = 0u;
+        if (c == 0 && t == 3) p.gclaim[(l + 2) % NACC] = 0u;
+        if (c == 0 && t == 4) p.gdone[(l + 2) % NACC] = 0u;
       }
 
       // ---- RMSNorm (engine.py:295; torch.nn.RMSNorm) -> f16 and fixed-point copies
@@ -1221,6 +1262,9 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
     for (int i = tid; i < NACC * 128; i += STACK_THREADS) p.zacc[i] = 0.0f;
     if (tid < NACC) p.hot_next[tid] = 0u;
     if (tid < NACC) p.zdone[tid] = 0u;
+    if (tid < NACC) p.gfill[tid] = 0u;
+    if (tid < NACC) p.gclaim[tid] = 0u;
+    if (tid < NACC) p.gdone[tid] = 0u;
     if (tid == 0) {
       *p.bar_count = 0;
       *p.exit_count = 0;
@@ -1288,6 +1332,10 @@ extern "C" int hc_ffn_stack(const hc_layer_desc* layers, int32_t n_layers, int32
   p.bar_count = reinterpret_cast<uint32_t*>(ws);
   p.hot_next = reinterpret_cast<uint32_t*>(ws + WS_HOT_NEXT);
   p.zdone = reinterpret_cast<uint32_t*>(ws + WS_ZDONE);
+  p.gfill = reinterpret_cast<uint32_t*>(ws + WS_GFILL);
+  p.gclaim = reinterpret_cast<uint32_t*>(ws + WS_GCLAIM);
+  p.gdone = reinterpret_cast<uint32_t*>(ws + WS_GDONE);
+  p.gpool = reinterpret_cast<int32_t*>(ws + WS_POOL);
   p.exit_count = reinterpret_cast<uint32_t*>(ws + WS_EXIT);
   p.yacc = reinterpret_cast<float*>(ws + WS_YACC);
   p.zacc = reinterpret_cast<float*>(ws + WS_ZACC);

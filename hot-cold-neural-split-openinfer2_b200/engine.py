@@ -165,10 +165,9 @@ class FFNStack:
         if self.L > 1:
             put("barrier_wait", us[1:, :, 0] - us[:-1, :, 8])
             put("layer", us[1:, :, 0] - us[:-1, :, 0])
-        put("issue_wdown_plan_wait", us[:, :, 11] - us[:, :, 10])
+        put("issue_wait_pool", us[:, :, 11] - us[:, :, 10])
         put("issue_cold", us[:, :, 12] - us[:, :, 11])
-        put("issue_static_hot", us[:, :, 13] - us[:, :, 12])
-        put("issue_dynamic_hot_wup", us[:, :, 14] - us[:, :, 13])
+        put("issue_hot", us[:, :, 14] - us[:, :, 13])
         put("own_words_after_start", us[:, :, 21] - us[:, :, 0])
         put("planner_wake_after_start", us[:, :, 22] - us[:, :, 0])
         put("plan_ready_after_start", us[:, :, 20] - us[:, :, 0])
@@ -183,7 +182,8 @@ class FFNStack:
         put("sg0_total", cyc[:, :, 27])
         put("issuer_slot_wait", us[:, :, 18])
         put("dynamic_hot_claimed[n]", t[:, :, 15])
-        put("cold_records[n]", t[:, :, 17])
+        put("cold_listed[n]", t[:, :, 17])
+        put("cold_taken[n]", t[:, :, 30])
         put("groups[n]", t[:, :, 19])
         return out
 

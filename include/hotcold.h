@@ -246,13 +246,14 @@ HC_API int64_t hc_ffn_stack_workspace_bytes(int32_t grid, int32_t inter);
  *              %globaltimer stamps (ns) per CTA and layer -- 0: layer start
  *              (grid barrier passed), 1: normalised input ready, 4-7:
  *              consumer subgroup 0-3 done, 9: partial y added, 8: grid
- *              barrier arrival; issuer 10: layer start, 11: cold list
- *              received, 12: cold issued, 13: static hot issued, 14: layer
+ *              barrier arrival; issuer 10: layer start, 11: the layer's
+ *              cold pool complete, 12/13: cold records issued, 14: layer
  *              sealed; 21: own mask words ready (stamped at the end of the
- *              previous layer), 22: planner took them, 20: cold list ready --
- *              plus 15: hot neurons claimed dynamically, 16: ns subgroup 0
- *              waited for fills, 17: active cold records, 18: ns the issuer
- *              waited for empty slots, 19: groups issued; SM cycles of
+ *              previous layer), 22: planner took them, 20: own cold list
+ *              published -- plus 15: hot neurons claimed, 30: cold records
+ *              taken from the pool, 17: active cold records of the own id
+ *              range, 18: ns the issuer waited for empty slots, 19: groups
+ *              issued; SM cycles of
  *              subgroup 0's poller: 16 waiting for fills, 2/3/23 on cold /
  *              hot / predictor groups, 24/25/26 in its group barrier / seeing
  *              the fills / releasing, 27 in total;
