@@ -168,9 +168,11 @@ class FFNStack:
         put("issue_wait_pool", us[:, :, 11] - us[:, :, 10])
         put("issue_cold", us[:, :, 12] - us[:, :, 11])
         put("issue_hot", us[:, :, 14] - us[:, :, 13])
-        put("own_words_after_start", us[:, :, 21] - us[:, :, 0])
-        put("planner_wake_after_start", us[:, :, 22] - us[:, :, 0])
-        put("plan_ready_after_start", us[:, :, 20] - us[:, :, 0])
+        for name, ev in (("own_words_after_start", 21), ("planner_wake_after_start", 22),
+                         ("plan_ready_after_start", 20)):
+            stamped = t[:, :, ev] > 0                  # layers where the event happened
+            if bool(stamped.any()):
+                put(name, (us[:, :, ev] - us[:, :, 0])[stamped])
         cyc = t / (1000.0 * clock_ghz)          # subgroup-0 counters are SM cycles
         put("sg0_poll_wait", cyc[:, :, 16])
         put("sg0_cold_groups", cyc[:, :, 2])
