@@ -123,6 +123,10 @@ struct StackParams {
   int n_layers;
   int inter;
   int words;                 // ceil(inter / 32)
+  int words_lo, words_n;     // mask words (neuron ids / 32) this GPU owns
+  int tp_size, tp_rank;      // GPUs sharing each layer's neurons, this GPU's index
+  void* const* peer_buf;     // [tp_size] every GPU's exchange buffer (device pointers)
+  uint32_t seq_base;         // launches so far x n_layers, identical on every GPU
   const float* x_in;
   uint32_t* masks;           // [n_layers][words]
   int masks_given;
@@ -171,21 +175,43 @@ __device__ __forceinline__ int64_t split_lo(int64_t n, int c, int G) { return n 
 // predictor tiles must fit a slot and split evenly over 4 threads per neuron
 __device__ __forceinline__ bool rank_ok(int r) { return r > 0 && r <= 96 && (r & 7) == 0; }
 
-// x_l[8t, 8t+8) = x_{l-1} + sum of the YCOPIES partial-y copies of layer l-1
+// Exchange buffer of one GPU (tensor-parallel mode): per slot (l % NACC) a
+// flag word per sender, then per slot a partial y [H] per sender.
+constexpr size_t XCHG_FLAGS = 256;     // bytes reserved for NACC x tp_size flags
+__device__ __forceinline__ uint32_t* xchg_flags(void* buf) { return reinterpret_cast<uint32_t*>(buf); }
+__device__ __forceinline__ float* xchg_y(void* buf, int slot, int sender, int tp) {
+  return reinterpret_cast<float*>(reinterpret_cast<char*>(buf) + XCHG_FLAGS) + ((size_t)slot * tp + sender) * H;
+}
+
+// This GPU's partial y of layer l (summed over its CTAs): the local accumulator.
+__device__ __forceinline__ void load_y_local(const StackParams& p, int l, int t, float4& a, float4& b) {
+  a = make_float4(0.f, 0.f, 0.f, 0.f);
+  b = a;
+#pragma unroll
+  for (int k = 0; k < YCOPIES; ++k) {
+    const float4* yv = reinterpret_cast<const float4*>(p.yacc + ((size_t)(l % NACC) * YCOPIES + k) * H + 8 * t);
+    const float4 u = __ldcg(yv), v = __ldcg(yv + 1);
+    a.x += u.x; a.y += u.y; a.z += u.z; a.w += u.w;
+    b.x += v.x; b.y += v.y; b.z += v.z; b.w += v.w;
+  }
+}
+
+// x_l[8t, 8t+8) = x_{l-1} + y_{l-1}; with several GPUs, y is the sum of every
+// GPU's partial in GPU order, so all GPUs compute identical bits.
 __device__ __forceinline__ void load_x(const StackParams& p, int lm1, int t, float (&x)[8]) {
   const float4* xv = reinterpret_cast<const float4*>(p.xbuf + (size_t)(lm1 % NACC) * H + 8 * t);
   float4 a = __ldcg(xv), b = __ldcg(xv + 1);
-  float4 ya[YCOPIES], yb[YCOPIES];
-#pragma unroll
-  for (int k = 0; k < YCOPIES; ++k) {
-    const float4* yv = reinterpret_cast<const float4*>(p.yacc + ((size_t)(lm1 % NACC) * YCOPIES + k) * H + 8 * t);
-    ya[k] = __ldcg(yv);
-    yb[k] = __ldcg(yv + 1);
-  }
-#pragma unroll
-  for (int k = 0; k < YCOPIES; ++k) {
-    a.x += ya[k].x; a.y += ya[k].y; a.z += ya[k].z; a.w += ya[k].w;
-    b.x += yb[k].x; b.y += yb[k].y; b.z += yb[k].z; b.w += yb[k].w;
+  for (int s = 0; s < p.tp_size; ++s) {
+    float4 u, v;
+    if (s == p.tp_rank) {
+      load_y_local(p, lm1, t, u, v);
+    } else {
+      const float4* yv = reinterpret_cast<const float4*>(xchg_y(p.peer_buf[p.tp_rank], lm1 % NACC, s, p.tp_size) + 8 * t);
+      u = __ldcg(yv);
+      v = __ldcg(yv + 1);
+    }
+    a.x += u.x; a.y += u.y; a.z += u.z; a.w += u.w;
+    b.x += v.x; b.y += v.y; b.z += v.z; b.w += v.w;
   }
   x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
 }
@@ -227,8 +253,8 @@ __device__ __forceinline__ Split make_split(const StackParams& p, const hc_layer
   s.n_static = 0;
   s.h0 = split_lo(s.n_static, c, G);
   s.h1 = split_lo(s.n_static, c + 1, G);
-  s.u0 = (int)split_lo(p.words, c, G);
-  s.u1 = (int)split_lo(p.words, c + 1, G);
+  s.u0 = p.words_lo + (int)split_lo(p.words_n, c, G);
+  s.u1 = p.words_lo + (int)split_lo(p.words_n, c + 1, G);
   const int nd = H / WD_ROWS;
   s.d0 = pred_next ? (int)split_lo(nd, c, G) : 0;
   s.d1 = pred_next ? (int)split_lo(nd, c + 1, G) : 0;
@@ -512,9 +538,10 @@ __device__ __forceinline__ void grid_arrive(const StackParams& p) {
   if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar_count) : "memory");
 }
 // ... and wait (thread 0 spins, bounded; result broadcast)
-__device__ bool grid_wait(StackSmem& sm, const StackParams& p, uint32_t target) {
+// (thread 0's part: spin on the counter; false on timeout or abort)
+__device__ bool grid_spin(StackSmem& sm, const StackParams& p, uint32_t target) {
   bool ok0 = true;
-  if (threadIdx.x == 0) {
+  {
     if (ld_acquire_u32(p.bar_count) < target) {
       const uint64_t t0 = globaltimer_ns();
       uint32_t spins = 0;
@@ -529,6 +556,67 @@ __device__ bool grid_wait(StackSmem& sm, const StackParams& p, uint32_t target) 
     __threadfence();
     if (!ok0 || ld_vol(&sm.abort) != 0) {
       ok0 = false;
+      sm.abort = 1;
+      atomicOr(p.status, HC_ERR_TIMEOUT);
+    }
+  }
+  return ok0;
+}
+__device__ bool grid_wait(StackSmem& sm, const StackParams& p, uint32_t target) {
+  bool ok0 = true;
+  if (threadIdx.x == 0) ok0 = grid_spin(sm, p, target);
+  return cons_broadcast(sm, ok0);
+}
+
+// Wait until y of layer lm1 is complete: every CTA of this GPU added its
+// partial; with several GPUs, CTA 0 then copies this GPU's partial into every
+// peer's exchange buffer (NVLink stores) and publishes the sequence number,
+// and every CTA waits (bounded) for all peers' numbers.
+__device__ bool layer_wait(StackSmem& sm, const StackParams& p, int lm1) {
+  const uint32_t target = (uint32_t)(lm1 + 1) * gridDim.x;
+  if (p.tp_size == 1) return grid_wait(sm, p, target);
+  const int t = threadIdx.x, slot = lm1 % NACC;
+  const uint32_t seq = p.seq_base + (uint32_t)lm1 + 1u;
+  bool ok0 = true;
+  if (t == 0) ok0 = grid_spin(sm, p, target);
+  if (blockIdx.x == 0) {
+    named_bar(1, CONS_THREADS);      // thread 0 saw every local partial; so does every thread now
+    float4 a, b;
+    load_y_local(p, lm1, t, a, b);
+    for (int s = 0; s < p.tp_size; ++s) {
+      if (s == p.tp_rank) continue;
+      float4* dst = reinterpret_cast<float4*>(xchg_y(p.peer_buf[s], slot, p.tp_rank, p.tp_size) + 8 * t);
+      dst[0] = a;
+      dst[1] = b;
+    }
+    named_bar(1, CONS_THREADS);
+    if (t == 0 && ok0) {           // on a local timeout the peers time out too
+      __threadfence_system();
+      for (int s = 0; s < p.tp_size; ++s) {
+        if (s == p.tp_rank) continue;
+        uint32_t* f = xchg_flags(p.peer_buf[s]) + slot * p.tp_size + p.tp_rank;
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(seq) : "memory");
+      }
+    }
+  }
+  if (t == 0 && ok0) {
+    const uint32_t* f = xchg_flags(p.peer_buf[p.tp_rank]) + slot * p.tp_size;
+    const uint64_t t0 = globaltimer_ns();
+    for (int s = 0; s < p.tp_size && ok0; ++s) {
+      if (s == p.tp_rank) continue;
+      uint32_t i = 0;
+      while (true) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f + s) : "memory");
+        if ((int32_t)(v - seq) >= 0) break;
+        if ((++i & 63) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+          ok0 = false;
+          break;
+        }
+        __nanosleep(32);
+      }
+    }
+    if (!ok0) {
       sm.abort = 1;
       atomicOr(p.status, HC_ERR_TIMEOUT);
     }
@@ -621,7 +709,8 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
     // predictor) -> the ascending list of its active cold records.
     const int lane = tid & 31;
     bool ok = true;
-    const int u0 = (int)split_lo(p.words, c, G), nw = (int)split_lo(p.words, c + 1, G) - u0;
+    const int u0 = p.words_lo + (int)split_lo(p.words_n, c, G);
+    const int nw = p.words_lo + (int)split_lo(p.words_n, c + 1, G) - u0;
     uint32_t pphase = 0, p0phase = 0;
     // one tile into pbuf with the planner's own bulk copy (bounded wait)
     auto load_tile = [&](const void* a, uint32_t abytes, const void* b, uint32_t bbytes, uint32_t boff) -> bool {
@@ -983,7 +1072,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         const float4 q0 = __ldg(src), q1 = __ldg(src + 1);
         x[0] = q0.x; x[1] = q0.y; x[2] = q0.z; x[3] = q0.w; x[4] = q1.x; x[5] = q1.y; x[6] = q1.z; x[7] = q1.w;
       } else {
-        ok = grid_wait(sm, p, (uint32_t)l * G);
+        ok = layer_wait(sm, p, l - 1);
         if (!ok) break;
         load_x(p, l - 1, t, x);
         if (p.x_hist && c == 0) {
@@ -1228,7 +1317,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
     // ---- output: x_L = x_{L-1} + y_{L-1}
     if (ok) {
       const int L = p.n_layers;
-      ok = grid_wait(sm, p, (uint32_t)L * G);
+      ok = layer_wait(sm, p, L - 1);
       if (ok && c == 0) {
         float xo[EPT];
         load_x(p, L - 1, t, xo);
@@ -1290,10 +1379,16 @@ extern "C" int64_t hc_ffn_stack_workspace_bytes(int32_t grid, int32_t inter) {
   return (int64_t)WS_BYTES;
 }
 
-extern "C" int hc_ffn_stack(const hc_layer_desc* layers, int32_t n_layers, int32_t inter, const float* x_in,
-                            uint32_t* masks, int32_t masks_given, float* x_out, float* x_hist, float eps,
-                            int32_t act, int32_t act_on_both, float logit_threshold, int32_t grid, void* workspace,
-                            int32_t* status, uint64_t* trace, hc_stream_t stream) {
+extern "C" int64_t hc_tp_buffer_bytes(int32_t tp_size) {
+  if (tp_size < 1 || (size_t)NACC * tp_size * sizeof(uint32_t) > XCHG_FLAGS) return -1;
+  return (int64_t)(XCHG_FLAGS + sizeof(float) * (size_t)NACC * tp_size * H);
+}
+
+extern "C" int hc_ffn_stack_tp(const hc_layer_desc* layers, int32_t n_layers, int32_t inter, const float* x_in,
+                               uint32_t* masks, int32_t masks_given, float* x_out, float* x_hist, float eps,
+                               int32_t act, int32_t act_on_both, float logit_threshold, int32_t grid,
+                               void* workspace, int32_t* status, uint64_t* trace, const hc_tp_desc* tp,
+                               hc_stream_t stream) {
   if (!layers || n_layers <= 0 || n_layers > 32767 || !x_in || !masks || !x_out || !workspace || !status)
     return HC_ERR_ARG;
   if (inter <= 0 || inter > 32768 || (inter & 3) != 0 || (act != HC_ACT_SILU && act != HC_ACT_RELU))
@@ -1304,7 +1399,17 @@ extern "C" int hc_ffn_stack(const hc_layer_desc* layers, int32_t n_layers, int32
   int G = grid > 0 ? grid : hc_ffn_stack_grid();
   if (G <= 0) return HC_ERR_CUDA;
   const int words = (inter + 31) / 32;
-  if ((words + G - 1) / G > OWN_WORDS) return HC_ERR_UNSUPPORTED;   // own neuron-id range too wide
+  int words_lo = 0, words_n = words, tp_size = 1, tp_rank = 0;
+  if (tp) {
+    if (tp->size < 1 || hc_tp_buffer_bytes(tp->size) < 0 || tp->rank < 0 || tp->rank >= tp->size ||
+        tp->words_lo < 0 || tp->words_n < 0 || tp->words_lo + tp->words_n > words || (tp->size > 1 && !tp->peer_buf))
+      return HC_ERR_ARG;
+    words_lo = tp->words_lo;
+    words_n = tp->words_n;
+    tp_size = tp->size;
+    tp_rank = tp->rank;
+  }
+  if ((words_n + G - 1) / G > OWN_WORDS) return HC_ERR_UNSUPPORTED;   // own neuron-id range too wide
   int dev = 0, smem_max = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
@@ -1319,6 +1424,12 @@ extern "C" int hc_ffn_stack(const hc_layer_desc* layers, int32_t n_layers, int32
   p.n_layers = n_layers;
   p.inter = inter;
   p.words = words;
+  p.words_lo = words_lo;
+  p.words_n = words_n;
+  p.tp_size = tp_size;
+  p.tp_rank = tp_rank;
+  p.peer_buf = tp ? tp->peer_buf : nullptr;
+  p.seq_base = tp ? tp->seq_base : 0u;
   p.x_in = x_in;
   p.masks = masks;
   p.masks_given = masks_given;
@@ -1346,4 +1457,12 @@ extern "C" int hc_ffn_stack(const hc_layer_desc* layers, int32_t n_layers, int32
   cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(ffn_stack_kernel), dim3(G),
                                               dim3(STACK_THREADS), args, smem, reinterpret_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? HC_OK : HC_ERR_CUDA;
+}
+
+extern "C" int hc_ffn_stack(const hc_layer_desc* layers, int32_t n_layers, int32_t inter, const float* x_in,
+                            uint32_t* masks, int32_t masks_given, float* x_out, float* x_hist, float eps,
+                            int32_t act, int32_t act_on_both, float logit_threshold, int32_t grid, void* workspace,
+                            int32_t* status, uint64_t* trace, hc_stream_t stream) {
+  return hc_ffn_stack_tp(layers, n_layers, inter, x_in, masks, masks_given, x_out, x_hist, eps, act, act_on_both,
+                         logit_threshold, grid, workspace, status, trace, nullptr, stream);
 }

@@ -61,6 +61,62 @@ class HotNeurons:
         return f[:, 0], f[:, 1], f[:, 2].t()
 
 
+# ─── Tensor parallelism over the neuron dimension ─────────────────────────────
+def split_range(n: int, rank: int, size: int):
+    """[lo, hi) of rank's share when n units are split over size ranks."""
+    return n * rank // size, n * (rank + 1) // size
+
+
+class TPGroup:
+    """The GPUs that share every layer's neurons, one process per GPU.
+
+    Each rank allocates its exchange buffer (``hc_tp_alloc``), publishes its
+    CUDA IPC handle through ``torch.distributed`` (any backend) and opens the
+    other ranks' buffers; the fused stack kernel then adds every GPU's partial
+    output of a layer by NVLink stores into those buffers.  Build one per
+    process with the process group initialised and this rank's device
+    current; call :meth:`close` before destroying the process group.
+    """
+
+    def __init__(self, group=None, device=None):
+        import ctypes
+        import torch.distributed as dist
+        self.size = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        with torch.cuda.device(self.device):
+            nbytes = int(N.lib.hc_tp_buffer_bytes(self.size))
+            if nbytes <= 0:
+                raise ValueError(f"tensor parallelism over {self.size} GPUs is not supported")
+            buf = ctypes.c_void_p()
+            N.check(N.lib.hc_tp_alloc(nbytes, ctypes.byref(buf)), "hc_tp_alloc")
+            self._own = buf.value
+            handle = (ctypes.c_uint8 * 64)()
+            N.check(N.lib.hc_ipc_get_handle(ctypes.c_void_p(self._own), handle), "hc_ipc_get_handle")
+            handles = [None] * self.size
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            self._opened, ptrs = [], []
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(self._own)
+                    continue
+                hb = (ctypes.c_uint8 * 64).from_buffer_copy(h)
+                peer = ctypes.c_void_p()
+                N.check(N.lib.hc_ipc_open(hb, ctypes.byref(peer)), "hc_ipc_open")
+                self._opened.append(peer.value)
+                ptrs.append(peer.value)
+            self.peer_buf = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+        self.launches = 0
+
+    def close(self):
+        for ptr in getattr(self, "_opened", []):
+            N.lib.hc_ipc_close(ptr)
+        self._opened = []
+        if getattr(self, "_own", None):
+            N.lib.hc_tp_free(self._own)
+            self._own = None
+
+
 # ─── Fused L-layer stack ──────────────────────────────────────────────────────
 class FFNStack:
     """L layers of the hot/cold sparse FFN on one GPU, batch 1.
@@ -74,8 +130,14 @@ class FFNStack:
     def __init__(self, store: ColdWeightStore, hot: Sequence[HotNeurons], norms: Sequence[Optional[torch.Tensor]],
                  predictors: Sequence[Optional[NeuronPredictor]], activation: str = "silu",
                  act_on_both: bool = False, eps: float = 1e-5, threshold: float = 0.5,
-                 layer_ids: Optional[Sequence[int]] = None, grid: int = 0, inter: Optional[int] = None):
+                 layer_ids: Optional[Sequence[int]] = None, grid: int = 0, inter: Optional[int] = None,
+                 tp: Optional[TPGroup] = None):
+        """With ``tp``, this GPU takes its share of every layer's neurons: hot
+        neurons [r n_hot / N, (r+1) n_hot / N) of each layer's hot list and
+        the cold ids of mask words [r W / N, (r+1) W / N); the output is
+        the whole layer stack's, identical on every rank."""
         self.store = store
+        self.tp = tp
         self.device = store.device
         self.L = len(hot)
         self.layer_ids = list(layer_ids) if layer_ids is not None else list(range(self.L))
@@ -83,6 +145,8 @@ class FFNStack:
         if self.inter % 4:
             raise ValueError("the fused kernel needs intermediate_dim % 4 == 0")
         self.words = (self.inter + 31) // 32
+        if tp is not None and tp.size > 1:
+            hot = [self._hot_share(h, tp) for h in hot]
         self.hot = list(hot)
         self.norms = [n.to(self.device, torch.float32).contiguous() if n is not None else None for n in norms]
         self.predictors = list(predictors)
@@ -91,7 +155,14 @@ class FFNStack:
         self.eps = float(eps)
         self.threshold = float(threshold)
         self.thr = logit_threshold(self.threshold)
-        self.fetch = torch.stack([store.fetch_bits(li, h.ids, self.inter) for li, h in zip(self.layer_ids, self.hot)])
+        # fetchable cold ids: every hot id of the layer (not only this rank's share) is excluded
+        self.fetch = torch.stack([store.fetch_bits(li, h.all_ids if hasattr(h, "all_ids") else h.ids, self.inter)
+                                  for li, h in zip(self.layer_ids, self.hot)])
+        if tp is not None and tp.size > 1:
+            self.words_lo, hi = split_range(self.words, tp.rank, tp.size)
+            self.words_n = hi - self.words_lo
+        else:
+            self.words_lo, self.words_n = 0, self.words
         descs, self._keep = [], []
         for l in range(self.L):
             li = self.layer_ids[l]
@@ -110,7 +181,7 @@ class FFNStack:
         self.grid = int(grid) if grid else int(N.lib.hc_ffn_stack_grid())
         if self.inter > 32768:
             raise ValueError("the fused kernel handles intermediate_dim <= 32768")
-        if (self.words + self.grid - 1) // self.grid * 32 > 1024:
+        if (self.words_n + self.grid - 1) // self.grid * 32 > 1024:
             raise ValueError(f"grid {self.grid} is too small for {self.inter} neurons per layer "
                              "(one CTA owns at most 1024 neuron ids)")
         self.ws = torch.zeros(int(N.lib.hc_ffn_stack_workspace_bytes(self.grid, self.inter)), dtype=torch.uint8,
@@ -136,11 +207,31 @@ class FFNStack:
         (zeroed) receives per-CTA phase timestamps and waits
         (see include/hotcold.h)."""
         out = self.x_out if out is None else out
-        N.check(N.lib.hc_ffn_stack(N.ptr(self.desc_dev), self.L, self.inter, N.ptr(x), N.ptr(self.masks),
-                                   1 if masks_given else 0, N.ptr(out), N.ptr(x_hist), self.eps, self.act,
-                                   1 if self.act_on_both else 0, self.thr, self.grid, N.ptr(self.ws),
-                                   N.ptr(self.status), N.ptr(trace), N.stream_handle()), "hc_ffn_stack")
+        tp = None
+        if self.tp is not None and self.tp.size > 1:
+            tp = N.TPDesc(size=self.tp.size, rank=self.tp.rank, words_lo=self.words_lo, words_n=self.words_n,
+                          peer_buf=N.ptr(self.tp.peer_buf), seq_base=(self.tp.launches * self.L) & 0xFFFFFFFF)
+            self.tp.launches += 1
+        N.check(N.lib.hc_ffn_stack_tp(N.ptr(self.desc_dev), self.L, self.inter, N.ptr(x), N.ptr(self.masks),
+                                      1 if masks_given else 0, N.ptr(out), N.ptr(x_hist), self.eps, self.act,
+                                      1 if self.act_on_both else 0, self.thr, self.grid, N.ptr(self.ws),
+                                      N.ptr(self.status), N.ptr(trace),
+                                      __import__("ctypes").byref(tp) if tp is not None else None,
+                                      N.stream_handle()), "hc_ffn_stack")
         return out
+
+    @staticmethod
+    def _hot_share(h: "HotNeurons", tp: TPGroup) -> "HotNeurons":
+        """This rank's slice of a layer's hot neurons (a view of the packed rows)."""
+        lo, hi = split_range(h.n, tp.rank, tp.size)
+        part = HotNeurons.__new__(HotNeurons)
+        part.device = h.device
+        part.all_ids = h.ids
+        part.ids = h.ids[lo:hi]
+        part.n = hi - lo
+        part.packed = h.packed[lo:hi] if hi > lo else h.packed[:1]
+        part.scales = h.scales[lo:hi].contiguous() if h.scales is not None and hi > lo else h.scales
+        return part
 
     def trace_summary(self, trace: torch.Tensor, clock_ghz: float = 1.965) -> dict:
         """Mean / max over CTAs of each phase (us, or counts) from a trace;
@@ -224,8 +315,10 @@ class FFNStack:
         N.read_status(self.status, "hc_ffn_stack")
 
     def active_counts(self) -> torch.Tensor:
-        """Active cold neurons per layer of the last forward (device)."""
-        m = (self.masks & self.fetch).to(torch.int64) & 0xFFFFFFFF
+        """Active cold neurons per layer of the last forward (this GPU's share
+        of the neuron ids under tensor parallelism)."""
+        own = slice(self.words_lo, self.words_lo + self.words_n)
+        m = (self.masks[:, own] & self.fetch[:, own]).to(torch.int64) & 0xFFFFFFFF
         return torch.stack([torch.tensor([bin(int(v)).count("1") for v in row.tolist()]).sum() for row in m.cpu()])
 
 

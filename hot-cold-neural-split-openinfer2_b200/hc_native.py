@@ -69,7 +69,21 @@ _SIGS = {
     "hc_ffn_stack_workspace_bytes": (c_i64, [c_i32, c_i32]),
     "hc_ffn_stack": (c_i32, [c_p, c_i32, c_i32, c_p, c_p, c_i32, c_p, c_p, c_f, c_i32, c_i32, c_f,
                              c_i32, c_p, c_p, c_p, c_p]),
+    "hc_tp_buffer_bytes": (c_i64, [c_i32]),
+    "hc_ffn_stack_tp": (c_i32, [c_p, c_i32, c_i32, c_p, c_p, c_i32, c_p, c_p, c_f, c_i32, c_i32, c_f,
+                                c_i32, c_p, c_p, c_p, c_p, c_p]),
+    "hc_tp_alloc": (c_i32, [c_i64, c_p]),
+    "hc_tp_free": (c_i32, [c_p]),
+    "hc_ipc_get_handle": (c_i32, [c_p, c_p]),
+    "hc_ipc_open": (c_i32, [c_p, c_p]),
+    "hc_ipc_close": (c_i32, [c_p]),
 }
+
+
+class TPDesc(ctypes.Structure):
+    """Mirror of hc_tp_desc (include/hotcold.h)."""
+    _fields_ = [("size", ctypes.c_int32), ("rank", ctypes.c_int32), ("words_lo", ctypes.c_int32),
+                ("words_n", ctypes.c_int32), ("peer_buf", ctypes.c_void_p), ("seq_base", ctypes.c_uint32)]
 
 
 def _load():

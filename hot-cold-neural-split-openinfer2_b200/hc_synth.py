@@ -42,10 +42,10 @@ class SynthStack:
     image: Optional[torch.Tensor] = None
     extra: dict = field(default_factory=dict)
 
-    def stack(self, grid: int = 0, threshold: float = 0.5, with_predictors: bool = True) -> FFNStack:
+    def stack(self, grid: int = 0, threshold: float = 0.5, with_predictors: bool = True, tp=None) -> FFNStack:
         preds = self.predictors if with_predictors else [None] * len(self.hot)
         return FFNStack(self.store, self.hot, self.norms, preds, self.activation, self.act_on_both, self.eps,
-                        threshold, grid=grid, inter=self.inter)
+                        threshold, grid=grid, inter=self.inter, tp=tp)
 
 
 def make_stack(n_layers: int = 32, inter: int = 14336, hot_frac: float = 0.2, rank: int = 64,

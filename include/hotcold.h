@@ -266,6 +266,49 @@ HC_API int hc_ffn_stack(const hc_layer_desc* layers, int32_t n_layers, int32_t i
                  int32_t act, int32_t act_on_both, float logit_threshold, int32_t grid,
                  void* workspace, int32_t* status, uint64_t* trace, hc_stream_t stream);
 
+/*
+ * Tensor-parallel decode stack: the neuron dimension of every layer is split
+ * over `size` GPUs, one process per GPU (the reference's down_proj is linear
+ * in the neuron dimension, engine.py:184-188, so y = sum over GPUs of each
+ * GPU's partial).  GPU `rank` holds its slice of the hot neurons (its own
+ * hc_layer_desc.hot / n_hot), computes the predictor logits and cold records
+ * of mask words [words_lo, words_lo + words_n), and runs the full W_down of
+ * every predictor.  Per layer, each GPU sums its CTAs' partial y, copies the
+ * sum into every peer's exchange buffer over NVLink (plain peer stores, no
+ * multicast) and publishes `seq_base + layer + 1` in a flag word; every GPU
+ * waits (bounded) for all peers' flags, then adds the partials in GPU order,
+ * so all GPUs hold bit-identical hidden states.
+ *   peer_buf   device array [size] of every GPU's exchange buffer
+ *              (hc_tp_buffer_bytes(size) bytes from hc_tp_alloc, zeroed once,
+ *              opened in the other processes with hc_ipc_open)
+ *   seq_base   launches so far x n_layers; every GPU passes the same value
+ * All `size` kernels must be running at the same time (one per GPU, issued
+ * by each rank in the same order); a GPU that does not reach a layer within
+ * 2 s makes the others return HC_ERR_TIMEOUT.  masks[] rows are written only
+ * for the mask words this GPU owns.
+ */
+typedef struct hc_tp_desc {
+  int32_t size, rank;
+  int32_t words_lo, words_n;
+  void* const* peer_buf;
+  uint32_t seq_base;
+} hc_tp_desc;
+
+HC_API int64_t hc_tp_buffer_bytes(int32_t tp_size);
+/* tp == NULL is hc_ffn_stack. */
+HC_API int hc_ffn_stack_tp(const hc_layer_desc* layers, int32_t n_layers, int32_t inter, const float* x_in,
+                    uint32_t* masks, int32_t masks_given, float* x_out, float* x_hist, float eps,
+                    int32_t act, int32_t act_on_both, float logit_threshold, int32_t grid,
+                    void* workspace, int32_t* status, uint64_t* trace, const hc_tp_desc* tp,
+                    hc_stream_t stream);
+
+/* Exchange-buffer plumbing for the tensor-parallel stack (host side). */
+HC_API int hc_tp_alloc(int64_t bytes, void** ptr);     /* cudaMalloc + zero on the current device */
+HC_API int hc_tp_free(void* ptr);
+HC_API int hc_ipc_get_handle(void* ptr, uint8_t* handle);          /* 64-byte cudaIpcMemHandle_t */
+HC_API int hc_ipc_open(const uint8_t* handle, void** ptr);         /* peer access enabled lazily */
+HC_API int hc_ipc_close(void* ptr);
+
 #ifdef __cplusplus
 }
 #endif

@@ -93,3 +93,17 @@ def test_layer_desc_layout_matches_c_struct():
     # 9 pointers + 4 int32 = 88 bytes, pointer-aligned
     assert ctypes.sizeof(N.LayerDesc) == 9 * 8 + 4 * 4
     assert N.LayerDesc.n_hot.offset == 72
+
+
+def test_tensor_parallel_host_pieces():
+    import hc_native as N
+    from engine import split_range
+    # every unit lands on exactly one rank, in order
+    for n, size in ((448, 2), (448, 8), (2867, 8), (5, 8)):
+        got = [split_range(n, r, size) for r in range(size)]
+        assert got[0][0] == 0 and got[-1][1] == n
+        assert all(got[i][1] == got[i + 1][0] for i in range(size - 1))
+    # hc_tp_desc layout: 4 int32, a pointer, a uint32
+    assert ctypes.sizeof(N.TPDesc) == 32 and N.TPDesc.peer_buf.offset == 16 and N.TPDesc.seq_base.offset == 24
+    assert N.lib.hc_tp_buffer_bytes(8) == 256 + 3 * 8 * 4096 * 4
+    assert N.lib.hc_tp_buffer_bytes(0) == -1 and N.lib.hc_tp_buffer_bytes(64) == -1
