@@ -208,6 +208,7 @@ def run_gpu(args):
     import torch
     import torch.distributed as dist
 
+    import engine
     import hc_native as N
     import hc_synth
 
@@ -219,8 +220,12 @@ def run_gpu(args):
                                 device_id=dev)
     syn = hc_synth.make_stack(n_layers=LAYERS, inter=INTER, hot_frac=0.2, rank=RANK, activation="relu",
                               act_on_both=True, seed=0, device=dev)
-    st = syn.stack()
-    gen = torch.Generator(device="cpu").manual_seed(100 + rank)
+    # N > 1: every layer's neurons are split over the GPUs (tensor parallelism,
+    # one in-kernel exchange of the partial output per layer); all ranks decode
+    # the same tokens, so the job's throughput is one rank's tokens/s
+    tp = engine.TPGroup(device=dev) if ws > 1 else None
+    st = syn.stack(tp=tp)
+    gen = torch.Generator(device="cpu").manual_seed(100)
     x_host = torch.randn(TOKENS, H, generator=gen).pin_memory()
     x_dev = x_host.to(dev)
     y_host = torch.empty(TOKENS, H).pin_memory()
@@ -232,15 +237,25 @@ def run_gpu(args):
             st.forward(x_dev[t], out=y_dev[t])
 
     # fetched cold neurons per token (deterministic: same tokens, same masks)
+    if ws > 1:
+        dist.barrier()
+        torch.cuda.synchronize()
+    own = slice(st.words_lo, st.words_lo + st.words_n)
     fetched = []
     for t in range(TOKENS):
         st.forward(x_dev[t], out=y_dev[t])
-        m = (st.masks & st.fetch).cpu().numpy().astype("uint32")
+        m = (st.masks[:, own] & st.fetch[:, own]).cpu().numpy().astype("uint32")
         fetched.append(int(sum(bin(int(w)).count("1") for w in m.reshape(-1))))
     st.check()
-    mean_fetched = sum(fetched) / len(fetched)          # summed over the 32 layers
-    # algorithmic bytes of one hc_ffn_stack launch (one token, 32 layers)
-    stack_bytes = LAYERS * N_HOT * HOT_BYTES + mean_fetched * COLD_BYTES + (LAYERS - 1) * PRED_BYTES + 2 * LAYERS * H * 4
+    mean_fetched = sum(fetched) / len(fetched)          # this GPU's share, summed over the 32 layers
+    # algorithmic bytes of one hc_ffn_stack launch on this GPU (one token, 32
+    # layers): its hot neurons, its fetched cold records, every predictor's
+    # W_down and its share of W_up / bias, x and y
+    n_hot_local = sum(h.n for h in st.hot) / LAYERS
+    share = st.words_n / st.words
+    pred_local = 4 * (RANK * H) + share * 4 * (INTER * RANK + INTER)
+    stack_bytes = (LAYERS * n_hot_local * HOT_BYTES + mean_fetched * COLD_BYTES + (LAYERS - 1) * pred_local
+                   + 2 * LAYERS * H * 4)
     token_bytes = stack_bytes + PRED_BYTES            # + layer-0 predictor launches
 
     for _ in range(max(args.warmup, 3)):
@@ -273,7 +288,7 @@ def run_gpu(args):
         t = torch.tensor([elapsed_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         elapsed_ms = float(t.item())
-    tokens_all = TOKENS * args.steps * ws
+    tokens_all = TOKENS * args.steps            # the ranks decode the same tokens together
     value = tokens_all / (elapsed_ms / 1e3)
     ms_per_step = elapsed_ms / args.steps
 
@@ -301,29 +316,39 @@ def run_gpu(args):
                 "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
                 "kernel": "hc_ffn_stack (ffn_stack_kernel)", "algorithmic_bytes_per_launch": int(stack_bytes),
                 "avg_launch_ms": round(avg_stack_ms, 5),
-                "token_frac": round(token_bytes * value / ws / 1e9 / peak, 4)}
+                "token_frac": round(token_bytes * value / 1e9 / peak, 4)}
+    if ws > 1:
+        roofline["traffic"] = None          # the committed capture is of the one-GPU launch
     line = None
+    if ws > 1:
+        dist.barrier()
+        torch.cuda.synchronize()
+        tp.close()
     if rank == 0:
-        dq = cold_dequant_bench(syn.store)
-        cpu = cpu_reference(4, 0, layers_per_step=2, budget_s=25.0)
+        dq = cold_dequant_bench(syn.store) if ws == 1 else None
+        cpu = cpu_reference(4, 0, layers_per_step=2, budget_s=25.0) if ws == 1 else None
         line = {"metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "e4m3/int4 weights, fp32 accumulate",
+                "scaling": "strong", "vs_baseline": None, "dtype": "e4m3/int4 weights, fp32 accumulate",
                 "data": "synthetic",
                 "config": {"workload": WORKLOAD, "layers": LAYERS, "hidden": H, "inter": INTER, "hot": N_HOT,
                            "rank": RANK, "batch": 1, "tokens_per_step": TOKENS,
                            "cold_fetched_per_token": round(mean_fetched, 1),
                            "cold_fetched_frac": round(mean_fetched / (LAYERS * (INTER - N_HOT)), 4),
                            "l2": "no flush: each token streams ~2.4 GB of weights, far above the 126 MB L2",
-                           "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU"},
+                           "parallelism": (f"tp{ws}: neurons of every layer split over {ws} GPUs, one in-kernel "
+                                           "NVLink exchange of the 16 KB partial output per layer") if ws > 1
+                           else "single GPU"},
                 "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s",
                         "h2d_bytes_per_step": TOKENS * H * 4, "d2h_bytes_per_step": TOKENS * H * 4},
                 "gpu_launches": args.steps * TOKENS * launches_per_token,
                 "roofline": roofline,
-                "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
-                "clocks": clocks,
-                "cold_dequant": {"unit": "GB/s", "peak": peak, "bytes_per_neuron": COLD_BYTES + 3 * H * 2,
-                                 "layers": LAYERS, "out_dtype": "bf16", "by_K": dq}}
+                "clocks": clocks}
+        if cpu is not None:
+            line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        if dq is not None:
+            line["cold_dequant"] = {"unit": "GB/s", "peak": peak, "bytes_per_neuron": COLD_BYTES + 3 * H * 2,
+                                    "layers": LAYERS, "out_dtype": "bf16", "by_K": dq}
         print(json.dumps(line), flush=True)
     if ws > 1:
         dist.barrier()

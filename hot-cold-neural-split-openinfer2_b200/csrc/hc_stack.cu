@@ -151,7 +151,7 @@ struct StackParams {
   uint64_t* trace;           // optional [n_layers][G][TRACE_EVENTS]
 };
 
-constexpr int TRACE_EVENTS = 32;
+constexpr int TRACE_EVENTS = 40;
 __device__ __forceinline__ void trace_ev(const StackParams& p, int l, int ev) {
   if (p.trace != nullptr) p.trace[((size_t)l * gridDim.x + blockIdx.x) * TRACE_EVENTS + ev] = globaltimer_ns();
 }
@@ -578,7 +578,10 @@ __device__ bool layer_wait(StackSmem& sm, const StackParams& p, int lm1) {
   const int t = threadIdx.x, slot = lm1 % NACC;
   const uint32_t seq = p.seq_base + (uint32_t)lm1 + 1u;
   bool ok0 = true;
-  if (t == 0) ok0 = grid_spin(sm, p, target);
+  if (t == 0) {
+    ok0 = grid_spin(sm, p, target);
+    trace_ev(p, lm1, 32);
+  }
   if (blockIdx.x == 0) {
     named_bar(1, CONS_THREADS);      // thread 0 saw every local partial; so does every thread now
     float4 a, b;
@@ -591,12 +594,17 @@ __device__ bool layer_wait(StackSmem& sm, const StackParams& p, int lm1) {
     }
     named_bar(1, CONS_THREADS);
     if (t == 0 && ok0) {           // on a local timeout the peers time out too
-      __threadfence_system();
+      trace_ev(p, lm1, 36);
+      // one release fence (cumulative over the CTA's stores above, ordered by
+      // the barrier) for all peers' flags
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
+      trace_ev(p, lm1, 33);
       for (int s = 0; s < p.tp_size; ++s) {
         if (s == p.tp_rank) continue;
         uint32_t* f = xchg_flags(p.peer_buf[s]) + slot * p.tp_size + p.tp_rank;
-        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(seq) : "memory");
+        asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(f), "r"(seq) : "memory");
       }
+      trace_ev(p, lm1, 34);
     }
   }
   if (t == 0 && ok0) {
@@ -620,6 +628,7 @@ __device__ bool layer_wait(StackSmem& sm, const StackParams& p, int lm1) {
       sm.abort = 1;
       atomicOr(p.status, HC_ERR_TIMEOUT);
     }
+    trace_ev(p, lm1, 35);
   }
   return cons_broadcast(sm, ok0);
 }

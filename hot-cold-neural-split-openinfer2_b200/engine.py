@@ -203,7 +203,7 @@ class FFNStack:
 
     def launch(self, x: torch.Tensor, masks_given: bool = False, x_hist: Optional[torch.Tensor] = None,
                out: Optional[torch.Tensor] = None, trace: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """One hc_ffn_stack launch.  ``trace`` (int64 [L, grid, 32], device)
+        """One hc_ffn_stack launch.  ``trace`` (int64 [L, grid, 40], device)
         (zeroed) receives per-CTA phase timestamps and waits
         (see include/hotcold.h)."""
         out = self.x_out if out is None else out
@@ -273,6 +273,13 @@ class FFNStack:
         put("sg0_observe", cyc[:, :, 25])
         put("sg0_release", cyc[:, :, 26])
         put("sg0_total", cyc[:, :, 27])
+        if t.shape[2] > 36 and bool((t[:, :, 32] > 0).any()):
+            # tensor parallel: local sum seen -> (CTA 0) push, fence, flags -> all peers seen
+            put("tp.local_seen_after_arrive", us[:, :, 32] - us[:, :, 8])
+            put("tp.cta0_push", us[:, 0, 36] - us[:, 0, 32])
+            put("tp.cta0_fence_sys", us[:, 0, 33] - us[:, 0, 36])
+            put("tp.cta0_flags", us[:, 0, 34] - us[:, 0, 33])
+            put("tp.peers_seen_after_local", us[:, :, 35] - us[:, :, 32])
         put("issuer_slot_wait", us[:, :, 18])
         put("dynamic_hot_claimed[n]", t[:, :, 15])
         put("cold_listed[n]", t[:, :, 17])

@@ -31,12 +31,25 @@ def main():
     import torch
     import hc_synth
 
+    # under torchrun (WORLD_SIZE > 1) the stack runs tensor-parallel, one GPU per rank
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    tp = None
+    if world > 1:
+        import torch.distributed as dist
+        import engine
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group("gloo")
+        tp = engine.TPGroup()
     syn = hc_synth.make_stack(n_layers=args.layers, inter=args.inter, activation="relu", act_on_both=True, seed=0,
                               predictors=args.what != "gather")
     if args.what == "stack":
-        st = syn.stack(grid=args.grid)
-        x = torch.randn(args.tokens, 4096, device="cuda")
-        trace = torch.zeros(args.layers, st.grid, 32, dtype=torch.int64, device="cuda") if args.trace else None
+        st = syn.stack(grid=args.grid, tp=tp)
+        if tp is not None:
+            dist.barrier()
+            torch.cuda.synchronize()
+        x = torch.randn(args.tokens, 4096, generator=torch.Generator().manual_seed(1)).cuda()   # same on every rank
+        trace = torch.zeros(args.layers, st.grid, 40, dtype=torch.int64, device="cuda") if args.trace else None
         for t in range(args.tokens):
             if trace is not None:
                 trace.zero_()          # keep the last token's stamps and waits
@@ -44,9 +57,13 @@ def main():
             st.launch(x[t], False, None, None, trace)
         torch.cuda.synchronize()
         st.check()
-        if trace is not None:
+        if trace is not None and rank == 0:
             for k, (mean, mx) in st.trace_summary(trace).items():
                 print(f"  {k:18s} mean {mean:9.2f} us   max {mx:9.2f} us")
+        if tp is not None:
+            dist.barrier()
+            tp.close()
+            dist.destroy_process_group()
     elif args.what == "gather":
         store = syn.store
         g = torch.Generator(device="cuda").manual_seed(7)

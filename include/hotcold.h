@@ -242,7 +242,7 @@ HC_API int64_t hc_ffn_stack_workspace_bytes(int32_t grid, int32_t inter);
  *   grid       0 = hc_ffn_stack_grid(); tests may pass fewer CTAs
  *   workspace  hc_ffn_stack_workspace_bytes(grid, inter), zeroed once; the
  *              kernel leaves it zeroed again when it completes
- *   trace      optional [n_layers][grid][32] uint64, zeroed by the caller:
+ *   trace      optional [n_layers][grid][40] uint64, zeroed by the caller:
  *              %globaltimer stamps (ns) per CTA and layer -- 0: layer start
  *              (grid barrier passed), 1: normalised input ready, 4-7:
  *              consumer subgroup 0-3 done, 9: partial y added, 8: grid
@@ -257,6 +257,9 @@ HC_API int64_t hc_ffn_stack_workspace_bytes(int32_t grid, int32_t inter);
  *              subgroup 0's poller: 16 waiting for fills, 2/3/23 on cold /
  *              hot / predictor groups, 24/25/26 in its group barrier / seeing
  *              the fills / releasing, 27 in total;
+ *              under tensor parallelism 32: local partials complete, 35: all
+ *              peers' partials seen; CTA 0 only: 36 pushed to the peers, 33
+ *              release fence done, 34 flags written;
  *              NULL = off
  * The layer outputs are sums of per-CTA float partials added with atomics, so
  * their last bits can differ between launches.
