@@ -204,6 +204,68 @@ def cold_dequant_bench(store, reps: int = 5):
     return out
 
 
+def batched_decode_bench(syn, steps: int, warmup: int, batches=(1, 8, 32, 64)):
+    """configs[4] on one GPU: the 32-layer stack for B tokens at once with
+    per-token Bernoulli(0.1) masks unioned per layer (BatchStack: hc_union_cold_layers
+    + hc_ffn_batch_layer per layer, tcgen05 tensor-core GEMMs), captured in one
+    CUDA graph per batch size.  `value` is device-resident; `e2e` adds the
+    pinned host->device copy of the B inputs and the device->host copy of the
+    outputs to every step."""
+    import torch
+    import hc_synth
+    peak, _ = _peaks()
+    bst = syn.batch_stack(max_batch=max(batches))
+    dev = syn.store.device
+    stream = torch.cuda.Stream(device=dev)
+    out = {}
+    for B in batches:
+        masks = hc_synth.bernoulli_words(LAYERS, B, INTER, 0.1, seed=2, device=dev)
+        gen = torch.Generator(device="cpu").manual_seed(200 + B)
+        x_host = torch.randn(B, H, generator=gen).pin_memory()
+        y_host = torch.empty(B, H).pin_memory()
+        x_in = x_host.to(dev)
+        y = torch.empty(B, H, device=dev)
+        bst.forward(x_in, masks=masks, out=y)                   # first call outside capture
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                bst.forward(x_in, masks=masks, out=y)
+        torch.cuda.current_stream().wait_stream(stream)
+        union = float(bst.count.float().mean().item())
+        for _ in range(max(warmup, 3)):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        e0.record()
+        for _ in range(steps):
+            x_in.copy_(x_host, non_blocking=True)
+            g.replay()
+            y_host.copy_(y, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / steps
+        bst.check()
+        # algorithmic bytes of one step: every hot neuron and every record of
+        # each layer's union once, plus the B hidden states in and out per layer
+        step_bytes = LAYERS * (N_HOT * HOT_BYTES + union * COLD_BYTES + 2 * B * H * 4)
+        gbs = step_bytes / (ms * 1e-3) / 1e9
+        out[str(B)] = {"tokens_per_s": round(B / (ms * 1e-3), 1), "ms_per_step": round(ms, 4),
+                       "e2e_tokens_per_s": round(B / (e2e_ms * 1e-3), 1),
+                       "union_records_per_layer": round(union, 1),
+                       "union_frac": round(union / (INTER - N_HOT), 4),
+                       "algorithmic_gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
+        del g
+    return out
+
+
 def run_gpu(args):
     import torch
     import torch.distributed as dist
@@ -326,6 +388,7 @@ def run_gpu(args):
         tp.close()
     if rank == 0:
         dq = cold_dequant_bench(syn.store) if ws == 1 else None
+        bd = batched_decode_bench(syn, args.steps, args.warmup) if ws == 1 else None
         cpu = cpu_reference(4, 0, layers_per_step=2, budget_s=25.0) if ws == 1 else None
         line = {"metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True,
@@ -346,6 +409,10 @@ def run_gpu(args):
                 "clocks": clocks}
         if cpu is not None:
             line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        if bd is not None:
+            line["batched_decode"] = {"workload": "configs[4] on 1 GPU: 32L 4096/14336 stack, B tokens, per-token "
+                                                  "Bernoulli(0.1) masks unioned per layer, tcgen05 GEMMs",
+                                      "unit": "tokens/s", "peak": peak, "by_B": bd}
         if dq is not None:
             line["cold_dequant"] = {"unit": "GB/s", "peak": peak, "bytes_per_neuron": COLD_BYTES + 3 * H * 2,
                                     "layers": LAYERS, "out_dtype": "bf16", "by_K": dq}

@@ -7,6 +7,9 @@
   with the predictor lookahead of DesdemonaEngine.forward (engine.py:421-438),
   run by one persistent cooperative kernel per token (``hc_ffn_stack``) plus
   the two predictor launches for layer 0's fetch set.
+* :class:`BatchStack` -- the same L layers for a batch of tokens sharing one
+  fetch set per layer (the union of the tokens' masks), every weight byte
+  read once per 8 tokens (``hc_union_cold`` + ``hc_ffn_batch_layer``).
 * :class:`SparseFFNLayer` -- the reference's per-layer module (same
   constructor) on the fused kernel.
 * :func:`sparse_ffn` -- the reference's function signature (engine.py:173-209)
@@ -14,6 +17,7 @@
 """
 from __future__ import annotations
 
+import ctypes
 from pathlib import Path
 from typing import Optional, Sequence
 
@@ -327,6 +331,121 @@ class FFNStack:
         own = slice(self.words_lo, self.words_lo + self.words_n)
         m = (self.masks[:, own] & self.fetch[:, own]).to(torch.int64) & 0xFFFFFFFF
         return torch.stack([torch.tensor([bin(int(v)).count("1") for v in row.tolist()]).sum() for row in m.cpu()])
+
+
+class BatchStack:
+    """L layers of the hot/cold sparse FFN for a batch of B tokens on one GPU.
+
+    forward(x [B, H]) computes, for l = 0..L-1, x_b <- x_b + sparse_ffn(
+    RMSNorm_l(x_b)) for every token b, with one fetch set per layer and
+    batch: the union over the batch's tokens of their active masks, & the
+    fetchable cold ids.  The masks are either given ([L, B, W] int32 words,
+    e.g. per-token Bernoulli draws) or the per-token predictions of each
+    layer's predictor on RMSNorm_l(x_b); a layer without a predictor fetches
+    every cold neuron (engine.py:282-283).  The reference's batched query
+    (engine.py:277-279) asks the predictor once, on the batch mean of the
+    normalised inputs; the union of per-token predictions contains every
+    neuron a single token's own prediction selects.
+    """
+
+    def __init__(self, store: ColdWeightStore, hot: Sequence[HotNeurons], norms: Sequence[Optional[torch.Tensor]],
+                 predictors: Optional[Sequence[Optional[NeuronPredictor]]] = None, activation: str = "silu",
+                 act_on_both: bool = False, eps: float = 1e-5, threshold: float = 0.5,
+                 layer_ids: Optional[Sequence[int]] = None, inter: Optional[int] = None, max_batch: int = 64):
+        self.store = store
+        self.device = store.device
+        self.L = len(hot)
+        self.layer_ids = list(layer_ids) if layer_ids is not None else list(range(self.L))
+        self.inter = int(inter or store.I)
+        self.words = (self.inter + 31) // 32
+        self.hot = list(hot)
+        self.norms = [n.to(self.device, torch.float32).contiguous() if n is not None else None for n in norms]
+        self.predictors = list(predictors) if predictors is not None else [None] * self.L
+        self.act = N.HC_ACT_RELU if activation == "relu" else N.HC_ACT_SILU
+        self.act_on_both = bool(act_on_both)
+        self.eps = float(eps)
+        self.threshold = float(threshold)
+        self.max_batch = int(max_batch)
+        self.fetch = torch.stack([store.fetch_bits(li, h.ids, self.inter) for li, h in zip(self.layer_ids, self.hot)])
+        self.descs, self._keep, self.max_cold = [], [], []
+        for l in range(self.L):
+            li = self.layer_ids[l]
+            rec = store.section_records(li)
+            self._keep.append(rec)
+            n_rec = int(store.n_rec_host[li])
+            self.max_cold.append(n_rec)
+            self.descs.append(N.LayerDesc(
+                hot=N.ptr(self.hot[l].packed), hot_scale=N.ptr(self.hot[l].scales), norm_w=N.ptr(self.norms[l]),
+                cold_records=N.ptr(rec), table=N.ptr(store.table[li]), fetch_bits=N.ptr(self.fetch[l]),
+                n_hot=self.hot[l].n, n_records=n_rec, inter=self.inter, rank=0))
+        max_neurons = max(h.n + c for h, c in zip(self.hot, self.max_cold))
+        self.ws = torch.zeros(int(N.lib.hc_ffn_batch_workspace_bytes(max(max_neurons, 1))), dtype=torch.uint8,
+                              device=self.device)
+        self.rec = torch.zeros(self.L, max(max(self.max_cold), 1), dtype=torch.int32, device=self.device)
+        self.count = torch.zeros(self.L, dtype=torch.int32, device=self.device)
+        self.pred_masks = torch.zeros(self.L, self.max_batch, self.words, dtype=torch.int32, device=self.device)
+        self.status = N.new_status(self.device)
+        self._all_ones = bits_to_words(torch.ones(self.inter, dtype=torch.bool).numpy(), self.inter).to(self.device)
+
+    def _layer_masks(self, l: int, x: torch.Tensor) -> torch.Tensor:
+        B = x.shape[0]
+        out = self.pred_masks[l, :B]
+        p = self.predictors[l]
+        if p is None:
+            out.copy_(self._all_ones.view(1, -1).expand(B, -1))
+        else:
+            p.predict_words(x, self.threshold, norm_w=self.norms[l], eps=self.eps, mask_out=out)
+        return out
+
+    def forward(self, x: torch.Tensor, masks: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                x_hist: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """x: fp32 [B, H] on the device (B <= max_batch); returns the stack's
+        output (``out`` if given, else a new tensor).  ``masks``: int32
+        [L, B, W]; ``x_hist`` (optional [L, B, H]) receives every layer's output."""
+        N.require_cuda(x)
+        B = x.shape[0]
+        if B < 1 or B > self.max_batch:
+            raise ValueError(f"batch {B} outside [1, {self.max_batch}]")
+        y = out if out is not None else torch.empty(B, HIDDEN_DIM, dtype=torch.float32, device=self.device)
+        y.copy_(x.reshape(B, HIDDEN_DIM))
+        if masks is not None:
+            masks = masks.to(self.device, torch.int32).contiguous()
+            if tuple(masks.shape) != (self.L, B, self.words):
+                raise ValueError(f"masks must be [L={self.L}, B={B}, W={self.words}] int32 words")
+        s = N.stream_handle()
+        if masks is not None and self._tables_contiguous():
+            # every layer's fetch set is known up front: one launch for all layers
+            t0 = self.store.table[self.layer_ids[0]]
+            N.check(N.lib.hc_union_cold_layers(N.ptr(masks), self.L, masks.stride(0), B, masks.stride(1),
+                                               self.inter, N.ptr(self.fetch), N.ptr(t0), N.ptr(self.rec),
+                                               self.rec.stride(0), N.ptr(self.count), s), "hc_union_cold_layers")
+        for l in range(self.L):
+            if masks is None or not self._tables_contiguous():
+                m = masks[l] if masks is not None else self._layer_masks(l, y)
+                N.check(N.lib.hc_union_cold(N.ptr(m), B, m.stride(0), self.inter, N.ptr(self.fetch[l]),
+                                            N.ptr(self.store.table[self.layer_ids[l]]), N.ptr(self.rec[l]),
+                                            N.ptr(self.count[l:l + 1]), s), "hc_union_cold")
+            N.check(N.lib.hc_ffn_batch_layer(ctypes.byref(self.descs[l]), N.ptr(y), B, N.ptr(self.rec[l]),
+                                             N.ptr(self.count[l:l + 1]), self.max_cold[l], self.eps, self.act,
+                                             1 if self.act_on_both else 0, N.ptr(self.ws), N.ptr(self.status), s),
+                    "hc_ffn_batch_layer")
+            if x_hist is not None:
+                x_hist[l].copy_(y)
+        return y
+
+    __call__ = forward
+
+    def _tables_contiguous(self) -> bool:
+        """Layer ids consecutive, so table rows of layer l sit at table[first + l]."""
+        ids = self.layer_ids
+        return all(b == a + 1 for a, b in zip(ids, ids[1:]))
+
+    def check(self):
+        N.read_status(self.status, "hc_ffn_batch_layer")
+
+    def union_counts(self) -> torch.Tensor:
+        """Cold records each layer fetched in the last forward."""
+        return self.count.cpu()
 
 
 # ─── Reference-compatible pieces ─────────────────────────────────────────────

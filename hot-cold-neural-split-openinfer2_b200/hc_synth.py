@@ -22,7 +22,7 @@ from typing import Optional
 import numpy as np
 import torch
 
-from engine import FFNStack, HotNeurons
+from engine import BatchStack, FFNStack, HotNeurons
 from predictor import NeuronPredictor
 from splitter import HIDDEN_DIM, ColdWeightStore, build_cold_image, build_records, hot_from_dense
 
@@ -46,6 +46,11 @@ class SynthStack:
         preds = self.predictors if with_predictors else [None] * len(self.hot)
         return FFNStack(self.store, self.hot, self.norms, preds, self.activation, self.act_on_both, self.eps,
                         threshold, grid=grid, inter=self.inter, tp=tp)
+
+    def batch_stack(self, threshold: float = 0.5, with_predictors: bool = False, max_batch: int = 64) -> BatchStack:
+        preds = self.predictors if with_predictors else None
+        return BatchStack(self.store, self.hot, self.norms, preds, self.activation, self.act_on_both, self.eps,
+                          threshold, inter=self.inter, max_batch=max_batch)
 
 
 def make_stack(n_layers: int = 32, inter: int = 14336, hot_frac: float = 0.2, rank: int = 64,
@@ -94,3 +99,16 @@ def make_stack(n_layers: int = 32, inter: int = 14336, hot_frac: float = 0.2, ra
     if keep_dense:
         out.extra["dense"] = dense
     return out
+
+
+def bernoulli_words(n_layers: int, batch: int, inter: int, p: float = 0.1, seed: int = 2, device="cuda"):
+    """Per-token Bernoulli(p) active masks as packed int32 words [L, B, W]
+    (bit j of word w = neuron 32w + j), drawn on the device from ``seed``."""
+    dev = torch.device(device)
+    W = (inter + 31) // 32
+    g = torch.Generator(device=dev).manual_seed(seed)
+    bits = torch.zeros(n_layers, batch, W * 32, dtype=torch.int64, device=dev)
+    bits[..., :inter] = (torch.rand(n_layers, batch, inter, generator=g, device=dev) < p).to(torch.int64)
+    shifts = torch.arange(32, dtype=torch.int64, device=dev)
+    words = (bits.view(n_layers, batch, W, 32) << shifts).sum(dim=-1)
+    return (words - ((words >> 31) << 32)).to(torch.int32)      # two's-complement view of the u32 words

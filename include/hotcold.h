@@ -312,6 +312,54 @@ HC_API int hc_ipc_get_handle(void* ptr, uint8_t* handle);          /* 64-byte cu
 HC_API int hc_ipc_open(const uint8_t* handle, void** ptr);         /* peer access enabled lazily */
 HC_API int hc_ipc_close(void* ptr);
 
+/* ======================================================================= */
+/* Batched decode (B tokens through one layer, one fetch set per batch)    */
+/* ======================================================================= */
+
+/*
+ * hc_union_cold -- the batched form of the id selection of
+ * SparseFFNLayer._cold_ids_for (engine.py:274-283): the cold records a batch
+ * fetches are the union of its tokens' active masks, restricted to fetch_bits,
+ * in ascending neuron-id order.
+ *   masks      [batch][token_stride] uint32 active bits, ceil(inter/32) words
+ *              per token; fetch_bits, table as in hc_layer_desc
+ *   rec_out    [n_records] int32 record indices; count [1] int32 output
+ * Single CTA; inter <= 65536.
+ */
+HC_API int hc_union_cold(const uint32_t* masks, int32_t batch, int64_t token_stride, int32_t inter,
+                         const uint32_t* fetch_bits, const int32_t* table, int32_t* rec_out,
+                         int32_t* count, hc_stream_t stream);
+/*
+ * The same for n_layers layers at once (one CTA per layer), when every
+ * layer's masks are known up front: layer l reads masks + l * layer_stride,
+ * fetch_bits + l * ceil(inter/32), table + l * 65536 and writes
+ * rec_out + l * rec_stride, count[l].
+ */
+HC_API int hc_union_cold_layers(const uint32_t* masks, int32_t n_layers, int64_t layer_stride, int32_t batch,
+                                int64_t token_stride, int32_t inter, const uint32_t* fetch_bits,
+                                const int32_t* table, int32_t* rec_out, int64_t rec_stride, int32_t* count,
+                                hc_stream_t stream);
+
+/*
+ * hc_ffn_batch_layer -- SparseFFNLayer.forward (engine.py:292-312) for a
+ * batch of B tokens sharing one fetch set: x_b += sparse_ffn(RMSNorm(x_b))
+ * over the layer's hot neurons and the cold records rec[0..*count).
+ *   layer      host pointer to the layer's hc_layer_desc (its device pointers
+ *              are used; the predictor fields are ignored)
+ *   x          [batch][4096] fp32 hidden states, updated in place
+ *   rec/count  device cold record list (hc_union_cold), at most max_cold
+ *              entries (more sets HC_ERR_RANGE and drops the excess)
+ *   workspace  hc_ffn_batch_workspace_bytes(n_hot + max_cold) bytes, zeroed once;
+ *              left zeroed again
+ * Tokens are processed 8 at a time; every weight byte is read once per 8.
+ * fp32 arithmetic on the decoded weights; the down projection is summed with
+ * float atomics, so its last bits can differ between launches.
+ */
+HC_API int64_t hc_ffn_batch_workspace_bytes(int32_t max_neurons);
+HC_API int hc_ffn_batch_layer(const hc_layer_desc* layer, float* x, int32_t batch, const int32_t* rec,
+                              const int32_t* count, int32_t max_cold, float eps, int32_t act,
+                              int32_t act_on_both, void* workspace, int32_t* status, hc_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,182 @@
+"""GPU parity of the batched decode path (hc_union_cold + hc_ffn_batch_layer).
+
+* the union of B tokens' masks & fetch_bits, compacted in ascending id order
+  through the record table, equals the numpy restatement bit for bit;
+* every layer's update x_{l+1} - x_l of every token equals the float64
+  oracle's sparse_ffn(RMSNorm(x_l)) over the hot neurons plus the union's
+  cold records (engine.py:173-209, :292-312) to rel-L2 <= 2e-3 (the north-star
+  bar is 1e-2): the tensor-core operands are f16 -- FP8 weights and INT4 q
+  exact, the normalised inputs, the INT4 gate/up q * scale products and the
+  activations rounded once each (~3e-4 RMS apiece), fp32 accumulation;
+* batches that are not a multiple of the 16-token MMA width, two passes, a batch of one against
+  the batch-1 fused stack, and the per-token predictor union.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import hotcold_oracle as O
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-3
+
+
+@pytest.fixture(scope="module")
+def M():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    import engine
+    import hc_native
+    import hc_synth
+    return engine, hc_native, hc_synth
+
+
+def _bernoulli_masks(L, B, inter, p, seed):
+    g = torch.Generator().manual_seed(seed)
+    bits = torch.rand(L, B, inter, generator=g) < p
+    return np.stack([np.stack([O.words_from_mask(bits[l, b].numpy()) for b in range(B)]) for l in range(L)]), bits
+
+
+def _oracle_store(syn):
+    host = syn.store.image.cpu().numpy().tobytes()
+    return O.ColdStoreOracle(host, syn.cold_index, {"hidden_dim": 4096})
+
+
+def _check_layers(syn, bst, x0, x_hist, union_ids, tol=TOL):
+    ostore = _oracle_store(syn)
+    L = len(syn.hot)
+    xs = [x0.double().cpu().numpy()] + [x_hist[l].double().cpu().numpy() for l in range(L)]
+    worst = 0.0
+    for l in range(L):
+        ids = union_ids[l]
+        rows = ostore.read_neurons(l, 0, list(ids)) if len(ids) else None
+        hot = tuple(t.double().cpu().numpy() for t in syn.hot[l].decoded())
+        ref = O.ffn_layer(xs[l], syn.norms[l].cpu().numpy(), syn.eps, syn.activation, syn.act_on_both, hot, rows)
+        for b in range(xs[l].shape[0]):
+            d_ref = ref[b] - xs[l][b]
+            d_gpu = xs[l + 1][b] - xs[l][b]
+            rel = np.linalg.norm(d_gpu - d_ref) / max(np.linalg.norm(d_ref), 1e-30)
+            worst = max(worst, rel)
+            assert rel <= tol, f"layer {l} token {b}: rel-L2 {rel:.3e}"
+    return worst
+
+
+def _union_ids(bst, bits_l, l):
+    fetch = O.mask_from_words(bst.fetch[l].cpu().numpy(), bst.inter)
+    return np.nonzero(bits_l.any(axis=0) & fetch)[0]
+
+
+def test_union_cold_matches_numpy(M):
+    engine, N, hc_synth = M
+    rng = np.random.default_rng(5)
+    inter = 5000                                     # 157 words, last word ragged
+    W = (inter + 31) // 32
+    for B in (1, 3, 64):
+        bits = rng.random((B, inter)) < 0.07
+        words = np.stack([O.words_from_mask(bits[b]) for b in range(B)])
+        fetch_mask = rng.random(inter) < 0.8
+        table = np.full(65536, -1, np.int32)
+        has = np.nonzero(fetch_mask)[0]
+        table[has] = rng.permutation(len(has)).astype(np.int32)
+        stride = W + 3                                # rows need not be packed
+        m = torch.zeros(B, stride, dtype=torch.int32)
+        m[:, :W] = torch.from_numpy(words)
+        m_d = m.cuda()
+        fetch_d = torch.from_numpy(O.words_from_mask(fetch_mask)).cuda()
+        table_d = torch.from_numpy(table).cuda()
+        rec = torch.full((inter,), -7, dtype=torch.int32, device="cuda")
+        cnt = torch.zeros(1, dtype=torch.int32, device="cuda")
+        N.check(N.lib.hc_union_cold(N.ptr(m_d), B, stride, inter, N.ptr(fetch_d), N.ptr(table_d), N.ptr(rec),
+                                    N.ptr(cnt), N.stream_handle()), "hc_union_cold")
+        torch.cuda.synchronize()
+        ids = np.nonzero(bits.any(axis=0) & fetch_mask)[0]
+        assert int(cnt.item()) == len(ids)
+        assert np.array_equal(rec[:len(ids)].cpu().numpy(), table[ids])
+
+
+@pytest.mark.parametrize("B", [1, 5, 16, 19, 40, 70])
+def test_batch_given_masks(M, B):
+    """Token counts that pad to every MMA width (16..64) and a second pass (70)."""
+    engine, N, hc_synth = M
+    syn = hc_synth.make_stack(n_layers=2, inter=1024, hot_frac=0.2, rank=64, activation="silu",
+                              act_on_both=False, seed=21, norm_std=0.1, predictors=False)
+    bst = syn.batch_stack(max_batch=80)
+    words, bits = _bernoulli_masks(2, B, syn.inter, 0.1, seed=B)
+    x0 = torch.randn(B, 4096, device="cuda", generator=torch.Generator(device="cuda").manual_seed(B))
+    x_hist = torch.empty(2, B, 4096, device="cuda")
+    out = bst.forward(x0, masks=torch.from_numpy(words), x_hist=x_hist)
+    bst.check()
+    assert torch.equal(out, x_hist[-1])
+    union = [_union_ids(bst, bits[l].numpy(), l) for l in range(2)]
+    assert bst.union_counts().tolist() == [len(u) for u in union]
+    _check_layers(syn, bst, x0, x_hist, union)
+
+
+def test_batch_dense_and_row_scaled_relu(M):
+    """dReLU with per-neuron hot scales, every cold record fetched (p = 1)."""
+    engine, N, hc_synth = M
+    syn = hc_synth.make_stack(n_layers=2, inter=2048, hot_frac=0.2, rank=64, activation="relu",
+                              act_on_both=True, seed=4, row_scale=True, predictors=False)
+    B = 9
+    bst = syn.batch_stack(max_batch=16)
+    words, bits = _bernoulli_masks(2, B, syn.inter, 1.0, seed=1)
+    x0 = torch.randn(B, 4096, device="cuda", generator=torch.Generator(device="cuda").manual_seed(2))
+    x_hist = torch.empty(2, B, 4096, device="cuda")
+    bst.forward(x0, masks=torch.from_numpy(words), x_hist=x_hist)
+    bst.check()
+    union = [_union_ids(bst, bits[l].numpy(), l) for l in range(2)]
+    assert len(union[0]) == syn.inter - syn.hot[0].n
+    _check_layers(syn, bst, x0, x_hist, union)
+
+
+def test_batch_of_one_matches_fused_stack(M):
+    engine, N, hc_synth = M
+    syn = hc_synth.make_stack(n_layers=3, inter=1024, hot_frac=0.2, rank=64, activation="relu",
+                              act_on_both=True, seed=8, predictors=False)
+    words, bits = _bernoulli_masks(3, 1, syn.inter, 0.3, seed=9)
+    x0 = torch.randn(4096, device="cuda", generator=torch.Generator(device="cuda").manual_seed(4))
+    bst = syn.batch_stack(max_batch=8)
+    yb = bst.forward(x0.view(1, -1), masks=torch.from_numpy(words))[0]
+    st = syn.stack()
+    ys = st.forward(x0, masks=torch.from_numpy(words[:, 0, :]).cuda())
+    bst.check()
+    st.check()
+    d = x0.double()
+    rel = ((yb.double() - ys.double()).norm() / (ys.double() - d).norm()).item()
+    assert rel < 3e-3, rel
+
+
+def test_batch_predictor_union(M):
+    engine, N, hc_synth = M
+    syn = hc_synth.make_stack(n_layers=2, inter=1024, hot_frac=0.2, rank=64, activation="relu",
+                              act_on_both=True, seed=13, norm_std=0.1)
+    B = 6
+    bst = syn.batch_stack(with_predictors=True, max_batch=8)
+    x0 = torch.randn(B, 4096, device="cuda", generator=torch.Generator(device="cuda").manual_seed(6))
+    x_hist = torch.empty(2, B, 4096, device="cuda")
+    bst.forward(x0, x_hist=x_hist)
+    bst.check()
+    union = []
+    for l in range(2):
+        per_tok = np.stack([O.mask_from_words(bst.pred_masks[l, b].cpu().numpy(), syn.inter) for b in range(B)])
+        union.append(_union_ids(bst, per_tok, l))
+    assert bst.union_counts().tolist() == [len(u) for u in union]
+    _check_layers(syn, bst, x0, x_hist, union)
+
+
+def test_batch_full_geometry_64_tokens(M):
+    """4096/14336 geometry, 64 tokens, per-token Bernoulli(0.1): the union
+    covers ~99.9% of the cold records; one layer checked against the oracle."""
+    engine, N, hc_synth = M
+    syn = hc_synth.make_stack(n_layers=1, inter=14336, hot_frac=0.2, rank=64, activation="relu",
+                              act_on_both=True, seed=3, predictors=False)
+    B = 64
+    bst = syn.batch_stack(max_batch=64)
+    words, bits = _bernoulli_masks(1, B, syn.inter, 0.1, seed=2)
+    x0 = torch.randn(B, 4096, device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))
+    x_hist = torch.empty(1, B, 4096, device="cuda")
+    bst.forward(x0, masks=torch.from_numpy(words), x_hist=x_hist)
+    bst.check()
+    union = [_union_ids(bst, bits[0].numpy(), 0)]
+    assert len(union[0]) > 0.99 * (syn.inter - syn.hot[0].n)
+    _check_layers(syn, bst, x0[:8], x_hist[:, :8], union)

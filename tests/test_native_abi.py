@@ -57,6 +57,12 @@ def test_argument_errors_are_reported_without_a_device():
     assert N.lib.hc_ffn_stack(None, 1, 64, None, None, 0, None, None, 1e-5, 0, 0, 0.0, 0, None, None,
                               None, None) == N.HC_ERR_ARG
     assert N.lib.hc_map_ids(None, -1, None, None, None, None, None) == N.HC_ERR_ARG
+    assert N.lib.hc_union_cold(None, 1, 32, 1024, None, None, None, None, None) == N.HC_ERR_ARG
+    assert N.lib.hc_union_cold_layers(None, 2, 0, 1, 32, 1024, None, None, None, 0, None, None) == N.HC_ERR_ARG
+    assert N.lib.hc_ffn_batch_layer(None, None, 4, None, None, 0, 1e-5, 0, 0, None, None, None) == N.HC_ERR_ARG
+    assert N.lib.hc_ffn_batch_workspace_bytes(0) == -1
+    # workspace grows with the neuron count it must hold (activations, partial sums)
+    assert N.lib.hc_ffn_batch_workspace_bytes(14336) > N.lib.hc_ffn_batch_workspace_bytes(1024) > 0
 
 
 def test_logit_threshold_reproduces_torch_sigmoid_decision():
