@@ -28,6 +28,10 @@
 // Shared-memory operand layout (SWIZZLE_NONE canonical form): 8x16-byte core
 // matrices; SBO = the byte stride between core matrices along M/N, LBO =
 // along K.  Every weight byte is read once per pass.
+#include <cuda.h>
+#include <string.h>
+#include <cudaTypedefs.h>
+
 #include "hc_common.cuh"
 
 namespace hcb {
@@ -101,6 +105,24 @@ __device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                "l"(src), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
+}
+
+// 2-D tiled tensor copy, coordinates {x (bytes), y (rows)}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+// four rows y0..y3 of a one-row-high box at byte offset x, stored one after another
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map, int x, int y0, int y1, int y2, int y3,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3),
+      "r"(smem_u32(bar))
+      : "memory");
 }
 
 // 8 consecutive fp32 columns of this thread's TMEM lane
@@ -178,8 +200,10 @@ struct LayerArgs {
   int max_cold;
   int relu, both;
   int32_t* status;
+  const uint8_t* flags;   // dense cold mode: [n_records] 1 = in the batch's fetch set; NULL = gathered list
 };
 
+// cold rows of the gathered work list
 __device__ __forceinline__ int cold_count(const LayerArgs& a) { return min(*a.count, a.max_cold); }
 __device__ __forceinline__ int checked_rec(const LayerArgs& a, int i) {
   const int r = __ldg(a.rec + i);
@@ -246,17 +270,29 @@ __global__ void __launch_bounds__(256) k_norm(const float* __restrict__ x, int n
 // contiguous ranges, one per CTA (G = grid size); unit x belongs to CTA
 // ((x + 1) G - 1) / U.  A unit is one 64-wide K step of one output tile.
 // ---------------------------------------------------------------------------
-constexpr int GU_PROD = 512;                       // k_gu producer threads: (row, matrix, K half)
+constexpr int GU_PROD = 512;                       // k_gu decoder threads: (row, matrix, K half)
 constexpr int GU_THREADS = GU_PROD + 64 + 128;     // + MMA warp + token-tile warp + 4 epilogue warps
+// Raw weights of one unit: two 8 KB matrix regions (gate, up).  Hot: 128 rows
+// x 64 bytes (one 2-D tensor copy per matrix).  Cold: row r's 48-byte window
+// of the unit's 32 field bytes (the field starts 2 bytes into it) at 48 r, and
+// the 16-byte window holding the row's fp16 group scale at 6144 + 16 r.
+constexpr int GU_REGION = 8192;
+constexpr int GU_RAW_SLOT = 2 * GU_REGION;
+constexpr int GU_COLD_WIN = 48;
+constexpr int GU_SCALE_OFF = TILE * GU_COLD_WIN;
 constexpr int GU_STAGES = 4;                       // k_gu: TMEM A stages = token-tile stages
+constexpr int GUX_STAGES = 4;                      // k_gu_p: token-tile stages (own ring)
+constexpr int GUP_GROUP = 4;                       // k_gu_p: units per bulk-copied group (up to 64 KB)
+constexpr int GUP_GSLOTS = 3;                      // k_gu_p: group slots (two groups in flight)
 constexpr int GU_A_COL = 256;                      // TMEM columns [256, 512): A stages of 64 columns
-constexpr int GU_SMEM_FLOOR = 120 * 1024;          // keeps k_gu at one CTA (all 512 TMEM columns) per SM
+constexpr int GU_SMEM_FLOOR = 120 * 1024;          // at least this much keeps k_gu at one CTA (all 512 TMEM columns) per SM
 constexpr int DN_PROD = 256;                       // k_down producer threads: (neuron, 32-row quarter)
 constexpr int DN_THREADS = DN_PROD + 32 + 128;
-constexpr int RAW_DEPTH = 4;                       // units of copies in flight per thread
-constexpr int GU_PIECES = 2;                       // per thread and unit: 2 weight pieces
+constexpr int RAW_DEPTH = 4;                       // k_down: units of copies in flight per thread
+constexpr int GU_DEPTH = 8;                        // k_gu: raw weight slots
+constexpr int GU_AHEAD = GU_DEPTH - 2;             // k_gu: copies issued this many units ahead, so a refilled
+                                                   // slot was last read two units back (no lockstep wait)
 constexpr int DN_PIECES = 5;                       // 2 weight, 2 act, 1 scale
-constexpr int GU_PSTRIDE = GU_PROD * 16;           // bytes between piece j and j + 1 of one raw slot
 constexpr int DN_PSTRIDE = DN_PROD * 16;
 constexpr int REC_AHEAD = RAW_DEPTH;               // k_down: record indices copied this many units early
 constexpr int REC_RING = 2 * RAW_DEPTH;
@@ -270,6 +306,10 @@ __device__ __forceinline__ void cp16(uint32_t dst, const void* src) {
 }
 __device__ __forceinline__ void cp4(uint32_t dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+// arrive on `bar` once this thread's earlier cp.async copies have landed (the arrival is one of the expected count)
+__device__ __forceinline__ void cp_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int K>
@@ -289,11 +329,24 @@ __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
 __device__ __forceinline__ __half half_of(uint32_t word, uint32_t upper) {
   return __ushort_as_half(static_cast<unsigned short>(upper ? (word >> 16) : (word & 0xFFFFu)));
 }
+__device__ __forceinline__ const void* align16(const void* p) {
+  return reinterpret_cast<const void*>(reinterpret_cast<uintptr_t>(p) & ~static_cast<uintptr_t>(15));
+}
 __device__ __forceinline__ const void* align4(const void* p) {
   return reinterpret_cast<const void*>(reinterpret_cast<uintptr_t>(p) & ~static_cast<uintptr_t>(3));
 }
 __device__ __forceinline__ uint32_t upper_half(const void* p) {
   return static_cast<uint32_t>((reinterpret_cast<uintptr_t>(p) >> 1) & 1);
+}
+// Bounded wait: the thread parks in try_wait (woken when the phase completes),
+// so waiting warps take few issue slots from the decoders.
+__device__ __forceinline__ bool bwait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = WAIT_NS) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 7) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
+  }
 }
 __device__ __forceinline__ void fail(const LayerArgs& a, volatile int* abort_flag) {
   atomicOr(a.status, HC_ERR_TIMEOUT);
@@ -302,11 +355,15 @@ __device__ __forceinline__ void fail(const LayerArgs& a, volatile int* abort_fla
 
 // barriers and TMEM slot after the operand stages and the raw ring
 struct Bars {
-  uint64_t* full;    // [4] producers -> MMA: stage filled
-  uint64_t* empty;   // [4] MMA commit -> producers: stage free
+  uint64_t* full;    // [8] producers -> MMA: stage filled
+  uint64_t* empty;   // [8] MMA commit -> producers: stage free
   uint64_t* accf;    // [2] MMA commit -> epilogue: accumulator buffer complete
   uint64_t* tfree;   // [2] epilogue -> MMA: accumulator buffer drained
-  uint64_t* xfull;   // [4] bulk copy -> MMA: token tile landed
+  uint64_t* xfull;   // [8] bulk copy -> MMA: token tile landed
+  uint64_t* xempty;  // [8] MMA commit -> token-tile warp: tile read
+  uint64_t* rawfull;   // [16] copies -> decoders: raw weights landed
+  uint64_t* rawempty;  // [16] decoders -> issuer: raw slot read
+  uint64_t* sfree;     // [2] decoders -> loader: scale buffer of a segment read
   uint32_t* tslot;
   volatile int* abort_flag;
 };
@@ -314,15 +371,20 @@ __device__ __forceinline__ Bars carve_bars(uint8_t* p) {
   Bars b;
   uint64_t* u = reinterpret_cast<uint64_t*>(p);
   b.full = u;
-  b.empty = u + 4;
-  b.accf = u + 8;
-  b.tfree = u + 10;
-  b.xfull = u + 12;
-  b.tslot = reinterpret_cast<uint32_t*>(u + 16);
-  b.abort_flag = reinterpret_cast<volatile int*>(u + 16) + 1;
+  b.empty = u + 8;
+  b.accf = u + 16;
+  b.tfree = u + 18;
+  b.xfull = u + 20;
+  b.rawfull = u + 28;
+  b.rawempty = u + 44;
+  b.sfree = u + 60;
+  b.xempty = u + 62;
+  b.tslot = reinterpret_cast<uint32_t*>(u + 70);
+  b.abort_flag = reinterpret_cast<volatile int*>(u + 70) + 1;
   return b;
 }
-__device__ __forceinline__ void init_bars(const Bars& b, int stages, int producers) {
+__device__ __forceinline__ void init_bars(const Bars& b, int stages, int producers, int rawfull_count = -1,
+                                          int xempty_count = 1) {
   for (int s = 0; s < stages; ++s) {
     mbar_init(&b.full[s], producers);
     mbar_init(&b.empty[s], 1);
@@ -331,11 +393,26 @@ __device__ __forceinline__ void init_bars(const Bars& b, int stages, int produce
     mbar_init(&b.accf[k], 1);
     mbar_init(&b.tfree[k], 128);
   }
-  for (int k = 0; k < 4; ++k) mbar_init(&b.xfull[k], 1);
+  for (int k = 0; k < 8; ++k) {
+    mbar_init(&b.xfull[k], 1);
+    mbar_init(&b.xempty[k], xempty_count);
+  }
+  for (int k = 0; k < 16; ++k) {
+    mbar_init(&b.rawfull[k], rawfull_count < 0 ? producers : rawfull_count);
+    mbar_init(&b.rawempty[k], producers);
+  }
+  for (int k = 0; k < 2; ++k) mbar_init(&b.sfree[k], producers);
   *b.abort_flag = 0;
   mbar_fence_init();
 }
-constexpr int BAR_BYTES = 160;
+constexpr int BAR_BYTES = 576;
+
+// Optional timeline of k_gu / k_down launches (profiling hook, off unless
+// hc_batch_set_trace gave a buffer): per CTA 64 %globaltimer stamps.
+constexpr int TRACE_SLOTS = 64;
+__device__ __forceinline__ void stamp(uint64_t* tr, int c, int e) {
+  if (tr) tr[(size_t)c * TRACE_SLOTS + e] = globaltimer_ns();
+}
 
 // ---------------------------------------------------------------------------
 // k_gu: gate and up GEMMs, D[128 neurons][N tokens], persistent.
@@ -344,16 +421,22 @@ constexpr int BAR_BYTES = 160;
 //   ("segments") of one or more tiles; each segment's fp32 partial goes to
 //   block (tile + CTA) of part [blocks][128][2N] (gate N, then up N), unique
 //   because ranges are contiguous.
+// Weights reach shared memory by TMA, GU_DEPTH units ahead: a hot unit is
+//   one 2-D tile per matrix (128 rows x 64 bytes of the packed hot rows); a
+//   cold unit is 32 four-row gathers per matrix of the 48-byte window that
+//   holds the unit's 32 field bytes (the field starts 2 bytes into it) plus
+//   32 gathers of the 16-byte window holding the group's fp16 scale.  Rows
+//   past the tile's end point past the tensor and read as zeros.
 // TMEM (512 columns): accumulator buffers tb = 0, 1 at columns [2N tb, 2N tb
 //   + 2N) (gate, up); A stages s = 0..3 at [256 + 64 s, +64) (gate 32
 //   columns, up 32 columns; column c of a row holds K elements 2c, 2c + 1).
-// Threads: 512 producers -- warp w decodes rows 32 (w & 3) + lane (its TMEM
-//   lane quarter) of matrix (w >> 2) & 1, K half w >> 3 of each unit, from a
-//   private cp.async ring RAW_DEPTH units deep, and stores the f16 pairs with
-//   tcgen05.st; warp 16 issues tcgen05.mma (A from TMEM, B = the token tile
-//   from shared memory, K-major: k-group stride 16 N, token-group stride
-//   128); warp 17 bulk-copies each unit's token tile; warps 18-21 drain
-//   finished accumulator buffers.
+// Threads: 512 decoders -- warp w decodes rows 32 (w & 3) + lane (its TMEM
+//   lane quarter) of matrix (w >> 2) & 1, K half w >> 3 of each unit to f16
+//   pairs and stores them with tcgen05.st; warp 16 issues tcgen05.mma (A from
+//   TMEM, B = the token tile in shared memory, K-major: k-group stride 16 N,
+//   token-group stride 128); warp 17 bulk-copies each unit's token tile;
+//   warp 18 issues the weight copies; warps 19-22 drain finished accumulator
+//   buffers.
 // ---------------------------------------------------------------------------
 struct GuParams {
   LayerArgs a;
@@ -361,9 +444,11 @@ struct GuParams {
   const uint8_t* xs_perm;
   float* part;
   int N, hot_tiles;
+  uint64_t* trace;
+  CUtensorMap tm_hot;      // packed hot rows: {12288 bytes, n_hot rows}, box {64, 128}
 };
 
-__global__ void __launch_bounds__(GU_THREADS, 1) k_gu(GuParams p) {
+__global__ void __launch_bounds__(GU_THREADS, 1) k_gu(const __grid_constant__ GuParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const LayerArgs& a = p.a;
@@ -374,14 +459,14 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu(GuParams p) {
   const int lo = range_lo(c, U, G), hi = range_lo(c + 1, U, G);
   if (lo >= hi) return;                                     // uniform: before any barrier
   const int nunits = hi - lo;
+  uint64_t* tr = p.trace;
+  if (t == 0) stamp(tr, c, 0);
 
   const int x_bytes = N * KC * 2;
-  const int raw_slot = GU_PIECES * GU_PSTRIDE;
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t xbase = sbase;                             // [GU_STAGES][x_bytes] token tiles
-  const uint32_t rbase = xbase + GU_STAGES * x_bytes;       // [RAW_DEPTH][GU_PIECES][GU_PROD][16]
-  const uint32_t scbase = rbase + RAW_DEPTH * raw_slot;     // [RAW_DEPTH][GU_PROD] 4-byte scale words
-  const Bars bar = carve_bars(smem + GU_STAGES * x_bytes + RAW_DEPTH * (raw_slot + GU_PROD * 4));
+  const uint32_t rbase = sbase;                             // [GU_DEPTH][GU_RAW_SLOT] raw weights (1 KB aligned)
+  const uint32_t xbase = rbase + GU_DEPTH * GU_RAW_SLOT;    // [GU_STAGES][x_bytes] token tiles
+  const Bars bar = carve_bars(smem + GU_DEPTH * GU_RAW_SLOT + GU_STAGES * x_bytes);
 
   if (t == 0) init_bars(bar, GU_STAGES, GU_PROD);
   if (warp == 0) tmem_alloc(bar.tslot, 512);
@@ -389,93 +474,112 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu(GuParams p) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *bar.tslot;
+  if (t == 0) stamp(tr, c, 1);
 
   if (t < GU_PROD) {
+    // ---- decoders, which also issue the weight copies GU_DEPTH - 1 units ahead.
+    // Cold unit: thread t copies piece t % 4 of row t / 4 for both matrices --
+    // pieces 0-2 the row's 48-byte field window, piece 3 the 16-byte window
+    // holding the group's fp16 scale -- so a warp's copy covers 8 whole rows.
+    // Hot unit: thread 0 issues one 2-D tensor copy per matrix.
     const int q = warp & 3, m = (warp >> 2) & 1, h = warp >> 3;
-    const int r = q * 32 + lane;
-    int curT = -1, kindT = 0;
-    const uint8_t* src = nullptr;
-    const uint8_t* scl = nullptr;
-    uint32_t meta = 0;                                      // 3 bits per raw slot: kind (2), scale half (1)
-    // record index of this thread's row in cold tile T (raw; checked where used)
-    auto raw_rec = [&](int T) -> int {
+    const int r = q * 32 + lane;                            // decoded row
+    const int crow = t >> 2, cpiece = t & 3;                // copied row and piece
+    const uint32_t a_lane = tmem + ((uint32_t)(q * 32) << 16) + GU_A_COL + 32 * m + 16 * h;
+    // record index of `row` in cold tile T: -1 past the union's end, -2 out of range
+    auto rec_of = [&](int T, int row) -> int {
       if (T < p.hot_tiles || T >= tiles) return -1;
-      const int row = (T - p.hot_tiles) * TILE + r;
-      return row < cnt ? __ldg(a.rec + row) : -1;
+      const int j = (T - p.hot_tiles) * TILE + row;
+      return j < cnt ? __ldg(a.rec + j) : -1;
     };
-    int nextT = lo >> 6, nextR = raw_rec(nextT);            // the next tile's record, loaded a tile early
+    auto checked = [&](int R) -> int {
+      if (R < -1 || R >= a.n_records) {
+        atomicOr(a.status, HC_ERR_RANGE);
+        return -2;
+      }
+      return R;
+    };
+    // issue side: tile being copied, its record for crow; next tile's, loaded a tile early
+    int cT = -1, cR = -1, cnT = lo >> 6, cnR = rec_of(cnT, crow);
     auto issue = [&](int i) {
       if (i < nunits) {
         const int x = lo + i, T = x >> 6, k = x & (H / KC - 1);
-        if (T != curT) {
-          curT = T;
-          const int R = T == nextT ? nextR : raw_rec(T);
-          nextT = T + 1;
-          nextR = raw_rec(nextT);
-          const bool hotT = T < p.hot_tiles;
-          const int row = (hotT ? T : T - p.hot_tiles) * TILE + r;
-          kindT = 0;
-          if (hotT) {
-            if (row < a.n_hot) {
-              src = a.hot + (size_t)row * HOT_ROW + (size_t)m * H;
-              kindT = 1;
-            }
-          } else if (row < cnt) {
-            if (R < 0 || R >= a.n_records) {
-              atomicOr(a.status, HC_ERR_RANGE);
-            } else {
-              const uint8_t* rb = a.cold + (size_t)R * REC_BYTES;
-              src = rb + (size_t)m * VEC_BYTES;             // aligned; the field starts at +2
-              scl = rb + SCALE_OFF + m * 2 * NGROUPS;
-              kindT = 2;
+        const int slot = i % GU_DEPTH, use = i / GU_DEPTH;
+        if (T != cT) {
+          cR = checked(T == cnT ? cnR : rec_of(T, crow));
+          cT = T;
+          cnT = T + 1;
+          cnR = rec_of(cnT, crow);
+        }
+        // the slot's previous unit has been decoded by every thread
+        if (use > 0 && !bwait(&bar.rawempty[slot], (use - 1) & 1)) fail(a, bar.abort_flag);
+        const uint32_t dst = rbase + slot * GU_RAW_SLOT;
+        if (T < p.hot_tiles) {
+          if (t == 0) {
+            mbar_arrive_expect_tx(&bar.rawfull[slot], 2 * KC * TILE);
+            tma_load_2d(dst, &p.tm_hot, k * KC, T * TILE, &bar.rawfull[slot]);
+            tma_load_2d(dst + GU_REGION, &p.tm_hot, H + k * KC, T * TILE, &bar.rawfull[slot]);
+          } else {
+            mbar_arrive(&bar.rawfull[slot]);
+          }
+        } else {
+          if (cR >= 0) {
+            const uint8_t* rb = a.cold + (size_t)cR * REC_BYTES;
+#pragma unroll
+            for (int mm = 0; mm < 2; ++mm) {
+              if (cpiece < 3)
+                cp16(dst + mm * GU_REGION + crow * GU_COLD_WIN + 16 * cpiece,
+                     rb + mm * VEC_BYTES + k * (KC / 2) + 16 * cpiece);
+              else
+                cp16(dst + mm * GU_REGION + GU_SCALE_OFF + crow * 16,
+                     align16(rb + SCALE_OFF + mm * 2 * NGROUPS + 2 * (k >> 1)));
             }
           }
+          cp_arrive(&bar.rawfull[slot]);
         }
-        const int slot = i % RAW_DEPTH;
-        const uint32_t d = rbase + slot * raw_slot + t * 16;
-        uint32_t md = kindT;
-        if (kindT == 1) {
-          const uint8_t* w = src + k * KC + 32 * h;
-          cp16(d, w);
-          cp16(d + GU_PSTRIDE, w + 16);
-        } else if (kindT == 2) {
-          const uint8_t* w = src + k * (KC / 2) + 16 * h;   // field bytes [32k + 16h, +16) at +2
-          cp16(d, w);
-          cp4(d + GU_PSTRIDE, w + 16);
-          const uint8_t* sp = scl + 2 * (k >> 1);           // group of 128 = two K steps
-          cp4(scbase + (slot * GU_PROD + t) * 4, align4(sp));
-          md |= upper_half(sp) << 2;
-        }
-        meta = (meta & ~(7u << (3 * slot))) | (md << (3 * slot));
       }
-      cp_commit();
     };
-#pragma unroll
-    for (int i = 0; i < RAW_DEPTH - 1; ++i) issue(i);
-    const uint32_t a_lane = tmem + ((uint32_t)(q * 32) << 16) + GU_A_COL + 32 * m + 16 * h;
+#pragma unroll 1
+    for (int i = 0; i < GU_AHEAD; ++i) issue(i);
+    int dT = -1, dR = -1, dnT = lo >> 6, dnR = rec_of(dnT, r);    // decode side: this row's record
     for (int i = 0; i < nunits; ++i) {
-      issue(i + RAW_DEPTH - 1);
-      cp_wait<RAW_DEPTH - 1>();                             // this thread's copies of unit i landed
-      const int s = i % GU_STAGES, round = i / GU_STAGES;
-      bool ok = round == 0 || mbar_wait(&bar.empty[s], (round - 1) & 1, WAIT_NS);
+      const int x = lo + i, T = x >> 6, k = x & (H / KC - 1);
+      if (T != dT) {
+        dR = T == dnT ? dnR : rec_of(T, r);
+        dT = T;
+        dnT = T + 1;
+        dnR = rec_of(dnT, r);
+      }
+      const int tw = 0;                                   // traced thread
+      if (t == tw && i >= 20 && i < 24) stamp(tr, c, 24 + (i - 20) * 6);
+      issue(i + GU_AHEAD);
+      if (t == tw && i >= 20 && i < 24) stamp(tr, c, (i - 20) * 6 + 25);
+      const int slot = i % GU_DEPTH, s = i % GU_STAGES, round = i / GU_STAGES;
+      bool ok = bwait(&bar.rawfull[slot], (i / GU_DEPTH) & 1);
+      if (t == 0 && i < 12) stamp(tr, c, 3 + i);
+      if (t == tw && i >= 20 && i < 24) stamp(tr, c, (i - 20) * 6 + 26);
+      ok = ok && (round == 0 || bwait(&bar.empty[s], (round - 1) & 1));
+      if (t == 0 && i < 12) stamp(tr, c, 15 + i);
+      if (t == tw && i >= 20 && i < 24) stamp(tr, c, (i - 20) * 6 + 27);
       if (!ok) fail(a, bar.abort_flag);
       // tcgen05.st is warp-collective: leave the loop as a whole warp
       if (!__all_sync(0xffffffffu, ok) || __any_sync(0xffffffffu, *bar.abort_flag != 0)) break;
       tc_fence_after();                                     // the MMAs that read stage s are done
-      const int slot = i % RAW_DEPTH;
-      const uint32_t d = rbase + slot * raw_slot + t * 16;
-      const uint32_t md = (meta >> (3 * slot)) & 7u;
+      const uint32_t reg = rbase + slot * GU_RAW_SLOT + m * GU_REGION;
       uint32_t v[16];
-      if ((md & 3) == 1) {
-        const uint4 w0 = lds128(d), w1 = lds128(d + GU_PSTRIDE);
+      if (T < p.hot_tiles) {
+        const uint4 w0 = lds128(reg + r * KC + 32 * h), w1 = lds128(reg + r * KC + 32 * h + 16);
         const uint4 p0 = fp8_piece_nat(w0.x, w0.y), p1 = fp8_piece_nat(w0.z, w0.w);
         const uint4 p2 = fp8_piece_nat(w1.x, w1.y), p3 = fp8_piece_nat(w1.z, w1.w);
         v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w; v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
         v[8] = p2.x; v[9] = p2.y; v[10] = p2.z; v[11] = p2.w; v[12] = p3.x; v[13] = p3.y; v[14] = p3.z; v[15] = p3.w;
-      } else if ((md & 3) == 2) {
-        const uint4 w0 = lds128(d);
-        const uint32_t w4 = lds32(d + GU_PSTRIDE);
-        const __half sc = half_of(lds32(scbase + (slot * GU_PROD + t) * 4), md >> 2);
+      } else if (dR >= 0 && dR < a.n_records) {
+        const uint32_t wa = reg + r * GU_COLD_WIN + 16 * h;
+        const uint4 w0 = lds128(wa);
+        const uint32_t w4 = lds32(wa + 16);
+        // fp16 scale of group k / 2 at record byte 6146 + 64 m + 2 (k / 2), in the copied 16-byte window
+        const uint32_t so = (2 + 2 * (k >> 1)) & 15;
+        const __half sc = half_of(lds32(reg + GU_SCALE_OFF + r * 16 + (so & ~3u)), (so >> 1) & 1);
         const uint4 p0 = scale_piece(int4_piece_perm(shift2(w0.x, w0.y)), sc);
         const uint4 p1 = scale_piece(int4_piece_perm(shift2(w0.y, w0.z)), sc);
         const uint4 p2 = scale_piece(int4_piece_perm(shift2(w0.z, w0.w)), sc);
@@ -484,11 +588,14 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu(GuParams p) {
         v[8] = p2.x; v[9] = p2.y; v[10] = p2.z; v[11] = p2.w; v[12] = p3.x; v[13] = p3.y; v[14] = p3.z; v[15] = p3.w;
       } else {
 #pragma unroll
-        for (int k = 0; k < 16; ++k) v[k] = 0u;
+        for (int j = 0; j < 16; ++j) v[j] = 0u;            // past the union's end, or a bad record
       }
+      if (t == tw && i >= 20 && i < 24) stamp(tr, c, (i - 20) * 6 + 28);
+      mbar_arrive(&bar.rawempty[slot]);                     // raw slot read
       tmem_st16(a_lane + 64 * s, v);
       tc_fence_before();
       mbar_arrive(&bar.full[s]);
+      if (t == tw && i >= 20 && i < 24) stamp(tr, c, (i - 20) * 6 + 29);
     }
     cp_wait<0>();
   } else if (t == GU_PROD) {
@@ -499,10 +606,9 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu(GuParams p) {
       const int k = (lo + i) & (H / KC - 1);
       const bool first = i == 0 || k == 0, last = i == nunits - 1 || k == H / KC - 1;
       const int tb = seg & 1;
-      if (first && seg >= 2 && !mbar_wait(&bar.tfree[tb], ((seg >> 1) - 1) & 1, WAIT_NS)) fail(a, bar.abort_flag);
+      if (first && seg >= 2 && !bwait(&bar.tfree[tb], ((seg >> 1) - 1) & 1)) fail(a, bar.abort_flag);
       const int s = i % GU_STAGES, round = i / GU_STAGES;
-      if (!mbar_wait(&bar.full[s], round & 1, WAIT_NS) || !mbar_wait(&bar.xfull[s], round & 1, WAIT_NS))
-        fail(a, bar.abort_flag);
+      if (!bwait(&bar.full[s], round & 1) || !bwait(&bar.xfull[s], round & 1)) fail(a, bar.abort_flag);
       if (*bar.abort_flag) break;
       tc_fence_after();
       const uint32_t X = xbase + s * x_bytes;
@@ -526,24 +632,26 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu(GuParams p) {
     for (int i = 0; i < nunits; ++i) {
       const int x = lo + i, T = x >> 6, k = x & (H / KC - 1);
       const int s = i % GU_STAGES, round = i / GU_STAGES;
-      if (round > 0 && !mbar_wait(&bar.empty[s], (round - 1) & 1, WAIT_NS)) fail(a, bar.abort_flag);
+      if (round > 0 && !bwait(&bar.empty[s], (round - 1) & 1)) fail(a, bar.abort_flag);
       if (*bar.abort_flag) break;
+      if (i == 0) stamp(tr, c, 54);
       mbar_arrive_expect_tx(&bar.xfull[s], x_bytes);
       bulk_copy(xbase + s * x_bytes, (T < p.hot_tiles ? p.xs_nat : p.xs_perm) + (size_t)k * x_bytes, x_bytes,
                 &bar.xfull[s]);
     }
   } else if (t >= GU_PROD + 64) {
-    // ---- epilogue: warp (18..21) & 3 reads TMEM lanes [32 q, 32 q + 32)
+    // ---- epilogue: warp (19..22) & 3 reads TMEM lanes [32 q, 32 q + 32)
     const int q = warp & 3, r = q * 32 + lane;
     int seg = 0;
     for (int x0 = lo; x0 < hi; ++seg) {
       const int T = x0 >> 6;
       const int x1 = min(hi, (T + 1) * (H / KC));
       const int tb = seg & 1;
-      const bool done = mbar_wait(&bar.accf[tb], (seg >> 1) & 1, WAIT_NS);
+      const bool done = bwait(&bar.accf[tb], (seg >> 1) & 1);
       if (!done) fail(a, bar.abort_flag);
       const bool go = __all_sync(0xffffffffu, done) && !__any_sync(0xffffffffu, *bar.abort_flag != 0);
       if (!go) break;
+      if (lane == 0 && warp == (GU_PROD + 64) / 32) stamp(tr, c, seg == 0 ? 52 : 53);
       tc_fence_after();
       const bool hotT = T < p.hot_tiles;
       const int row = (hotT ? T : T - p.hot_tiles) * TILE + r;
@@ -564,6 +672,10 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu(GuParams p) {
   }
   tc_fence_before();
   __syncthreads();
+  if (t == 0) {
+    stamp(tr, c, 56);
+    if (tr) tr[(size_t)c * TRACE_SLOTS + 57] = (uint64_t)nunits;
+  }
   if (warp == 0) {
     tc_fence_after();
     tmem_free(tmem, 512);
@@ -624,6 +736,7 @@ struct DownParams {
   float* y;
   int N, stages;
   uint32_t tmem_cols;
+  uint64_t* trace;
 };
 
 __global__ void __launch_bounds__(DN_THREADS, 1) k_down(DownParams p) {
@@ -662,7 +775,8 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down(DownParams p) {
     auto rec_copy = [&](int u) {
       if (u >= nunits) return;
       const int slot = ((lo + u) % nsub) * KC + q;
-      if (slot >= a.n_hot && slot < total) cp4(recbase + ((u % REC_RING) * DN_PROD + t) * 4, a.rec + (slot - a.n_hot));
+      if (slot >= a.n_hot && slot < total)
+        cp4(recbase + ((u % REC_RING) * DN_PROD + t) * 4, a.rec + (slot - a.n_hot));
     };
     auto issue = [&](int i) {
       rec_copy(i + REC_AHEAD);
@@ -713,7 +827,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down(DownParams p) {
       issue(i + RAW_DEPTH - 1);
       cp_wait<RAW_DEPTH - 1>();
       const int s = i % p.stages, round = i / p.stages;
-      if (round > 0 && !mbar_wait(&bar.empty[s], (round - 1) & 1, WAIT_NS)) fail(a, bar.abort_flag);
+      if (round > 0 && !bwait(&bar.empty[s], (round - 1) & 1)) fail(a, bar.abort_flag);
       if (*bar.abort_flag) break;
       const int rs = i % RAW_DEPTH;
       const uint32_t d = rbase + rs * raw_slot + t * 16;
@@ -760,9 +874,9 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down(DownParams p) {
       const int sub = (lo + i) % nsub;
       const bool first = i == 0 || sub == 0, last = i == nunits - 1 || sub == nsub - 1;
       const int tb = seg & 1;
-      if (first && seg >= 2 && !mbar_wait(&bar.tfree[tb], ((seg >> 1) - 1) & 1, WAIT_NS)) fail(a, bar.abort_flag);
+      if (first && seg >= 2 && !bwait(&bar.tfree[tb], ((seg >> 1) - 1) & 1)) fail(a, bar.abort_flag);
       const int s = i % p.stages, round = i / p.stages;
-      if (!mbar_wait(&bar.full[s], round & 1, WAIT_NS)) fail(a, bar.abort_flag);
+      if (!bwait(&bar.full[s], round & 1)) fail(a, bar.abort_flag);
       if (*bar.abort_flag) break;
       tc_fence_after();
       const uint32_t st = sbase + s * stage_bytes;
@@ -784,7 +898,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down(DownParams p) {
       const int et = x0 / nsub;
       const int x1 = min(hi, (et + 1) * nsub);
       const int tb = seg & 1;
-      const bool done = mbar_wait(&bar.accf[tb], (seg >> 1) & 1, WAIT_NS);
+      const bool done = bwait(&bar.accf[tb], (seg >> 1) & 1);
       if (!done) fail(a, bar.abort_flag);
       const bool go = __all_sync(0xffffffffu, done) && !__any_sync(0xffffffffu, *bar.abort_flag != 0);
       if (!go) break;
@@ -814,6 +928,561 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down(DownParams p) {
   }
 }
 
+constexpr int DD_DEPTH = 8;                         // k_down_p: weight block slots (8 KB each)
+constexpr int DD_ACTS = 4;                          // k_down_p: activation block slots
+constexpr int DD_STAGES = 4;                        // k_down_p: f16 operand stages
+
+// ===========================================================================
+// Packed dense mode.  Once per layer (hc_batch_pack), the weights are copied
+// into unit-major blocks so that every 64-wide K step of a 128-row gate/up
+// tile, and every 64-neuron step of a 128-row down tile, is ONE contiguous
+// block read by ONE bulk copy.  Neuron slots: hot neurons [0, 128 ht) (ht =
+// ceil(n_hot / 128), padded with zero rows), then every record of the section
+// in storage order [128 ht, 128 ht + n_records).  Block layouts (16-byte
+// chunks are XOR-swizzled so the decoders' 16-byte shared-memory reads of 8
+// neighbouring rows fall on distinct banks):
+//   gate/up hot   [m 2][row 128][64 B]  e4m3, chunk c of row r at c ^ ((r >> 1) & 3)      16384 B
+//   gate/up cold  [m 2][row 128][32 B]  INT4 field bytes, chunk c at c ^ ((r >> 2) & 1)
+//                 + [m][row] fp16 group scale                                              8704 B
+//   down hot      [row 64][128 B]       e4m3 of output rows 128 et .., chunk c at c ^ (row & 7)  8192 B
+//   down cold     [row 64][64 B]        INT4 field bytes + [row] fp16 group scale             4224 B
+// ===========================================================================
+constexpr int PG_HOT = 16384, PG_COLD = 8704, PD_HOT = 8192, PD_COLD = 4224;
+
+struct PackLayout {
+  int hot_tiles, cold_tiles, hot_blocks, cold_blocks;
+  size_t gu_hot, gu_cold, dn_hot, dn_cold, total;
+};
+__host__ __device__ inline PackLayout pack_layout(int n_hot, int n_records) {
+  PackLayout L;
+  L.hot_tiles = (n_hot + TILE - 1) / TILE;
+  L.cold_tiles = (n_records + TILE - 1) / TILE;
+  L.hot_blocks = 2 * L.hot_tiles;
+  L.cold_blocks = (n_records + KC - 1) / KC;
+  size_t o = 0;
+  L.gu_hot = o;  o += (size_t)L.hot_tiles * (H / KC) * PG_HOT;
+  L.gu_cold = o; o += (size_t)L.cold_tiles * (H / KC) * PG_COLD;
+  L.dn_hot = o;  o += (size_t)(H / TILE) * L.hot_blocks * PD_HOT;
+  L.dn_cold = o; o += (size_t)(H / TILE) * L.cold_blocks * PD_COLD;
+  L.total = (o + 1023) / 1024 * 1024;
+  return L;
+}
+
+// one thread per 16-byte output chunk (scales: one thread per fp16)
+__global__ void k_pack(const uint8_t* __restrict__ hot, int n_hot, const uint8_t* __restrict__ cold, int n_records,
+                       uint8_t* __restrict__ out) {
+  const PackLayout L = pack_layout(n_hot, n_records);
+  const int64_t n_gu_hot = (int64_t)L.hot_tiles * (H / KC) * PG_HOT / 16;
+  const int64_t n_gu_cold = (int64_t)L.cold_tiles * (H / KC) * (2 * TILE * 2);       // 16-byte chunks
+  const int64_t n_gu_sc = (int64_t)L.cold_tiles * (H / KC) * (2 * TILE);             // fp16 scales
+  const int64_t n_dn_hot = (int64_t)(H / TILE) * L.hot_blocks * PD_HOT / 16;
+  const int64_t n_dn_cold = (int64_t)(H / TILE) * L.cold_blocks * (KC * 4);
+  const int64_t n_dn_sc = (int64_t)(H / TILE) * L.cold_blocks * KC;
+  const int64_t total = n_gu_hot + n_gu_cold + n_gu_sc + n_dn_hot + n_dn_cold + n_dn_sc;
+  auto field16 = [&](const uint8_t* p) {          // 16 unaligned bytes
+    uint8_t b[16];
+    for (int i = 0; i < 16; ++i) b[i] = p[i];
+    return *reinterpret_cast<const uint4*>(b);
+  };
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t k = i;
+    if (k < n_gu_hot) {                           // (unit, m, row, c)
+      const int c = k & 3, r = (k >> 2) & 127, m = (k >> 9) & 1;
+      const int64_t unit = k >> 10;
+      const int T = (int)(unit / (H / KC)), kb = (int)(unit % (H / KC));
+      const int row = T * TILE + r;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (row < n_hot) v = *reinterpret_cast<const uint4*>(hot + (size_t)row * HOT_ROW + m * H + kb * KC + 16 * c);
+      *reinterpret_cast<uint4*>(out + L.gu_hot + unit * PG_HOT + m * (TILE * KC) + r * KC +
+                                16 * (c ^ ((r >> 1) & 3))) = v;
+      continue;
+    }
+    k -= n_gu_hot;
+    if (k < n_gu_cold) {                          // (unit, m, row, c)
+      const int c = k & 1, r = (k >> 1) & 127, m = (k >> 8) & 1;
+      const int64_t unit = k >> 9;
+      const int T = (int)(unit / (H / KC)), kb = (int)(unit % (H / KC));
+      const int R = T * TILE + r;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (R < n_records) v = field16(cold + (size_t)R * REC_BYTES + 2 + m * VEC_BYTES + kb * (KC / 2) + 16 * c);
+      *reinterpret_cast<uint4*>(out + L.gu_cold + unit * PG_COLD + m * (TILE * 32) + r * 32 +
+                                16 * (c ^ ((r >> 2) & 1))) = v;
+      continue;
+    }
+    k -= n_gu_cold;
+    if (k < n_gu_sc) {                            // (unit, m, row)
+      const int r = k & 127, m = (k >> 7) & 1;
+      const int64_t unit = k >> 8;
+      const int T = (int)(unit / (H / KC)), kb = (int)(unit % (H / KC));
+      const int R = T * TILE + r;
+      uint16_t v = 0;
+      if (R < n_records) {
+        const uint8_t* sp = cold + (size_t)R * REC_BYTES + SCALE_OFF + m * 2 * NGROUPS + 2 * (kb >> 1);
+        v = (uint16_t)(sp[0] | (sp[1] << 8));
+      }
+      *reinterpret_cast<uint16_t*>(out + L.gu_cold + unit * PG_COLD + 2 * TILE * 32 + (m * TILE + r) * 2) = v;
+      continue;
+    }
+    k -= n_gu_sc;
+    if (k < n_dn_hot) {                           // (et, block, q, c)
+      const int c = k & 7, q = (k >> 3) & 63;
+      const int64_t ub = k >> 9;                  // et * hot_blocks + block
+      const int et = (int)(ub / L.hot_blocks), nb = (int)(ub % L.hot_blocks);
+      const int n = nb * KC + q;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (n < n_hot) v = *reinterpret_cast<const uint4*>(hot + (size_t)n * HOT_ROW + 2 * H + et * TILE + 16 * c);
+      *reinterpret_cast<uint4*>(out + L.dn_hot + ub * PD_HOT + q * TILE + 16 * (c ^ (q & 7))) = v;
+      continue;
+    }
+    k -= n_dn_hot;
+    if (k < n_dn_cold) {                          // (et, block, q, c)
+      const int c = k & 3, q = (k >> 2) & 63;
+      const int64_t ub = k >> 8;
+      const int et = (int)(ub / L.cold_blocks), nb = (int)(ub % L.cold_blocks);
+      const int R = nb * KC + q;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (R < n_records) v = field16(cold + (size_t)R * REC_BYTES + 2 + 2 * VEC_BYTES + et * (TILE / 2) + 16 * c);
+      *reinterpret_cast<uint4*>(out + L.dn_cold + ub * PD_COLD + q * 64 + 16 * c) = v;
+      continue;
+    }
+    k -= n_dn_cold;
+    {                                             // (et, block, q)
+      const int q = k & 63;
+      const int64_t ub = k >> 6;
+      const int et = (int)(ub / L.cold_blocks), nb = (int)(ub % L.cold_blocks);
+      const int R = nb * KC + q;
+      uint16_t v = 0;
+      if (R < n_records) {
+        const uint8_t* sp = cold + (size_t)R * REC_BYTES + SCALE_OFF + 4 * NGROUPS + 2 * et;
+        v = (uint16_t)(sp[0] | (sp[1] << 8));
+      }
+      *reinterpret_cast<uint16_t*>(out + L.dn_cold + ub * PD_COLD + KC * 64 + q * 2) = v;
+    }
+  }
+}
+
+// 16-byte chunk index swizzle of activation rows (2N bytes) written by k_act_p,
+// read by k_down_p: keeps the reads of 8 neighbouring rows on distinct banks
+__host__ __device__ inline int act_swz(int slot, int N) {
+  return N == 64 ? (slot & 7) : N == 32 ? ((slot >> 1) & 3) : N == 16 ? ((slot >> 2) & 1) : 0;
+}
+
+struct PackedParams {
+  LayerArgs a;
+  const uint8_t* packed;
+  const uint8_t* xs_nat;
+  const uint8_t* xs_perm;
+  float* part;
+  int N;
+  uint64_t* trace;
+};
+
+// ---------------------------------------------------------------------------
+// k_gu_p: k_gu over the packed blocks.  Units x = (tile x / 64, K step x % 64)
+// over hot tiles then cold tiles (all records); thread 0 bulk-copies each
+// unit's block GU_AHEAD units ahead; decoders as in k_gu.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(GU_THREADS, 1) k_gu_p(const __grid_constant__ PackedParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const LayerArgs& a = p.a;
+  const PackLayout L = pack_layout(a.n_hot, a.n_records);
+  const int N = p.N, G = gridDim.x, c = blockIdx.x;
+  const int tiles = L.hot_tiles + L.cold_tiles;
+  const int U = tiles * (H / KC);
+  const int lo = range_lo(c, U, G), hi = range_lo(c + 1, U, G);
+  if (lo >= hi) return;
+  const int nunits = hi - lo;
+  uint64_t* tr = p.trace;
+  if (t == 0) stamp(tr, c, 0);
+
+  const int x_bytes = N * KC * 2;
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t rbase = sbase;                             // [GUP_GSLOTS][GUP_GROUP * PG_HOT] raw unit groups
+  const uint32_t xbase = rbase + GUP_GSLOTS * GUP_GROUP * PG_HOT;   // [GUX_STAGES][x_bytes] token tiles
+  const Bars bar = carve_bars(smem + GUP_GSLOTS * GUP_GROUP * PG_HOT + GUX_STAGES * x_bytes);
+  // packed source and size of local unit i; a group's units sit back to back in its slot
+  auto usrc = [&](int i) -> const uint8_t* {
+    const int x = lo + i;
+    return p.packed + (x < L.hot_tiles * (H / KC) ? L.gu_hot + (size_t)x * PG_HOT
+                                                   : L.gu_cold + (size_t)(x - L.hot_tiles * (H / KC)) * PG_COLD);
+  };
+  auto usize = [&](int i) -> uint32_t { return lo + i < L.hot_tiles * (H / KC) ? PG_HOT : PG_COLD; };
+
+  // group g = local units [4 g, 4 g + 4): one bulk copy per run of contiguous blocks (the hot
+  // blocks, then the cold ones), issued by lane 1 of the token-tile warp two groups ahead
+  const int ngroups = (nunits + GUP_GROUP - 1) / GUP_GROUP;
+  auto issue = [&](int g) {
+    if (g >= ngroups) return;
+    const int slot = g % GUP_GSLOTS, use = g / GUP_GSLOTS;
+    if (use > 0 && !bwait(&bar.rawempty[slot], (use - 1) & 1)) fail(a, bar.abort_flag);
+    const int i0 = g * GUP_GROUP, i1 = min(nunits, i0 + GUP_GROUP);
+    uint32_t total = 0;
+    for (int i = i0; i < i1; ++i) total += usize(i);
+    mbar_arrive_expect_tx(&bar.rawfull[slot], total);
+    uint32_t off = 0;
+    for (int i = i0; i < i1;) {
+      int j = i + 1;
+      uint32_t run = usize(i);
+      while (j < i1 && usrc(j) == usrc(j - 1) + usize(j - 1)) run += usize(j++);
+      bulk_copy(rbase + slot * (GUP_GROUP * PG_HOT) + off, usrc(i), run, &bar.rawfull[slot]);
+      off += run;
+      i = j;
+    }
+  };
+
+  if (t == 0) init_bars(bar, GU_STAGES, GU_PROD, 1);
+  if (warp == 0) tmem_alloc(bar.tslot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *bar.tslot;
+
+  if (t < GU_PROD) {
+    const int q = warp & 3, m = (warp >> 2) & 1, h = warp >> 3;
+    const int r = q * 32 + lane;
+    const uint32_t a_lane = tmem + ((uint32_t)(q * 32) << 16) + GU_A_COL + 32 * m + 16 * h;
+    for (int i = 0; i < nunits; ++i) {
+      const bool tw = t == 0 && i >= 20 && i < 24;
+      if (tw) stamp(tr, c, 24 + (i - 20) * 6);
+      const int g = i / GUP_GROUP, jg = i % GUP_GROUP;
+      const int x = lo + i, T = x >> 6, kb = x & (H / KC - 1);
+      const int slot = g % GUP_GSLOTS, s = i % GU_STAGES, round = i / GU_STAGES;
+      bool ok = bwait(&bar.rawfull[slot], (g / GUP_GSLOTS) & 1);
+      if (tw) stamp(tr, c, 24 + (i - 20) * 6 + 1);
+      ok = ok && (round == 0 || bwait(&bar.empty[s], (round - 1) & 1));
+      if (tw) stamp(tr, c, 24 + (i - 20) * 6 + 2);
+      if (!ok) fail(a, bar.abort_flag);
+      if (!__all_sync(0xffffffffu, ok) || __any_sync(0xffffffffu, *bar.abort_flag != 0)) break;
+      tc_fence_after();
+      uint32_t uoff = 0;
+      for (int i2 = g * GUP_GROUP; i2 < i; ++i2) uoff += usize(i2);
+      const uint32_t blk = rbase + slot * (GUP_GROUP * PG_HOT) + uoff;
+      uint32_t v[16];
+      if (T < L.hot_tiles) {
+        const uint32_t row = blk + m * (TILE * KC) + r * KC;
+        const int sw = (r >> 1) & 3;
+        const uint4 w0 = lds128(row + (((2 * h) ^ sw) << 4)), w1 = lds128(row + (((2 * h + 1) ^ sw) << 4));
+        const uint4 p0 = fp8_piece_nat(w0.x, w0.y), p1 = fp8_piece_nat(w0.z, w0.w);
+        const uint4 p2 = fp8_piece_nat(w1.x, w1.y), p3 = fp8_piece_nat(w1.z, w1.w);
+        v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w; v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
+        v[8] = p2.x; v[9] = p2.y; v[10] = p2.z; v[11] = p2.w; v[12] = p3.x; v[13] = p3.y; v[14] = p3.z; v[15] = p3.w;
+      } else {
+        const uint4 w = lds128(blk + m * (TILE * 32) + r * 32 + ((h ^ ((r >> 2) & 1)) << 4));
+        const uint32_t sw = lds32(blk + 2 * TILE * 32 + ((m * TILE + r) * 2 & ~3));
+        const __half sc = half_of(sw, r & 1);
+        const uint4 p0 = scale_piece(int4_piece_perm(w.x), sc), p1 = scale_piece(int4_piece_perm(w.y), sc);
+        const uint4 p2 = scale_piece(int4_piece_perm(w.z), sc), p3 = scale_piece(int4_piece_perm(w.w), sc);
+        v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w; v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
+        v[8] = p2.x; v[9] = p2.y; v[10] = p2.z; v[11] = p2.w; v[12] = p3.x; v[13] = p3.y; v[14] = p3.z; v[15] = p3.w;
+      }
+      (void)kb;
+      if (tw) stamp(tr, c, 24 + (i - 20) * 6 + 3);
+      if (jg == GUP_GROUP - 1 || i == nunits - 1) mbar_arrive(&bar.rawempty[slot]);   // group read
+      tmem_st16(a_lane + 64 * s, v);
+      tc_fence_before();
+      mbar_arrive(&bar.full[s]);
+      if (tw) stamp(tr, c, 24 + (i - 20) * 6 + 4);
+    }
+  } else if (t == GU_PROD) {
+    const uint32_t idesc = idesc_f16(N, 0, 0);
+    int seg = 0;
+    for (int i = 0; i < nunits; ++i) {
+      const int kb = (lo + i) & (H / KC - 1);
+      const bool first = i == 0 || kb == 0, last = i == nunits - 1 || kb == H / KC - 1;
+      const int tb = seg & 1;
+      if (first && seg >= 2 && !bwait(&bar.tfree[tb], ((seg >> 1) - 1) & 1)) fail(a, bar.abort_flag);
+      const int s = i % GU_STAGES, round = i / GU_STAGES;
+      const int xs = i % GUX_STAGES;
+      const bool tw = i >= 20 && i < 24;
+      if (tw) stamp(tr, c, 48 + (i - 20) * 3);
+      if (!bwait(&bar.full[s], round & 1)) fail(a, bar.abort_flag);
+      if (tw) stamp(tr, c, 48 + (i - 20) * 3 + 1);
+      if (!bwait(&bar.xfull[xs], (i / GUX_STAGES) & 1)) fail(a, bar.abort_flag);
+      if (tw) stamp(tr, c, 48 + (i - 20) * 3 + 2);
+      if (*bar.abort_flag) break;
+      tc_fence_after();
+      const uint32_t X = xbase + xs * x_bytes;
+      const uint32_t dt = tmem + tb * 2 * N;
+      const uint32_t at = tmem + GU_A_COL + 64 * s;
+#pragma unroll
+      for (int j = 0; j < KC / 16; ++j) {
+        const uint64_t bd = sdesc(X + j * 2 * 16 * N, 16 * N, 128);
+        const uint32_t acc = !(first && j == 0);
+        umma_f16_ts(dt, at + 8 * j, bd, idesc, acc);
+        umma_f16_ts(dt + N, at + 32 + 8 * j, bd, idesc, acc);
+      }
+      umma_commit(&bar.empty[s]);
+      umma_commit(&bar.xempty[xs]);
+      if (last) {
+        umma_commit(&bar.accf[tb]);
+        ++seg;
+      }
+    }
+  } else if (t == GU_PROD + 33) {
+    for (int g = 0; g < ngroups && !*bar.abort_flag; ++g) issue(g);
+  } else if (t == GU_PROD + 32) {
+    // token tiles, up to GUX_STAGES units ahead of the MMAs
+    for (int i = 0; i < nunits; ++i) {
+      const int x = lo + i, T = x >> 6, kb = x & (H / KC - 1);
+      const int xs = i % GUX_STAGES, round = i / GUX_STAGES;
+      if (round > 0 && !bwait(&bar.xempty[xs], (round - 1) & 1)) fail(a, bar.abort_flag);
+      if (*bar.abort_flag) break;
+      mbar_arrive_expect_tx(&bar.xfull[xs], x_bytes);
+      bulk_copy(xbase + xs * x_bytes, (T < L.hot_tiles ? p.xs_nat : p.xs_perm) + (size_t)kb * x_bytes, x_bytes,
+                &bar.xfull[xs]);
+    }
+  } else if (t >= GU_PROD + 64) {
+    const int q = warp & 3, r = q * 32 + lane;
+    int seg = 0;
+    for (int x0 = lo; x0 < hi; ++seg) {
+      const int T = x0 >> 6;
+      const int x1 = min(hi, (T + 1) * (H / KC));
+      const int tb = seg & 1;
+      const bool done = bwait(&bar.accf[tb], (seg >> 1) & 1);
+      if (!done) fail(a, bar.abort_flag);
+      const bool go = __all_sync(0xffffffffu, done) && !__any_sync(0xffffffffu, *bar.abort_flag != 0);
+      if (!go) break;
+      tc_fence_after();
+      float* dst = p.part + ((size_t)(T + c) * TILE + r) * (2 * N);
+      for (int col = 0; col < 2 * N; col += 8) {
+        float v[8];
+        tmem_ld8(tmem + ((uint32_t)(q * 32) << 16) + tb * 2 * N + col, v);
+        reinterpret_cast<float4*>(dst + col)[0] = make_float4(v[0], v[1], v[2], v[3]);
+        reinterpret_cast<float4*>(dst + col)[1] = make_float4(v[4], v[5], v[6], v[7]);
+      }
+      tc_fence_before();
+      mbar_arrive(&bar.tfree[tb]);
+      x0 = x1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (t == 0) stamp(tr, c, 56);
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_free(tmem, 512);
+  }
+}
+
+// act[slot][b] (swizzled 16-byte chunks) for every packed slot; records outside the fetch set -> 0
+__global__ void __launch_bounds__(256) k_act_p(LayerArgs a, const float* __restrict__ part, int G, int N,
+                                               __half* __restrict__ act) {
+  const PackLayout L = pack_layout(a.n_hot, a.n_records);
+  const int U = (L.hot_tiles + L.cold_tiles) * (H / KC);
+  const int slots = (L.hot_blocks + L.cold_blocks) * KC;
+  const int groups = N / 8;
+  const int i = blockIdx.x * 256 + threadIdx.x;
+  const int slot = i / groups, g = i % groups;
+  if (slot >= slots) return;
+  const int hot_slots = L.hot_tiles * TILE;
+  bool live;
+  float sg = 1.0f, su = 1.0f, sd = 1.0f;
+  if (slot < hot_slots) {
+    live = slot < a.n_hot;
+    if (live && a.hot_scale) {
+      sg = __ldg(a.hot_scale + (size_t)slot * 3);
+      su = __ldg(a.hot_scale + (size_t)slot * 3 + 1);
+      sd = __ldg(a.hot_scale + (size_t)slot * 3 + 2);
+    }
+  } else {
+    const int j = slot - hot_slots;
+    live = j < a.n_records && __ldg(a.flags + j);
+  }
+  __half o[8];
+  if (live) {
+    const int T = slot / TILE, r = slot % TILE;
+    const int c0 = unit_owner(T * (H / KC), U, G), c1 = unit_owner(T * (H / KC) + H / KC - 1, U, G);
+    float gs[8], us[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) gs[e] = us[e] = 0.0f;
+    for (int cc = c0; cc <= c1; ++cc) {
+      const float* row = part + ((size_t)(T + cc) * TILE + r) * (2 * N) + g * 8;
+      const float4 g0 = reinterpret_cast<const float4*>(row)[0], g1 = reinterpret_cast<const float4*>(row)[1];
+      const float4 u0 = reinterpret_cast<const float4*>(row + N)[0], u1 = reinterpret_cast<const float4*>(row + N)[1];
+      gs[0] += g0.x; gs[1] += g0.y; gs[2] += g0.z; gs[3] += g0.w; gs[4] += g1.x; gs[5] += g1.y; gs[6] += g1.z; gs[7] += g1.w;
+      us[0] += u0.x; us[1] += u0.y; us[2] += u0.z; us[3] += u0.w; us[4] += u1.x; us[5] += u1.y; us[6] += u1.z; us[7] += u1.w;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = __float2half_rn(gated(gs[e] * sg, us[e] * su, a.relu, a.both) * sd);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = __float2half_rn(0.0f);
+  }
+  *reinterpret_cast<uint4*>(act + (size_t)slot * N + ((g ^ act_swz(slot, N)) * 8)) = *reinterpret_cast<const uint4*>(o);
+}
+
+// ---------------------------------------------------------------------------
+// k_down_p: k_down over the packed blocks.  Unit x = (output tile x / nblk,
+// 64-slot block x % nblk); thread 0 bulk-copies the block's weights and its
+// 64 activation rows DD_AHEAD units ahead.
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(DN_THREADS, 1) k_down_p(const __grid_constant__ PackedParams p, const __half* act,
+                                                          float* y, uint32_t tmem_cols) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const LayerArgs& a = p.a;
+  const PackLayout L = pack_layout(a.n_hot, a.n_records);
+  const int N = p.N, G = gridDim.x, c = blockIdx.x;
+  const int nblk = L.hot_blocks + L.cold_blocks;
+  const int U = (H / TILE) * nblk;
+  const int lo = range_lo(c, U, G), hi = range_lo(c + 1, U, G);
+  if (lo >= hi) return;
+  const int nunits = hi - lo;
+
+  const int b_bytes = KC * N * 2;
+  const int stage_bytes = A_TILE_BYTES + b_bytes;
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t wbase = sbase;                             // [DD_DEPTH][PD_HOT] weight blocks
+  const uint32_t abase = wbase + DD_DEPTH * PD_HOT;         // [DD_ACTS][KC * 2 NMAX] activation blocks
+  const uint32_t stbase = abase + DD_ACTS * KC * NMAX * 2;  // [DD_STAGES][stage_bytes]
+  const Bars bar = carve_bars(smem + DD_DEPTH * PD_HOT + DD_ACTS * KC * NMAX * 2 + DD_STAGES * stage_bytes);
+
+  if (t == 0) init_bars(bar, DD_STAGES, DN_PROD, 1, DN_PROD);
+  if (warp == 0) tmem_alloc(bar.tslot, tmem_cols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *bar.tslot;
+
+  // lane 1 of the MMA warp: weight blocks DD_AHEAD units ahead (DRAM), activation blocks DD_ACT_AHEAD ahead (L2)
+  auto issue_w = [&](int i) {
+    if (i >= nunits) return;
+    const int x = lo + i, et = x / nblk, nb = x % nblk;
+    const int slot = i % DD_DEPTH, use = i / DD_DEPTH;
+    if (use > 0 && !bwait(&bar.rawempty[slot], (use - 1) & 1)) fail(a, bar.abort_flag);
+    const bool hotB = nb < L.hot_blocks;
+    const uint8_t* src = p.packed + (hotB ? L.dn_hot + ((size_t)et * L.hot_blocks + nb) * PD_HOT
+                                          : L.dn_cold + ((size_t)et * L.cold_blocks + (nb - L.hot_blocks)) * PD_COLD);
+    const uint32_t wbytes = hotB ? PD_HOT : PD_COLD;
+    mbar_arrive_expect_tx(&bar.rawfull[slot], wbytes);
+    bulk_copy(wbase + slot * PD_HOT, src, wbytes, &bar.rawfull[slot]);
+  };
+  auto issue_a = [&](int i) {
+    if (i >= nunits) return;
+    const int nb = (lo + i) % nblk;
+    const int slot = i % DD_ACTS, use = i / DD_ACTS;
+    if (use > 0 && !bwait(&bar.xempty[slot], (use - 1) & 1)) fail(a, bar.abort_flag);
+    mbar_arrive_expect_tx(&bar.xfull[slot], b_bytes);
+    bulk_copy(abase + slot * (KC * NMAX * 2), act + (size_t)nb * KC * N, b_bytes, &bar.xfull[slot]);
+  };
+  if (t < DN_PROD) {
+    const int q = t >> 2, j = t & 3;
+    const int groups = N / 8;
+    for (int i = 0; i < nunits; ++i) {
+      const int x = lo + i, et = x / nblk, nb = x % nblk;
+      const int rs = i % DD_DEPTH, as = i % DD_ACTS, s = i % DD_STAGES, round = i / DD_STAGES;
+      bool ok = bwait(&bar.rawfull[rs], (i / DD_DEPTH) & 1) && bwait(&bar.xfull[as], (i / DD_ACTS) & 1);
+      ok = ok && (round == 0 || bwait(&bar.empty[s], (round - 1) & 1));
+      if (!ok) fail(a, bar.abort_flag);
+      if (*bar.abort_flag) break;
+      const uint32_t raw = wbase + rs * PD_HOT;
+      const uint32_t actb = abase + as * (KC * NMAX * 2);
+      const uint32_t A = stbase + s * stage_bytes + (q >> 3) * 2048 + (4 * j) * 128 + (q & 7) * 16;
+      const uint32_t B = stbase + s * stage_bytes + A_TILE_BYTES + (q >> 3) * 16 * N + (q & 7) * 16;
+      const int slot_q = nb * KC + q;
+      const int asw = act_swz(slot_q, N);
+      if (nb < L.hot_blocks) {
+        const uint32_t row = raw + q * TILE;
+        const uint4 w0 = lds128(row + (((2 * j) ^ (q & 7)) << 4));
+        const uint4 w1 = lds128(row + (((2 * j + 1) ^ (q & 7)) << 4));
+        sts128(A + 0 * 128, fp8_piece_perm(w0.x, w0.y));
+        sts128(A + 1 * 128, fp8_piece_perm(w0.z, w0.w));
+        sts128(A + 2 * 128, fp8_piece_perm(w1.x, w1.y));
+        sts128(A + 3 * 128, fp8_piece_perm(w1.z, w1.w));
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int g = j + 4 * hh;
+          if (g < groups) sts128(B + g * 128, lds128(actb + q * N * 2 + ((g ^ asw) << 4)));
+        }
+      } else {
+        const uint4 w = lds128(raw + q * 64 + 16 * j);
+        const __half ds = half_of(lds32(raw + KC * 64 + ((q * 2) & ~3)), q & 1);
+        sts128(A + 0 * 128, int4_piece_perm(w.x));
+        sts128(A + 1 * 128, int4_piece_perm(w.y));
+        sts128(A + 2 * 128, int4_piece_perm(w.z));
+        sts128(A + 3 * 128, int4_piece_perm(w.w));
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int g = j + 4 * hh;
+          if (g < groups) sts128(B + g * 128, scale_piece(lds128(actb + q * N * 2 + ((g ^ asw) << 4)), ds));
+        }
+      }
+      (void)et;
+      mbar_arrive(&bar.rawempty[rs]);
+      mbar_arrive(&bar.xempty[as]);
+      fence_async_smem();
+      mbar_arrive(&bar.full[s]);
+    }
+  } else if (t == DN_PROD + 1) {
+    // weights run DD_DEPTH - DD_ACTS units further ahead than the activation blocks
+    for (int i = 0; i < nunits && !*bar.abort_flag; ++i) {
+      issue_w(i);
+      if (i >= DD_DEPTH - DD_ACTS) issue_a(i - (DD_DEPTH - DD_ACTS));
+    }
+    for (int i = max(0, nunits - (DD_DEPTH - DD_ACTS)); i < nunits && !*bar.abort_flag; ++i) issue_a(i);
+  } else if (t == DN_PROD) {
+    const uint32_t idesc = idesc_f16(N, 1, 1);
+    int seg = 0;
+    for (int i = 0; i < nunits; ++i) {
+      const int nb = (lo + i) % nblk;
+      const bool first = i == 0 || nb == 0, last = i == nunits - 1 || nb == nblk - 1;
+      const int tb = seg & 1;
+      if (first && seg >= 2 && !bwait(&bar.tfree[tb], ((seg >> 1) - 1) & 1)) fail(a, bar.abort_flag);
+      const int s = i % DD_STAGES, round = i / DD_STAGES;
+      if (!bwait(&bar.full[s], round & 1)) fail(a, bar.abort_flag);
+      if (*bar.abort_flag) break;
+      tc_fence_after();
+      const uint32_t st = stbase + s * stage_bytes;
+      const uint32_t dt = tmem + tb * N;
+#pragma unroll
+      for (int k = 0; k < KC / 16; ++k)
+        umma_f16(dt, sdesc(st + k * 2 * 2048, 2048, 128), sdesc(st + A_TILE_BYTES + k * 2 * 16 * N, 16 * N, 128),
+                 idesc, !(first && k == 0));
+      umma_commit(&bar.empty[s]);
+      if (last) {
+        umma_commit(&bar.accf[tb]);
+        ++seg;
+      }
+    }
+  } else if (t >= DN_PROD + 32) {
+    const int qd = warp & 3, m = qd * 32 + lane;
+    int seg = 0;
+    for (int x0 = lo; x0 < hi; ++seg) {
+      const int et = x0 / nblk;
+      const int x1 = min(hi, (et + 1) * nblk);
+      const int tb = seg & 1;
+      const bool done = bwait(&bar.accf[tb], (seg >> 1) & 1);
+      if (!done) fail(a, bar.abort_flag);
+      const bool go = __all_sync(0xffffffffu, done) && !__any_sync(0xffffffffu, *bar.abort_flag != 0);
+      if (!go) break;
+      tc_fence_after();
+      const int e = et * TILE + (m & ~7) + perm8(m & 7);
+      float* yr = y + (size_t)e * N;
+      for (int col = 0; col < N; col += 8) {
+        float v[8];
+        tmem_ld8(tmem + ((uint32_t)(qd * 32) << 16) + tb * N + col, v);
+        asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(yr + col), "f"(v[0]), "f"(v[1]),
+                     "f"(v[2]), "f"(v[3])
+                     : "memory");
+        asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(yr + col + 4), "f"(v[4]), "f"(v[5]),
+                     "f"(v[6]), "f"(v[7])
+                     : "memory");
+      }
+      tc_fence_before();
+      mbar_arrive(&bar.tfree[tb]);
+      x0 = x1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_free(tmem, tmem_cols);
+  }
+}
+
 // x_b[e] += y[e][b] for b < nb; y is cleared for the next pass
 __global__ void __launch_bounds__(256) k_resid(float* __restrict__ x, int nb, int N, float* __restrict__ y) {
   const int e = blockIdx.x * 256 + threadIdx.x, g = blockIdx.y;
@@ -834,7 +1503,8 @@ __global__ void __launch_bounds__(256) k_resid(float* __restrict__ x, int nb, in
 __global__ void __launch_bounds__(1024) k_union(const uint32_t* __restrict__ masks, int64_t layer_stride, int batch,
                                                 int64_t token_stride, int words, const uint32_t* __restrict__ fetch,
                                                 const int32_t* __restrict__ table, int32_t* __restrict__ rec_out,
-                                                int64_t rec_stride, int32_t* __restrict__ count) {
+                                                int64_t rec_stride, int32_t* __restrict__ count,
+                                                uint8_t* __restrict__ flags, int64_t flag_stride) {
   __shared__ int warp_tot[32];
   __shared__ int base_s;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -843,6 +1513,10 @@ __global__ void __launch_bounds__(1024) k_union(const uint32_t* __restrict__ mas
   fetch += (size_t)layer * words;
   table += (size_t)layer * TABLE_SIZE;
   rec_out += (size_t)layer * rec_stride;
+  if (flags) {
+    flags += (size_t)layer * flag_stride;
+    for (int64_t i = tid; i < flag_stride; i += 1024) flags[i] = 0;
+  }
   if (tid == 0) base_s = 0;
   __syncthreads();
   for (int w0 = 0; w0 < words; w0 += 1024) {
@@ -883,7 +1557,9 @@ __global__ void __launch_bounds__(1024) k_union(const uint32_t* __restrict__ mas
     while (m) {
       const int bit = __ffs(m) - 1;
       m &= m - 1;
-      rec_out[pos++] = __ldg(table + w * 32 + bit);
+      const int r = __ldg(table + w * 32 + bit);
+      rec_out[pos++] = r;
+      if (flags && r >= 0 && r < flag_stride) flags[r] = 1;
     }
     __syncthreads();
     if (tid == 0) base_s += warp_tot[31];
@@ -918,54 +1594,118 @@ static uint32_t tmem_cols_for(int n) {
   return c;
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link)
+static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+// rows of `row_bytes` bytes, one after another from `base` (16-byte aligned), read in boxes of box_x bytes x box_y rows
+static bool encode_rows(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_x,
+                        uint32_t box_y, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn = tmap_encoder();
+  if (!fn || rows == 0) return false;
+  cuuint64_t dims[2] = {row_bytes, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_x, box_y};
+  cuuint32_t es[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static uint64_t* g_trace_gu = nullptr;
+static uint64_t* g_trace_down = nullptr;
+
 }  // namespace hcb
 
 using namespace hcb;
 
+extern "C" int hc_batch_set_trace(uint64_t* gu, uint64_t* down) {
+  g_trace_gu = gu;
+  g_trace_down = down;
+  return HC_OK;
+}
+
 extern "C" int64_t hc_ffn_batch_workspace_bytes(int32_t max_neurons) {
   if (max_neurons <= 0) return -1;
-  return (int64_t)ws_layout(max_neurons).total;
+  return (int64_t)ws_layout((int64_t)max_neurons + 2 * TILE).total;   // + the packed mode's slot padding
+}
+
+extern "C" int64_t hc_batch_pack_bytes(int32_t n_hot, int32_t n_records) {
+  if (n_hot < 0 || n_records < 0) return -1;
+  return (int64_t)pack_layout(n_hot, n_records).total;
+}
+
+extern "C" int hc_batch_pack(const hc_layer_desc* layer, void* packed, hc_stream_t stream) {
+  if (!layer || !packed || !layer->hot || (layer->n_records > 0 && !layer->cold_records) || layer->n_hot < 0 ||
+      (reinterpret_cast<uintptr_t>(packed) & 15) || (reinterpret_cast<uintptr_t>(layer->hot) & 15))
+    return HC_ERR_ARG;
+  k_pack<<<1184, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      layer->hot, layer->n_hot, layer->cold_records, layer->n_records, static_cast<uint8_t*>(packed));
+  return cudaGetLastError() == cudaSuccess ? HC_OK : HC_ERR_CUDA;
 }
 
 extern "C" int hc_union_cold(const uint32_t* masks, int32_t batch, int64_t token_stride, int32_t inter,
                              const uint32_t* fetch_bits, const int32_t* table, int32_t* rec_out, int32_t* count,
                              hc_stream_t stream) {
-  return hc_union_cold_layers(masks, 1, 0, batch, token_stride, inter, fetch_bits, table, rec_out, 0, count, stream);
+  return hc_union_cold_layers(masks, 1, 0, batch, token_stride, inter, fetch_bits, table, rec_out, 0, count, nullptr,
+                              0, stream);
 }
 
 extern "C" int hc_union_cold_layers(const uint32_t* masks, int32_t n_layers, int64_t layer_stride, int32_t batch,
                                     int64_t token_stride, int32_t inter, const uint32_t* fetch_bits,
                                     const int32_t* table, int32_t* rec_out, int64_t rec_stride, int32_t* count,
-                                    hc_stream_t stream) {
+                                    uint8_t* flags_out, int64_t flag_stride, hc_stream_t stream) {
   if (!masks || !fetch_bits || !table || !rec_out || !count || n_layers <= 0 || batch <= 0 || inter <= 0 ||
-      inter > 65536 || (n_layers > 1 && rec_stride <= 0))
+      inter > 65536 || (n_layers > 1 && rec_stride <= 0) || (flags_out && flag_stride <= 0))
     return HC_ERR_ARG;
   k_union<<<n_layers, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      masks, layer_stride, batch, token_stride, (inter + 31) / 32, fetch_bits, table, rec_out, rec_stride, count);
+      masks, layer_stride, batch, token_stride, (inter + 31) / 32, fetch_bits, table, rec_out, rec_stride, count,
+      flags_out, flag_stride);
   return cudaGetLastError() == cudaSuccess ? HC_OK : HC_ERR_CUDA;
 }
 
-extern "C" int hc_ffn_batch_layer(const hc_layer_desc* layer, float* x, int32_t batch, const int32_t* rec,
-                                  const int32_t* count, int32_t max_cold, float eps, int32_t act,
-                                  int32_t act_on_both, void* workspace, int32_t* status, hc_stream_t stream) {
+extern "C" int hc_ffn_batch_layer(const hc_layer_desc* layer, const void* packed, float* x, int32_t batch,
+                                  const int32_t* rec, const int32_t* count, int32_t max_cold,
+                                  const uint8_t* rec_flags, float eps, int32_t act, int32_t act_on_both,
+                                  void* workspace, int32_t* status, hc_stream_t stream) {
   if (!layer || !x || batch <= 0 || !rec || !count || max_cold < 0 || !workspace || !status ||
-      (act != HC_ACT_SILU && act != HC_ACT_RELU))
+      (act != HC_ACT_SILU && act != HC_ACT_RELU) || (rec_flags && !packed) ||
+      (packed && (reinterpret_cast<uintptr_t>(packed) & 15)))
     return HC_ERR_ARG;
+  if (rec_flags) max_cold = layer->n_records;        // packed: every record of the section
   if (!layer->hot || !layer->cold_records || layer->n_hot < 0 || max_cold > layer->n_records)
     return HC_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(workspace) & 15) ||
       (reinterpret_cast<uintptr_t>(layer->hot) & 15) || (reinterpret_cast<uintptr_t>(layer->cold_records) & 15))
     return HC_ERR_ARG;
-  constexpr int GU_RAW = RAW_DEPTH * (GU_PIECES * GU_PSTRIDE + GU_PROD * 4);
+  constexpr int GU_RAW = GU_DEPTH * GU_RAW_SLOT;
   constexpr int GU_SMEM = GU_STAGES * NMAX * KC * 2 + GU_RAW + BAR_BYTES;
-  static_assert(GU_SMEM <= GU_SMEM_FLOOR, "k_gu shared memory");
+  constexpr int GU_SMEM_LAUNCH = GU_SMEM > GU_SMEM_FLOOR ? GU_SMEM : GU_SMEM_FLOOR;
+  static_assert(GU_SMEM_LAUNCH <= 227 * 1024, "k_gu shared memory");
   constexpr int DN_RAW = RAW_DEPTH * DN_PIECES * DN_PSTRIDE + REC_RING * DN_PROD * 4;
-  constexpr int GU_SMEM_MAX = GU_SMEM_FLOOR;
+  constexpr int GU_SMEM_MAX = GU_SMEM_LAUNCH;
+  constexpr int GUP_SMEM_NEED = GUP_GSLOTS * GUP_GROUP * PG_HOT + GUX_STAGES * NMAX * KC * 2 + BAR_BYTES;
+  constexpr int GUP_SMEM = GUP_SMEM_NEED > GU_SMEM_FLOOR ? GUP_SMEM_NEED : GU_SMEM_FLOOR;
+  constexpr int DDP_SMEM =
+      DD_DEPTH * PD_HOT + DD_ACTS * KC * NMAX * 2 + DD_STAGES * (A_TILE_BYTES + KC * NMAX * 2) + BAR_BYTES;
+  static_assert(GUP_SMEM <= 227 * 1024 && DDP_SMEM <= 227 * 1024, "packed kernels' shared memory");
   constexpr int DN_SMEM_MAX = 3 * (A_TILE_BYTES + KC * NMAX * 2) + DN_RAW + BAR_BYTES;
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(k_gu, cudaFuncAttributeMaxDynamicSharedMemorySize, GU_SMEM_MAX) != cudaSuccess ||
-        cudaFuncSetAttribute(k_down, cudaFuncAttributeMaxDynamicSharedMemorySize, DN_SMEM_MAX) != cudaSuccess)
+        cudaFuncSetAttribute(k_down, cudaFuncAttributeMaxDynamicSharedMemorySize, DN_SMEM_MAX) != cudaSuccess ||
+        cudaFuncSetAttribute(k_gu_p, cudaFuncAttributeMaxDynamicSharedMemorySize, GUP_SMEM) != cudaSuccess ||
+        cudaFuncSetAttribute(k_down_p, cudaFuncAttributeMaxDynamicSharedMemorySize, DDP_SMEM) != cudaSuccess)
       return HC_ERR_CUDA;
     attr = true;
   }
@@ -976,7 +1716,7 @@ extern "C" int hc_ffn_batch_layer(const hc_layer_desc* layer, float* x, int32_t 
   const int ctas = sms < MAX_CTAS ? sms : MAX_CTAS;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int max_total = layer->n_hot + max_cold;
-  const WsLayout wl = ws_layout(max_total > 0 ? max_total : 1);
+  const WsLayout wl = ws_layout((int64_t)max_total + 2 * TILE);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
 
   LayerArgs la;
@@ -991,6 +1731,7 @@ extern "C" int hc_ffn_batch_layer(const hc_layer_desc* layer, float* x, int32_t 
   la.relu = act == HC_ACT_RELU;
   la.both = act_on_both != 0;
   la.status = status;
+  la.flags = rec_flags;
 
   const int hot_tiles = (layer->n_hot + TILE - 1) / TILE;
   const int tiles_max = hot_tiles + (max_cold + TILE - 1) / TILE;
@@ -999,16 +1740,41 @@ extern "C" int hc_ffn_batch_layer(const hc_layer_desc* layer, float* x, int32_t 
     const int N = (nb + 15) / 16 * 16;
     float* xb = x + (size_t)b0 * H;
     k_norm<<<N, 256, 0, s>>>(xb, nb, N, layer->norm_w, eps, ws + wl.xs_nat, ws + wl.xs_perm);
-    if (max_total > 0) {
+    if (rec_flags && max_total > 0) {
+      const PackLayout L = pack_layout(layer->n_hot, layer->n_records);
+      PackedParams pp;
+      memset(&pp, 0, sizeof(pp));
+      pp.a = la;
+      pp.packed = static_cast<const uint8_t*>(packed);
+      pp.xs_nat = ws + wl.xs_nat;
+      pp.xs_perm = ws + wl.xs_perm;
+      pp.part = reinterpret_cast<float*>(ws + wl.part);
+      pp.N = N;
+      pp.trace = g_trace_gu;
+      const int gu_units = (L.hot_tiles + L.cold_tiles) * (H / KC);
+      const int gu_grid = gu_units < ctas ? gu_units : ctas;
+      k_gu_p<<<gu_grid, GU_THREADS, GUP_SMEM, s>>>(pp);
+      const int slots = (L.hot_blocks + L.cold_blocks) * KC;
+      __half* actb = reinterpret_cast<__half*>(ws + wl.act);
+      k_act_p<<<(slots * (N / 8) + 255) / 256, 256, 0, s>>>(la, pp.part, gu_grid, N, actb);
+      const int dn_units = (H / TILE) * (L.hot_blocks + L.cold_blocks);
+      const int dn_grid = dn_units < ctas ? dn_units : ctas;
+      k_down_p<<<dn_grid, DN_THREADS, DDP_SMEM, s>>>(pp, actb, reinterpret_cast<float*>(ws + wl.y),
+                                                      tmem_cols_for(2 * N));
+    } else if (max_total > 0) {
       GuParams g;
+      memset(&g, 0, sizeof(g));
       g.a = la;
       g.xs_nat = ws + wl.xs_nat;
       g.xs_perm = ws + wl.xs_perm;
       g.part = reinterpret_cast<float*>(ws + wl.part);
       g.N = N;
       g.hot_tiles = hot_tiles;
+      g.trace = g_trace_gu;
+      if (layer->n_hot > 0 && !encode_rows(&g.tm_hot, layer->hot, HOT_ROW, layer->n_hot, KC, TILE))
+        return HC_ERR_CUDA;
       const int gu_grid = tiles_max * (H / KC) < ctas ? tiles_max * (H / KC) : ctas;
-      k_gu<<<gu_grid, GU_THREADS, GU_SMEM_FLOOR, s>>>(g);
+      k_gu<<<gu_grid, GU_THREADS, GU_SMEM_LAUNCH, s>>>(g);
 
       const int act_threads = max_total * (N / 8);
       k_act<<<(act_threads + 255) / 256, 256, 0, s>>>(la, g.part, hot_tiles, gu_grid, N,
@@ -1021,10 +1787,12 @@ extern "C" int hc_ffn_batch_layer(const hc_layer_desc* layer, float* x, int32_t 
       d.N = N;
       d.stages = 3;
       d.tmem_cols = tmem_cols_for(2 * N);
+      d.trace = g_trace_down;
       const int dn_units = (H / TILE) * ((max_total + KC - 1) / KC);
       const int dn_grid = dn_units < ctas ? dn_units : ctas;
       const int dn_smem = d.stages * (A_TILE_BYTES + KC * N * 2) + DN_RAW + BAR_BYTES;
       k_down<<<dn_grid, DN_THREADS, dn_smem, s>>>(d);
+
     }
     k_resid<<<dim3(H / 256, N / 4), 256, 0, s>>>(xb, nb, N, reinterpret_cast<float*>(ws + wl.y));
   }

@@ -351,7 +351,14 @@ class BatchStack:
     def __init__(self, store: ColdWeightStore, hot: Sequence[HotNeurons], norms: Sequence[Optional[torch.Tensor]],
                  predictors: Optional[Sequence[Optional[NeuronPredictor]]] = None, activation: str = "silu",
                  act_on_both: bool = False, eps: float = 1e-5, threshold: float = 0.5,
-                 layer_ids: Optional[Sequence[int]] = None, inter: Optional[int] = None, max_batch: int = 64):
+                 layer_ids: Optional[Sequence[int]] = None, inter: Optional[int] = None, max_batch: int = 64,
+                 dense_min_batch: int = 8):
+        """Batches of at least ``dense_min_batch`` tokens use the dense mode of
+        hc_ffn_batch_layer: every record streamed, in storage order, from a
+        packed copy of the layer made once here (hc_batch_pack, about the
+        layer's own size again), and masked by the union -- their union covers
+        most of each section, and whole contiguous blocks stream faster than
+        per-record pieces."""
         self.store = store
         self.device = store.device
         self.L = len(hot)
@@ -383,6 +390,18 @@ class BatchStack:
                               device=self.device)
         self.rec = torch.zeros(self.L, max(max(self.max_cold), 1), dtype=torch.int32, device=self.device)
         self.count = torch.zeros(self.L, dtype=torch.int32, device=self.device)
+        self.dense_min_batch = int(dense_min_batch)
+        self.flag_stride = (max(max(self.max_cold), 1) + 15) // 16 * 16
+        self.flags = torch.zeros(self.L, self.flag_stride, dtype=torch.uint8, device=self.device)
+        # dense mode streams a packed copy of each layer (hc_batch_pack), built once here
+        self.packed = [None] * self.L
+        if self.dense_min_batch <= self.max_batch:
+            s = N.stream_handle()
+            for l in range(self.L):
+                nbytes = int(N.lib.hc_batch_pack_bytes(self.hot[l].n, self.max_cold[l]))
+                buf = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+                N.check(N.lib.hc_batch_pack(ctypes.byref(self.descs[l]), N.ptr(buf), s), "hc_batch_pack")
+                self.packed[l] = buf
         self.pred_masks = torch.zeros(self.L, self.max_batch, self.words, dtype=torch.int32, device=self.device)
         self.status = N.new_status(self.device)
         self._all_ones = bits_to_words(torch.ones(self.inter, dtype=torch.bool).numpy(), self.inter).to(self.device)
@@ -413,20 +432,27 @@ class BatchStack:
             if tuple(masks.shape) != (self.L, B, self.words):
                 raise ValueError(f"masks must be [L={self.L}, B={B}, W={self.words}] int32 words")
         s = N.stream_handle()
+        dense = B >= self.dense_min_batch
+        flags = self.flags if dense else None
         if masks is not None and self._tables_contiguous():
             # every layer's fetch set is known up front: one launch for all layers
             t0 = self.store.table[self.layer_ids[0]]
             N.check(N.lib.hc_union_cold_layers(N.ptr(masks), self.L, masks.stride(0), B, masks.stride(1),
                                                self.inter, N.ptr(self.fetch), N.ptr(t0), N.ptr(self.rec),
-                                               self.rec.stride(0), N.ptr(self.count), s), "hc_union_cold_layers")
+                                               self.rec.stride(0), N.ptr(self.count), N.ptr(flags),
+                                               self.flag_stride, s), "hc_union_cold_layers")
         for l in range(self.L):
             if masks is None or not self._tables_contiguous():
                 m = masks[l] if masks is not None else self._layer_masks(l, y)
-                N.check(N.lib.hc_union_cold(N.ptr(m), B, m.stride(0), self.inter, N.ptr(self.fetch[l]),
-                                            N.ptr(self.store.table[self.layer_ids[l]]), N.ptr(self.rec[l]),
-                                            N.ptr(self.count[l:l + 1]), s), "hc_union_cold")
-            N.check(N.lib.hc_ffn_batch_layer(ctypes.byref(self.descs[l]), N.ptr(y), B, N.ptr(self.rec[l]),
-                                             N.ptr(self.count[l:l + 1]), self.max_cold[l], self.eps, self.act,
+                N.check(N.lib.hc_union_cold_layers(N.ptr(m), 1, 0, B, m.stride(0), self.inter, N.ptr(self.fetch[l]),
+                                                   N.ptr(self.store.table[self.layer_ids[l]]), N.ptr(self.rec[l]),
+                                                   0, N.ptr(self.count[l:l + 1]),
+                                                   N.ptr(flags[l]) if dense else None, self.flag_stride, s),
+                        "hc_union_cold_layers")
+            N.check(N.lib.hc_ffn_batch_layer(ctypes.byref(self.descs[l]), N.ptr(self.packed[l]), N.ptr(y), B,
+                                             N.ptr(self.rec[l]),
+                                             N.ptr(self.count[l:l + 1]), self.max_cold[l],
+                                             N.ptr(flags[l]) if dense else None, self.eps, self.act,
                                              1 if self.act_on_both else 0, N.ptr(self.ws), N.ptr(self.status), s),
                     "hc_ffn_batch_layer")
             if x_hist is not None:

@@ -333,12 +333,14 @@ HC_API int hc_union_cold(const uint32_t* masks, int32_t batch, int64_t token_str
  * The same for n_layers layers at once (one CTA per layer), when every
  * layer's masks are known up front: layer l reads masks + l * layer_stride,
  * fetch_bits + l * ceil(inter/32), table + l * 65536 and writes
- * rec_out + l * rec_stride, count[l].
+ * rec_out + l * rec_stride, count[l].  flags_out (optional, [n_layers][flag_stride]
+ * bytes, flag_stride >= every layer's record count) receives 1 for each record
+ * in the union and 0 elsewhere -- the input of the dense cold mode below.
  */
 HC_API int hc_union_cold_layers(const uint32_t* masks, int32_t n_layers, int64_t layer_stride, int32_t batch,
                                 int64_t token_stride, int32_t inter, const uint32_t* fetch_bits,
                                 const int32_t* table, int32_t* rec_out, int64_t rec_stride, int32_t* count,
-                                hc_stream_t stream);
+                                uint8_t* flags_out, int64_t flag_stride, hc_stream_t stream);
 
 /*
  * hc_ffn_batch_layer -- SparseFFNLayer.forward (engine.py:292-312) for a
@@ -349,6 +351,14 @@ HC_API int hc_union_cold_layers(const uint32_t* masks, int32_t n_layers, int64_t
  *   x          [batch][4096] fp32 hidden states, updated in place
  *   rec/count  device cold record list (hc_union_cold), at most max_cold
  *              entries (more sets HC_ERR_RANGE and drops the excess)
+ *   packed     the layer's packed copy (hc_batch_pack) or NULL; required
+ *              when rec_flags is given
+ *   rec_flags  NULL: compute the listed records.  Otherwise dense mode:
+ *              every record of the section is streamed from `packed` (one
+ *              bulk copy per tile step instead of per-record pieces) and
+ *              rec_flags[n_records] (1 = in the fetch set) zeroes the rest --
+ *              the same result, cheaper once the union covers a large part of
+ *              the section; max_cold is then the section's record count
  *   workspace  hc_ffn_batch_workspace_bytes(n_hot + max_cold) bytes, zeroed once;
  *              left zeroed again
  * Tokens are processed 8 at a time; every weight byte is read once per 8.
@@ -356,9 +366,27 @@ HC_API int hc_union_cold_layers(const uint32_t* masks, int32_t n_layers, int64_t
  * float atomics, so its last bits can differ between launches.
  */
 HC_API int64_t hc_ffn_batch_workspace_bytes(int32_t max_neurons);
-HC_API int hc_ffn_batch_layer(const hc_layer_desc* layer, float* x, int32_t batch, const int32_t* rec,
-                              const int32_t* count, int32_t max_cold, float eps, int32_t act,
-                              int32_t act_on_both, void* workspace, int32_t* status, hc_stream_t stream);
+/*
+ * Profiling hook: later hc_ffn_batch_layer launches write %globaltimer
+ * stamps of their gate/up and down kernels into gu / down ([grid][64] uint64,
+ * device; NULL = off).  Not for concurrent use.
+ */
+HC_API int hc_batch_set_trace(uint64_t* gu, uint64_t* down);
+HC_API int hc_ffn_batch_layer(const hc_layer_desc* layer, const void* packed, float* x, int32_t batch,
+                              const int32_t* rec, const int32_t* count, int32_t max_cold,
+                              const uint8_t* rec_flags, float eps, int32_t act, int32_t act_on_both,
+                              void* workspace, int32_t* status, hc_stream_t stream);
+/*
+ * Packed copy of a layer for the dense mode of hc_ffn_batch_layer: the hot
+ * rows and every cold record re-laid out once, unit-major, so that each
+ * 64-wide K step of a 128-row gate/up tile and each 64-neuron step of a
+ * 128-row down tile is one contiguous block (INT4 bytes without the record's
+ * 2-byte offset, fp16 scales beside them).  Values are copied bit for bit.
+ * hc_batch_pack_bytes: size of the copy; hc_batch_pack: fills it (layer is a
+ * host pointer; its hot / cold_records device pointers are read).
+ */
+HC_API int64_t hc_batch_pack_bytes(int32_t n_hot, int32_t n_records);
+HC_API int hc_batch_pack(const hc_layer_desc* layer, void* packed, hc_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -66,6 +66,22 @@ def _union_ids(bst, bits_l, l):
     return np.nonzero(bits_l.any(axis=0) & fetch)[0]
 
 
+def test_union_flags_mark_union_records(M):
+    engine, N, hc_synth = M
+    syn = hc_synth.make_stack(n_layers=2, inter=1024, hot_frac=0.2, rank=64, predictors=False)
+    bst = syn.batch_stack(max_batch=8, dense_min_batch=1)
+    words, bits = _bernoulli_masks(2, 3, syn.inter, 0.2, seed=4)
+    bst.forward(torch.randn(3, 4096, device="cuda"), masks=torch.from_numpy(words))
+    bst.check()
+    for l in range(2):
+        n = int(bst.union_counts()[l])
+        recs = bst.rec[l, :n].cpu().numpy()
+        flags = bst.flags[l].cpu().numpy()
+        expect = np.zeros_like(flags)
+        expect[recs] = 1
+        assert np.array_equal(flags, expect)
+
+
 def test_union_cold_matches_numpy(M):
     engine, N, hc_synth = M
     rng = np.random.default_rng(5)
@@ -94,13 +110,15 @@ def test_union_cold_matches_numpy(M):
         assert np.array_equal(rec[:len(ids)].cpu().numpy(), table[ids])
 
 
+@pytest.mark.parametrize("dense", [False, True])
 @pytest.mark.parametrize("B", [1, 5, 16, 19, 40, 70])
-def test_batch_given_masks(M, B):
-    """Token counts that pad to every MMA width (16..64) and a second pass (70)."""
+def test_batch_given_masks(M, B, dense):
+    """Token counts that pad to every MMA width (16..64) and a second pass (70);
+    the gathered union and the dense cold mode (every record, union-masked)."""
     engine, N, hc_synth = M
     syn = hc_synth.make_stack(n_layers=2, inter=1024, hot_frac=0.2, rank=64, activation="silu",
                               act_on_both=False, seed=21, norm_std=0.1, predictors=False)
-    bst = syn.batch_stack(max_batch=80)
+    bst = syn.batch_stack(max_batch=80, dense_min_batch=1 if dense else 1000)
     words, bits = _bernoulli_masks(2, B, syn.inter, 0.1, seed=B)
     x0 = torch.randn(B, 4096, device="cuda", generator=torch.Generator(device="cuda").manual_seed(B))
     x_hist = torch.empty(2, B, 4096, device="cuda")

@@ -58,8 +58,14 @@ def test_argument_errors_are_reported_without_a_device():
                               None, None) == N.HC_ERR_ARG
     assert N.lib.hc_map_ids(None, -1, None, None, None, None, None) == N.HC_ERR_ARG
     assert N.lib.hc_union_cold(None, 1, 32, 1024, None, None, None, None, None) == N.HC_ERR_ARG
-    assert N.lib.hc_union_cold_layers(None, 2, 0, 1, 32, 1024, None, None, None, 0, None, None) == N.HC_ERR_ARG
-    assert N.lib.hc_ffn_batch_layer(None, None, 4, None, None, 0, 1e-5, 0, 0, None, None, None) == N.HC_ERR_ARG
+    assert N.lib.hc_union_cold_layers(None, 2, 0, 1, 32, 1024, None, None, None, 0, None, None, 0,
+                                      None) == N.HC_ERR_ARG
+    assert N.lib.hc_ffn_batch_layer(None, None, None, 4, None, None, 0, None, 1e-5, 0, 0, None, None,
+                                    None) == N.HC_ERR_ARG
+    assert N.lib.hc_batch_pack(None, None, None) == N.HC_ERR_ARG
+    # packed copy: 16 KB per hot gate/up step, 8.5 KB per cold one, 8 / 4.1 KB per down step
+    assert N.lib.hc_batch_pack_bytes(2867, 11469) >= (23 * 64 * 16384 + 90 * 64 * 8704 + 32 * 46 * 8192
+                                                      + 32 * 180 * 4224)
     assert N.lib.hc_ffn_batch_workspace_bytes(0) == -1
     # workspace grows with the neuron count it must hold (activations, partial sums)
     assert N.lib.hc_ffn_batch_workspace_bytes(14336) > N.lib.hc_ffn_batch_workspace_bytes(1024) > 0
