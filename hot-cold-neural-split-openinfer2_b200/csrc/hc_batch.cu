@@ -11,12 +11,13 @@
 //              decoder (each 8-element run stored as 0,4,1,5,2,6,3,7) for the
 //              cold rows -- a dot product may permute K as long as both
 //              operands do
-//   k_gu       gate and up GEMMs, D[128 neurons][N tokens] per CTA over a
-//              K range: 256 producer threads decode FP8 rows (exact in f16)
-//              or INT4 rows (q * group scale, rounded once to f16) into
-//              K-major shared-memory tiles; one thread issues tcgen05.mma
-//              per 16-K step; 8 warps move the accumulators out of TMEM as
-//              fp32 partial sums (K split over up to 4 CTAs to fill the GPU)
+//   k_gu       gate and up GEMMs, D[128 neurons][N tokens], persistent over
+//              64-wide K steps of every tile: 512 decoder threads turn FP8
+//              rows (exact in f16) or INT4 rows (q * group scale, rounded
+//              once to f16) into the A operand in TMEM (tcgen05.st); one
+//              thread issues tcgen05.mma with A from TMEM and the token tile
+//              from shared memory; 4 warps move finished accumulators out of
+//              TMEM as fp32 partial sums of the CTA's K range
 //   k_act      sum of the K partials, per-neuron FP8 scales, gated
 //              activation -> act [slot][N] f16
 //   k_down     D[128 output rows][N tokens] per CTA over a neuron range:
@@ -24,6 +25,15 @@
 //              B = act (times the INT4 group scale of the CTA's 128 rows);
 //              the tile is added to y [4096][N] with vector float atomics
 //   k_resid    x_b += y[:, b]; y = 0
+//
+// Two ways to reach the cold records:
+//   gathered   (k_gu, k_act, k_down) the union's ascending record list is
+//              walked; each record's fields are fetched where they lie in the
+//              store (cp.async windows around the 2-byte field offset)
+//   packed     (k_gu_p, k_act_p, k_down_p) for large batches, where the union
+//              covers most records: a load-time unit-major copy of the layer
+//              (hc_batch_pack) is streamed whole with one bulk copy per block,
+//              and records outside the union get a zero activation
 //
 // Shared-memory operand layout (SWIZZLE_NONE canonical form): 8x16-byte core
 // matrices; SBO = the byte stride between core matrices along M/N, LBO =
@@ -363,7 +373,6 @@ struct Bars {
   uint64_t* xempty;  // [8] MMA commit -> token-tile warp: tile read
   uint64_t* rawfull;   // [16] copies -> decoders: raw weights landed
   uint64_t* rawempty;  // [16] decoders -> issuer: raw slot read
-  uint64_t* sfree;     // [2] decoders -> loader: scale buffer of a segment read
   uint32_t* tslot;
   volatile int* abort_flag;
 };
@@ -377,10 +386,9 @@ __device__ __forceinline__ Bars carve_bars(uint8_t* p) {
   b.xfull = u + 20;
   b.rawfull = u + 28;
   b.rawempty = u + 44;
-  b.sfree = u + 60;
-  b.xempty = u + 62;
-  b.tslot = reinterpret_cast<uint32_t*>(u + 70);
-  b.abort_flag = reinterpret_cast<volatile int*>(u + 70) + 1;
+  b.xempty = u + 60;
+  b.tslot = reinterpret_cast<uint32_t*>(u + 68);
+  b.abort_flag = reinterpret_cast<volatile int*>(u + 68) + 1;
   return b;
 }
 __device__ __forceinline__ void init_bars(const Bars& b, int stages, int producers, int rawfull_count = -1,
@@ -401,7 +409,6 @@ __device__ __forceinline__ void init_bars(const Bars& b, int stages, int produce
     mbar_init(&b.rawfull[k], rawfull_count < 0 ? producers : rawfull_count);
     mbar_init(&b.rawempty[k], producers);
   }
-  for (int k = 0; k < 2; ++k) mbar_init(&b.sfree[k], producers);
   *b.abort_flag = 0;
   mbar_fence_init();
 }
@@ -421,12 +428,14 @@ __device__ __forceinline__ void stamp(uint64_t* tr, int c, int e) {
 //   ("segments") of one or more tiles; each segment's fp32 partial goes to
 //   block (tile + CTA) of part [blocks][128][2N] (gate N, then up N), unique
 //   because ranges are contiguous.
-// Weights reach shared memory by TMA, GU_DEPTH units ahead: a hot unit is
-//   one 2-D tile per matrix (128 rows x 64 bytes of the packed hot rows); a
-//   cold unit is 32 four-row gathers per matrix of the 48-byte window that
-//   holds the unit's 32 field bytes (the field starts 2 bytes into it) plus
-//   32 gathers of the 16-byte window holding the group's fp16 scale.  Rows
-//   past the tile's end point past the tensor and read as zeros.
+// Weights reach shared memory GU_AHEAD units ahead of their decode, in
+//   GU_DEPTH raw slots: a hot unit is one 2-D tensor copy per matrix (128
+//   rows x 64 bytes of the packed hot rows, issued by thread 0); a cold unit
+//   is copied with cp.async by the decoders themselves, thread t taking piece
+//   t % 4 of row t / 4 of both matrices (three 16-byte pieces of the 48-byte
+//   window holding the unit's 32 field bytes, which start 2 bytes into it,
+//   and the 16-byte window holding the group's fp16 scale).  Rows past the
+//   union's end decode as zeros.
 // TMEM (512 columns): accumulator buffers tb = 0, 1 at columns [2N tb, 2N tb
 //   + 2N) (gate, up); A stages s = 0..3 at [256 + 64 s, +64) (gate 32
 //   columns, up 32 columns; column c of a row holds K elements 2c, 2c + 1).
@@ -435,8 +444,7 @@ __device__ __forceinline__ void stamp(uint64_t* tr, int c, int e) {
 //   pairs and stores them with tcgen05.st; warp 16 issues tcgen05.mma (A from
 //   TMEM, B = the token tile in shared memory, K-major: k-group stride 16 N,
 //   token-group stride 128); warp 17 bulk-copies each unit's token tile;
-//   warp 18 issues the weight copies; warps 19-22 drain finished accumulator
-//   buffers.
+//   warps 18-21 drain finished accumulator buffers.
 // ---------------------------------------------------------------------------
 struct GuParams {
   LayerArgs a;
@@ -468,7 +476,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu(const __grid_constant__ Gu
   const uint32_t xbase = rbase + GU_DEPTH * GU_RAW_SLOT;    // [GU_STAGES][x_bytes] token tiles
   const Bars bar = carve_bars(smem + GU_DEPTH * GU_RAW_SLOT + GU_STAGES * x_bytes);
 
-  if (t == 0) init_bars(bar, GU_STAGES, GU_PROD);
+  if (t == 0) init_bars(bar, GU_STAGES, GU_PROD / 32, GU_PROD);   // decoders signal per warp; copies per thread
   if (warp == 0) tmem_alloc(bar.tslot, 512);
   tc_fence_before();
   __syncthreads();
@@ -477,7 +485,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu(const __grid_constant__ Gu
   if (t == 0) stamp(tr, c, 1);
 
   if (t < GU_PROD) {
-    // ---- decoders, which also issue the weight copies GU_DEPTH - 1 units ahead.
+    // ---- decoders, which also issue the weight copies GU_AHEAD units ahead.
     // Cold unit: thread t copies piece t % 4 of row t / 4 for both matrices --
     // pieces 0-2 the row's 48-byte field window, piece 3 the 16-byte window
     // holding the group's fp16 scale -- so a warp's copy covers 8 whole rows.
@@ -550,17 +558,10 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu(const __grid_constant__ Gu
         dnT = T + 1;
         dnR = rec_of(dnT, r);
       }
-      const int tw = 0;                                   // traced thread
-      if (t == tw && i >= 20 && i < 24) stamp(tr, c, 24 + (i - 20) * 6);
       issue(i + GU_AHEAD);
-      if (t == tw && i >= 20 && i < 24) stamp(tr, c, (i - 20) * 6 + 25);
       const int slot = i % GU_DEPTH, s = i % GU_STAGES, round = i / GU_STAGES;
       bool ok = bwait(&bar.rawfull[slot], (i / GU_DEPTH) & 1);
-      if (t == 0 && i < 12) stamp(tr, c, 3 + i);
-      if (t == tw && i >= 20 && i < 24) stamp(tr, c, (i - 20) * 6 + 26);
       ok = ok && (round == 0 || bwait(&bar.empty[s], (round - 1) & 1));
-      if (t == 0 && i < 12) stamp(tr, c, 15 + i);
-      if (t == tw && i >= 20 && i < 24) stamp(tr, c, (i - 20) * 6 + 27);
       if (!ok) fail(a, bar.abort_flag);
       // tcgen05.st is warp-collective: leave the loop as a whole warp
       if (!__all_sync(0xffffffffu, ok) || __any_sync(0xffffffffu, *bar.abort_flag != 0)) break;
@@ -590,12 +591,12 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu(const __grid_constant__ Gu
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] = 0u;            // past the union's end, or a bad record
       }
-      if (t == tw && i >= 20 && i < 24) stamp(tr, c, (i - 20) * 6 + 28);
-      mbar_arrive(&bar.rawempty[slot]);                     // raw slot read
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar.rawempty[slot]);      // raw slot read by the warp
       tmem_st16(a_lane + 64 * s, v);
       tc_fence_before();
-      mbar_arrive(&bar.full[s]);
-      if (t == tw && i >= 20 && i < 24) stamp(tr, c, (i - 20) * 6 + 29);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar.full[s]);
     }
     cp_wait<0>();
   } else if (t == GU_PROD) {
@@ -634,13 +635,12 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu(const __grid_constant__ Gu
       const int s = i % GU_STAGES, round = i / GU_STAGES;
       if (round > 0 && !bwait(&bar.empty[s], (round - 1) & 1)) fail(a, bar.abort_flag);
       if (*bar.abort_flag) break;
-      if (i == 0) stamp(tr, c, 54);
       mbar_arrive_expect_tx(&bar.xfull[s], x_bytes);
       bulk_copy(xbase + s * x_bytes, (T < p.hot_tiles ? p.xs_nat : p.xs_perm) + (size_t)k * x_bytes, x_bytes,
                 &bar.xfull[s]);
     }
   } else if (t >= GU_PROD + 64) {
-    // ---- epilogue: warp (19..22) & 3 reads TMEM lanes [32 q, 32 q + 32)
+    // ---- epilogue: warp (18..21) & 3 reads TMEM lanes [32 q, 32 q + 32)
     const int q = warp & 3, r = q * 32 + lane;
     int seg = 0;
     for (int x0 = lo; x0 < hi; ++seg) {
@@ -651,7 +651,6 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu(const __grid_constant__ Gu
       if (!done) fail(a, bar.abort_flag);
       const bool go = __all_sync(0xffffffffu, done) && !__any_sync(0xffffffffu, *bar.abort_flag != 0);
       if (!go) break;
-      if (lane == 0 && warp == (GU_PROD + 64) / 32) stamp(tr, c, seg == 0 ? 52 : 53);
       tc_fence_after();
       const bool hotT = T < p.hot_tiles;
       const int row = (hotT ? T : T - p.hot_tiles) * TILE + r;
@@ -759,7 +758,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down(DownParams p) {
   const uint32_t recbase = rbase + RAW_DEPTH * raw_slot;    // [REC_RING][DN_PROD] record indices
   const Bars bar = carve_bars(smem + p.stages * stage_bytes + RAW_DEPTH * raw_slot + REC_RING * DN_PROD * 4);
 
-  if (t == 0) init_bars(bar, p.stages, DN_PROD);
+  if (t == 0) init_bars(bar, p.stages, DN_PROD / 32);
   if (warp == 0) tmem_alloc(bar.tslot, p.tmem_cols);
   tc_fence_before();
   __syncthreads();
@@ -828,7 +827,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down(DownParams p) {
       cp_wait<RAW_DEPTH - 1>();
       const int s = i % p.stages, round = i / p.stages;
       if (round > 0 && !bwait(&bar.empty[s], (round - 1) & 1)) fail(a, bar.abort_flag);
-      if (*bar.abort_flag) break;
+      if (__any_sync(0xffffffffu, *bar.abort_flag != 0)) break;     // warp-uniform: the warp signals as one
       const int rs = i % RAW_DEPTH;
       const uint32_t d = rbase + rs * raw_slot + t * 16;
       const uint32_t md = (meta >> (3 * rs)) & 7u;
@@ -864,7 +863,8 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down(DownParams p) {
         }
       }
       fence_async_smem();
-      mbar_arrive(&bar.full[s]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar.full[s]);
     }
     cp_wait<0>();
   } else if (t == DN_PROD) {
@@ -1079,8 +1079,11 @@ struct PackedParams {
 
 // ---------------------------------------------------------------------------
 // k_gu_p: k_gu over the packed blocks.  Units x = (tile x / 64, K step x % 64)
-// over hot tiles then cold tiles (all records); thread 0 bulk-copies each
-// unit's block GU_AHEAD units ahead; decoders as in k_gu.
+// over hot tiles then cold tiles (every record of the section).  Lane 1 of
+// warp 17 bulk-copies groups of GUP_GROUP units (one copy per run of
+// contiguous blocks, up to 64 KB) into GUP_GSLOTS group slots; lane 0 of warp
+// 17 copies the token tiles into their own GUX_STAGES ring; decoders, MMA
+// thread and epilogue as in k_gu, the decoders reading the swizzled blocks.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(GU_THREADS, 1) k_gu_p(const __grid_constant__ PackedParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -1131,7 +1134,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu_p(const __grid_constant__ 
     }
   };
 
-  if (t == 0) init_bars(bar, GU_STAGES, GU_PROD, 1);
+  if (t == 0) init_bars(bar, GU_STAGES, GU_PROD / 32, 1);    // decoders signal per warp
   if (warp == 0) tmem_alloc(bar.tslot, 512);
   tc_fence_before();
   __syncthreads();
@@ -1143,15 +1146,11 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu_p(const __grid_constant__ 
     const int r = q * 32 + lane;
     const uint32_t a_lane = tmem + ((uint32_t)(q * 32) << 16) + GU_A_COL + 32 * m + 16 * h;
     for (int i = 0; i < nunits; ++i) {
-      const bool tw = t == 0 && i >= 20 && i < 24;
-      if (tw) stamp(tr, c, 24 + (i - 20) * 6);
       const int g = i / GUP_GROUP, jg = i % GUP_GROUP;
       const int x = lo + i, T = x >> 6, kb = x & (H / KC - 1);
       const int slot = g % GUP_GSLOTS, s = i % GU_STAGES, round = i / GU_STAGES;
       bool ok = bwait(&bar.rawfull[slot], (g / GUP_GSLOTS) & 1);
-      if (tw) stamp(tr, c, 24 + (i - 20) * 6 + 1);
       ok = ok && (round == 0 || bwait(&bar.empty[s], (round - 1) & 1));
-      if (tw) stamp(tr, c, 24 + (i - 20) * 6 + 2);
       if (!ok) fail(a, bar.abort_flag);
       if (!__all_sync(0xffffffffu, ok) || __any_sync(0xffffffffu, *bar.abort_flag != 0)) break;
       tc_fence_after();
@@ -1177,12 +1176,12 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu_p(const __grid_constant__ 
         v[8] = p2.x; v[9] = p2.y; v[10] = p2.z; v[11] = p2.w; v[12] = p3.x; v[13] = p3.y; v[14] = p3.z; v[15] = p3.w;
       }
       (void)kb;
-      if (tw) stamp(tr, c, 24 + (i - 20) * 6 + 3);
-      if (jg == GUP_GROUP - 1 || i == nunits - 1) mbar_arrive(&bar.rawempty[slot]);   // group read
+      __syncwarp();
+      if (lane == 0 && (jg == GUP_GROUP - 1 || i == nunits - 1)) mbar_arrive(&bar.rawempty[slot]);   // group read
       tmem_st16(a_lane + 64 * s, v);
       tc_fence_before();
-      mbar_arrive(&bar.full[s]);
-      if (tw) stamp(tr, c, 24 + (i - 20) * 6 + 4);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar.full[s]);
     }
   } else if (t == GU_PROD) {
     const uint32_t idesc = idesc_f16(N, 0, 0);
@@ -1194,12 +1193,8 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu_p(const __grid_constant__ 
       if (first && seg >= 2 && !bwait(&bar.tfree[tb], ((seg >> 1) - 1) & 1)) fail(a, bar.abort_flag);
       const int s = i % GU_STAGES, round = i / GU_STAGES;
       const int xs = i % GUX_STAGES;
-      const bool tw = i >= 20 && i < 24;
-      if (tw) stamp(tr, c, 48 + (i - 20) * 3);
       if (!bwait(&bar.full[s], round & 1)) fail(a, bar.abort_flag);
-      if (tw) stamp(tr, c, 48 + (i - 20) * 3 + 1);
       if (!bwait(&bar.xfull[xs], (i / GUX_STAGES) & 1)) fail(a, bar.abort_flag);
-      if (tw) stamp(tr, c, 48 + (i - 20) * 3 + 2);
       if (*bar.abort_flag) break;
       tc_fence_after();
       const uint32_t X = xbase + xs * x_bytes;
@@ -1314,8 +1309,11 @@ __global__ void __launch_bounds__(256) k_act_p(LayerArgs a, const float* __restr
 
 // ---------------------------------------------------------------------------
 // k_down_p: k_down over the packed blocks.  Unit x = (output tile x / nblk,
-// 64-slot block x % nblk); thread 0 bulk-copies the block's weights and its
-// 64 activation rows DD_AHEAD units ahead.
+// 64-slot block x % nblk).  Lane 1 of the MMA warp bulk-copies each unit's
+// weight block into a DD_DEPTH ring and its 64 activation rows into a DD_ACTS
+// ring, the weights DD_DEPTH - DD_ACTS units further ahead; 256 producers
+// build the f16 A / B stages (DD_STAGES), one thread issues the MMAs, and 4
+// epilogue warps add each finished tile into y with vector reductions.
 // ---------------------------------------------------------------------------
 
 __global__ void __launch_bounds__(DN_THREADS, 1) k_down_p(const __grid_constant__ PackedParams p, const __half* act,
@@ -1339,14 +1337,14 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down_p(const __grid_constant_
   const uint32_t stbase = abase + DD_ACTS * KC * NMAX * 2;  // [DD_STAGES][stage_bytes]
   const Bars bar = carve_bars(smem + DD_DEPTH * PD_HOT + DD_ACTS * KC * NMAX * 2 + DD_STAGES * stage_bytes);
 
-  if (t == 0) init_bars(bar, DD_STAGES, DN_PROD, 1, DN_PROD);
+  if (t == 0) init_bars(bar, DD_STAGES, DN_PROD / 32, 1, DN_PROD / 32);   // producers signal per warp
   if (warp == 0) tmem_alloc(bar.tslot, tmem_cols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *bar.tslot;
 
-  // lane 1 of the MMA warp: weight blocks DD_AHEAD units ahead (DRAM), activation blocks DD_ACT_AHEAD ahead (L2)
+  // lane 1 of the MMA warp: weight blocks (from DRAM) and activation blocks (from L2)
   auto issue_w = [&](int i) {
     if (i >= nunits) return;
     const int x = lo + i, et = x / nblk, nb = x % nblk;
@@ -1376,7 +1374,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down_p(const __grid_constant_
       bool ok = bwait(&bar.rawfull[rs], (i / DD_DEPTH) & 1) && bwait(&bar.xfull[as], (i / DD_ACTS) & 1);
       ok = ok && (round == 0 || bwait(&bar.empty[s], (round - 1) & 1));
       if (!ok) fail(a, bar.abort_flag);
-      if (*bar.abort_flag) break;
+      if (!__all_sync(0xffffffffu, ok) || __any_sync(0xffffffffu, *bar.abort_flag != 0)) break;
       const uint32_t raw = wbase + rs * PD_HOT;
       const uint32_t actb = abase + as * (KC * NMAX * 2);
       const uint32_t A = stbase + s * stage_bytes + (q >> 3) * 2048 + (4 * j) * 128 + (q & 7) * 16;
@@ -1410,10 +1408,13 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down_p(const __grid_constant_
         }
       }
       (void)et;
-      mbar_arrive(&bar.rawempty[rs]);
-      mbar_arrive(&bar.xempty[as]);
       fence_async_smem();
-      mbar_arrive(&bar.full[s]);
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bar.rawempty[rs]);
+        mbar_arrive(&bar.xempty[as]);
+        mbar_arrive(&bar.full[s]);
+      }
     }
   } else if (t == DN_PROD + 1) {
     // weights run DD_DEPTH - DD_ACTS units further ahead than the activation blocks

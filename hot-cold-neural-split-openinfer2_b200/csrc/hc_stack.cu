@@ -10,13 +10,15 @@
 //
 // One persistent cooperative launch, one CTA per SM, one grid barrier per
 // layer.  CTA c owns a contiguous neuron-id range (its predictor logits and
-// the active cold records in it), a static slice of the first quarter of the
-// hot neurons and a slice of the next predictor's W_down rows; the other hot
-// neurons are claimed two at a time from a global counter, so CTAs with few
-// active cold records take more hot work.  Layer l+1's logits are computed at
-// the end of layer l, once a global counter shows every CTA has added its
-// W_down partials, so layer l+1's cold list is built, and its records are
-// streamed in, while the grid waits at the layer boundary.
+// the active cold records in it) and a slice of the next predictor's W_down
+// rows.  Every CTA publishes its ascending list of active cold records into a
+// per-layer global pool; the issuers of all CTAs then take records from that
+// pool, COLD_CLAIM at a time, and afterwards claim hot neurons two at a time
+// from a per-layer counter, so the work of a layer spreads evenly over the
+// SMs whatever the distribution of active ids.  Layer l+1's logits are
+// computed at the end of layer l, once a global counter shows every CTA has
+// added its W_down partials, so layer l+1's cold list is built, and its
+// records are streamed in, while the grid waits at the layer boundary.
 //
 // Roles:
 //  * issuer warp: streams the CTA's groups (cold records, hot neurons)
@@ -34,8 +36,9 @@
 //    (f16 x f16 products, fp32 sums); INT4 rows with RMSNorm(x) as 16-bit
 //    fixed point (two byte digits per element, dp4a, exact integer sums).
 // Layer boundary: the subgroups' partial y are summed in shared memory, added
-// to a per-layer global accumulator with vector atomics, and after the grid
-// barrier every CTA reads x_{l+1} = x_l + y_l.  The float atomics make the
+// to a per-layer global accumulator with one 16 KB bulk reduction
+// (cp.reduce.async.bulk add.f32, performed in L2), and after the grid barrier
+// every CTA reads x_{l+1} = x_l + y_l.  The float reductions make the
 // summation order, and so the last bits, vary between runs.
 // Every wait on another agent (slot, mbarrier, grid barrier) is bounded by a
 // time limit; on expiry the kernel ORs HC_ERR_TIMEOUT into the status word,

@@ -5,6 +5,7 @@ Used as the target of ncu captures (small cases) and launch lists:
     python hc_profile.py --what stack --layers 4 --tokens 3
     python hc_profile.py --what gather --layers 4 --k 4096
     python hc_profile.py --what predictor --tokens 3
+    python hc_profile.py --what batch --layers 2 --batch 64 --tokens 3
 
 Everything runs through the public API; nothing is skipped inside a launch.
 """
@@ -19,12 +20,14 @@ sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--what", choices=["stack", "gather", "predictor"], default="stack")
+    ap.add_argument("--what", choices=["stack", "gather", "predictor", "batch"], default="stack")
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--inter", type=int, default=14336)
     ap.add_argument("--tokens", type=int, default=3)
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--grid", type=int, default=0)
+    ap.add_argument("--batch", type=int, default=64, help="tokens per batched step (--what batch)")
+    ap.add_argument("--dense-min-batch", type=int, default=8, help="smallest batch run in the packed dense mode")
     ap.add_argument("--trace", action="store_true", help="print per-phase durations from the device trace")
     args = ap.parse_args()
 
@@ -42,7 +45,7 @@ def main():
         dist.init_process_group("gloo")
         tp = engine.TPGroup()
     syn = hc_synth.make_stack(n_layers=args.layers, inter=args.inter, activation="relu", act_on_both=True, seed=0,
-                              predictors=args.what != "gather")
+                              predictors=args.what not in ("gather", "batch"))
     if args.what == "stack":
         st = syn.stack(grid=args.grid, tp=tp)
         if tp is not None:
@@ -64,6 +67,15 @@ def main():
             dist.barrier()
             tp.close()
             dist.destroy_process_group()
+    elif args.what == "batch":
+        # per-token Bernoulli(0.1) masks unioned per layer; --tokens batched steps
+        bst = syn.batch_stack(max_batch=max(args.batch, 1), dense_min_batch=args.dense_min_batch)
+        masks = hc_synth.bernoulli_words(args.layers, args.batch, args.inter, 0.1, seed=2)
+        x = torch.randn(args.batch, 4096, generator=torch.Generator().manual_seed(1)).cuda()
+        for _ in range(args.tokens):
+            bst.forward(x, masks=masks)
+        torch.cuda.synchronize()
+        bst.check()
     elif args.what == "gather":
         store = syn.store
         g = torch.Generator(device="cuda").manual_seed(7)
