@@ -298,6 +298,10 @@ constexpr int GU_A_COL = 256;                      // TMEM columns [256, 512): A
 constexpr int GU_SMEM_FLOOR = 120 * 1024;          // at least this much keeps k_gu at one CTA (all 512 TMEM columns) per SM
 constexpr int DN_PROD = 256;                       // k_down producer threads: (neuron, 32-row quarter)
 constexpr int DN_THREADS = DN_PROD + 32 + 128;
+// The packed kernels' weight-copy issuer runs in a warp of its own: two lanes of
+// one warp that block in different mbarrier waits serialise each other.
+constexpr int GUP_THREADS = GU_THREADS + 32;       // k_gu_p: + issuer warp (warp 22)
+constexpr int DNP_THREADS = DN_THREADS + 32;       // k_down_p: + issuer warp (warp 13)
 constexpr int RAW_DEPTH = 4;                       // k_down: units of copies in flight per thread
 constexpr int GU_DEPTH = 8;                        // k_gu: raw weight slots
 constexpr int GU_AHEAD = GU_DEPTH - 2;             // k_gu: copies issued this many units ahead, so a refilled
@@ -766,7 +770,9 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down(DownParams p) {
   const uint32_t tmem = *bar.tslot;
 
   if (t < DN_PROD) {
-    const int q = t >> 2, j = t & 3;
+    // neuron q, output rows [32 j, 32 j + 32): a quarter-warp holds 8 neurons of one j,
+    // so its 16-byte stage stores land on distinct banks
+    const int q = (warp << 3) | (lane & 7), j = lane >> 3;
     const int groups = N / 8;
     uint32_t meta = 0;                        // 3 bits per raw slot: kind (2), scale half (1)
     // record index of the neuron of unit u, copied REC_AHEAD units before the
@@ -945,7 +951,8 @@ constexpr int DD_STAGES = 4;                        // k_down_p: f16 operand sta
 //   gate/up cold  [m 2][row 128][32 B]  INT4 field bytes, chunk c at c ^ ((r >> 2) & 1)
 //                 + [m][row] fp16 group scale                                              8704 B
 //   down hot      [row 64][128 B]       e4m3 of output rows 128 et .., chunk c at c ^ (row & 7)  8192 B
-//   down cold     [row 64][64 B]        INT4 field bytes + [row] fp16 group scale             4224 B
+//   down cold     [row 64][64 B]        INT4 field bytes, chunk c at c ^ ((row >> 1) & 3),
+//                 + [row] fp16 group scale                                                4224 B
 // ===========================================================================
 constexpr int PG_HOT = 16384, PG_COLD = 8704, PD_HOT = 8192, PD_COLD = 4224;
 
@@ -1042,7 +1049,7 @@ __global__ void k_pack(const uint8_t* __restrict__ hot, int n_hot, const uint8_t
       const int R = nb * KC + q;
       uint4 v = make_uint4(0, 0, 0, 0);
       if (R < n_records) v = field16(cold + (size_t)R * REC_BYTES + 2 + 2 * VEC_BYTES + et * (TILE / 2) + 16 * c);
-      *reinterpret_cast<uint4*>(out + L.dn_cold + ub * PD_COLD + q * 64 + 16 * c) = v;
+      *reinterpret_cast<uint4*>(out + L.dn_cold + ub * PD_COLD + q * 64 + 16 * (c ^ ((q >> 1) & 3))) = v;
       continue;
     }
     k -= n_dn_cold;
@@ -1079,13 +1086,13 @@ struct PackedParams {
 
 // ---------------------------------------------------------------------------
 // k_gu_p: k_gu over the packed blocks.  Units x = (tile x / 64, K step x % 64)
-// over hot tiles then cold tiles (every record of the section).  Lane 1 of
-// warp 17 bulk-copies groups of GUP_GROUP units (one copy per run of
+// over hot tiles then cold tiles (every record of the section).  Lane 0 of
+// warp 22 bulk-copies groups of GUP_GROUP units (one copy per run of
 // contiguous blocks, up to 64 KB) into GUP_GSLOTS group slots; lane 0 of warp
 // 17 copies the token tiles into their own GUX_STAGES ring; decoders, MMA
 // thread and epilogue as in k_gu, the decoders reading the swizzled blocks.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(GU_THREADS, 1) k_gu_p(const __grid_constant__ PackedParams p) {
+__global__ void __launch_bounds__(GUP_THREADS, 1) k_gu_p(const __grid_constant__ PackedParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const LayerArgs& a = p.a;
@@ -1113,7 +1120,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu_p(const __grid_constant__ 
   auto usize = [&](int i) -> uint32_t { return lo + i < L.hot_tiles * (H / KC) ? PG_HOT : PG_COLD; };
 
   // group g = local units [4 g, 4 g + 4): one bulk copy per run of contiguous blocks (the hot
-  // blocks, then the cold ones), issued by lane 1 of the token-tile warp two groups ahead
+  // blocks, then the cold ones), issued by the issuer warp two groups ahead
   const int ngroups = (nunits + GUP_GROUP - 1) / GUP_GROUP;
   auto issue = [&](int g) {
     if (g >= ngroups) return;
@@ -1214,7 +1221,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu_p(const __grid_constant__ 
         ++seg;
       }
     }
-  } else if (t == GU_PROD + 33) {
+  } else if (t == GU_PROD + 192) {
     for (int g = 0; g < ngroups && !*bar.abort_flag; ++g) issue(g);
   } else if (t == GU_PROD + 32) {
     // token tiles, up to GUX_STAGES units ahead of the MMAs
@@ -1227,7 +1234,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu_p(const __grid_constant__ 
       bulk_copy(xbase + xs * x_bytes, (T < L.hot_tiles ? p.xs_nat : p.xs_perm) + (size_t)kb * x_bytes, x_bytes,
                 &bar.xfull[xs]);
     }
-  } else if (t >= GU_PROD + 64) {
+  } else if (t >= GU_PROD + 64 && t < GU_PROD + 192) {
     const int q = warp & 3, r = q * 32 + lane;
     int seg = 0;
     for (int x0 = lo; x0 < hi; ++seg) {
@@ -1309,14 +1316,14 @@ __global__ void __launch_bounds__(256) k_act_p(LayerArgs a, const float* __restr
 
 // ---------------------------------------------------------------------------
 // k_down_p: k_down over the packed blocks.  Unit x = (output tile x / nblk,
-// 64-slot block x % nblk).  Lane 1 of the MMA warp bulk-copies each unit's
+// 64-slot block x % nblk).  Lane 0 of warp 13 bulk-copies each unit's
 // weight block into a DD_DEPTH ring and its 64 activation rows into a DD_ACTS
 // ring, the weights DD_DEPTH - DD_ACTS units further ahead; 256 producers
 // build the f16 A / B stages (DD_STAGES), one thread issues the MMAs, and 4
 // epilogue warps add each finished tile into y with vector reductions.
 // ---------------------------------------------------------------------------
 
-__global__ void __launch_bounds__(DN_THREADS, 1) k_down_p(const __grid_constant__ PackedParams p, const __half* act,
+__global__ void __launch_bounds__(DNP_THREADS, 1) k_down_p(const __grid_constant__ PackedParams p, const __half* act,
                                                           float* y, uint32_t tmem_cols) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
@@ -1344,7 +1351,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down_p(const __grid_constant_
   tc_fence_after();
   const uint32_t tmem = *bar.tslot;
 
-  // lane 1 of the MMA warp: weight blocks (from DRAM) and activation blocks (from L2)
+  // issuer (warp 13): weight blocks (from DRAM) and activation blocks (from L2)
   auto issue_w = [&](int i) {
     if (i >= nunits) return;
     const int x = lo + i, et = x / nblk, nb = x % nblk;
@@ -1366,7 +1373,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down_p(const __grid_constant_
     bulk_copy(abase + slot * (KC * NMAX * 2), act + (size_t)nb * KC * N, b_bytes, &bar.xfull[slot]);
   };
   if (t < DN_PROD) {
-    const int q = t >> 2, j = t & 3;
+    const int q = (warp << 3) | (lane & 7), j = lane >> 3;   // as in k_down: conflict-free stage stores
     const int groups = N / 8;
     for (int i = 0; i < nunits; ++i) {
       const int x = lo + i, et = x / nblk, nb = x % nblk;
@@ -1395,7 +1402,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down_p(const __grid_constant_
           if (g < groups) sts128(B + g * 128, lds128(actb + q * N * 2 + ((g ^ asw) << 4)));
         }
       } else {
-        const uint4 w = lds128(raw + q * 64 + 16 * j);
+        const uint4 w = lds128(raw + q * 64 + 16 * (j ^ ((q >> 1) & 3)));
         const __half ds = half_of(lds32(raw + KC * 64 + ((q * 2) & ~3)), q & 1);
         sts128(A + 0 * 128, int4_piece_perm(w.x));
         sts128(A + 1 * 128, int4_piece_perm(w.y));
@@ -1416,7 +1423,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down_p(const __grid_constant_
         mbar_arrive(&bar.full[s]);
       }
     }
-  } else if (t == DN_PROD + 1) {
+  } else if (t == DN_PROD + 160) {
     // weights run DD_DEPTH - DD_ACTS units further ahead than the activation blocks
     for (int i = 0; i < nunits && !*bar.abort_flag; ++i) {
       issue_w(i);
@@ -1447,7 +1454,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down_p(const __grid_constant_
         ++seg;
       }
     }
-  } else if (t >= DN_PROD + 32) {
+  } else if (t >= DN_PROD + 32 && t < DN_PROD + 160) {
     const int qd = warp & 3, m = qd * 32 + lane;
     int seg = 0;
     for (int x0 = lo; x0 < hi; ++seg) {
@@ -1754,13 +1761,13 @@ extern "C" int hc_ffn_batch_layer(const hc_layer_desc* layer, const void* packed
       pp.trace = g_trace_gu;
       const int gu_units = (L.hot_tiles + L.cold_tiles) * (H / KC);
       const int gu_grid = gu_units < ctas ? gu_units : ctas;
-      k_gu_p<<<gu_grid, GU_THREADS, GUP_SMEM, s>>>(pp);
+      k_gu_p<<<gu_grid, GUP_THREADS, GUP_SMEM, s>>>(pp);
       const int slots = (L.hot_blocks + L.cold_blocks) * KC;
       __half* actb = reinterpret_cast<__half*>(ws + wl.act);
       k_act_p<<<(slots * (N / 8) + 255) / 256, 256, 0, s>>>(la, pp.part, gu_grid, N, actb);
       const int dn_units = (H / TILE) * (L.hot_blocks + L.cold_blocks);
       const int dn_grid = dn_units < ctas ? dn_units : ctas;
-      k_down_p<<<dn_grid, DN_THREADS, DDP_SMEM, s>>>(pp, actb, reinterpret_cast<float*>(ws + wl.y),
+      k_down_p<<<dn_grid, DNP_THREADS, DDP_SMEM, s>>>(pp, actb, reinterpret_cast<float*>(ws + wl.y),
                                                       tmem_cols_for(2 * N));
     } else if (max_total > 0) {
       GuParams g;
