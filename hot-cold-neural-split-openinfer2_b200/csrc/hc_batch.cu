@@ -71,8 +71,8 @@ __host__ __device__ constexpr uint32_t idesc_f16(int n, int a_mn, int b_mn) {
 __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-      ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -96,8 +96,8 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
                                             uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-      ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
 // 16 consecutive 32-bit columns of this thread's TMEM lane, then wait for the store
@@ -110,6 +110,16 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16
       "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
       : "memory");
 }
+// the same store without the wait (several stores, then one tmem_wait_st)
+__device__ __forceinline__ void tmem_st16_nowait(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // global -> shared bulk copy (16-byte aligned, size % 16 == 0) completing on `bar`
 __device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
@@ -291,7 +301,6 @@ constexpr int GU_RAW_SLOT = 2 * GU_REGION;
 constexpr int GU_COLD_WIN = 48;
 constexpr int GU_SCALE_OFF = TILE * GU_COLD_WIN;
 constexpr int GU_STAGES = 4;                       // k_gu: TMEM A stages = token-tile stages
-constexpr int GUX_STAGES = 4;                      // k_gu_p: token-tile stages (own ring)
 constexpr int GUP_GROUP = 4;                       // k_gu_p: units per bulk-copied group (up to 64 KB)
 constexpr int GUP_GSLOTS = 3;                      // k_gu_p: group slots (two groups in flight)
 constexpr int GU_A_COL = 256;                      // TMEM columns [256, 512): A stages of 64 columns
@@ -300,8 +309,10 @@ constexpr int DN_PROD = 256;                       // k_down producer threads: (
 constexpr int DN_THREADS = DN_PROD + 32 + 128;
 // The packed kernels' weight-copy issuer runs in a warp of its own: two lanes of
 // one warp that block in different mbarrier waits serialise each other.
-constexpr int GUP_THREADS = GU_THREADS + 32;       // k_gu_p: + issuer warp (warp 22)
-constexpr int DNP_THREADS = DN_THREADS + 32;       // k_down_p: + issuer warp (warp 13)
+constexpr int GUP_THREADS = GU_THREADS + 64;       // k_gu_p: + issuer warp (warp 22) + up-MMA warp (warp 23)
+constexpr int DNP_PROD = 2 * DN_PROD;              // k_down_p: two producer groups of 8 warps
+constexpr int DNP_THREADS = DNP_PROD + 64 + 128 + 32;   // + 2 MMA warps + 4 epilogue warps + issuer warp (warp 22)
+constexpr int GUP_DEC_WARPS = GU_PROD / 64;        // k_gu_p: warps of one decoder group (two groups)
 constexpr int RAW_DEPTH = 4;                       // k_down: units of copies in flight per thread
 constexpr int GU_DEPTH = 8;                        // k_gu: raw weight slots
 constexpr int GU_AHEAD = GU_DEPTH - 2;             // k_gu: copies issued this many units ahead, so a refilled
@@ -396,13 +407,13 @@ __device__ __forceinline__ Bars carve_bars(uint8_t* p) {
   return b;
 }
 __device__ __forceinline__ void init_bars(const Bars& b, int stages, int producers, int rawfull_count = -1,
-                                          int xempty_count = 1) {
+                                          int xempty_count = 1, int rawempty_count = -1, int mma_issuers = 1) {
   for (int s = 0; s < stages; ++s) {
     mbar_init(&b.full[s], producers);
-    mbar_init(&b.empty[s], 1);
+    mbar_init(&b.empty[s], mma_issuers);
   }
   for (int k = 0; k < 2; ++k) {
-    mbar_init(&b.accf[k], 1);
+    mbar_init(&b.accf[k], mma_issuers);
     mbar_init(&b.tfree[k], 128);
   }
   for (int k = 0; k < 8; ++k) {
@@ -411,7 +422,7 @@ __device__ __forceinline__ void init_bars(const Bars& b, int stages, int produce
   }
   for (int k = 0; k < 16; ++k) {
     mbar_init(&b.rawfull[k], rawfull_count < 0 ? producers : rawfull_count);
-    mbar_init(&b.rawempty[k], producers);
+    mbar_init(&b.rawempty[k], rawempty_count < 0 ? producers : rawempty_count);
   }
   *b.abort_flag = 0;
   mbar_fence_init();
@@ -1089,8 +1100,9 @@ struct PackedParams {
 // over hot tiles then cold tiles (every record of the section).  Lane 0 of
 // warp 22 bulk-copies groups of GUP_GROUP units (one copy per run of
 // contiguous blocks, up to 64 KB) into GUP_GSLOTS group slots; lane 0 of warp
-// 17 copies the token tiles into their own GUX_STAGES ring; decoders, MMA
-// thread and epilogue as in k_gu, the decoders reading the swizzled blocks.
+// 17 copies the token tiles (one per A stage, freed with it); two decoder
+// groups of 8 warps take alternate units (each warp a whole K step of its
+// rows); warps 16 and 23 issue the gate and the up MMAs; epilogue as in k_gu.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(GUP_THREADS, 1) k_gu_p(const __grid_constant__ PackedParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -1109,8 +1121,8 @@ __global__ void __launch_bounds__(GUP_THREADS, 1) k_gu_p(const __grid_constant__
   const int x_bytes = N * KC * 2;
   const uint32_t sbase = smem_u32(smem);
   const uint32_t rbase = sbase;                             // [GUP_GSLOTS][GUP_GROUP * PG_HOT] raw unit groups
-  const uint32_t xbase = rbase + GUP_GSLOTS * GUP_GROUP * PG_HOT;   // [GUX_STAGES][x_bytes] token tiles
-  const Bars bar = carve_bars(smem + GUP_GSLOTS * GUP_GROUP * PG_HOT + GUX_STAGES * x_bytes);
+  const uint32_t xbase = rbase + GUP_GSLOTS * GUP_GROUP * PG_HOT;   // [GU_STAGES][x_bytes] token tiles
+  const Bars bar = carve_bars(smem + GUP_GSLOTS * GUP_GROUP * PG_HOT + GU_STAGES * x_bytes);
   // packed source and size of local unit i; a group's units sit back to back in its slot
   auto usrc = [&](int i) -> const uint8_t* {
     const int x = lo + i;
@@ -1141,7 +1153,9 @@ __global__ void __launch_bounds__(GUP_THREADS, 1) k_gu_p(const __grid_constant__
     }
   };
 
-  if (t == 0) init_bars(bar, GU_STAGES, GU_PROD / 32, 1);    // decoders signal per warp
+  // full: the 8 warps of the unit's decoder group; rawempty: those 8 warps for each of a group's units
+  // empty / accf: one commit from each of the two MMA issuers (a tcgen05.commit costs about as much as an MMA)
+  if (t == 0) init_bars(bar, GU_STAGES, GUP_DEC_WARPS, 1, 1, GUP_DEC_WARPS * GUP_GROUP, 2);
   if (warp == 0) tmem_alloc(bar.tslot, 512);
   tc_fence_before();
   __syncthreads();
@@ -1149,12 +1163,16 @@ __global__ void __launch_bounds__(GUP_THREADS, 1) k_gu_p(const __grid_constant__
   const uint32_t tmem = *bar.tslot;
 
   if (t < GU_PROD) {
-    const int q = warp & 3, m = (warp >> 2) & 1, h = warp >> 3;
+    // Two decoder groups of 8 warps take alternate units, so that one unit's
+    // latency chain (waits, shared loads, decode, TMEM store, signal) overlaps
+    // the other's.  Warp (q, m) of a group decodes rows 32 q .. 32 q + 31 (its
+    // TMEM lane quarter) of matrix m over the unit's whole 64-wide K step.
+    const int q = warp & 3, m = (warp >> 2) & 1, gd = warp >> 3;
     const int r = q * 32 + lane;
-    const uint32_t a_lane = tmem + ((uint32_t)(q * 32) << 16) + GU_A_COL + 32 * m + 16 * h;
-    for (int i = 0; i < nunits; ++i) {
-      const int g = i / GUP_GROUP, jg = i % GUP_GROUP;
-      const int x = lo + i, T = x >> 6, kb = x & (H / KC - 1);
+    const uint32_t a_lane = tmem + ((uint32_t)(q * 32) << 16) + GU_A_COL + 32 * m;
+    for (int i = gd; i < nunits; i += 2) {
+      const int g = i / GUP_GROUP;
+      const int x = lo + i, T = x >> 6;
       const int slot = g % GUP_GSLOTS, s = i % GU_STAGES, round = i / GU_STAGES;
       bool ok = bwait(&bar.rawfull[slot], (g / GUP_GSLOTS) & 1);
       ok = ok && (round == 0 || bwait(&bar.empty[s], (round - 1) & 1));
@@ -1164,33 +1182,48 @@ __global__ void __launch_bounds__(GUP_THREADS, 1) k_gu_p(const __grid_constant__
       uint32_t uoff = 0;
       for (int i2 = g * GUP_GROUP; i2 < i; ++i2) uoff += usize(i2);
       const uint32_t blk = rbase + slot * (GUP_GROUP * PG_HOT) + uoff;
-      uint32_t v[16];
+      uint32_t v0[16], v1[16];
       if (T < L.hot_tiles) {
         const uint32_t row = blk + m * (TILE * KC) + r * KC;
         const int sw = (r >> 1) & 3;
-        const uint4 w0 = lds128(row + (((2 * h) ^ sw) << 4)), w1 = lds128(row + (((2 * h + 1) ^ sw) << 4));
+        const uint4 w0 = lds128(row + ((0 ^ sw) << 4)), w1 = lds128(row + ((1 ^ sw) << 4));
+        const uint4 w2 = lds128(row + ((2 ^ sw) << 4)), w3 = lds128(row + ((3 ^ sw) << 4));
         const uint4 p0 = fp8_piece_nat(w0.x, w0.y), p1 = fp8_piece_nat(w0.z, w0.w);
         const uint4 p2 = fp8_piece_nat(w1.x, w1.y), p3 = fp8_piece_nat(w1.z, w1.w);
-        v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w; v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
-        v[8] = p2.x; v[9] = p2.y; v[10] = p2.z; v[11] = p2.w; v[12] = p3.x; v[13] = p3.y; v[14] = p3.z; v[15] = p3.w;
+        v0[0] = p0.x; v0[1] = p0.y; v0[2] = p0.z; v0[3] = p0.w; v0[4] = p1.x; v0[5] = p1.y; v0[6] = p1.z; v0[7] = p1.w;
+        v0[8] = p2.x; v0[9] = p2.y; v0[10] = p2.z; v0[11] = p2.w; v0[12] = p3.x; v0[13] = p3.y; v0[14] = p3.z; v0[15] = p3.w;
+        const uint4 p4 = fp8_piece_nat(w2.x, w2.y), p5 = fp8_piece_nat(w2.z, w2.w);
+        const uint4 p6 = fp8_piece_nat(w3.x, w3.y), p7 = fp8_piece_nat(w3.z, w3.w);
+        v1[0] = p4.x; v1[1] = p4.y; v1[2] = p4.z; v1[3] = p4.w; v1[4] = p5.x; v1[5] = p5.y; v1[6] = p5.z; v1[7] = p5.w;
+        v1[8] = p6.x; v1[9] = p6.y; v1[10] = p6.z; v1[11] = p6.w; v1[12] = p7.x; v1[13] = p7.y; v1[14] = p7.z; v1[15] = p7.w;
       } else {
-        const uint4 w = lds128(blk + m * (TILE * 32) + r * 32 + ((h ^ ((r >> 2) & 1)) << 4));
-        const uint32_t sw = lds32(blk + 2 * TILE * 32 + ((m * TILE + r) * 2 & ~3));
-        const __half sc = half_of(sw, r & 1);
-        const uint4 p0 = scale_piece(int4_piece_perm(w.x), sc), p1 = scale_piece(int4_piece_perm(w.y), sc);
-        const uint4 p2 = scale_piece(int4_piece_perm(w.z), sc), p3 = scale_piece(int4_piece_perm(w.w), sc);
-        v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w; v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
-        v[8] = p2.x; v[9] = p2.y; v[10] = p2.z; v[11] = p2.w; v[12] = p3.x; v[13] = p3.y; v[14] = p3.z; v[15] = p3.w;
+        const uint32_t rowc = blk + m * (TILE * 32) + r * 32;
+        const int sw = (r >> 2) & 1;
+        const uint4 w0 = lds128(rowc + ((0 ^ sw) << 4)), w1 = lds128(rowc + ((1 ^ sw) << 4));
+        const uint32_t scw = lds32(blk + 2 * TILE * 32 + ((m * TILE + r) * 2 & ~3));
+        const __half sc = half_of(scw, r & 1);
+        const uint4 p0 = scale_piece(int4_piece_perm(w0.x), sc), p1 = scale_piece(int4_piece_perm(w0.y), sc);
+        const uint4 p2 = scale_piece(int4_piece_perm(w0.z), sc), p3 = scale_piece(int4_piece_perm(w0.w), sc);
+        v0[0] = p0.x; v0[1] = p0.y; v0[2] = p0.z; v0[3] = p0.w; v0[4] = p1.x; v0[5] = p1.y; v0[6] = p1.z; v0[7] = p1.w;
+        v0[8] = p2.x; v0[9] = p2.y; v0[10] = p2.z; v0[11] = p2.w; v0[12] = p3.x; v0[13] = p3.y; v0[14] = p3.z; v0[15] = p3.w;
+        const uint4 p4 = scale_piece(int4_piece_perm(w1.x), sc), p5 = scale_piece(int4_piece_perm(w1.y), sc);
+        const uint4 p6 = scale_piece(int4_piece_perm(w1.z), sc), p7 = scale_piece(int4_piece_perm(w1.w), sc);
+        v1[0] = p4.x; v1[1] = p4.y; v1[2] = p4.z; v1[3] = p4.w; v1[4] = p5.x; v1[5] = p5.y; v1[6] = p5.z; v1[7] = p5.w;
+        v1[8] = p6.x; v1[9] = p6.y; v1[10] = p6.z; v1[11] = p6.w; v1[12] = p7.x; v1[13] = p7.y; v1[14] = p7.z; v1[15] = p7.w;
       }
-      (void)kb;
       __syncwarp();
-      if (lane == 0 && (jg == GUP_GROUP - 1 || i == nunits - 1)) mbar_arrive(&bar.rawempty[slot]);   // group read
-      tmem_st16(a_lane + 64 * s, v);
+      if (lane == 0) mbar_arrive(&bar.rawempty[slot]);      // this warp's reads of the unit are done
+      tmem_st16_nowait(a_lane + 64 * s, v0);                 // K [0, 32) of the step
+      tmem_st16_nowait(a_lane + 64 * s + 16, v1);            // K [32, 64)
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar.full[s]);
     }
-  } else if (t == GU_PROD) {
+  } else if (t == GU_PROD || t == GU_PROD + 224) {
+    // MMA issuers: warp 16 the gate accumulator, warp 23 the up accumulator (one
+    // tcgen05.mma takes ~135 cycles to issue, so two threads double the rate)
+    const int mu = t == GU_PROD ? 0 : 1;
     const uint32_t idesc = idesc_f16(N, 0, 0);
     int seg = 0;
     for (int i = 0; i < nunits; ++i) {
@@ -1199,23 +1232,17 @@ __global__ void __launch_bounds__(GUP_THREADS, 1) k_gu_p(const __grid_constant__
       const int tb = seg & 1;
       if (first && seg >= 2 && !bwait(&bar.tfree[tb], ((seg >> 1) - 1) & 1)) fail(a, bar.abort_flag);
       const int s = i % GU_STAGES, round = i / GU_STAGES;
-      const int xs = i % GUX_STAGES;
       if (!bwait(&bar.full[s], round & 1)) fail(a, bar.abort_flag);
-      if (!bwait(&bar.xfull[xs], (i / GUX_STAGES) & 1)) fail(a, bar.abort_flag);
+      if (!bwait(&bar.xfull[s], round & 1)) fail(a, bar.abort_flag);
       if (*bar.abort_flag) break;
       tc_fence_after();
-      const uint32_t X = xbase + xs * x_bytes;
-      const uint32_t dt = tmem + tb * 2 * N;
-      const uint32_t at = tmem + GU_A_COL + 64 * s;
+      const uint32_t X = xbase + s * x_bytes;
+      const uint32_t dt = tmem + tb * 2 * N + mu * N;
+      const uint32_t at = tmem + GU_A_COL + 64 * s + 32 * mu;
 #pragma unroll
-      for (int j = 0; j < KC / 16; ++j) {
-        const uint64_t bd = sdesc(X + j * 2 * 16 * N, 16 * N, 128);
-        const uint32_t acc = !(first && j == 0);
-        umma_f16_ts(dt, at + 8 * j, bd, idesc, acc);
-        umma_f16_ts(dt + N, at + 32 + 8 * j, bd, idesc, acc);
-      }
-      umma_commit(&bar.empty[s]);
-      umma_commit(&bar.xempty[xs]);
+      for (int j = 0; j < KC / 16; ++j)
+        umma_f16_ts(dt, at + 8 * j, sdesc(X + j * 2 * 16 * N, 16 * N, 128), idesc, !(first && j == 0));
+      umma_commit(&bar.empty[s]);                          // frees A stage s and token tile s
       if (last) {
         umma_commit(&bar.accf[tb]);
         ++seg;
@@ -1224,17 +1251,17 @@ __global__ void __launch_bounds__(GUP_THREADS, 1) k_gu_p(const __grid_constant__
   } else if (t == GU_PROD + 192) {
     for (int g = 0; g < ngroups && !*bar.abort_flag; ++g) issue(g);
   } else if (t == GU_PROD + 32) {
-    // token tiles, up to GUX_STAGES units ahead of the MMAs
+    // token tiles: tile s belongs to A stage s and is freed by the same commits
     for (int i = 0; i < nunits; ++i) {
       const int x = lo + i, T = x >> 6, kb = x & (H / KC - 1);
-      const int xs = i % GUX_STAGES, round = i / GUX_STAGES;
-      if (round > 0 && !bwait(&bar.xempty[xs], (round - 1) & 1)) fail(a, bar.abort_flag);
+      const int s = i % GU_STAGES, round = i / GU_STAGES;
+      if (round > 0 && !bwait(&bar.empty[s], (round - 1) & 1)) fail(a, bar.abort_flag);
       if (*bar.abort_flag) break;
-      mbar_arrive_expect_tx(&bar.xfull[xs], x_bytes);
-      bulk_copy(xbase + xs * x_bytes, (T < L.hot_tiles ? p.xs_nat : p.xs_perm) + (size_t)kb * x_bytes, x_bytes,
-                &bar.xfull[xs]);
+      mbar_arrive_expect_tx(&bar.xfull[s], x_bytes);
+      bulk_copy(xbase + s * x_bytes, (T < L.hot_tiles ? p.xs_nat : p.xs_perm) + (size_t)kb * x_bytes, x_bytes,
+                &bar.xfull[s]);
     }
-  } else if (t >= GU_PROD + 64 && t < GU_PROD + 192) {
+  } else if (t >= GU_PROD + 64 && t < GU_PROD + 192) {                 // epilogue warps 18-21
     const int q = warp & 3, r = q * 32 + lane;
     int seg = 0;
     for (int x0 = lo; x0 < hi; ++seg) {
@@ -1316,11 +1343,13 @@ __global__ void __launch_bounds__(256) k_act_p(LayerArgs a, const float* __restr
 
 // ---------------------------------------------------------------------------
 // k_down_p: k_down over the packed blocks.  Unit x = (output tile x / nblk,
-// 64-slot block x % nblk).  Lane 0 of warp 13 bulk-copies each unit's
+// 64-slot block x % nblk).  Lane 0 of warp 22 bulk-copies each unit's
 // weight block into a DD_DEPTH ring and its 64 activation rows into a DD_ACTS
-// ring, the weights DD_DEPTH - DD_ACTS units further ahead; 256 producers
-// build the f16 A / B stages (DD_STAGES), one thread issues the MMAs, and 4
-// epilogue warps add each finished tile into y with vector reductions.
+// ring, the weights DD_DEPTH - DD_ACTS units further ahead; two producer
+// groups of 8 warps build the f16 A / B stages (DD_STAGES) of alternate units;
+// two threads issue the MMAs (even / odd 16-neuron steps into two accumulator
+// chains), and 4 epilogue warps add each finished tile into y with vector
+// reductions.
 // ---------------------------------------------------------------------------
 
 __global__ void __launch_bounds__(DNP_THREADS, 1) k_down_p(const __grid_constant__ PackedParams p, const __half* act,
@@ -1344,14 +1373,15 @@ __global__ void __launch_bounds__(DNP_THREADS, 1) k_down_p(const __grid_constant
   const uint32_t stbase = abase + DD_ACTS * KC * NMAX * 2;  // [DD_STAGES][stage_bytes]
   const Bars bar = carve_bars(smem + DD_DEPTH * PD_HOT + DD_ACTS * KC * NMAX * 2 + DD_STAGES * stage_bytes);
 
-  if (t == 0) init_bars(bar, DD_STAGES, DN_PROD / 32, 1, DN_PROD / 32);   // producers signal per warp
+  // full / rawempty / xempty: the 8 warps of the unit's producer group; empty / accf: both MMA issuers
+  if (t == 0) init_bars(bar, DD_STAGES, DN_PROD / 32, 1, DN_PROD / 32, DN_PROD / 32, 2);
   if (warp == 0) tmem_alloc(bar.tslot, tmem_cols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *bar.tslot;
 
-  // issuer (warp 13): weight blocks (from DRAM) and activation blocks (from L2)
+  // issuer (warp 22): weight blocks (from DRAM) and activation blocks (from L2)
   auto issue_w = [&](int i) {
     if (i >= nunits) return;
     const int x = lo + i, et = x / nblk, nb = x % nblk;
@@ -1372,10 +1402,14 @@ __global__ void __launch_bounds__(DNP_THREADS, 1) k_down_p(const __grid_constant
     mbar_arrive_expect_tx(&bar.xfull[slot], b_bytes);
     bulk_copy(abase + slot * (KC * NMAX * 2), act + (size_t)nb * KC * N, b_bytes, &bar.xfull[slot]);
   };
-  if (t < DN_PROD) {
-    const int q = (warp << 3) | (lane & 7), j = lane >> 3;   // as in k_down: conflict-free stage stores
+  if (t < DNP_PROD) {
+    // two producer groups of 8 warps take alternate units; in a group, thread
+    // (q, j) builds neuron q, output rows [32 j, 32 j + 32) (a quarter-warp
+    // holds 8 neurons of one j: conflict-free stage stores)
+    const int gd = warp >> 3;
+    const int q = ((warp & 7) << 3) | (lane & 7), j = lane >> 3;
     const int groups = N / 8;
-    for (int i = 0; i < nunits; ++i) {
+    for (int i = gd; i < nunits; i += 2) {
       const int x = lo + i, et = x / nblk, nb = x % nblk;
       const int rs = i % DD_DEPTH, as = i % DD_ACTS, s = i % DD_STAGES, round = i / DD_STAGES;
       bool ok = bwait(&bar.rawfull[rs], (i / DD_DEPTH) & 1) && bwait(&bar.xfull[as], (i / DD_ACTS) & 1);
@@ -1423,14 +1457,17 @@ __global__ void __launch_bounds__(DNP_THREADS, 1) k_down_p(const __grid_constant
         mbar_arrive(&bar.full[s]);
       }
     }
-  } else if (t == DN_PROD + 160) {
+  } else if (t == DNP_PROD + 192) {
     // weights run DD_DEPTH - DD_ACTS units further ahead than the activation blocks
     for (int i = 0; i < nunits && !*bar.abort_flag; ++i) {
       issue_w(i);
       if (i >= DD_DEPTH - DD_ACTS) issue_a(i - (DD_DEPTH - DD_ACTS));
     }
     for (int i = max(0, nunits - (DD_DEPTH - DD_ACTS)); i < nunits && !*bar.abort_flag; ++i) issue_a(i);
-  } else if (t == DN_PROD) {
+  } else if (t == DNP_PROD || t == DNP_PROD + 32) {
+    // two MMA issuers (warps 16, 17): chain ch accumulates the unit's 16-neuron
+    // steps ch and ch + 2 into its own TMEM columns; the epilogue adds the chains
+    const int ch = t == DNP_PROD ? 0 : 1;
     const uint32_t idesc = idesc_f16(N, 1, 1);
     int seg = 0;
     for (int i = 0; i < nunits; ++i) {
@@ -1443,18 +1480,20 @@ __global__ void __launch_bounds__(DNP_THREADS, 1) k_down_p(const __grid_constant
       if (*bar.abort_flag) break;
       tc_fence_after();
       const uint32_t st = stbase + s * stage_bytes;
-      const uint32_t dt = tmem + tb * N;
+      const uint32_t dt = tmem + (2 * tb + ch) * N;
 #pragma unroll
-      for (int k = 0; k < KC / 16; ++k)
+      for (int kk = 0; kk < 2; ++kk) {
+        const int k = ch + 2 * kk;
         umma_f16(dt, sdesc(st + k * 2 * 2048, 2048, 128), sdesc(st + A_TILE_BYTES + k * 2 * 16 * N, 16 * N, 128),
-                 idesc, !(first && k == 0));
+                 idesc, !(first && kk == 0));
+      }
       umma_commit(&bar.empty[s]);
       if (last) {
         umma_commit(&bar.accf[tb]);
         ++seg;
       }
     }
-  } else if (t >= DN_PROD + 32 && t < DN_PROD + 160) {
+  } else if (t >= DNP_PROD + 64 && t < DNP_PROD + 192) {              // epilogue warps 18-21
     const int qd = warp & 3, m = qd * 32 + lane;
     int seg = 0;
     for (int x0 = lo; x0 < hi; ++seg) {
@@ -1469,8 +1508,11 @@ __global__ void __launch_bounds__(DNP_THREADS, 1) k_down_p(const __grid_constant
       const int e = et * TILE + (m & ~7) + perm8(m & 7);
       float* yr = y + (size_t)e * N;
       for (int col = 0; col < N; col += 8) {
-        float v[8];
-        tmem_ld8(tmem + ((uint32_t)(qd * 32) << 16) + tb * N + col, v);
+        float v[8], v1[8];
+        tmem_ld8(tmem + ((uint32_t)(qd * 32) << 16) + 2 * tb * N + col, v);
+        tmem_ld8(tmem + ((uint32_t)(qd * 32) << 16) + (2 * tb + 1) * N + col, v1);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] += v1[u];
         asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(yr + col), "f"(v[0]), "f"(v[1]),
                      "f"(v[2]), "f"(v[3])
                      : "memory");
@@ -1702,7 +1744,7 @@ extern "C" int hc_ffn_batch_layer(const hc_layer_desc* layer, const void* packed
   static_assert(GU_SMEM_LAUNCH <= 227 * 1024, "k_gu shared memory");
   constexpr int DN_RAW = RAW_DEPTH * DN_PIECES * DN_PSTRIDE + REC_RING * DN_PROD * 4;
   constexpr int GU_SMEM_MAX = GU_SMEM_LAUNCH;
-  constexpr int GUP_SMEM_NEED = GUP_GSLOTS * GUP_GROUP * PG_HOT + GUX_STAGES * NMAX * KC * 2 + BAR_BYTES;
+  constexpr int GUP_SMEM_NEED = GUP_GSLOTS * GUP_GROUP * PG_HOT + GU_STAGES * NMAX * KC * 2 + BAR_BYTES;
   constexpr int GUP_SMEM = GUP_SMEM_NEED > GU_SMEM_FLOOR ? GUP_SMEM_NEED : GU_SMEM_FLOOR;
   constexpr int DDP_SMEM =
       DD_DEPTH * PD_HOT + DD_ACTS * KC * NMAX * 2 + DD_STAGES * (A_TILE_BYTES + KC * NMAX * 2) + BAR_BYTES;
@@ -1768,7 +1810,7 @@ extern "C" int hc_ffn_batch_layer(const hc_layer_desc* layer, const void* packed
       const int dn_units = (H / TILE) * (L.hot_blocks + L.cold_blocks);
       const int dn_grid = dn_units < ctas ? dn_units : ctas;
       k_down_p<<<dn_grid, DNP_THREADS, DDP_SMEM, s>>>(pp, actb, reinterpret_cast<float*>(ws + wl.y),
-                                                      tmem_cols_for(2 * N));
+                                                      tmem_cols_for(4 * N));
     } else if (max_total > 0) {
       GuParams g;
       memset(&g, 0, sizeof(g));
