@@ -23,8 +23,9 @@
 //   k_down     D[128 output rows][N tokens] per CTA over a neuron range:
 //              A = down columns (FP8 exact, INT4 q exact; MN-major tiles),
 //              B = act (times the INT4 group scale of the CTA's 128 rows);
-//              the tile is added to y [4096][N] with vector float atomics
-//   k_resid    x_b += y[:, b]; y = 0
+//              the epilogue adds the tile straight into the residual rows
+//              x_b with float reductions (a warp covers 32 consecutive
+//              elements of one token)
 //
 // Two ways to reach the cold records:
 //   gathered   (k_gu, k_act, k_down) the union's ascending record list is
@@ -735,20 +736,27 @@ __global__ void __launch_bounds__(256) k_act(LayerArgs a, const float* __restric
 }
 
 // ---------------------------------------------------------------------------
-// k_down: y[e][b] += sum_n down[n][e] * act[n][b], persistent.
+// k_down: x_b[e] += sum_n down[n][e] * act[n][b], persistent.
 //   Unit x = (output tile x / nsub, neuron step x % nsub), nsub = ceil(slots
 //   / 64).  Producer thread (q, j): neuron q of the step, rows [32 j, 32 j +
 //   32) of the tile.  Stage: A 128 rows x 64 neurons f16 MN-major (row-group
 //   stride 128 B = SBO, neuron-group stride 2048 B = LBO; rows of a 16-byte
 //   piece in the order 0,4,1,5,2,6,3,7); B 64 neurons x N tokens MN-major
 //   (token-group stride 128 B, neuron-group stride 16 N).  Each segment's
-//   tile is added to y [4096][N] with vector float atomics.
+//   tile is added into the residual rows x_b with float reductions.
 // ---------------------------------------------------------------------------
+// xe[b * H] += v[b - col] for tokens b in [col, col + 8) below nb (xe = row e of token 0)
+__device__ __forceinline__ void add_to_rows(float* xe, int col, int nb, const float (&v)[8]) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    if (col + k < nb) asm volatile("red.global.add.f32 [%0], %1;" ::"l"(xe + (size_t)(col + k) * H), "f"(v[k]) : "memory");
+}
+
 struct DownParams {
   LayerArgs a;
   const __half* act;
-  float* y;
-  int N, stages;
+  float* x;                 // the pass's token rows [nb][4096], updated in place
+  int N, nb, stages;
   uint32_t tmem_cols;
   uint64_t* trace;
 };
@@ -921,16 +929,10 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down(DownParams p) {
       if (!go) break;
       tc_fence_after();
       const int e = et * TILE + (m & ~7) + perm8(m & 7);
-      float* yr = p.y + (size_t)e * N;
       for (int col = 0; col < N; col += 8) {
         float v[8];
         tmem_ld8(tmem + ((uint32_t)(qd * 32) << 16) + tb * N + col, v);
-        asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(yr + col), "f"(v[0]), "f"(v[1]),
-                     "f"(v[2]), "f"(v[3])
-                     : "memory");
-        asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(yr + col + 4), "f"(v[4]), "f"(v[5]),
-                     "f"(v[6]), "f"(v[7])
-                     : "memory");
+        add_to_rows(p.x + e, col, p.nb, v);
       }
       tc_fence_before();
       mbar_arrive(&bar.tfree[tb]);
@@ -1348,12 +1350,12 @@ __global__ void __launch_bounds__(256) k_act_p(LayerArgs a, const float* __restr
 // ring, the weights DD_DEPTH - DD_ACTS units further ahead; two producer
 // groups of 8 warps build the f16 A / B stages (DD_STAGES) of alternate units;
 // two threads issue the MMAs (even / odd 16-neuron steps into two accumulator
-// chains), and 4 epilogue warps add each finished tile into y with vector
-// reductions.
+// chains), and 4 epilogue warps add each finished tile into the residual
+// rows x_b with float reductions.
 // ---------------------------------------------------------------------------
 
 __global__ void __launch_bounds__(DNP_THREADS, 1) k_down_p(const __grid_constant__ PackedParams p, const __half* act,
-                                                          float* y, uint32_t tmem_cols) {
+                                                          float* x, int nb, uint32_t tmem_cols) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const LayerArgs& a = p.a;
@@ -1506,19 +1508,13 @@ __global__ void __launch_bounds__(DNP_THREADS, 1) k_down_p(const __grid_constant
       if (!go) break;
       tc_fence_after();
       const int e = et * TILE + (m & ~7) + perm8(m & 7);
-      float* yr = y + (size_t)e * N;
       for (int col = 0; col < N; col += 8) {
         float v[8], v1[8];
         tmem_ld8(tmem + ((uint32_t)(qd * 32) << 16) + 2 * tb * N + col, v);
         tmem_ld8(tmem + ((uint32_t)(qd * 32) << 16) + (2 * tb + 1) * N + col, v1);
 #pragma unroll
         for (int u = 0; u < 8; ++u) v[u] += v1[u];
-        asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(yr + col), "f"(v[0]), "f"(v[1]),
-                     "f"(v[2]), "f"(v[3])
-                     : "memory");
-        asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(yr + col + 4), "f"(v[4]), "f"(v[5]),
-                     "f"(v[6]), "f"(v[7])
-                     : "memory");
+        add_to_rows(x + e, col, nb, v);
       }
       tc_fence_before();
       mbar_arrive(&bar.tfree[tb]);
@@ -1531,18 +1527,6 @@ __global__ void __launch_bounds__(DNP_THREADS, 1) k_down_p(const __grid_constant
     tc_fence_after();
     tmem_free(tmem, tmem_cols);
   }
-}
-
-// x_b[e] += y[e][b] for b < nb; y is cleared for the next pass
-__global__ void __launch_bounds__(256) k_resid(float* __restrict__ x, int nb, int N, float* __restrict__ y) {
-  const int e = blockIdx.x * 256 + threadIdx.x, g = blockIdx.y;
-  float4* yr = reinterpret_cast<float4*>(y + (size_t)e * N) + g;
-  const float4 v = *yr;
-  const float vv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int k = 0; k < 4; ++k)
-    if (4 * g + k < nb) x[(size_t)(4 * g + k) * H + e] += vv[k];
-  *yr = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 // ---------------------------------------------------------------------------
@@ -1622,7 +1606,7 @@ __global__ void __launch_bounds__(1024) k_union(const uint32_t* __restrict__ mas
 // host side
 // ---------------------------------------------------------------------------
 struct WsLayout {
-  size_t xs_nat, xs_perm, act, part, y, total;
+  size_t xs_nat, xs_perm, act, part, total;
 };
 static size_t align_up(size_t v, size_t al) { return (v + al - 1) / al * al; }
 static WsLayout ws_layout(int64_t max_neurons) {
@@ -1634,7 +1618,6 @@ static WsLayout ws_layout(int64_t max_neurons) {
   w.xs_perm = o; o = align_up(o + xs, 1024);
   w.act = o; o = align_up(o + (size_t)max_neurons * NMAX * 2, 1024);
   w.part = o; o = align_up(o + blocks * TILE * 2 * NMAX * 4, 1024);
-  w.y = o; o = align_up(o + (size_t)H * NMAX * 4, 1024);
   w.total = o;
   return w;
 }
@@ -1809,8 +1792,7 @@ extern "C" int hc_ffn_batch_layer(const hc_layer_desc* layer, const void* packed
       k_act_p<<<(slots * (N / 8) + 255) / 256, 256, 0, s>>>(la, pp.part, gu_grid, N, actb);
       const int dn_units = (H / TILE) * (L.hot_blocks + L.cold_blocks);
       const int dn_grid = dn_units < ctas ? dn_units : ctas;
-      k_down_p<<<dn_grid, DNP_THREADS, DDP_SMEM, s>>>(pp, actb, reinterpret_cast<float*>(ws + wl.y),
-                                                      tmem_cols_for(4 * N));
+      k_down_p<<<dn_grid, DNP_THREADS, DDP_SMEM, s>>>(pp, actb, xb, nb, tmem_cols_for(4 * N));
     } else if (max_total > 0) {
       GuParams g;
       memset(&g, 0, sizeof(g));
@@ -1833,7 +1815,8 @@ extern "C" int hc_ffn_batch_layer(const hc_layer_desc* layer, const void* packed
       DownParams d;
       d.a = la;
       d.act = reinterpret_cast<const __half*>(ws + wl.act);
-      d.y = reinterpret_cast<float*>(ws + wl.y);
+      d.x = xb;
+      d.nb = nb;
       d.N = N;
       d.stages = 3;
       d.tmem_cols = tmem_cols_for(2 * N);
@@ -1844,7 +1827,6 @@ extern "C" int hc_ffn_batch_layer(const hc_layer_desc* layer, const void* packed
       k_down<<<dn_grid, DN_THREADS, dn_smem, s>>>(d);
 
     }
-    k_resid<<<dim3(H / 256, N / 4), 256, 0, s>>>(xb, nb, N, reinterpret_cast<float*>(ws + wl.y));
   }
   return cudaGetLastError() == cudaSuccess ? HC_OK : HC_ERR_CUDA;
 }
