@@ -359,11 +359,13 @@ HC_API int hc_union_cold_layers(const uint32_t* masks, int32_t n_layers, int64_t
  *              rec_flags[n_records] (1 = in the fetch set) zeroes the rest --
  *              the same result, cheaper once the union covers a large part of
  *              the section; max_cold is then the section's record count
- *   workspace  hc_ffn_batch_workspace_bytes(n_hot + max_cold) bytes, zeroed once;
- *              left zeroed again
- * Tokens are processed 8 at a time; every weight byte is read once per 8.
- * fp32 arithmetic on the decoded weights; the down projection is summed with
- * float atomics, so its last bits can differ between launches.
+ *   workspace  hc_ffn_batch_workspace_bytes(n_hot + max_cold) bytes (scratch;
+ *              no initial contents needed)
+ * Tokens are processed 64 at a time on the tcgen05 tensor cores: every weight
+ * byte is read once per 64 tokens.  Operands are f16 (FP8 weights and INT4 q
+ * exact; RMSNorm(x), q * group scale and the activations rounded once each),
+ * accumulation fp32.  Each down tile is added into x with float reductions,
+ * so the last bits can differ between launches.
  */
 HC_API int64_t hc_ffn_batch_workspace_bytes(int32_t max_neurons);
 /*
