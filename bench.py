@@ -208,7 +208,7 @@ def batched_decode_bench(syn, steps: int, warmup: int, batches=(1, 8, 32, 64)):
     """configs[4] on one GPU: the 32-layer stack for B tokens at once with
     per-token Bernoulli(0.1) masks unioned per layer (BatchStack: hc_union_cold_layers
     + hc_ffn_batch_layer per layer, tcgen05 tensor-core GEMMs), captured in one
-    CUDA graph per batch size.  `value` is device-resident; `e2e` adds the
+    CUDA graph per batch size; B = 1 runs the fused batch-1 stack kernel.  `value` is device-resident; `e2e` adds the
     pinned host->device copy of the B inputs and the device->host copy of the
     outputs to every step."""
     import torch
@@ -227,27 +227,32 @@ def batched_decode_bench(syn, steps: int, warmup: int, batches=(1, 8, 32, 64)):
         y = torch.empty(B, H, device=dev)
         bst.forward(x_in, masks=masks, out=y)                   # first call outside capture
         torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        stream.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(stream):
-            with torch.cuda.graph(g, stream=stream):
-                bst.forward(x_in, masks=masks, out=y)
-        torch.cuda.current_stream().wait_stream(stream)
+        # B = 1 runs the fused stack (one cooperative launch per token): launched
+        # directly; larger batches replay one captured graph per step
+        g = None
+        if B > 1:
+            g = torch.cuda.CUDAGraph()
+            stream.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(stream):
+                with torch.cuda.graph(g, stream=stream):
+                    bst.forward(x_in, masks=masks, out=y)
+            torch.cuda.current_stream().wait_stream(stream)
+        step = g.replay if g is not None else (lambda: bst.forward(x_in, masks=masks, out=y))
         union = float(bst.count.float().mean().item())
         for _ in range(max(warmup, 3)):
-            g.replay()
+            step()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(steps):
-            g.replay()
+            step()
         e1.record()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / steps
         e0.record()
         for _ in range(steps):
             x_in.copy_(x_host, non_blocking=True)
-            g.replay()
+            step()
             y_host.copy_(y, non_blocking=True)
         e1.record()
         torch.cuda.synchronize()

@@ -352,13 +352,15 @@ class BatchStack:
                  predictors: Optional[Sequence[Optional[NeuronPredictor]]] = None, activation: str = "silu",
                  act_on_both: bool = False, eps: float = 1e-5, threshold: float = 0.5,
                  layer_ids: Optional[Sequence[int]] = None, inter: Optional[int] = None, max_batch: int = 64,
-                 dense_min_batch: int = 8):
+                 dense_min_batch: int = 8, single_token_stack: bool = True):
         """Batches of at least ``dense_min_batch`` tokens use the dense mode of
         hc_ffn_batch_layer: every record streamed, in storage order, from a
         packed copy of the layer made once here (hc_batch_pack, about the
         layer's own size again), and masked by the union -- their union covers
         most of each section, and whole contiguous blocks stream faster than
-        per-record pieces."""
+        per-record pieces.  A single token with given masks runs the fused
+        batch-1 stack kernel (FFNStack) instead of the tensor-core kernels
+        unless ``single_token_stack`` is False."""
         self.store = store
         self.device = store.device
         self.L = len(hot)
@@ -368,11 +370,14 @@ class BatchStack:
         self.hot = list(hot)
         self.norms = [n.to(self.device, torch.float32).contiguous() if n is not None else None for n in norms]
         self.predictors = list(predictors) if predictors is not None else [None] * self.L
+        self.activation = activation
         self.act = N.HC_ACT_RELU if activation == "relu" else N.HC_ACT_SILU
         self.act_on_both = bool(act_on_both)
         self.eps = float(eps)
         self.threshold = float(threshold)
         self.max_batch = int(max_batch)
+        self._single_stack = None
+        self.single_token_stack = bool(single_token_stack)
         self.fetch = torch.stack([store.fetch_bits(li, h.ids, self.inter) for li, h in zip(self.layer_ids, self.hot)])
         self.descs, self._keep, self.max_cold = [], [], []
         for l in range(self.L):
@@ -441,6 +446,19 @@ class BatchStack:
                                                self.inter, N.ptr(self.fetch), N.ptr(t0), N.ptr(self.rec),
                                                self.rec.stride(0), N.ptr(self.count), N.ptr(flags),
                                                self.flag_stride, s), "hc_union_cold_layers")
+        if B == 1 and masks is not None and self.single_token_stack and self.inter % 4 == 0:
+            # one token: the fused stack kernel (one persistent launch for every layer)
+            st = self._single()
+            st.forward(x.reshape(HIDDEN_DIM), masks=masks[:, 0, :], x_hist=x_hist[:, 0] if x_hist is not None else None,
+                       out=y[0])
+            if not self._tables_contiguous():
+                for l in range(self.L):          # keep union_counts() / rec meaningful
+                    m = masks[l]
+                    N.check(N.lib.hc_union_cold_layers(N.ptr(m), 1, 0, B, m.stride(0), self.inter,
+                                                       N.ptr(self.fetch[l]), N.ptr(self.store.table[self.layer_ids[l]]),
+                                                       N.ptr(self.rec[l]), 0, N.ptr(self.count[l:l + 1]), None,
+                                                       self.flag_stride, s), "hc_union_cold_layers")
+            return y
         for l in range(self.L):
             if masks is None or not self._tables_contiguous():
                 m = masks[l] if masks is not None else self._layer_masks(l, y)
@@ -461,6 +479,14 @@ class BatchStack:
 
     __call__ = forward
 
+    def _single(self) -> "FFNStack":
+        """The batch-1 stack over the same layers (built on first use)."""
+        if self._single_stack is None:
+            self._single_stack = FFNStack(self.store, self.hot, self.norms, [None] * self.L, self.activation,
+                                          self.act_on_both, self.eps, self.threshold, layer_ids=self.layer_ids,
+                                          inter=self.inter)
+        return self._single_stack
+
     def _tables_contiguous(self) -> bool:
         """Layer ids consecutive, so table rows of layer l sit at table[first + l]."""
         ids = self.layer_ids
@@ -468,6 +494,8 @@ class BatchStack:
 
     def check(self):
         N.read_status(self.status, "hc_ffn_batch_layer")
+        if self._single_stack is not None:
+            self._single_stack.check()
 
     def union_counts(self) -> torch.Tensor:
         """Cold records each layer fetched in the last forward."""

@@ -114,11 +114,13 @@ def test_union_cold_matches_numpy(M):
 @pytest.mark.parametrize("B", [1, 5, 16, 19, 40, 70])
 def test_batch_given_masks(M, B, dense):
     """Token counts that pad to every MMA width (16..64) and a second pass (70);
-    the gathered union and the dense cold mode (every record, union-masked)."""
+    the gathered union and the dense cold mode (every record, union-masked).
+    B = 1 runs the tensor-core kernels (dense False / True) here; the default
+    single-token route through the fused stack is checked below."""
     engine, N, hc_synth = M
     syn = hc_synth.make_stack(n_layers=2, inter=1024, hot_frac=0.2, rank=64, activation="silu",
                               act_on_both=False, seed=21, norm_std=0.1, predictors=False)
-    bst = syn.batch_stack(max_batch=80, dense_min_batch=1 if dense else 1000)
+    bst = syn.batch_stack(max_batch=80, dense_min_batch=1 if dense else 1000, single_token_stack=False)
     words, bits = _bernoulli_masks(2, B, syn.inter, 0.1, seed=B)
     x0 = torch.randn(B, 4096, device="cuda", generator=torch.Generator(device="cuda").manual_seed(B))
     x_hist = torch.empty(2, B, 4096, device="cuda")
@@ -128,6 +130,25 @@ def test_batch_given_masks(M, B, dense):
     union = [_union_ids(bst, bits[l].numpy(), l) for l in range(2)]
     assert bst.union_counts().tolist() == [len(u) for u in union]
     _check_layers(syn, bst, x0, x_hist, union)
+
+
+def test_single_token_routes_to_stack(M):
+    """B = 1 with given masks: the fused stack kernel, checked against the oracle
+    layer by layer (rel-L2 <= 1e-3, the stack's own bar)."""
+    engine, N, hc_synth = M
+    syn = hc_synth.make_stack(n_layers=3, inter=1024, hot_frac=0.2, rank=64, activation="relu",
+                              act_on_both=True, seed=17, norm_std=0.1, predictors=False)
+    bst = syn.batch_stack(max_batch=8)
+    words, bits = _bernoulli_masks(3, 1, syn.inter, 0.3, seed=3)
+    x0 = torch.randn(1, 4096, device="cuda", generator=torch.Generator(device="cuda").manual_seed(9))
+    x_hist = torch.empty(3, 1, 4096, device="cuda")
+    out = bst.forward(x0, masks=torch.from_numpy(words), x_hist=x_hist)
+    bst.check()
+    assert bst._single_stack is not None
+    assert torch.equal(out, x_hist[-1])
+    union = [_union_ids(bst, bits[l].numpy(), l) for l in range(3)]
+    assert bst.union_counts().tolist() == [len(u) for u in union]
+    _check_layers(syn, bst, x0, x_hist, union, tol=1e-3)
 
 
 def test_batch_dense_and_row_scaled_relu(M):
@@ -153,7 +174,7 @@ def test_batch_of_one_matches_fused_stack(M):
                               act_on_both=True, seed=8, predictors=False)
     words, bits = _bernoulli_masks(3, 1, syn.inter, 0.3, seed=9)
     x0 = torch.randn(4096, device="cuda", generator=torch.Generator(device="cuda").manual_seed(4))
-    bst = syn.batch_stack(max_batch=8)
+    bst = syn.batch_stack(max_batch=8, single_token_stack=False)     # the tensor-core kernels at B = 1
     yb = bst.forward(x0.view(1, -1), masks=torch.from_numpy(words))[0]
     st = syn.stack()
     ys = st.forward(x0, masks=torch.from_numpy(words[:, 0, :]).cuda())
