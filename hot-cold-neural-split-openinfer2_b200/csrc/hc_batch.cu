@@ -1707,10 +1707,10 @@ extern "C" int hc_union_cold_layers(const uint32_t* masks, int32_t n_layers, int
   return cudaGetLastError() == cudaSuccess ? HC_OK : HC_ERR_CUDA;
 }
 
-extern "C" int hc_ffn_batch_layer(const hc_layer_desc* layer, const void* packed, float* x, int32_t batch,
-                                  const int32_t* rec, const int32_t* count, int32_t max_cold,
-                                  const uint8_t* rec_flags, float eps, int32_t act, int32_t act_on_both,
-                                  void* workspace, int32_t* status, hc_stream_t stream) {
+// y_out == nullptr: x_b += FFN(x_b); else y_out_b += FFN(x_b) and x is only read
+static int batch_layer(const hc_layer_desc* layer, const void* packed, float* x, int32_t batch, const int32_t* rec,
+                       const int32_t* count, int32_t max_cold, const uint8_t* rec_flags, float eps, int32_t act,
+                       int32_t act_on_both, void* workspace, float* y_out, int32_t* status, hc_stream_t stream) {
   if (!layer || !x || batch <= 0 || !rec || !count || max_cold < 0 || !workspace || !status ||
       (act != HC_ACT_SILU && act != HC_ACT_RELU) || (rec_flags && !packed) ||
       (packed && (reinterpret_cast<uintptr_t>(packed) & 15)))
@@ -1719,6 +1719,7 @@ extern "C" int hc_ffn_batch_layer(const hc_layer_desc* layer, const void* packed
   if (!layer->hot || !layer->cold_records || layer->n_hot < 0 || max_cold > layer->n_records)
     return HC_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(workspace) & 15) ||
+      (reinterpret_cast<uintptr_t>(y_out) & 15) ||
       (reinterpret_cast<uintptr_t>(layer->hot) & 15) || (reinterpret_cast<uintptr_t>(layer->cold_records) & 15))
     return HC_ERR_ARG;
   constexpr int GU_RAW = GU_DEPTH * GU_RAW_SLOT;
@@ -1772,6 +1773,7 @@ extern "C" int hc_ffn_batch_layer(const hc_layer_desc* layer, const void* packed
     const int nb = batch - b0 < NMAX ? batch - b0 : NMAX;
     const int N = (nb + 15) / 16 * 16;
     float* xb = x + (size_t)b0 * H;
+    float* ob = (y_out ? y_out : x) + (size_t)b0 * H;      // where the down tiles are added
     k_norm<<<N, 256, 0, s>>>(xb, nb, N, layer->norm_w, eps, ws + wl.xs_nat, ws + wl.xs_perm);
     if (rec_flags && max_total > 0) {
       const PackLayout L = pack_layout(layer->n_hot, layer->n_records);
@@ -1792,7 +1794,7 @@ extern "C" int hc_ffn_batch_layer(const hc_layer_desc* layer, const void* packed
       k_act_p<<<(slots * (N / 8) + 255) / 256, 256, 0, s>>>(la, pp.part, gu_grid, N, actb);
       const int dn_units = (H / TILE) * (L.hot_blocks + L.cold_blocks);
       const int dn_grid = dn_units < ctas ? dn_units : ctas;
-      k_down_p<<<dn_grid, DNP_THREADS, DDP_SMEM, s>>>(pp, actb, xb, nb, tmem_cols_for(4 * N));
+      k_down_p<<<dn_grid, DNP_THREADS, DDP_SMEM, s>>>(pp, actb, ob, nb, tmem_cols_for(4 * N));
     } else if (max_total > 0) {
       GuParams g;
       memset(&g, 0, sizeof(g));
@@ -1815,7 +1817,7 @@ extern "C" int hc_ffn_batch_layer(const hc_layer_desc* layer, const void* packed
       DownParams d;
       d.a = la;
       d.act = reinterpret_cast<const __half*>(ws + wl.act);
-      d.x = xb;
+      d.x = ob;
       d.nb = nb;
       d.N = N;
       d.stages = 3;
@@ -1829,4 +1831,21 @@ extern "C" int hc_ffn_batch_layer(const hc_layer_desc* layer, const void* packed
     }
   }
   return cudaGetLastError() == cudaSuccess ? HC_OK : HC_ERR_CUDA;
+}
+
+extern "C" int hc_ffn_batch_layer(const hc_layer_desc* layer, const void* packed, float* x, int32_t batch,
+                                  const int32_t* rec, const int32_t* count, int32_t max_cold,
+                                  const uint8_t* rec_flags, float eps, int32_t act, int32_t act_on_both,
+                                  void* workspace, int32_t* status, hc_stream_t stream) {
+  return batch_layer(layer, packed, x, batch, rec, count, max_cold, rec_flags, eps, act, act_on_both, workspace,
+                     nullptr, status, stream);
+}
+
+extern "C" int hc_ffn_batch_layer_partial(const hc_layer_desc* layer, const void* packed, const float* x,
+                                          int32_t batch, const int32_t* rec, const int32_t* count, int32_t max_cold,
+                                          const uint8_t* rec_flags, float eps, int32_t act, int32_t act_on_both,
+                                          void* workspace, float* y_out, int32_t* status, hc_stream_t stream) {
+  if (!y_out) return HC_ERR_ARG;
+  return batch_layer(layer, packed, const_cast<float*>(x), batch, rec, count, max_cold, rec_flags, eps, act,
+                     act_on_both, workspace, y_out, status, stream);
 }

@@ -27,7 +27,7 @@ import torch.nn.functional as F
 
 import hc_native as N
 from predictor import NeuronPredictor, PredictorRegistry, logit_threshold, unpack_mask
-from splitter import HIDDEN_DIM, ColdWeightStore, bits_to_words
+from splitter import HIDDEN_DIM, NEURON_RECORD_BYTES, ColdWeightStore, bits_to_words
 
 
 # ─── Hot neurons ──────────────────────────────────────────────────────────────
@@ -69,6 +69,13 @@ class HotNeurons:
 def split_range(n: int, rank: int, size: int):
     """[lo, hi) of rank's share when n units are split over size ranks."""
     return n * rank // size, n * (rank + 1) // size
+
+
+class _Share:
+    """(rank, size) of a neuron split, for the share helpers."""
+
+    def __init__(self, rank: int, size: int):
+        self.rank, self.size = rank, size
 
 
 class TPGroup:
@@ -352,7 +359,7 @@ class BatchStack:
                  predictors: Optional[Sequence[Optional[NeuronPredictor]]] = None, activation: str = "silu",
                  act_on_both: bool = False, eps: float = 1e-5, threshold: float = 0.5,
                  layer_ids: Optional[Sequence[int]] = None, inter: Optional[int] = None, max_batch: int = 64,
-                 dense_min_batch: int = 8, single_token_stack: bool = True):
+                 dense_min_batch: int = 8, single_token_stack: bool = True, shard=None, group=None):
         """Batches of at least ``dense_min_batch`` tokens use the dense mode of
         hc_ffn_batch_layer: every record streamed, in storage order, from a
         packed copy of the layer made once here (hc_batch_pack, about the
@@ -360,7 +367,15 @@ class BatchStack:
         most of each section, and whole contiguous blocks stream faster than
         per-record pieces.  A single token with given masks runs the fused
         batch-1 stack kernel (FFNStack) instead of the tensor-core kernels
-        unless ``single_token_stack`` is False."""
+        unless ``single_token_stack`` is False.
+
+        ``shard=(rank, size)``: this GPU takes hot neurons [rank n_hot / size,
+        (rank+1) n_hot / size) of each layer's hot list and the cold records
+        with section indices in [rank n_rec / size, (rank+1) n_rec / size);
+        each layer's partial output [B, 4096] is summed over the ``group``
+        (torch.distributed, NCCL) with one all-reduce before x += y, so every
+        rank ends with the whole stack's output.  Sharded batches always
+        stream the packed copy of the share (the union's flags select)."""
         self.store = store
         self.device = store.device
         self.L = len(hot)
@@ -378,25 +393,37 @@ class BatchStack:
         self.max_batch = int(max_batch)
         self._single_stack = None
         self.single_token_stack = bool(single_token_stack)
+        self.shard = (0, 1) if shard is None else (int(shard[0]), int(shard[1]))
+        self.group = group
+        if not 0 <= self.shard[0] < self.shard[1]:
+            raise ValueError(f"bad shard {shard}")
         self.fetch = torch.stack([store.fetch_bits(li, h.ids, self.inter) for li, h in zip(self.layer_ids, self.hot)])
-        self.descs, self._keep, self.max_cold = [], [], []
+        rank, size = self.shard
+        if size > 1:
+            self.hot = [FFNStack._hot_share(h, _Share(rank, size)) for h in self.hot]
+        self.descs, self._keep, self.max_cold, self.rec_lo = [], [], [], []
         for l in range(self.L):
             li = self.layer_ids[l]
             rec = store.section_records(li)
             self._keep.append(rec)
-            n_rec = int(store.n_rec_host[li])
-            self.max_cold.append(n_rec)
+            r0, r1 = split_range(int(store.n_rec_host[li]), rank, size)
+            self.rec_lo.append(r0)
+            self.max_cold.append(r1 - r0)
             self.descs.append(N.LayerDesc(
                 hot=N.ptr(self.hot[l].packed), hot_scale=N.ptr(self.hot[l].scales), norm_w=N.ptr(self.norms[l]),
-                cold_records=N.ptr(rec), table=N.ptr(store.table[li]), fetch_bits=N.ptr(self.fetch[l]),
-                n_hot=self.hot[l].n, n_records=n_rec, inter=self.inter, rank=0))
+                cold_records=N.ptr(rec) + r0 * NEURON_RECORD_BYTES, table=N.ptr(store.table[li]),
+                fetch_bits=N.ptr(self.fetch[l]), n_hot=self.hot[l].n, n_records=r1 - r0, inter=self.inter, rank=0))
+        # the union (and its flags) always covers the whole section
+        self.sec_records = [int(store.n_rec_host[li]) for li in self.layer_ids]
         max_neurons = max(h.n + c for h, c in zip(self.hot, self.max_cold))
         self.ws = torch.zeros(int(N.lib.hc_ffn_batch_workspace_bytes(max(max_neurons, 1))), dtype=torch.uint8,
                               device=self.device)
-        self.rec = torch.zeros(self.L, max(max(self.max_cold), 1), dtype=torch.int32, device=self.device)
+        self.rec = torch.zeros(self.L, max(max(self.sec_records), 1), dtype=torch.int32, device=self.device)
         self.count = torch.zeros(self.L, dtype=torch.int32, device=self.device)
-        self.dense_min_batch = int(dense_min_batch)
-        self.flag_stride = (max(max(self.max_cold), 1) + 15) // 16 * 16
+        self.dense_min_batch = 1 if size > 1 else int(dense_min_batch)
+        self.flag_stride = (max(max(self.sec_records), 1) + 15) // 16 * 16
+        self.part = torch.zeros(self.max_batch, HIDDEN_DIM, dtype=torch.float32, device=self.device) \
+            if size > 1 else None
         self.flags = torch.zeros(self.L, self.flag_stride, dtype=torch.uint8, device=self.device)
         # dense mode streams a packed copy of each layer (hc_batch_pack), built once here
         self.packed = [None] * self.L
@@ -446,7 +473,7 @@ class BatchStack:
                                                self.inter, N.ptr(self.fetch), N.ptr(t0), N.ptr(self.rec),
                                                self.rec.stride(0), N.ptr(self.count), N.ptr(flags),
                                                self.flag_stride, s), "hc_union_cold_layers")
-        if B == 1 and masks is not None and self.single_token_stack and self.inter % 4 == 0:
+        if B == 1 and masks is not None and self.single_token_stack and self.shard[1] == 1 and self.inter % 4 == 0:
             # one token: the fused stack kernel (one persistent launch for every layer)
             st = self._single()
             st.forward(x.reshape(HIDDEN_DIM), masks=masks[:, 0, :], x_hist=x_hist[:, 0] if x_hist is not None else None,
@@ -467,12 +494,25 @@ class BatchStack:
                                                    0, N.ptr(self.count[l:l + 1]),
                                                    N.ptr(flags[l]) if dense else None, self.flag_stride, s),
                         "hc_union_cold_layers")
-            N.check(N.lib.hc_ffn_batch_layer(ctypes.byref(self.descs[l]), N.ptr(self.packed[l]), N.ptr(y), B,
-                                             N.ptr(self.rec[l]),
-                                             N.ptr(self.count[l:l + 1]), self.max_cold[l],
-                                             N.ptr(flags[l]) if dense else None, self.eps, self.act,
-                                             1 if self.act_on_both else 0, N.ptr(self.ws), N.ptr(self.status), s),
-                    "hc_ffn_batch_layer")
+            if self.part is None:
+                N.check(N.lib.hc_ffn_batch_layer(ctypes.byref(self.descs[l]), N.ptr(self.packed[l]), N.ptr(y), B,
+                                                 N.ptr(self.rec[l]),
+                                                 N.ptr(self.count[l:l + 1]), self.max_cold[l],
+                                                 N.ptr(flags[l]) if dense else None, self.eps, self.act,
+                                                 1 if self.act_on_both else 0, N.ptr(self.ws), N.ptr(self.status), s),
+                        "hc_ffn_batch_layer")
+            else:
+                # this GPU's share of the layer into part, then one all-reduce of [B, 4096]
+                import torch.distributed as dist
+                part = self.part[:B]
+                part.zero_()
+                N.check(N.lib.hc_ffn_batch_layer_partial(
+                    ctypes.byref(self.descs[l]), N.ptr(self.packed[l]), N.ptr(y), B, N.ptr(self.rec[l]),
+                    N.ptr(self.count[l:l + 1]), self.max_cold[l], N.ptr(flags[l]) + self.rec_lo[l], self.eps,
+                    self.act, 1 if self.act_on_both else 0, N.ptr(self.ws), N.ptr(part), N.ptr(self.status), s),
+                    "hc_ffn_batch_layer_partial")
+                dist.all_reduce(part, group=self.group)
+                y.add_(part)
             if x_hist is not None:
                 x_hist[l].copy_(y)
         return y

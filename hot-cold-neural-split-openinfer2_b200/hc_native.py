@@ -83,6 +83,8 @@ _SIGS = {
     "hc_ffn_batch_workspace_bytes": (c_i64, [c_i32]),
     "hc_batch_set_trace": (c_i32, [c_p, c_p]),
     "hc_ffn_batch_layer": (c_i32, [c_p, c_p, c_p, c_i32, c_p, c_p, c_i32, c_p, c_f, c_i32, c_i32, c_p, c_p, c_p]),
+    "hc_ffn_batch_layer_partial": (c_i32, [c_p, c_p, c_p, c_i32, c_p, c_p, c_i32, c_p, c_f, c_i32, c_i32, c_p, c_p, c_p,
+                                           c_p]),
     "hc_batch_pack_bytes": (c_i64, [c_i32, c_i32]),
     "hc_batch_pack": (c_i32, [c_p, c_p, c_p]),
 }

@@ -48,11 +48,12 @@ class SynthStack:
                         threshold, grid=grid, inter=self.inter, tp=tp)
 
     def batch_stack(self, threshold: float = 0.5, with_predictors: bool = False, max_batch: int = 64,
-                    dense_min_batch: int = 8, single_token_stack: bool = True) -> BatchStack:
+                    dense_min_batch: int = 8, single_token_stack: bool = True, shard=None,
+                    group=None) -> BatchStack:
         preds = self.predictors if with_predictors else None
         return BatchStack(self.store, self.hot, self.norms, preds, self.activation, self.act_on_both, self.eps,
                           threshold, inter=self.inter, max_batch=max_batch, dense_min_batch=dense_min_batch,
-                          single_token_stack=single_token_stack)
+                          single_token_stack=single_token_stack, shard=shard, group=group)
 
 
 def make_stack(n_layers: int = 32, inter: int = 14336, hot_frac: float = 0.2, rank: int = 64,

@@ -379,6 +379,19 @@ HC_API int hc_ffn_batch_layer(const hc_layer_desc* layer, const void* packed, fl
                               const uint8_t* rec_flags, float eps, int32_t act, int32_t act_on_both,
                               void* workspace, int32_t* status, hc_stream_t stream);
 /*
+ * hc_ffn_batch_layer_partial -- the same layer, with its output added into
+ * y_out ([batch][4096] fp32, device; the caller zeroes it) instead of x, which
+ * is only read.  This is the per-GPU step of the neuron-sharded batched decode
+ * (engine.py:184-188: down_proj is linear in the neuron dimension): each GPU
+ * passes the descriptor of its share of the layer's hot neurons and cold
+ * records, and the partial outputs are summed across GPUs (one all-reduce of
+ * [batch][4096] per layer) before x += y.
+ */
+HC_API int hc_ffn_batch_layer_partial(const hc_layer_desc* layer, const void* packed, const float* x, int32_t batch,
+                                      const int32_t* rec, const int32_t* count, int32_t max_cold,
+                                      const uint8_t* rec_flags, float eps, int32_t act, int32_t act_on_both,
+                                      void* workspace, float* y_out, int32_t* status, hc_stream_t stream);
+/*
  * Packed copy of a layer for the dense mode of hc_ffn_batch_layer: the hot
  * rows and every cold record re-laid out once, unit-major, so that each
  * 64-wide K step of a 128-row gate/up tile and each 64-neuron step of a

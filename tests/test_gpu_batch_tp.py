@@ -1,0 +1,81 @@
+"""Neuron-sharded batched decode over two GPUs (one process each, NCCL).
+
+Each GPU streams its share of every layer (half of the hot list, half of
+the section's records, packed) and the layers' partial outputs are summed
+with one NCCL all-reduce of [B, 4096] per layer.  The result must match the
+same batch on one GPU (float summation order aside) and be identical on both
+ranks.  Skipped on machines with fewer than two GPUs.
+"""
+import os
+import socket
+
+import pytest
+import torch
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG = os.path.join(REPO, "hot-cold-neural-split-openinfer2_b200")
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, out_dir):
+    import sys
+    sys.path.insert(0, PKG)
+    import datetime
+    import torch.distributed as dist
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120), device_id=dev)
+    import hc_synth
+    L, inter = 3, 4096
+    syn = hc_synth.make_stack(n_layers=L, inter=inter, hot_frac=0.2, activation="relu", act_on_both=True,
+                              seed=31, predictors=False, device=dev)
+    res = {}
+    for B in (1, 40):
+        masks = hc_synth.bernoulli_words(L, B, inter, 0.1, seed=5 + B, device=dev)
+        x0 = torch.randn(B, 4096, generator=torch.Generator().manual_seed(B)).to(dev)
+        bst = syn.batch_stack(max_batch=64, shard=(rank, world))
+        hist = torch.empty(L, B, 4096, device=dev)
+        dist.barrier()
+        y = bst.forward(x0, masks=masks, x_hist=hist)
+        torch.cuda.synchronize()
+        bst.check()
+        res[f"tp{B}"] = hist.cpu().clone()
+        res[f"count{B}"] = bst.union_counts().cpu().clone()
+        if rank == 0:
+            one = syn.batch_stack(max_batch=64, single_token_stack=False)
+            h1 = torch.empty(L, B, 4096, device=dev)
+            one.forward(x0, masks=masks, x_hist=h1)
+            torch.cuda.synchronize()
+            one.check()
+            res[f"one{B}"] = h1.cpu().clone()
+            res[f"x0_{B}"] = x0.cpu().clone()
+        del bst
+    torch.save(res, os.path.join(out_dir, f"rank{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_sharded_batch_matches_one_gpu(tmp_path):
+    import torch.multiprocessing as mp
+    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    r0 = torch.load(tmp_path / "rank0.pt")
+    r1 = torch.load(tmp_path / "rank1.pt")
+    for B in (1, 40):
+        assert torch.equal(r0[f"tp{B}"], r1[f"tp{B}"])                 # the all-reduce leaves identical bits
+        assert torch.equal(r0[f"count{B}"], r1[f"count{B}"])
+        x0 = r0[f"x0_{B}"].double()
+        prev = x0
+        for l in range(r0[f"tp{B}"].shape[0]):
+            d_tp = r0[f"tp{B}"][l].double() - prev
+            d_one = r0[f"one{B}"][l].double() - prev
+            rel = ((d_tp - d_one).norm() / d_one.norm()).item()
+            assert rel < 1e-4, (B, l, rel)      # same f16 operands, different float summation order only
+            prev = r0[f"one{B}"][l].double()

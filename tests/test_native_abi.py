@@ -62,6 +62,8 @@ def test_argument_errors_are_reported_without_a_device():
                                       None) == N.HC_ERR_ARG
     assert N.lib.hc_ffn_batch_layer(None, None, None, 4, None, None, 0, None, 1e-5, 0, 0, None, None,
                                     None) == N.HC_ERR_ARG
+    assert N.lib.hc_ffn_batch_layer_partial(None, None, None, 4, None, None, 0, None, 1e-5, 0, 0, None, None,
+                                            None, None) == N.HC_ERR_ARG
     assert N.lib.hc_batch_pack(None, None, None) == N.HC_ERR_ARG
     # packed copy: 16 KB per hot gate/up step, 8.5 KB per cold one, 8 / 4.1 KB per down step
     assert N.lib.hc_batch_pack_bytes(2867, 11469) >= (23 * 64 * 16384 + 90 * 64 * 8704 + 32 * 46 * 8192
