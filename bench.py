@@ -204,17 +204,21 @@ def cold_dequant_bench(store, reps: int = 5):
     return out
 
 
-def batched_decode_bench(syn, steps: int, warmup: int, batches=(1, 8, 32, 64)):
+def batched_decode_bench(syn, steps: int, warmup: int, batches=(1, 8, 32, 64), shard=None):
     """configs[4] on one GPU: the 32-layer stack for B tokens at once with
     per-token Bernoulli(0.1) masks unioned per layer (BatchStack: hc_union_cold_layers
     + hc_ffn_batch_layer per layer, tcgen05 tensor-core GEMMs), captured in one
-    CUDA graph per batch size; B = 1 runs the fused batch-1 stack kernel.  `value` is device-resident; `e2e` adds the
+    CUDA graph per batch size; B = 1 runs the fused batch-1 stack kernel.
+    ``shard=(rank, size)`` (every rank calls this): each GPU streams its share
+    of every layer and the partial outputs are summed by one NCCL all-reduce
+    per layer, inside the captured graph; times are the max over ranks.  `value` is device-resident; `e2e` adds the
     pinned host->device copy of the B inputs and the device->host copy of the
     outputs to every step."""
     import torch
     import hc_synth
     peak, _ = _peaks()
-    bst = syn.batch_stack(max_batch=max(batches))
+    import torch.distributed as dist
+    bst = syn.batch_stack(max_batch=max(batches), shard=shard)
     dev = syn.store.device
     stream = torch.cuda.Stream(device=dev)
     out = {}
@@ -231,11 +235,18 @@ def batched_decode_bench(syn, steps: int, warmup: int, batches=(1, 8, 32, 64)):
         # directly; larger batches replay one captured graph per step
         g = None
         if B > 1:
+            if shard is not None and shard[1] > 1:
+                dist.barrier()
+                torch.cuda.synchronize()
             g = torch.cuda.CUDAGraph()
             stream.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(stream):
-                with torch.cuda.graph(g, stream=stream):
-                    bst.forward(x_in, masks=masks, out=y)
+            try:
+                with torch.cuda.stream(stream):
+                    with torch.cuda.graph(g, stream=stream):
+                        bst.forward(x_in, masks=masks, out=y)
+            except RuntimeError as e:       # a collective that cannot be captured: launch eagerly
+                print(f"batched decode B={B}: graph capture failed ({str(e)[:120]}); eager launches", file=sys.stderr)
+                g = None
             torch.cuda.current_stream().wait_stream(stream)
         step = g.replay if g is not None else (lambda: bst.forward(x_in, masks=masks, out=y))
         union = float(bst.count.float().mean().item())
@@ -258,15 +269,21 @@ def batched_decode_bench(syn, steps: int, warmup: int, batches=(1, 8, 32, 64)):
         torch.cuda.synchronize()
         e2e_ms = e0.elapsed_time(e1) / steps
         bst.check()
+        if shard is not None and shard[1] > 1:
+            t = torch.tensor([ms, e2e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms, e2e_ms = (float(v) for v in t.tolist())
         # algorithmic bytes of one step: every hot neuron and every record of
         # each layer's union once, plus the B hidden states in and out per layer
         step_bytes = LAYERS * (N_HOT * HOT_BYTES + union * COLD_BYTES + 2 * B * H * 4)
         gbs = step_bytes / (ms * 1e-3) / 1e9
+        n_gpu = shard[1] if shard is not None else 1
         out[str(B)] = {"tokens_per_s": round(B / (ms * 1e-3), 1), "ms_per_step": round(ms, 4),
                        "e2e_tokens_per_s": round(B / (e2e_ms * 1e-3), 1),
                        "union_records_per_layer": round(union, 1),
                        "union_frac": round(union / (INTER - N_HOT), 4),
-                       "algorithmic_gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
+                       "algorithmic_gbs": round(gbs, 1), "frac": round(gbs / (peak * n_gpu), 4),
+                       "graph": g is not None}
         del g
     return out
 
@@ -387,10 +404,13 @@ def run_gpu(args):
     if ws > 1:
         roofline["traffic"] = None          # the committed capture is of the one-GPU launch
     line = None
+    bd_tp = None
     if ws > 1:
         dist.barrier()
         torch.cuda.synchronize()
         tp.close()
+        # configs[4] across the GPUs: B = 64, every layer's neurons sharded, one NCCL all-reduce per layer
+        bd_tp = batched_decode_bench(syn, args.steps, args.warmup, batches=(64,), shard=(rank, ws))
     if rank == 0:
         dq = cold_dequant_bench(syn.store) if ws == 1 else None
         bd = batched_decode_bench(syn, args.steps, args.warmup) if ws == 1 else None
@@ -418,6 +438,12 @@ def run_gpu(args):
             line["batched_decode"] = {"workload": "configs[4] on 1 GPU: 32L 4096/14336 stack, B tokens, per-token "
                                                   "Bernoulli(0.1) masks unioned per layer, tcgen05 GEMMs",
                                       "unit": "tokens/s", "peak": peak, "by_B": bd}
+        if bd_tp is not None:
+            line["batched_decode"] = {"workload": f"configs[4] on {ws} GPUs: 32L 4096/14336 stack, B tokens, "
+                                                  "per-token Bernoulli(0.1) masks unioned per layer; every layer's "
+                                                  f"hot neurons and cold records split over {ws} GPUs, one NCCL "
+                                                  "all-reduce of the [B, 4096] partial output per layer",
+                                      "unit": "tokens/s (whole job)", "peak": peak, "by_B": bd_tp}
         if dq is not None:
             line["cold_dequant"] = {"unit": "GB/s", "peak": peak, "bytes_per_neuron": COLD_BYTES + 3 * H * 2,
                                     "layers": LAYERS, "out_dtype": "bf16", "by_K": dq}
