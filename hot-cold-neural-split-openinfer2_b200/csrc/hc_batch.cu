@@ -41,6 +41,7 @@
 // along K.  Every weight byte is read once per pass.
 #include <cuda.h>
 #include <string.h>
+#include <utility>
 #include <cudaTypedefs.h>
 
 #include "hc_common.cuh"
@@ -121,6 +122,16 @@ __device__ __forceinline__ void tmem_st16_nowait(uint32_t taddr, const uint32_t 
       : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// Programmatic dependent launch (the packed-mode kernels are launched with
+// programmatic stream serialisation): a kernel lets the next one be scheduled
+// as soon as every one of its CTAs has started, and the next one does its
+// independent set-up (barriers, TMEM, weight copies) before waiting, in
+// pdl_wait, for its predecessor to complete with all its memory visible.
+// Without the launch attribute both are no-ops.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 // global -> shared bulk copy (16-byte aligned, size % 16 == 0) completing on `bar`
 __device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
@@ -244,6 +255,8 @@ __global__ void __launch_bounds__(256) k_norm(const float* __restrict__ x, int n
                                               float eps, uint8_t* __restrict__ xs_nat, uint8_t* __restrict__ xs_perm) {
   __shared__ float red[8];
   const int b = blockIdx.x, t = threadIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();                                   // x is the previous layer's output
   float rstd = 0.0f;
   if (b < nb) {
     const float4* src = reinterpret_cast<const float4*>(x + (size_t)b * H);
@@ -1116,6 +1129,7 @@ __global__ void __launch_bounds__(GUP_THREADS, 1) k_gu_p(const __grid_constant__
   const int U = tiles * (H / KC);
   const int lo = range_lo(c, U, G), hi = range_lo(c + 1, U, G);
   if (lo >= hi) return;
+  pdl_launch_dependents();
   const int nunits = hi - lo;
   uint64_t* tr = p.trace;
   if (t == 0) stamp(tr, c, 0);
@@ -1254,6 +1268,7 @@ __global__ void __launch_bounds__(GUP_THREADS, 1) k_gu_p(const __grid_constant__
     for (int g = 0; g < ngroups && !*bar.abort_flag; ++g) issue(g);
   } else if (t == GU_PROD + 32) {
     // token tiles: tile s belongs to A stage s and is freed by the same commits
+    pdl_wait();                                 // the tiles are k_norm's output
     for (int i = 0; i < nunits; ++i) {
       const int x = lo + i, T = x >> 6, kb = x & (H / KC - 1);
       const int s = i % GU_STAGES, round = i / GU_STAGES;
@@ -1299,6 +1314,8 @@ __global__ void __launch_bounds__(GUP_THREADS, 1) k_gu_p(const __grid_constant__
 // act[slot][b] (swizzled 16-byte chunks) for every packed slot; records outside the fetch set -> 0
 __global__ void __launch_bounds__(256) k_act_p(LayerArgs a, const float* __restrict__ part, int G, int N,
                                                __half* __restrict__ act) {
+  pdl_launch_dependents();
+  pdl_wait();                                   // part is k_gu_p's output
   const PackLayout L = pack_layout(a.n_hot, a.n_records);
   const int U = (L.hot_tiles + L.cold_tiles) * (H / KC);
   const int slots = (L.hot_blocks + L.cold_blocks) * KC;
@@ -1365,6 +1382,7 @@ __global__ void __launch_bounds__(DNP_THREADS, 1) k_down_p(const __grid_constant
   const int U = (H / TILE) * nblk;
   const int lo = range_lo(c, U, G), hi = range_lo(c + 1, U, G);
   if (lo >= hi) return;
+  pdl_launch_dependents();
   const int nunits = hi - lo;
 
   const int b_bytes = KC * N * 2;
@@ -1398,6 +1416,7 @@ __global__ void __launch_bounds__(DNP_THREADS, 1) k_down_p(const __grid_constant
   };
   auto issue_a = [&](int i) {
     if (i >= nunits) return;
+    if (i == 0) pdl_wait();                     // the activation rows are k_act_p's output
     const int nb = (lo + i) % nblk;
     const int slot = i % DD_ACTS, use = i / DD_ACTS;
     if (use > 0 && !bwait(&bar.xempty[slot], (use - 1) & 1)) fail(a, bar.abort_flag);
@@ -1662,6 +1681,22 @@ static uint64_t* g_trace_down = nullptr;
 
 using namespace hcb;
 
+// launch with programmatic stream serialisation (see pdl_wait)
+template <typename... P, typename... A>
+static cudaError_t launch_pdl(void (*kernel)(P...), int grid, int block, size_t smem, cudaStream_t s, A&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<A>(args)...);
+}
+
 extern "C" int hc_batch_set_trace(uint64_t* gu, uint64_t* down) {
   g_trace_gu = gu;
   g_trace_down = down;
@@ -1774,8 +1809,11 @@ static int batch_layer(const hc_layer_desc* layer, const void* packed, float* x,
     const int N = (nb + 15) / 16 * 16;
     float* xb = x + (size_t)b0 * H;
     float* ob = (y_out ? y_out : x) + (size_t)b0 * H;      // where the down tiles are added
-    k_norm<<<N, 256, 0, s>>>(xb, nb, N, layer->norm_w, eps, ws + wl.xs_nat, ws + wl.xs_perm);
     if (rec_flags && max_total > 0) {
+      // packed mode: the four kernels overlap each one's set-up with its predecessor's tail
+      if (launch_pdl(k_norm, N, 256, 0, s, (const float*)xb, nb, N, layer->norm_w, eps, ws + wl.xs_nat,
+                     ws + wl.xs_perm) != cudaSuccess)
+        return HC_ERR_CUDA;
       const PackLayout L = pack_layout(layer->n_hot, layer->n_records);
       PackedParams pp;
       memset(&pp, 0, sizeof(pp));
@@ -1788,14 +1826,19 @@ static int batch_layer(const hc_layer_desc* layer, const void* packed, float* x,
       pp.trace = g_trace_gu;
       const int gu_units = (L.hot_tiles + L.cold_tiles) * (H / KC);
       const int gu_grid = gu_units < ctas ? gu_units : ctas;
-      k_gu_p<<<gu_grid, GUP_THREADS, GUP_SMEM, s>>>(pp);
+      if (launch_pdl(k_gu_p, gu_grid, GUP_THREADS, GUP_SMEM, s, pp) != cudaSuccess) return HC_ERR_CUDA;
       const int slots = (L.hot_blocks + L.cold_blocks) * KC;
       __half* actb = reinterpret_cast<__half*>(ws + wl.act);
-      k_act_p<<<(slots * (N / 8) + 255) / 256, 256, 0, s>>>(la, pp.part, gu_grid, N, actb);
+      if (launch_pdl(k_act_p, (slots * (N / 8) + 255) / 256, 256, 0, s, la, (const float*)pp.part, gu_grid, N,
+                     actb) != cudaSuccess)
+        return HC_ERR_CUDA;
       const int dn_units = (H / TILE) * (L.hot_blocks + L.cold_blocks);
       const int dn_grid = dn_units < ctas ? dn_units : ctas;
-      k_down_p<<<dn_grid, DNP_THREADS, DDP_SMEM, s>>>(pp, actb, ob, nb, tmem_cols_for(4 * N));
+      if (launch_pdl(k_down_p, dn_grid, DNP_THREADS, DDP_SMEM, s, pp, (const __half*)actb, ob, nb,
+                     tmem_cols_for(4 * N)) != cudaSuccess)
+        return HC_ERR_CUDA;
     } else if (max_total > 0) {
+      k_norm<<<N, 256, 0, s>>>(xb, nb, N, layer->norm_w, eps, ws + wl.xs_nat, ws + wl.xs_perm);
       GuParams g;
       memset(&g, 0, sizeof(g));
       g.a = la;
