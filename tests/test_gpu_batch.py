@@ -151,6 +151,44 @@ def test_single_token_routes_to_stack(M):
     _check_layers(syn, bst, x0, x_hist, union, tol=1e-3)
 
 
+@pytest.mark.parametrize("dense", [False, True])
+def test_batch_empty_union(M, dense):
+    """No token activates a cold neuron: only the hot neurons contribute (the
+    dense mode streams every record and zeroes all of them)."""
+    engine, N, hc_synth = M
+    syn = hc_synth.make_stack(n_layers=2, inter=1024, hot_frac=0.2, rank=64, activation="silu",
+                              act_on_both=False, seed=41, norm_std=0.1, predictors=False)
+    bst = syn.batch_stack(max_batch=16, dense_min_batch=1 if dense else 1000)
+    B = 12
+    words, bits = _bernoulli_masks(2, B, syn.inter, 0.0, seed=1)
+    x0 = torch.randn(B, 4096, device="cuda", generator=torch.Generator(device="cuda").manual_seed(3))
+    x_hist = torch.empty(2, B, 4096, device="cuda")
+    bst.forward(x0, masks=torch.from_numpy(words), x_hist=x_hist)
+    bst.check()
+    assert bst.union_counts().tolist() == [0, 0]
+    _check_layers(syn, bst, x0, x_hist, [np.zeros(0, np.int64)] * 2)
+
+
+@pytest.mark.parametrize("dense", [False, True])
+@pytest.mark.parametrize("B", [1, 12])
+def test_batch_without_hot_neurons(M, B, dense):
+    """A split with no hot neurons (every neuron in the cold store); B = 1 also
+    takes the fused stack kernel through the single-token route."""
+    engine, N, hc_synth = M
+    syn = hc_synth.make_stack(n_layers=2, inter=1024, hot_frac=0.0, rank=64, activation="relu",
+                              act_on_both=True, seed=43, norm_std=0.1, predictors=False)
+    assert syn.hot[0].n == 0
+    bst = syn.batch_stack(max_batch=16, dense_min_batch=1 if dense else 1000)
+    words, bits = _bernoulli_masks(2, B, syn.inter, 0.2, seed=2)
+    x0 = torch.randn(B, 4096, device="cuda", generator=torch.Generator(device="cuda").manual_seed(5))
+    x_hist = torch.empty(2, B, 4096, device="cuda")
+    bst.forward(x0, masks=torch.from_numpy(words), x_hist=x_hist)
+    bst.check()
+    union = [_union_ids(bst, bits[l].numpy(), l) for l in range(2)]
+    assert bst.union_counts().tolist() == [len(u) for u in union]
+    _check_layers(syn, bst, x0, x_hist, union)
+
+
 def test_batch_dense_and_row_scaled_relu(M):
     """dReLU with per-neuron hot scales, every cold record fetched (p = 1)."""
     engine, N, hc_synth = M
