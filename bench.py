@@ -314,7 +314,8 @@ def run_gpu(args):
     x_dev = x_host.to(dev)
     y_host = torch.empty(TOKENS, H).pin_memory()
     y_dev = torch.empty(TOKENS, H, device=dev)
-    launches_per_token = 3            # predictor (2 launches) + fused stack
+    pred0 = st.pred0_in_kernel()      # layer 0's predictor inside the stack kernel
+    launches_per_token = 1 if pred0 else 3          # fused stack (+ 2 predictor launches otherwise)
 
     def step_resident():
         for t in range(TOKENS):
@@ -338,9 +339,9 @@ def run_gpu(args):
     n_hot_local = sum(h.n for h in st.hot) / LAYERS
     share = st.words_n / st.words
     pred_local = 4 * (RANK * H) + share * 4 * (INTER * RANK + INTER)
-    stack_bytes = (LAYERS * n_hot_local * HOT_BYTES + mean_fetched * COLD_BYTES + (LAYERS - 1) * pred_local
-                   + 2 * LAYERS * H * 4)
-    token_bytes = stack_bytes + PRED_BYTES            # + layer-0 predictor launches
+    stack_bytes = (LAYERS * n_hot_local * HOT_BYTES + mean_fetched * COLD_BYTES
+                   + (LAYERS if pred0 else LAYERS - 1) * pred_local + 2 * LAYERS * H * 4)
+    token_bytes = stack_bytes + (0 if pred0 else PRED_BYTES)     # + layer-0 predictor launches
 
     for _ in range(max(args.warmup, 3)):
         step_resident()
@@ -358,9 +359,10 @@ def run_gpu(args):
     for s in range(args.steps):
         evs = ev[s]
         for t in range(TOKENS):
-            st.first_mask(x_dev[t])
+            if not pred0:
+                st.first_mask(x_dev[t])
             evs[t][0].record(stream)
-            st.launch(x_dev[t], False, None, y_dev[t])
+            st.launch(x_dev[t], 2 if pred0 else False, None, y_dev[t])
             evs[t][1].record(stream)
     t_end.record(stream)
     torch.cuda.synchronize()

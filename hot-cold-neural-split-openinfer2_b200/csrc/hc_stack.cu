@@ -99,6 +99,7 @@ struct StackSmem {
   float ystage[H];                  // subgroup partial y (element 32u+k at k*128+u); earlier in the
                                     // layer, the planner's W_down rows RMSNorm_{l+1}(x_l)
   float z[128];                     // planner: bottleneck of the next layer's predictor
+  float rstd0;                      // consumers -> planner: 1 / RMS of x_0 (layer 0's own prediction)
   int2 chunk[H / SPT];              // per 32 elements: (-8 * sum of the fixed-point values, bits of 2^-s)
   float zred[NWARPS];
   float red[NSG][2][SG_WARPS][2 * NB_COLD];
@@ -139,6 +140,7 @@ struct StackParams {
   int relu;
   int both;
   float thr;
+  int pred0;                 // layer 0's mask words are predicted in the kernel too (masks_given == 2)
   uint32_t* bar_count;
   uint32_t* exit_count;
   uint32_t* hot_next;        // [NACC] hot-neuron claims per layer
@@ -266,6 +268,12 @@ __device__ __forceinline__ Split make_split(const StackParams& p, const hc_layer
 // layer l computes its own mask words from its predictor (else they are given or all ones)
 __device__ __forceinline__ bool layer_logits(const StackParams& p, const hc_layer_desc& d, int l) {
   return l > 0 && !p.masks_given && d.pred_w_up != nullptr && rank_ok(d.rank);
+}
+// layer 0 predicts its own mask words in the kernel (requested, and it has a usable predictor)
+__device__ __forceinline__ bool first_pred(const StackParams& p) {
+  if (!p.pred0) return false;
+  const hc_layer_desc& d = p.layers[0];
+  return d.pred_w_up != nullptr && d.pred_w_down_t != nullptr && rank_ok(d.rank);
 }
 __device__ __forceinline__ bool next_pred(const StackParams& p, int l) {
   if (l + 1 >= p.n_layers || p.masks_given) return false;
@@ -807,96 +815,129 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
     auto words_without_predictor = [&](int l) -> uint32_t {
       uint32_t* mrow = p.masks + (size_t)l * p.words;
       if (lane >= nw) return 0u;
-      if (l == 0 || p.masks_given) return __ldcg(mrow + u0 + lane);
+      if ((l == 0 && !p.pred0) || p.masks_given) return __ldcg(mrow + u0 + lane);
       // no predictor: fetch every cold neuron (engine.py:282-283)
       const int valid = min(32, p.inter - 32 * (u0 + lane));
       const uint32_t m = valid >= 32 ? 0xffffffffu : ((1u << valid) - 1u);
       mrow[u0 + lane] = m;
       return m;
     };
-    preload(0);
-    build(0, words_without_predictor(0));
+    // W_down tiles [d0, d1) of layer lp's predictor on the normalised rows
+    // xrow(r) -> z of layer lp (slot lp % NACC), then the tile count
+    auto wdown = [&](const hc_layer_desc& dp, int lp, int d0, int d1, auto xrow) -> bool {
+      const int rank = dp.rank;
+      for (int tile = d0; tile < d1; ++tile) {
+        if (!load_tile(dp.pred_w_down_t + (size_t)tile * WD_ROWS * rank, WD_ROWS * rank * 4, nullptr, 0, 0))
+          return false;
+        const float* t = reinterpret_cast<const float*>(sm.pbuf);
+        for (int r = lane; r < rank; r += 32) {
+          float acc = 0.0f;
+#pragma unroll 8
+          for (int row = 0; row < WD_ROWS; ++row) acc = fmaf(t[row * rank + r], xrow(tile * WD_ROWS + row), acc);
+          atomicAdd(p.zacc + (size_t)(lp % NACC) * 128 + r, acc);
+        }
+        __syncwarp();      // pbuf is reused by the next copy
+      }
+      return true;
+    };
+    auto wdown_count = [&](int lp, int d0, int d1) {
+      if (lane == 0 && d1 > d0) {
+        __threadfence();
+        atomicAdd(p.zdone + lp % NACC, (uint32_t)(d1 - d0));
+      }
+    };
+    // once every CTA's W_down tiles of layer lp are in: the logits of the own
+    // neuron-id range -> own mask words (lane w holds word w), also stored in
+    // masks row lp
+    auto own_logits = [&](const hc_layer_desc& dp, int lp, uint32_t& own) -> bool {
+      const int rank = dp.rank;
+      bool good = true;
+      if (lane == 0) {
+        const uint32_t* cnt = p.zdone + lp % NACC;
+        const uint64_t t0 = globaltimer_ns();
+        uint32_t i = 0;
+        while (ld_acquire_u32(cnt) < (uint32_t)WD_TILES) {
+          if ((++i & 63) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+            good = false;
+            break;
+          }
+          __nanosleep(100);
+        }
+      }
+      if (!__shfl_sync(0xffffffffu, good, 0)) return false;
+      __syncwarp();      // lane 0's acquire orders every lane's reads of z below
+      for (int i = lane; i < rank; i += 32) sm.z[i] = __ldcg(p.zacc + (size_t)(lp % NACC) * 128 + i);
+      __syncwarp();
+      // one W_up tile (32 neurons == one mask word) at a time
+      for (int w = 0; w < nw; ++w) {
+        const int tile = u0 + w;
+        const int rows = min(WU_ROWS, p.inter - tile * WU_ROWS);
+        if (!load_tile(dp.pred_w_up + (size_t)tile * WU_ROWS * rank, rows * rank * 4,
+                       dp.pred_b_up + (size_t)tile * WU_ROWS, rows * 4, WU_ROWS * rank * 4))
+          return false;
+        const float* t = reinterpret_cast<const float*>(sm.pbuf);
+        float acc = 0.0f;
+        if (lane < rows) {
+          // lane = neuron; the rotated start keeps the 32 rows on distinct banks
+          const float* row = t + lane * rank;
+          int k = lane % rank;
+          for (int i = 0; i < rank; ++i) {
+            acc = fmaf(row[k], sm.z[k], acc);
+            k = (k + 1 == rank) ? 0 : k + 1;
+          }
+          acc += t[WU_ROWS * rank + lane];
+        }
+        const uint32_t word = __ballot_sync(0xffffffffu, lane < rows && acc >= p.thr);
+        if (lane == w) own = word;
+        __syncwarp();
+      }
+      if (lane < nw) p.masks[(size_t)lp * p.words + u0 + lane] = own;
+      if (lane == 0) trace_ev(p, lp, 21);
+      return true;
+    };
+    const int nd = H / WD_ROWS;
+    const int d0 = (int)split_lo(nd, c, G), d1 = (int)split_lo(nd, c + 1, G);
+    if (first_pred(p)) {
+      // ---- layer 0's own prediction on RMSNorm_0(x_0) (engine.py:422), as for
+      // the later layers, once the consumers have x_0's RMS
+      const hc_layer_desc& d0l = p.layers[0];
+      if (lane == 0) ok = mbar_wait(&sm.phase0_done, p0phase & 1u, WAIT_LIMIT_NS);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      // the layer-0 arrival is also the one the loop below waits for at l = 0
+      if (!next_pred(p, 0)) ++p0phase;
+      const float rstd0 = sm.rstd0;
+      uint32_t own = 0;
+      if (ok)
+        ok = wdown(d0l, 0, d0, d1, [&](int r) {
+          return __ldg(p.x_in + r) * rstd0 * (d0l.norm_w ? __ldg(d0l.norm_w + r) : 1.0f);
+        });
+      if (ok) wdown_count(0, d0, d1);
+      preload(0);
+      if (ok && nw > 0) ok = own_logits(d0l, 0, own);
+      if (ok) build(0, own);
+    } else {
+      preload(0);
+      build(0, words_without_predictor(0));
+    }
     for (int l = 0; l + 1 < p.n_layers && ok; ++l) {
       const bool pred_next = next_pred(p, l);
       const hc_layer_desc& dn = p.layers[l + 1];
-      const int rank = pred_next ? dn.rank : 0;
       uint32_t own = 0;
       if (pred_next) {
         // ---- W_down rows [d0, d1) of layer l+1's predictor on RMSNorm_{l+1}(x_l)
-        const int nd = H / WD_ROWS;
-        const int d0 = (int)split_lo(nd, c, G), d1 = (int)split_lo(nd, c + 1, G);
         // (one phase per layer with a next predictor, like wdown_done)
         if (lane == 0) ok = mbar_wait(&sm.phase0_done, p0phase & 1u, WAIT_LIMIT_NS);
         ++p0phase;
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
-        for (int tile = d0; tile < d1 && ok; ++tile) {
-          ok = load_tile(dn.pred_w_down_t + (size_t)tile * WD_ROWS * rank, WD_ROWS * rank * 4, nullptr, 0, 0);
-          if (!ok) break;
-          const float* t = reinterpret_cast<const float*>(sm.pbuf);
-          const float* xr = xs + (tile - d0) * WD_ROWS;
-          for (int r = lane; r < rank; r += 32) {
-            float acc = 0.0f;
-#pragma unroll 8
-            for (int row = 0; row < WD_ROWS; ++row) acc = fmaf(t[row * rank + r], xr[row], acc);
-            atomicAdd(p.zacc + (size_t)((l + 1) % NACC) * 128 + r, acc);
-          }
-          __syncwarp();      // pbuf is reused by the next copy
-        }
+        ok = wdown(dn, l + 1, d0, d1, [&](int r) { return xs[r - d0 * WD_ROWS]; });
         if (!ok) break;
-        if (lane == 0) {
-          mbar_arrive(&sm.wdown_done);       // ystage is the consumers' again
-          if (d1 > d0) {
-            __threadfence();
-            atomicAdd(p.zdone + (l + 1) % NACC, (uint32_t)(d1 - d0));
-          }
-        }
+        if (lane == 0) mbar_arrive(&sm.wdown_done);       // ystage is the consumers' again
+        wdown_count(l + 1, d0, d1);
         preload(l + 1);
         if (nw > 0) {
-          // ---- z of layer l+1 is complete once all W_down tiles were added
-          if (lane == 0) {
-            const uint32_t* cnt = p.zdone + (l + 1) % NACC;
-            const uint64_t t0 = globaltimer_ns();
-            uint32_t i = 0;
-            while (ld_acquire_u32(cnt) < (uint32_t)WD_TILES) {
-              if ((++i & 63) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
-                ok = false;
-                break;
-              }
-              __nanosleep(100);
-            }
-          }
-          ok = __shfl_sync(0xffffffffu, ok, 0);
+          ok = own_logits(dn, l + 1, own);
           if (!ok) break;
-          __syncwarp();      // lane 0's acquire orders every lane's reads of z below
-          for (int i = lane; i < rank; i += 32) sm.z[i] = __ldcg(p.zacc + (size_t)((l + 1) % NACC) * 128 + i);
-          __syncwarp();
-          // ---- own logits: one W_up tile (32 neurons == one mask word) at a time
-          for (int w = 0; w < nw && ok; ++w) {
-            const int tile = u0 + w;
-            const int rows = min(WU_ROWS, p.inter - tile * WU_ROWS);
-            ok = load_tile(dn.pred_w_up + (size_t)tile * WU_ROWS * rank, rows * rank * 4,
-                           dn.pred_b_up + (size_t)tile * WU_ROWS, rows * 4, WU_ROWS * rank * 4);
-            if (!ok) break;
-            const float* t = reinterpret_cast<const float*>(sm.pbuf);
-            float acc = 0.0f;
-            if (lane < rows) {
-              // lane = neuron; the rotated start keeps the 32 rows on distinct banks
-              const float* row = t + lane * rank;
-              int k = lane % rank;
-              for (int i = 0; i < rank; ++i) {
-                acc = fmaf(row[k], sm.z[k], acc);
-                k = (k + 1 == rank) ? 0 : k + 1;
-              }
-              acc += t[WU_ROWS * rank + lane];
-            }
-            const uint32_t word = __ballot_sync(0xffffffffu, lane < rows && acc >= p.thr);
-            if (lane == w) own = word;
-            __syncwarp();
-          }
-          if (!ok) break;
-          if (lane < nw) p.masks[(size_t)(l + 1) * p.words + u0 + lane] = own;
-          if (lane == 0) trace_ev(p, l + 1, 21);
         }
       } else {
         preload(l + 1);
@@ -1171,6 +1212,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         sum += __shfl_xor_sync(0xffffffffu, sum, 1);
         sum += __shfl_xor_sync(0xffffffffu, sum, 2);
         if ((t & 3) == 0) sm.chunk[t >> 2] = make_int2(-8 * sum, __float_as_int(isc));
+        if (l == 0 && t == 0) sm.rstd0 = rstd;       // layer 0's own prediction (first_pred)
         if (pred_next) {
           // the rows of this CTA's W_down tiles of the next predictor: RMSNorm_{l+1}(x_l)
           const int r0 = sp.d0 * WD_ROWS, r1 = sp.d1 * WD_ROWS;
@@ -1186,7 +1228,8 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
       if (t == 0) *reinterpret_cast<volatile int32_t*>(&sm.cons_layer) = l;
       named_bar(1, CONS_THREADS);
       if (t == 0) {
-        if (pred_next) mbar_arrive(&sm.phase0_done);     // the planner's W_down rows (xs) are written
+        // the planner's W_down rows (xs), and at layer 0 the RMS of x_0, are written
+        if (pred_next || (l == 0 && first_pred(p))) mbar_arrive(&sm.phase0_done);
         trace_ev(p, l, 1);
       }
 
@@ -1403,6 +1446,7 @@ extern "C" int hc_ffn_stack_tp(const hc_layer_desc* layers, int32_t n_layers, in
                                hc_stream_t stream) {
   if (!layers || n_layers <= 0 || n_layers > 32767 || !x_in || !masks || !x_out || !workspace || !status)
     return HC_ERR_ARG;
+  if (masks_given < 0 || masks_given > 2) return HC_ERR_ARG;
   if (inter <= 0 || inter > 32768 || (inter & 3) != 0 || (act != HC_ACT_SILU && act != HC_ACT_RELU))
     return HC_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(x_in) & 15) || (reinterpret_cast<uintptr_t>(x_out) & 15) ||
@@ -1444,7 +1488,8 @@ extern "C" int hc_ffn_stack_tp(const hc_layer_desc* layers, int32_t n_layers, in
   p.seq_base = tp ? tp->seq_base : 0u;
   p.x_in = x_in;
   p.masks = masks;
-  p.masks_given = masks_given;
+  p.masks_given = masks_given == 1;
+  p.pred0 = masks_given == 2;
   p.x_out = x_out;
   p.x_hist = x_hist;
   p.eps = eps;

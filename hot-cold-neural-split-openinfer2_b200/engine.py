@@ -203,8 +203,15 @@ class FFNStack:
         ones = torch.ones(self.inter, dtype=torch.bool)
         self._all_ones = bits_to_words(ones.numpy(), self.inter).to(self.device)
 
+    def pred0_in_kernel(self) -> bool:
+        """Layer 0's predictor runs inside the stack kernel (hc_ffn_stack with
+        masks_given = 2) -- the kernel supports its rank."""
+        p0 = self.predictors[0]
+        return p0 is not None and 0 < p0.rank <= 96 and p0.rank % 8 == 0
+
     def first_mask(self, x: torch.Tensor):
-        """Layer 0's predicted set from RMSNorm_0(x) (engine.py:422), on device."""
+        """Layer 0's predicted set from RMSNorm_0(x) (engine.py:422), on device
+        (separate predictor launches; ``forward`` lets the stack kernel do it)."""
         p0 = self.predictors[0]
         if p0 is None:
             self.masks[0].copy_(self._all_ones)
@@ -212,9 +219,11 @@ class FFNStack:
             p0.predict_words(x.view(1, -1), self.threshold, norm_w=self.norms[0], eps=self.eps,
                              mask_out=self.masks[0:1])
 
-    def launch(self, x: torch.Tensor, masks_given: bool = False, x_hist: Optional[torch.Tensor] = None,
+    def launch(self, x: torch.Tensor, masks_given=False, x_hist: Optional[torch.Tensor] = None,
                out: Optional[torch.Tensor] = None, trace: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """One hc_ffn_stack launch.  ``trace`` (int64 [L, grid, 40], device)
+        """One hc_ffn_stack launch.  ``masks_given``: False (row 0 of
+        ``self.masks`` holds layer 0's set), True (every row given) or 2 (the
+        kernel predicts layer 0 too).  ``trace`` (int64 [L, grid, 40], device)
         (zeroed) receives per-CTA phase timestamps and waits
         (see include/hotcold.h)."""
         out = self.x_out if out is None else out
@@ -223,8 +232,9 @@ class FFNStack:
             tp = N.TPDesc(size=self.tp.size, rank=self.tp.rank, words_lo=self.words_lo, words_n=self.words_n,
                           peer_buf=N.ptr(self.tp.peer_buf), seq_base=(self.tp.launches * self.L) & 0xFFFFFFFF)
             self.tp.launches += 1
+        mg = 2 if masks_given == 2 else (1 if masks_given else 0)
         N.check(N.lib.hc_ffn_stack_tp(N.ptr(self.desc_dev), self.L, self.inter, N.ptr(x), N.ptr(self.masks),
-                                      1 if masks_given else 0, N.ptr(out), N.ptr(x_hist), self.eps, self.act,
+                                      mg, N.ptr(out), N.ptr(x_hist), self.eps, self.act,
                                       1 if self.act_on_both else 0, self.thr, self.grid, N.ptr(self.ws),
                                       N.ptr(self.status), N.ptr(trace),
                                       __import__("ctypes").byref(tp) if tp is not None else None,
@@ -307,6 +317,8 @@ class FFNStack:
         if masks is not None:
             self.masks.copy_(masks)
             return self.launch(x, True, x_hist, out)
+        if self.pred0_in_kernel():
+            return self.launch(x, 2, x_hist, out)
         self.first_mask(x)
         return self.launch(x, False, x_hist, out)
 
@@ -324,8 +336,7 @@ class FFNStack:
         xi, yo = self._io_in[:T], self._io_out[:T]
         xi.copy_(x_host, non_blocking=True)
         for t in range(T):
-            self.first_mask(xi[t])
-            self.launch(xi[t], False, None, yo[t])
+            self.forward(xi[t], out=yo[t])
         y_host.copy_(yo, non_blocking=True)
         return y_host
 

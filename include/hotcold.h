@@ -229,12 +229,16 @@ HC_API int64_t hc_ffn_stack_workspace_bytes(int32_t grid, int32_t inter);
  *              [c*W/grid, (c+1)*W/grid), W = ceil(inter/32), and at most 1024
  *              of them, i.e. ceil(W/grid)*32 <= 1024 (else HC_ERR_UNSUPPORTED)
  *   x_in       [4096] fp32 input hidden state (batch 1)
- *   masks      [n_layers][ceil(inter/32)] uint32 predicted-active bits: row 0
- *              must be filled by the caller; row l+1 is written by the kernel
- *              from layer l+1's predictor (all ones when that layer has no
- *              predictor -- the reference's fetch-everything fallback,
- *              engine.py:282-283) unless `masks_given` = 1, in which case
- *              every row is an input.  The cold neurons a layer computes are
+ *   masks      [n_layers][ceil(inter/32)] uint32 predicted-active bits.
+ *              masks_given = 0: row 0 is filled by the caller (e.g. by
+ *              hc_predictor_forward on x_in); row l+1 is written by the kernel
+ *              from layer l+1's predictor on RMSNorm_{l+1}(x_l) (all ones when
+ *              that layer has no predictor -- the reference's fetch-everything
+ *              fallback, engine.py:282-283).  masks_given = 2: the same, and
+ *              row 0 too is written by the kernel, from layer 0's predictor on
+ *              RMSNorm_0(x_in) (engine.py:422; all ones without a predictor),
+ *              saving the caller's predictor launches.  masks_given = 1: every
+ *              row is an input.  The cold neurons a layer computes are
  *              masks[l] & fetch_bits.
  *   x_out      [4096] fp32 output; x_hist optional [n_layers][4096] fp32
  *   eps        RMSNorm epsilon; act = HC_ACT_*; act_on_both = dReLU form

@@ -82,6 +82,33 @@ def test_stack_predictor_lookahead(M, act, both, grid):
     assert n_flip <= 4
 
 
+@pytest.mark.parametrize("grid", [0, 5])
+def test_stack_layer0_prediction_in_kernel(M, grid):
+    """forward() lets the stack kernel predict layer 0 too (masks_given = 2);
+    the separate predictor launches (first_mask) give the same sets outside the
+    float rounding band, and the same outputs within the kernel's bar."""
+    engine, hc_synth, predictor, splitter = M
+    syn = hc_synth.make_stack(n_layers=3, inter=2048, hot_frac=0.2, rank=64, activation="relu", act_on_both=True,
+                              seed=12, norm_std=0.1)
+    st = syn.stack(grid=grid)
+    assert st.pred0_in_kernel()
+    x0 = torch.randn(4096, device="cuda", generator=torch.Generator(device="cuda").manual_seed(8))
+    hist_a = torch.empty(3, 4096, device="cuda")
+    st.forward(x0, x_hist=hist_a)                       # in-kernel layer-0 prediction
+    st.check()
+    masks_a = st.masks.clone()
+    n_flip = _check_stack(M, syn, st, x0, hist_a, masks_a.cpu().numpy(), True)
+    assert n_flip <= 3
+    st.first_mask(x0)                                   # separate launches, then the kernel
+    hist_b = torch.empty(3, 4096, device="cuda")
+    st.launch(x0, False, hist_b)
+    st.check()
+    assert int((masks_a[0] ^ st.masks[0]).ne(0).sum()) <= 2
+    if torch.equal(masks_a, st.masks):
+        rel = ((hist_a - hist_b).double().norm() / (hist_b.double() - x0.double()).norm()).item()
+        assert rel < TOL, rel          # float reductions: the last bits differ between runs
+
+
 def test_stack_given_masks_bernoulli(M):
     engine, hc_synth, predictor, splitter = M
     syn = hc_synth.make_stack(n_layers=3, inter=2048, hot_frac=0.2, rank=64, activation="silu",
