@@ -56,8 +56,11 @@ def main():
         for t in range(args.tokens):
             if trace is not None:
                 trace.zero_()          # keep the last token's stamps and waits
-            st.first_mask(x[t])
-            st.launch(x[t], False, None, None, trace)
+            if st.pred0_in_kernel():
+                st.launch(x[t], 2, None, None, trace)      # layer 0's predictor inside the kernel
+            else:
+                st.first_mask(x[t])
+                st.launch(x[t], False, None, None, trace)
         torch.cuda.synchronize()
         st.check()
         if trace is not None and rank == 0:
