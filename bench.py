@@ -174,15 +174,16 @@ def run_reference(args):
 # ----------------------------------------------------------------------------
 # GPU arm
 # ----------------------------------------------------------------------------
-def cold_dequant_bench(store, reps: int = 5):
+def cold_dequant_bench(store, reps: int = 5, ks=(256, 1024, 4096, 8192)):
     """gather K seeded-random records per layer for all 32
-    layers, dequantised to bf16 (6336 B read + 24576 B written per neuron)."""
+    layers, dequantised to bf16 (6336 B read + 24576 B written per neuron).
+    With a store in pinned host memory the records cross PCIe (`read_gbs`)."""
     import torch
     peak, _ = _peaks()
     out = {}
     g = torch.Generator(device=store.device).manual_seed(7)
     nrec = int(store.n_rec_host.min())
-    for K in (256, 1024, 4096, 8192):
+    for K in ks:
         rec = torch.randint(0, nrec, (store.n_layers, K), generator=g, device=store.device, dtype=torch.int32)
         buf = torch.empty(3, store.n_layers, K, H, dtype=torch.bfloat16, device=store.device)
         for _ in range(2):
@@ -198,7 +199,8 @@ def cold_dequant_bench(store, reps: int = 5):
         neurons = K * store.n_layers
         gbs = neurons * (COLD_BYTES + 3 * H * 2) / (ms * 1e-3) / 1e9
         out[str(K)] = {"ms": round(ms, 4), "neurons_per_s": neurons / (ms * 1e-3), "gbs": round(gbs, 1),
-                       "frac": round(gbs / peak, 4)}
+                       "frac": round(gbs / peak, 4),
+                       "read_gbs": round(neurons * COLD_BYTES / (ms * 1e-3) / 1e9, 1)}
         del buf
     store.check()
     return out
@@ -415,6 +417,16 @@ def run_gpu(args):
         bd_tp = batched_decode_bench(syn, args.steps, args.warmup, batches=(64,), shard=(rank, ws))
     if rank == 0:
         dq = cold_dequant_bench(syn.store) if ws == 1 else None
+        dq_pinned = None
+        if ws == 1:
+            # the same gather with the cold file image in pinned host memory (PCIe-bound)
+            from splitter import ColdWeightStore
+            pstore = ColdWeightStore(syn.store.image, syn.cold_index, {"hidden_dim": H, "intermediate_dim": INTER},
+                                     device=dev, source="pinned")
+            dq_pinned = cold_dequant_bench(pstore, reps=3, ks=(256, 1024, 4096))
+            for v in dq_pinned.values():
+                v.pop("frac", None)            # bound by PCIe, not HBM
+            del pstore
         bd = batched_decode_bench(syn, args.steps, args.warmup) if ws == 1 else None
         cpu = cpu_reference(4, 0, layers_per_step=2, budget_s=25.0) if ws == 1 else None
         line = {"metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
@@ -449,6 +461,10 @@ def run_gpu(args):
         if dq is not None:
             line["cold_dequant"] = {"unit": "GB/s", "peak": peak, "bytes_per_neuron": COLD_BYTES + 3 * H * 2,
                                     "layers": LAYERS, "out_dtype": "bf16", "by_K": dq}
+        if dq_pinned is not None:
+            line["cold_dequant_pinned"] = {"unit": "GB/s", "source": "pinned host memory read over PCIe by the "
+                                           "gather kernel; read_gbs = 6336 B per neuron / time",
+                                           "layers": LAYERS, "out_dtype": "bf16", "by_K": dq_pinned}
         print(json.dumps(line), flush=True)
     if ws > 1:
         dist.barrier()
