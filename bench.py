@@ -414,7 +414,11 @@ def run_gpu(args):
         torch.cuda.synchronize()
         tp.close()
         # configs[4] across the GPUs: B = 64, every layer's neurons sharded, one NCCL all-reduce per layer
-        bd_tp = batched_decode_bench(syn, args.steps, args.warmup, batches=(64,), shard=(rank, ws))
+        # (every rank takes the same path; a failure is reported in the line instead of losing it)
+        try:
+            bd_tp = batched_decode_bench(syn, args.steps, args.warmup, batches=(64,), shard=(rank, ws))
+        except Exception as e:          # noqa: BLE001 -- reported, not hidden
+            bd_tp = {"error": f"{type(e).__name__}: {str(e)[:160]}"}
     if rank == 0:
         dq = cold_dequant_bench(syn.store) if ws == 1 else None
         dq_pinned = None

@@ -77,5 +77,8 @@ def test_sharded_batch_matches_one_gpu(tmp_path):
             d_tp = r0[f"tp{B}"][l].double() - prev
             d_one = r0[f"one{B}"][l].double() - prev
             rel = ((d_tp - d_one).norm() / d_one.norm()).item()
-            assert rel < 1e-4, (B, l, rel)      # same f16 operands, different float summation order only
+            # Float summation order differs between the sharded and the one-GPU runs, so
+            # f16-rounded operands (RMSNorm(x), activations) can differ in their last bit
+            # from layer 1 on; the batched parity bar (f16 operands) applies.
+            assert rel < 2e-3, (B, l, rel)
             prev = r0[f"one{B}"][l].double()
