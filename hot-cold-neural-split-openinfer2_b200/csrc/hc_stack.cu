@@ -6,7 +6,9 @@
 // neurons selected by the predictor, summed in-kernel (exact by linearity of
 // down_proj in the neuron dimension, engine.py:184-188).  Layer l+1's
 // predictor runs on layer l's input, as DesdemonaEngine.forward's lookahead
-// prefetch does (engine.py:421-438).
+// prefetch does (engine.py:421-438).  Layer 0's mask words are the caller's
+// (masks_given = 0) or, with masks_given = 2, predicted by the kernel itself
+// at its start from RMSNorm_0(x_0) (engine.py:422), the same way.
 //
 // One persistent cooperative launch, one CTA per SM, one grid barrier per
 // layer.  CTA c owns a contiguous neuron-id range (its predictor logits and
