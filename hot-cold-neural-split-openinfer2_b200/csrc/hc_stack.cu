@@ -267,10 +267,6 @@ __device__ __forceinline__ Split make_split(const StackParams& p, const hc_layer
   s.d1 = pred_next ? (int)split_lo(nd, c + 1, G) : 0;
   return s;
 }
-// layer l computes its own mask words from its predictor (else they are given or all ones)
-__device__ __forceinline__ bool layer_logits(const StackParams& p, const hc_layer_desc& d, int l) {
-  return l > 0 && !p.masks_given && d.pred_w_up != nullptr && rank_ok(d.rank);
-}
 // layer 0 predicts its own mask words in the kernel (requested, and it has a usable predictor)
 __device__ __forceinline__ bool first_pred(const StackParams& p) {
   if (!p.pred0) return false;
