@@ -1116,6 +1116,18 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
       const Split sp = make_split(p, d, pred_next, c, G);
       const hc_layer_desc* dn = pred_next ? &p.layers[l + 1] : nullptr;
 
+      // this layer's RMSNorm weights, loaded before the barrier wait below so
+      // that their latency hides behind it
+      float nw[EPT];
+      if (d.norm_w) {
+        const float4* wsrc = reinterpret_cast<const float4*>(d.norm_w + EPT * t);
+        const float4 w0 = __ldg(wsrc), w1 = __ldg(wsrc + 1);
+        nw[0] = w0.x; nw[1] = w0.y; nw[2] = w0.z; nw[3] = w0.w; nw[4] = w1.x; nw[5] = w1.y; nw[6] = w1.z; nw[7] = w1.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < EPT; ++i) nw[i] = 1.0f;
+      }
+
       // ---- layer boundary: x_l = x_{l-1} + y_{l-1} once every CTA has added its part
       float x[EPT];
       if (l == 0) {
@@ -1159,15 +1171,6 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
 
       // ---- RMSNorm (engine.py:295; torch.nn.RMSNorm) -> f16 and fixed-point copies
       {
-        float nw[EPT];
-        if (d.norm_w) {
-          const float4* wsrc = reinterpret_cast<const float4*>(d.norm_w + EPT * t);
-          const float4 w0 = __ldg(wsrc), w1 = __ldg(wsrc + 1);
-          nw[0] = w0.x; nw[1] = w0.y; nw[2] = w0.z; nw[3] = w0.w; nw[4] = w1.x; nw[5] = w1.y; nw[6] = w1.z; nw[7] = w1.w;
-        } else {
-#pragma unroll
-          for (int i = 0; i < EPT; ++i) nw[i] = 1.0f;
-        }
         float ss = 0.0f;
 #pragma unroll
         for (int i = 0; i < EPT; ++i) ss = fmaf(x[i], x[i], ss);
