@@ -56,6 +56,13 @@ def test_argument_errors_are_reported_without_a_device():
                                       None, None, None, None, None, None, None, None) == N.HC_ERR_ARG
     assert N.lib.hc_ffn_stack(None, 1, 64, None, None, 0, None, None, 1e-5, 0, 0, 0.0, 0, None, None,
                               None, None) == N.HC_ERR_ARG
+    # masks_given is 0 (row 0 given), 1 (all given) or 2 (layer 0 predicted in the kernel); checked
+    # before any device work, so fake aligned pointers suffice here
+    fake = 256
+    assert N.lib.hc_ffn_stack(fake, 1, 64, fake, fake, 3, fake, None, 1e-5, 0, 0, 0.0, 0, fake, fake,
+                              None, None) == N.HC_ERR_ARG
+    assert N.lib.hc_ffn_stack(fake, 1, 64, fake, fake, -1, fake, None, 1e-5, 0, 0, 0.0, 0, fake, fake,
+                              None, None) == N.HC_ERR_ARG
     assert N.lib.hc_map_ids(None, -1, None, None, None, None, None) == N.HC_ERR_ARG
     assert N.lib.hc_union_cold(None, 1, 32, 1024, None, None, None, None, None) == N.HC_ERR_ARG
     assert N.lib.hc_union_cold_layers(None, 2, 0, 1, 32, 1024, None, None, None, 0, None, None, 0,
