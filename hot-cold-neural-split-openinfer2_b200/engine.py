@@ -22,6 +22,7 @@ from pathlib import Path
 from typing import Optional, Sequence
 
 import torch
+import torch.distributed
 import torch.nn as nn
 import torch.nn.functional as F
 
@@ -514,7 +515,6 @@ class BatchStack:
                         "hc_ffn_batch_layer")
             else:
                 # this GPU's share of the layer into part, then one all-reduce of [B, 4096]
-                import torch.distributed as dist
                 part = self.part[:B]
                 part.zero_()
                 N.check(N.lib.hc_ffn_batch_layer_partial(
@@ -522,7 +522,7 @@ class BatchStack:
                     N.ptr(self.count[l:l + 1]), self.max_cold[l], N.ptr(flags[l]) + self.rec_lo[l], self.eps,
                     self.act, 1 if self.act_on_both else 0, N.ptr(self.ws), N.ptr(part), N.ptr(self.status), s),
                     "hc_ffn_batch_layer_partial")
-                dist.all_reduce(part, group=self.group)
+                torch.distributed.all_reduce(part, group=self.group)
                 y.add_(part)
             if x_hist is not None:
                 x_hist[l].copy_(y)
