@@ -213,7 +213,7 @@ def batched_decode_bench(syn, steps: int, warmup: int, batches=(1, 8, 32, 64), s
     CUDA graph per batch size; B = 1 runs the fused batch-1 stack kernel.
     ``shard=(rank, size)`` (every rank calls this): each GPU streams its share
     of every layer and the partial outputs are summed by one NCCL all-reduce
-    per layer, inside the captured graph; times are the max over ranks.  `value` is device-resident; `e2e` adds the
+    per layer, launched eagerly; times are the max over ranks.  `value` is device-resident; `e2e` adds the
     pinned host->device copy of the B inputs and the device->host copy of the
     outputs to every step."""
     import torch
@@ -234,12 +234,12 @@ def batched_decode_bench(syn, steps: int, warmup: int, batches=(1, 8, 32, 64), s
         bst.forward(x_in, masks=masks, out=y)                   # first call outside capture
         torch.cuda.synchronize()
         # B = 1 runs the fused stack (one cooperative launch per token): launched
-        # directly; larger batches replay one captured graph per step
+        # directly; larger batches replay one captured graph per step.  Sharded
+        # batches launch eagerly: every all-reduce stays under the process
+        # group's timeout (a collective inside a replayed graph is not watched).
         g = None
-        if B > 1:
-            if shard is not None and shard[1] > 1:
-                dist.barrier()
-                torch.cuda.synchronize()
+        sharded = shard is not None and shard[1] > 1
+        if B > 1 and not sharded:
             g = torch.cuda.CUDAGraph()
             stream.wait_stream(torch.cuda.current_stream())
             try:
@@ -255,6 +255,9 @@ def batched_decode_bench(syn, steps: int, warmup: int, batches=(1, 8, 32, 64), s
         for _ in range(max(warmup, 3)):
             step()
         torch.cuda.synchronize()
+        if sharded:
+            dist.barrier()                      # the ranks start the timed steps together
+            torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(steps):
