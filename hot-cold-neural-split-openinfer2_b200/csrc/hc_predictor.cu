@@ -16,6 +16,8 @@
 //      mask word; the last CTA compacts row 0 into the ordered id list.
 #include "hc_common.cuh"
 
+#include <cuda.h>
+
 #include <mutex>
 
 namespace hc {
@@ -214,6 +216,24 @@ extern "C" int64_t hc_predictor_workspace_bytes(int32_t batch, int32_t rank, int
   return 256 + (int64_t)sizeof(float) * ((H / PRED_KCHUNK) * batch * rank + batch * rank);
 }
 
+namespace hc {
+// Host-side argument checks shared by both entry points (HC_OK or HC_ERR_ARG),
+// done before anything is enqueued.
+static int pred_check_args(const float* x, int32_t batch, const float* w_down, const float* w_up, const float* b_up,
+                           int32_t rank, int32_t inter, const uint32_t* mask_out, const uint32_t* fetch_bits,
+                           const int32_t* ids_out, const int32_t* count_out) {
+  if (!x || !w_down || !w_up || !b_up || !mask_out) return HC_ERR_ARG;
+  if (batch <= 0 || batch > PRED_MAX_BATCH || rank <= 0 || rank > PRED_MAX_RANK || (rank & 3) != 0 ||
+      inter <= 0 || inter > TABLE_SIZE)
+    return HC_ERR_ARG;
+  if (fetch_bits && (!ids_out || !count_out)) return HC_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(w_down) & 15) || (reinterpret_cast<uintptr_t>(w_up) & 15) ||
+      (reinterpret_cast<uintptr_t>(x) & 15))
+    return HC_ERR_ARG;
+  return HC_OK;
+}
+}  // namespace hc
+
 extern "C" int hc_predictor_forward(const float* x, int32_t batch, const float* norm_w, float eps,
                                     const float* w_down, const float* w_up,
                                     const float* b_up, int32_t rank, int32_t inter, float logit_threshold,
@@ -222,14 +242,9 @@ extern "C" int hc_predictor_forward(const float* x, int32_t batch, const float* 
                                     int32_t* rec_out, int32_t* count_out, void* workspace, int32_t* status,
                                     hc_stream_t stream) {
   (void)status;
-  if (!x || !w_down || !w_up || !b_up || !mask_out || !workspace) return HC_ERR_ARG;
-  if (batch <= 0 || batch > PRED_MAX_BATCH || rank <= 0 || rank > PRED_MAX_RANK || (rank & 3) != 0 ||
-      inter <= 0 || inter > TABLE_SIZE)
-    return HC_ERR_ARG;
-  if (fetch_bits && (!ids_out || !count_out)) return HC_ERR_ARG;
-  if ((reinterpret_cast<uintptr_t>(w_down) & 15) || (reinterpret_cast<uintptr_t>(w_up) & 15) ||
-      (reinterpret_cast<uintptr_t>(workspace) & 15) || (reinterpret_cast<uintptr_t>(x) & 15))
-    return HC_ERR_ARG;
+  const int chk = pred_check_args(x, batch, w_down, w_up, b_up, rank, inter, mask_out, fetch_bits, ids_out, count_out);
+  if (chk != HC_OK) return chk;
+  if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 15)) return HC_ERR_ARG;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   PredWs ws = pred_ws(workspace, batch, rank);
   pred_down_kernel<<<H / PRED_KCHUNK, 256, 0, s>>>(x, batch, norm_w, eps, w_down, rank, ws);
@@ -255,9 +270,42 @@ constexpr size_t STATIC_PRED_BYTES =
     256 + sizeof(float) * ((size_t)(H / PRED_KCHUNK) * STATIC_PRED_MAX_BR + STATIC_PRED_MAX_BR);
 static __device__ __align__(256) unsigned char g_pred_scratch[STATIC_PRED_BYTES];
 
+// The array's device address, looked up once per device and context: a new
+// context on the same ordinal (after cudaDeviceReset) loads the module again,
+// so the cached address is keyed on the driver's unique context id.
 constexpr int MAX_DEVICES = 64;
-static void* g_pred_scratch_addr[MAX_DEVICES] = {};
+struct ScratchAddr {
+  void* ptr = nullptr;
+  unsigned long long ctx_id = 0;
+};
+static ScratchAddr g_pred_scratch_addr[MAX_DEVICES];
 static std::mutex g_pred_scratch_mu;
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+// Unique id of the calling thread's current context (0 when it cannot be read).
+static unsigned long long current_ctx_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static bool looked_up = false;
+  if (!looked_up) {
+    void* f1 = nullptr;
+    void* f2 = nullptr;
+    cudaDriverEntryPointQueryResult q1, q2;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f1, cudaEnableDefault, &q1) == cudaSuccess &&
+        q1 == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(f1);
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &f2, cudaEnableDefault, &q2) == cudaSuccess &&
+        q2 == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(f2);
+    looked_up = true;
+  }
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
 }  // namespace hc
 
 extern "C" int hc_predictor_forward_static(const float* x, int32_t batch, const float* norm_w, float eps,
@@ -266,18 +314,24 @@ extern "C" int hc_predictor_forward_static(const float* x, int32_t batch, const 
                                            float* probs_out, float* logits_out, const uint32_t* fetch_bits,
                                            const int32_t* table, int32_t* ids_out, int32_t* rec_out,
                                            int32_t* count_out, int32_t* status, hc_stream_t stream) {
-  if (batch <= 0 || rank <= 0 || (int64_t)batch * rank > STATIC_PRED_MAX_BR) return HC_ERR_UNSUPPORTED;
+  // every argument is checked before the shared array is touched
+  const int chk = pred_check_args(x, batch, w_down, w_up, b_up, rank, inter, mask_out, fetch_bits, ids_out, count_out);
+  if (chk != HC_OK) return chk;
+  if ((int64_t)batch * rank > STATIC_PRED_MAX_BR) return HC_ERR_UNSUPPORTED;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) return HC_ERR_CUDA;
   void* ws = nullptr;
   {
-    // first call on this device (current device): resolve the array's device address once
+    // first call on this device (and context): resolve the array's device address
+    const unsigned long long ctx = current_ctx_id();
     std::lock_guard<std::mutex> lock(g_pred_scratch_mu);
-    ws = g_pred_scratch_addr[dev];
-    if (ws == nullptr) {
+    ScratchAddr& a = g_pred_scratch_addr[dev];
+    if (a.ptr == nullptr || ctx == 0 || a.ctx_id != ctx) {
       if (cudaGetSymbolAddress(&ws, g_pred_scratch) != cudaSuccess || ws == nullptr) return HC_ERR_CUDA;
-      g_pred_scratch_addr[dev] = ws;
+      a.ptr = ws;
+      a.ctx_id = current_ctx_id();     // the lookup made the device's context current
     }
+    ws = a.ptr;
   }
   // the array keeps the previous call's contents: restart the two completion counters at zero
   if (cudaMemsetAsync(ws, 0, 256, reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess) return HC_ERR_CUDA;

@@ -164,12 +164,15 @@ HC_API int hc_predictor_forward(const float* x, int32_t batch, const float* norm
  * that owns every allocation).  The scratch is a file-scope device array of
  * about 66 KB inside the library (held by every GPU that loads it until the
  * process exits), so it supports batch * rank <= 512 and returns
- * HC_ERR_UNSUPPORTED beyond that without launching anything.  The first call
- * on a device looks up that array's address (cudaGetSymbolAddress) for the
- * current device; make that first call before any stream capture.  Each call
- * clears the array's counters on `stream` first; calls that overlap on the
- * GPU share the array and race, so serialise them (one stream, or events).
- * Nothing here calls cudaMalloc or cudaFree.
+ * HC_ERR_UNSUPPORTED beyond that without launching anything.  Bad arguments
+ * return HC_ERR_ARG, as for hc_predictor_forward, before anything is
+ * enqueued.  The first call on a device looks up that array's address
+ * (cudaGetSymbolAddress) for the current device and context, and again after
+ * the device's context was replaced (cudaDeviceReset); make that first call
+ * before any stream capture.  Each call clears the array's counters on
+ * `stream` first; calls that overlap on the GPU share the array and race, so
+ * serialise them (one stream, or events).  Nothing here calls cudaMalloc or
+ * cudaFree.
  */
 HC_API int hc_predictor_forward_static(const float* x, int32_t batch, const float* norm_w, float eps,
                                        const float* w_down, const float* w_up, const float* b_up,

@@ -64,6 +64,19 @@ def test_argument_errors_are_reported_without_a_device():
     assert N.lib.hc_ffn_stack(fake, 1, 64, fake, fake, -1, fake, None, 1e-5, 0, 0, 0.0, 0, fake, fake,
                               None, None) == N.HC_ERR_ARG
     assert N.lib.hc_map_ids(None, -1, None, None, None, None, None) == N.HC_ERR_ARG
+    # the allocation-free predictor checks its arguments before it touches its device array:
+    # non-positive sizes and missing pointers are argument errors, as for every other entry point
+    for batch, rank in ((0, 64), (-1, 64), (1, 0), (1, -8)):
+        assert N.lib.hc_predictor_forward_static(fake, batch, None, 0.0, fake, fake, fake, rank, 1024, 0.0, fake,
+                                                 None, None, None, None, None, None, None, None,
+                                                 None) == N.HC_ERR_ARG, (batch, rank)
+    assert N.lib.hc_predictor_forward_static(None, 1, None, 0.0, fake, fake, fake, 64, 1024, 0.0, fake, None,
+                                             None, None, None, None, None, None, None, None) == N.HC_ERR_ARG
+    assert N.lib.hc_predictor_forward_static(fake, 1, None, 0.0, fake, fake, fake, 64, 1024, 0.0, None, None,
+                                             None, None, None, None, None, None, None, None) == N.HC_ERR_ARG
+    # an unaligned input row is rejected too (x + 4 bytes)
+    assert N.lib.hc_predictor_forward_static(fake + 4, 1, None, 0.0, fake, fake, fake, 64, 1024, 0.0, fake, None,
+                                             None, None, None, None, None, None, None, None) == N.HC_ERR_ARG
     assert N.lib.hc_union_cold(None, 1, 32, 1024, None, None, None, None, None) == N.HC_ERR_ARG
     assert N.lib.hc_union_cold_layers(None, 2, 0, 1, 32, 1024, None, None, None, 0, None, None, 0,
                                       None) == N.HC_ERR_ARG
