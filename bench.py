@@ -18,7 +18,6 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -113,15 +112,18 @@ def _physical_gpu(local: int) -> int:
     return local
 
 
+TRAFFIC_JSON = os.path.join(REPO, "profiles", "ffn_stack_traffic.json")
+
+
 def _profile_traffic():
-    """dram bytes per hc_ffn_stack launch from the committed ncu summary."""
-    path = os.path.join(REPO, "profiles", "ffn_stack_32L_decode.md")
+    """DRAM bytes per hc_ffn_stack launch, from the committed ncu summary
+    (profiles/ffn_stack_traffic.json: dram__bytes_read.sum + write.sum of a
+    capture, scaled to one 32-layer launch)."""
     try:
-        txt = open(path).read()
-    except OSError:
+        with open(TRAFFIC_JSON) as f:
+            return float(json.load(f)["traffic_bytes_per_launch"])
+    except (OSError, KeyError, ValueError):
         return None
-    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", txt)
-    return float(m.group(1)) if m else None
 
 
 # ----------------------------------------------------------------------------
@@ -148,7 +150,20 @@ def cpu_reference(steps: int, warmup: int, layers_per_step: int = 2, budget_s: f
             break
     per_layer = sum(times) / (len(times) * layers_per_step)
     tok_s = 1.0 / (per_layer * LAYERS)
+    # read_neurons alone (splitter.py:354-403 through the port), 256 seeded ids per call
+    store = layers[0]["store"]
+    rng = __import__("numpy").random.default_rng(7)
+    tab = store.record_index_table(0)
+    present = __import__("numpy").nonzero(tab >= 0)[0]
+    ids = rng.choice(present, size=min(256, len(present)), replace=False).tolist()
+    n_read, t_read = 0, 0.0
+    while t_read < 2.0:
+        t0 = time.perf_counter()
+        store.read_neurons(0, 0, ids)
+        t_read += time.perf_counter() - t0
+        n_read += len(ids)
     return {"value": tok_s, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "read_neurons_per_s": n_read / t_read,
             "sample": f"{len(times)} token(s) x {layers_per_step} of 32 layers (same geometry/seeds class, "
                       f"~{int(statistics.mean(fetched))} cold neurons fetched per layer), timed per layer and "
                       f"scaled to 32 layers",
@@ -291,6 +306,39 @@ def batched_decode_bench(syn, steps: int, warmup: int, batches=(1, 8, 32, 64), s
                        "graph": g is not None}
         del g
     return out
+
+
+def config0_quality(dev):
+    """one 4096/14336 SwiGLU layer, hot 20% FP8 with per-row absmax
+    scales, cold 80% INT4, one N(0, 1) token, Bernoulli(0.1) active cold mask,
+    run through the fused stack kernel; the hot+cold output against the dense
+    fp32 FFN over the same neurons (hot + active cold), computed in float64 on
+    the host as the checker.  The reference reports 9.5-17.5% for its
+    mixed-precision split against fp32 (its BENCHMARKS.md:41)."""
+    import numpy as np
+    import torch
+    import hc_synth
+    syn = hc_synth.make_stack(n_layers=1, inter=INTER, hot_frac=0.2, activation="silu", act_on_both=False, seed=0,
+                              row_scale=True, predictors=False, keep_dense=True, device=dev)
+    masks = hc_synth.bernoulli_words(1, 1, INTER, 0.1, seed=2, device=dev)[:, 0].contiguous()
+    x0 = torch.randn(H, device=dev, generator=torch.Generator(device=dev).manual_seed(1))
+    st = syn.stack(with_predictors=False)
+    y = st.forward(x0, masks=masks).double().cpu().numpy()
+    st.check()
+    gate, up, down, hot_ids = (t.numpy().astype(np.float64) for t in syn.extra["dense"][0])
+    from splitter import words_to_bits
+    active = words_to_bits(masks[0], INTER) & words_to_bits(st.fetch[0], INTER)
+    ids = np.concatenate([hot_ids.astype(np.int64), np.nonzero(active)[0]])
+    x = x0.double().cpu().numpy()
+    xn = x / np.sqrt(np.mean(x * x) + syn.eps)
+    g, u = gate[ids] @ xn, up[ids] @ xn
+    dense = (g / (1.0 + np.exp(-g)) * u) @ down[:, ids].T
+    rel = float(np.linalg.norm((y - x) - dense) / np.linalg.norm(dense))
+    return {"workload": "configs[0]: 1 SwiGLU layer 4096/14336, hot 20% FP8 e4m3 with per-row absmax scale, cold 80% "
+                        "INT4 records, 1 N(0,1) token, Bernoulli(0.1) active cold mask",
+            "neurons": int(len(ids)), "cold_active": int(active.sum()),
+            "rel_l2_vs_dense_fp32": round(rel, 4),
+            "reference_figure": "9.5-17.5% (mixed FP8/INT4 split vs fp32, reference BENCHMARKS.md:41)"}
 
 
 def run_gpu(args):
@@ -436,6 +484,7 @@ def run_gpu(args):
             del pstore
         bd = batched_decode_bench(syn, args.steps, args.warmup) if ws == 1 else None
         cpu = cpu_reference(4, 0, layers_per_step=2, budget_s=25.0) if ws == 1 else None
+        q0 = config0_quality(dev) if ws == 1 else None
         line = {"metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "e4m3/int4 weights, fp32 accumulate",
@@ -455,6 +504,8 @@ def run_gpu(args):
                 "clocks": clocks}
         if cpu is not None:
             line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        if q0 is not None:
+            line["config0_quality"] = q0
         if bd is not None:
             line["batched_decode"] = {"workload": "configs[4] on 1 GPU: 32L 4096/14336 stack, B tokens, per-token "
                                                   "Bernoulli(0.1) masks unioned per layer, tcgen05 GEMMs",
@@ -468,6 +519,13 @@ def run_gpu(args):
         if dq is not None:
             line["cold_dequant"] = {"unit": "GB/s", "peak": peak, "bytes_per_neuron": COLD_BYTES + 3 * H * 2,
                                     "layers": LAYERS, "out_dtype": "bf16", "by_K": dq}
+            if cpu is not None:
+                # the same read (record lookup + 3 x dequantize_int4 per neuron) on the host cores, same run
+                rate = cpu["read_neurons_per_s"]
+                line["cold_dequant"]["cpu_read_neurons_per_s"] = round(rate, 1)
+                line["cold_dequant"]["cpu_sample"] = "read_neurons of 256 seeded ids per call, repeated for 2 s"
+                for v in dq.values():
+                    v["vs_cpu"] = round(v["neurons_per_s"] / rate, 1)
         if dq_pinned is not None:
             line["cold_dequant_pinned"] = {"unit": "GB/s", "source": "pinned host memory read over PCIe by the "
                                            "gather kernel; read_gbs = 6336 B per neuron / time",
@@ -479,14 +537,109 @@ def run_gpu(args):
     return line
 
 
+# ----------------------------------------------------------------------------
+# Profiling targets (small cases for ncu captures, launch lists and traces)
+# ----------------------------------------------------------------------------
+def run_profile(args):
+    """One kernel of the path on a seeded synthetic model, through the public
+    API, for ncu captures and device traces (nothing is skipped inside a
+    launch).  Targets: stack (hc_ffn_stack; --masks-p P gives Bernoulli(P)
+    fetch sets instead of the predictors), gather (hc_cold_gather_dequant),
+    predictor (hc_predictor_forward), batch (hc_ffn_batch_layer, B tokens).
+    --trace prints the stack kernel's per-phase table (device timestamps)."""
+    import torch
+    import hc_synth
+    ws, rank, local = _dist()
+    tp = None
+    if ws > 1:
+        import torch.distributed as dist
+        import engine
+        torch.cuda.set_device(local)
+        dist.init_process_group("gloo")
+        tp = engine.TPGroup()
+    what = args.profile_target
+    syn = hc_synth.make_stack(n_layers=args.layers, inter=args.inter, activation="relu", act_on_both=True, seed=0,
+                              predictors=what not in ("gather", "batch") and args.masks_p <= 0)
+    if what == "stack":
+        st = syn.stack(tp=tp)
+        if tp is not None:
+            dist.barrier()
+            torch.cuda.synchronize()
+        x = torch.randn(args.tokens, H, generator=torch.Generator().manual_seed(1)).cuda()   # same on every rank
+        masks = None
+        if args.masks_p > 0:
+            masks = hc_synth.bernoulli_words(args.layers, 1, args.inter, args.masks_p, seed=2)[:, 0].contiguous()
+        trace = torch.zeros(args.layers, st.grid, 40, dtype=torch.int64, device="cuda") if args.trace else None
+        for t in range(args.tokens):
+            if trace is not None:
+                trace.zero_()          # keep the last token's stamps and waits
+            if masks is not None:
+                st.masks.copy_(masks)
+                st.launch(x[t], True, None, None, trace)
+            elif st.pred0_in_kernel():
+                st.launch(x[t], 2, None, None, trace)      # layer 0's predictor inside the kernel
+            else:
+                st.first_mask(x[t])
+                st.launch(x[t], False, None, None, trace)
+        torch.cuda.synchronize()
+        st.check()
+        if trace is not None and rank == 0:
+            fetched = int(st.active_counts().sum())
+            print(f"stack trace: {args.layers} layers, {fetched / args.layers:.0f} cold records per layer")
+            for k, (mean, mx) in st.trace_summary(trace).items():
+                print(f"  {k:28s} mean {mean:9.2f}   max {mx:9.2f}")
+        if tp is not None:
+            dist.barrier()
+            tp.close()
+            dist.destroy_process_group()
+    elif what == "batch":
+        # configs[4]: per-token Bernoulli(0.1) masks unioned per layer; --tokens batched steps
+        bst = syn.batch_stack(max_batch=max(args.batch, 1), dense_min_batch=args.dense_min_batch)
+        masks = hc_synth.bernoulli_words(args.layers, args.batch, args.inter, 0.1, seed=2)
+        x = torch.randn(args.batch, H, generator=torch.Generator().manual_seed(1)).cuda()
+        for _ in range(args.tokens):
+            bst.forward(x, masks=masks)
+        torch.cuda.synchronize()
+        bst.check()
+    elif what == "gather":
+        store = syn.store
+        g = torch.Generator(device="cuda").manual_seed(7)
+        rec = torch.randint(0, int(store.n_rec_host.min()), (store.n_layers, args.k), generator=g, device="cuda",
+                            dtype=torch.int32)
+        out = torch.empty(3, store.n_layers, args.k, H, dtype=torch.bfloat16, device="cuda")
+        for _ in range(args.tokens):
+            store.gather_layers(range(store.n_layers), rec, out=out, out_dtype=torch.bfloat16)
+        torch.cuda.synchronize()
+        store.check()
+    else:
+        p = syn.predictors[0]
+        x = torch.randn(args.tokens, H, device="cuda")
+        for t in range(args.tokens):
+            p.predict_words(x[t:t + 1], norm_w=syn.norms[0], eps=syn.eps)
+        torch.cuda.synchronize()
+    print("profile target done")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    # profiling targets (not a bench line): one kernel on a small synthetic case
+    ap.add_argument("--profile-target", choices=["stack", "gather", "predictor", "batch"], default=None)
+    ap.add_argument("--layers", type=int, default=4)
+    ap.add_argument("--inter", type=int, default=INTER)
+    ap.add_argument("--tokens", type=int, default=3)
+    ap.add_argument("--k", type=int, default=4096, help="records per layer (--profile-target gather)")
+    ap.add_argument("--batch", type=int, default=64, help="tokens per batched step (--profile-target batch)")
+    ap.add_argument("--dense-min-batch", type=int, default=8)
+    ap.add_argument("--masks-p", type=float, default=0.0, help="stack: Bernoulli(P) fetch sets instead of predictors")
+    ap.add_argument("--trace", action="store_true", help="stack: print the per-phase table of the device trace")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.profile_target:
+        run_profile(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_gpu(args)

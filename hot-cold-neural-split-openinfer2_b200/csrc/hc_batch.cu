@@ -55,6 +55,7 @@ constexpr int KC = 64;               // K per pipeline stage
 constexpr int HOT_ROW = 3 * H;       // packed hot neuron: gate row | up row | down column (e4m3)
 constexpr int A_TILE_BYTES = TILE * KC * 2;    // 16 KB of f16
 constexpr uint64_t WAIT_NS = 1000000000ull;
+constexpr uint64_t DRAIN_NS = 2000000000ull;       // copies and MMAs in flight complete by themselves
 
 // ---------------------------------------------------------------------------
 // tcgen05 helpers
@@ -402,6 +403,8 @@ struct Bars {
   uint64_t* xempty;  // [8] MMA commit -> token-tile warp: tile read
   uint64_t* rawfull;   // [16] copies -> decoders: raw weights landed
   uint64_t* rawempty;  // [16] decoders -> issuer: raw slot read
+  uint64_t* tmaf;      // [8] k_gu: tensor copy of a hot unit landed (count 1, armed by its issuer)
+  uint64_t* mdrain;    // [2] MMA issuer i: every tcgen05 operation it issued has completed
   uint32_t* tslot;
   volatile int* abort_flag;
 };
@@ -418,6 +421,8 @@ __device__ __forceinline__ Bars carve_bars(uint8_t* p) {
   b.xempty = u + 60;
   b.tslot = reinterpret_cast<uint32_t*>(u + 68);
   b.abort_flag = reinterpret_cast<volatile int*>(u + 68) + 1;
+  b.tmaf = u + 69;
+  b.mdrain = u + 77;
   return b;
 }
 __device__ __forceinline__ void init_bars(const Bars& b, int stages, int producers, int rawfull_count = -1,
@@ -438,10 +443,29 @@ __device__ __forceinline__ void init_bars(const Bars& b, int stages, int produce
     mbar_init(&b.rawfull[k], rawfull_count < 0 ? producers : rawfull_count);
     mbar_init(&b.rawempty[k], rawempty_count < 0 ? producers : rawempty_count);
   }
+  for (int k = 0; k < 8; ++k) mbar_init(&b.tmaf[k], 1);
+  for (int k = 0; k < 2; ++k) mbar_init(&b.mdrain[k], 1);
   *b.abort_flag = 0;
   mbar_fence_init();
 }
-constexpr int BAR_BYTES = 576;
+constexpr int BAR_BYTES = 640;
+
+// Exit drain (every path, including an expired wait): a thread that armed
+// count-1 barriers with copies waits, bounded, for the last armed phase of
+// each slot; armed[s] = times slot s was armed.
+template <int NS>
+__device__ __forceinline__ void drain_slots(uint64_t* bars, const int (&armed)[NS], const LayerArgs& a) {
+#pragma unroll 1
+  for (int s = 0; s < NS; ++s)
+    if (armed[s] > 0 && !bwait(&bars[s], (armed[s] - 1) & 1, DRAIN_NS)) atomicOr(a.status, HC_ERR_TIMEOUT);
+}
+// ... and an MMA issuer waits until every tcgen05 operation it issued has
+// completed before the CTA frees its TMEM and exits.
+__device__ __forceinline__ void drain_mma(uint64_t* bar, const LayerArgs& a) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+  if (!bwait(bar, 0, DRAIN_NS)) atomicOr(a.status, HC_ERR_TIMEOUT);
+}
 
 // Optional timeline of k_gu / k_down launches (profiling hook, off unless
 // hc_batch_set_trace gave a buffer): per CTA 64 %globaltimer stamps.
@@ -538,8 +562,11 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu(const __grid_constant__ Gu
     };
     // issue side: tile being copied, its record for crow; next tile's, loaded a tile early
     int cT = -1, cR = -1, cnT = lo >> 6, cnR = rec_of(cnT, crow);
+    int tma_armed[GU_DEPTH];                                // thread 0: hot-unit tensor copies per raw slot
+#pragma unroll
+    for (int k = 0; k < GU_DEPTH; ++k) tma_armed[k] = 0;
     auto issue = [&](int i) {
-      if (i < nunits) {
+      if (i < nunits && !*bar.abort_flag) {
         const int x = lo + i, T = x >> 6, k = x & (H / KC - 1);
         const int slot = i % GU_DEPTH, use = i / GU_DEPTH;
         if (T != cT) {
@@ -548,17 +575,23 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu(const __grid_constant__ Gu
           cnT = T + 1;
           cnR = rec_of(cnT, crow);
         }
-        // the slot's previous unit has been decoded by every thread
-        if (use > 0 && !bwait(&bar.rawempty[slot], (use - 1) & 1)) fail(a, bar.abort_flag);
+        // the slot's previous unit has been decoded by every thread; if that wait
+        // expires, nothing more is copied into the slot (it may still be read)
+        if (use > 0 && !bwait(&bar.rawempty[slot], (use - 1) & 1)) {
+          fail(a, bar.abort_flag);
+          return;
+        }
         const uint32_t dst = rbase + slot * GU_RAW_SLOT;
         if (T < p.hot_tiles) {
+          // the tensor copies complete on tmaf[slot] (count 1), so their landing can be
+          // awaited on every path; rawfull counts every thread's arrival as for cold units
           if (t == 0) {
-            mbar_arrive_expect_tx(&bar.rawfull[slot], 2 * KC * TILE);
-            tma_load_2d(dst, &p.tm_hot, k * KC, T * TILE, &bar.rawfull[slot]);
-            tma_load_2d(dst + GU_REGION, &p.tm_hot, H + k * KC, T * TILE, &bar.rawfull[slot]);
-          } else {
-            mbar_arrive(&bar.rawfull[slot]);
+            mbar_arrive_expect_tx(&bar.tmaf[slot], 2 * KC * TILE);
+            tma_load_2d(dst, &p.tm_hot, k * KC, T * TILE, &bar.tmaf[slot]);
+            tma_load_2d(dst + GU_REGION, &p.tm_hot, H + k * KC, T * TILE, &bar.tmaf[slot]);
+            ++tma_armed[slot];
           }
+          mbar_arrive(&bar.rawfull[slot]);
         } else {
           if (cR >= 0) {
             const uint8_t* rb = a.cold + (size_t)cR * REC_BYTES;
@@ -590,6 +623,8 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu(const __grid_constant__ Gu
       issue(i + GU_AHEAD);
       const int slot = i % GU_DEPTH, s = i % GU_STAGES, round = i / GU_STAGES;
       bool ok = bwait(&bar.rawfull[slot], (i / GU_DEPTH) & 1);
+      // hot units come first in a CTA's range, so every earlier use of this slot was hot too
+      ok = ok && (T >= p.hot_tiles || bwait(&bar.tmaf[slot], (i / GU_DEPTH) & 1));
       ok = ok && (round == 0 || bwait(&bar.empty[s], (round - 1) & 1));
       if (!ok) fail(a, bar.abort_flag);
       // tcgen05.st is warp-collective: leave the loop as a whole warp
@@ -628,6 +663,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu(const __grid_constant__ Gu
       if (lane == 0) mbar_arrive(&bar.full[s]);
     }
     cp_wait<0>();
+    if (t == 0) drain_slots(bar.tmaf, tma_armed, a);
   } else if (t == GU_PROD) {
     // ---- MMA issuer
     const uint32_t idesc = idesc_f16(N, 0, 0);
@@ -657,8 +693,10 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu(const __grid_constant__ Gu
         ++seg;
       }
     }
+    drain_mma(&bar.mdrain[0], a);
   } else if (t == GU_PROD + 32) {
     // ---- token tiles: unit i's K step of the hot or cold operand tile set
+    int x_armed[GU_STAGES] = {};
     for (int i = 0; i < nunits; ++i) {
       const int x = lo + i, T = x >> 6, k = x & (H / KC - 1);
       const int s = i % GU_STAGES, round = i / GU_STAGES;
@@ -667,7 +705,9 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gu(const __grid_constant__ Gu
       mbar_arrive_expect_tx(&bar.xfull[s], x_bytes);
       bulk_copy(xbase + s * x_bytes, (T < p.hot_tiles ? p.xs_nat : p.xs_perm) + (size_t)k * x_bytes, x_bytes,
                 &bar.xfull[s]);
+      ++x_armed[s];
     }
+    drain_slots(bar.xfull, x_armed, a);
   } else if (t >= GU_PROD + 64) {
     // ---- epilogue: warp (18..21) & 3 reads TMEM lanes [32 q, 32 q + 32)
     const int q = warp & 3, r = q * 32 + lane;
@@ -929,6 +969,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down(DownParams p) {
         ++seg;
       }
     }
+    drain_mma(&bar.mdrain[0], a);
   } else if (t >= DN_PROD + 32) {
     const int qd = warp & 3, m = qd * 32 + lane;
     int seg = 0;
@@ -1150,10 +1191,16 @@ __global__ void __launch_bounds__(GUP_THREADS, 1) k_gu_p(const __grid_constant__
   // group g = local units [4 g, 4 g + 4): one bulk copy per run of contiguous blocks (the hot
   // blocks, then the cold ones), issued by the issuer warp two groups ahead
   const int ngroups = (nunits + GUP_GROUP - 1) / GUP_GROUP;
+  int g_armed[GUP_GSLOTS] = {};                             // issuer: group copies per slot
   auto issue = [&](int g) {
     if (g >= ngroups) return;
     const int slot = g % GUP_GSLOTS, use = g / GUP_GSLOTS;
-    if (use > 0 && !bwait(&bar.rawempty[slot], (use - 1) & 1)) fail(a, bar.abort_flag);
+    // if the slot is not released in time, nothing more is copied into it (it may still be read)
+    if (use > 0 && !bwait(&bar.rawempty[slot], (use - 1) & 1)) {
+      fail(a, bar.abort_flag);
+      return;
+    }
+    ++g_armed[slot];
     const int i0 = g * GUP_GROUP, i1 = min(nunits, i0 + GUP_GROUP);
     uint32_t total = 0;
     for (int i = i0; i < i1; ++i) total += usize(i);
@@ -1264,11 +1311,14 @@ __global__ void __launch_bounds__(GUP_THREADS, 1) k_gu_p(const __grid_constant__
         ++seg;
       }
     }
+    drain_mma(&bar.mdrain[mu], a);
   } else if (t == GU_PROD + 192) {
     for (int g = 0; g < ngroups && !*bar.abort_flag; ++g) issue(g);
+    drain_slots(bar.rawfull, g_armed, a);
   } else if (t == GU_PROD + 32) {
     // token tiles: tile s belongs to A stage s and is freed by the same commits
     pdl_wait();                                 // the tiles are k_norm's output
+    int x_armed[GU_STAGES] = {};
     for (int i = 0; i < nunits; ++i) {
       const int x = lo + i, T = x >> 6, kb = x & (H / KC - 1);
       const int s = i % GU_STAGES, round = i / GU_STAGES;
@@ -1277,7 +1327,9 @@ __global__ void __launch_bounds__(GUP_THREADS, 1) k_gu_p(const __grid_constant__
       mbar_arrive_expect_tx(&bar.xfull[s], x_bytes);
       bulk_copy(xbase + s * x_bytes, (T < L.hot_tiles ? p.xs_nat : p.xs_perm) + (size_t)kb * x_bytes, x_bytes,
                 &bar.xfull[s]);
+      ++x_armed[s];
     }
+    drain_slots(bar.xfull, x_armed, a);
   } else if (t >= GU_PROD + 64 && t < GU_PROD + 192) {                 // epilogue warps 18-21
     const int q = warp & 3, r = q * 32 + lane;
     int seg = 0;
@@ -1402,11 +1454,17 @@ __global__ void __launch_bounds__(DNP_THREADS, 1) k_down_p(const __grid_constant
   const uint32_t tmem = *bar.tslot;
 
   // issuer (warp 22): weight blocks (from DRAM) and activation blocks (from L2)
+  int w_armed[DD_DEPTH] = {}, a_armed[DD_ACTS] = {};       // issuer: copies per weight / activation slot
   auto issue_w = [&](int i) {
-    if (i >= nunits) return;
+    if (i >= nunits || *bar.abort_flag) return;
     const int x = lo + i, et = x / nblk, nb = x % nblk;
     const int slot = i % DD_DEPTH, use = i / DD_DEPTH;
-    if (use > 0 && !bwait(&bar.rawempty[slot], (use - 1) & 1)) fail(a, bar.abort_flag);
+    // if the slot is not released in time, nothing more is copied into it (it may still be read)
+    if (use > 0 && !bwait(&bar.rawempty[slot], (use - 1) & 1)) {
+      fail(a, bar.abort_flag);
+      return;
+    }
+    ++w_armed[slot];
     const bool hotB = nb < L.hot_blocks;
     const uint8_t* src = p.packed + (hotB ? L.dn_hot + ((size_t)et * L.hot_blocks + nb) * PD_HOT
                                           : L.dn_cold + ((size_t)et * L.cold_blocks + (nb - L.hot_blocks)) * PD_COLD);
@@ -1415,11 +1473,15 @@ __global__ void __launch_bounds__(DNP_THREADS, 1) k_down_p(const __grid_constant
     bulk_copy(wbase + slot * PD_HOT, src, wbytes, &bar.rawfull[slot]);
   };
   auto issue_a = [&](int i) {
-    if (i >= nunits) return;
+    if (i >= nunits || *bar.abort_flag) return;
     if (i == 0) pdl_wait();                     // the activation rows are k_act_p's output
     const int nb = (lo + i) % nblk;
     const int slot = i % DD_ACTS, use = i / DD_ACTS;
-    if (use > 0 && !bwait(&bar.xempty[slot], (use - 1) & 1)) fail(a, bar.abort_flag);
+    if (use > 0 && !bwait(&bar.xempty[slot], (use - 1) & 1)) {
+      fail(a, bar.abort_flag);
+      return;
+    }
+    ++a_armed[slot];
     mbar_arrive_expect_tx(&bar.xfull[slot], b_bytes);
     bulk_copy(abase + slot * (KC * NMAX * 2), act + (size_t)nb * KC * N, b_bytes, &bar.xfull[slot]);
   };
@@ -1485,6 +1547,8 @@ __global__ void __launch_bounds__(DNP_THREADS, 1) k_down_p(const __grid_constant
       if (i >= DD_DEPTH - DD_ACTS) issue_a(i - (DD_DEPTH - DD_ACTS));
     }
     for (int i = max(0, nunits - (DD_DEPTH - DD_ACTS)); i < nunits && !*bar.abort_flag; ++i) issue_a(i);
+    drain_slots(bar.rawfull, w_armed, a);
+    drain_slots(bar.xfull, a_armed, a);
   } else if (t == DNP_PROD || t == DNP_PROD + 32) {
     // two MMA issuers (warps 16, 17): chain ch accumulates the unit's 16-neuron
     // steps ch and ch + 2 into its own TMEM columns; the epilogue adds the chains
@@ -1514,6 +1578,7 @@ __global__ void __launch_bounds__(DNP_THREADS, 1) k_down_p(const __grid_constant
         ++seg;
       }
     }
+    drain_mma(&bar.mdrain[ch], a);
   } else if (t >= DNP_PROD + 64 && t < DNP_PROD + 192) {              // epilogue warps 18-21
     const int qd = warp & 3, m = qd * 32 + lane;
     int seg = 0;

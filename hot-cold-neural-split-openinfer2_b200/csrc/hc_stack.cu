@@ -75,7 +75,7 @@ constexpr int YCOPIES = 1;              // CTA c adds its partial y into copy c 
 constexpr int COLD_CLAIM = 8;           // cold records taken from the layer's pool per claim
 constexpr int POOL_CAP = 32768;         // cold-pool entries per layer (>= inter)
 constexpr int WD_TILES = 4096 / 32;     // W_down tiles of a predictor (H / WD_ROWS)
-constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;   // 2 s
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;   // 2 s: default limit of every wait on another agent
 static_assert(HALF_BYTES % 128 == 0 && REC_SLOT_OFF % 16 == 0, "halves must stay 16-byte aligned");
 static_assert(HOT_BYTES <= HALF_BYTES && REC_SLOT_OFF + REC_COPY <= HALF_BYTES, "half too small");
 static_assert(WU_ROWS * 96 * 4 + WU_ROWS * 4 <= HALF_BYTES, "predictor tiles must fit a half");
@@ -156,6 +156,7 @@ struct StackParams {
   float* xbuf;               // [NACC][H]   x_l, written by CTA 0
   int32_t* status;
   uint64_t* trace;           // optional [n_layers][G][TRACE_EVENTS]
+  uint64_t wait_ns;          // limit of every wait on another agent (CTA, GPU, copy engine)
 };
 
 constexpr int TRACE_EVENTS = 40;
@@ -312,7 +313,7 @@ __device__ __forceinline__ float cons_sum(StackSmem& sm, float a) {
 // poller's observation of the completed phase reaches the rest of its
 // subgroup through the subgroup barrier that follows.
 __device__ __forceinline__ int poll_pos(StackSmem& sm, uint32_t q, int e, uint32_t par, int l, int gi,
-                                        uint64_t* waited) {
+                                        uint64_t* waited, uint64_t limit_ns) {
   if (ld_vol_u(&sm.info[e].pos) == q && mbar_test_wait(&sm.full[e], par)) return (sm.info[e].layer == l) ? 1 : 0;
   const uint64_t c0 = (waited != nullptr) ? (uint64_t)clock64() : 0;
   const uint64_t t0 = globaltimer_ns();
@@ -330,7 +331,7 @@ __device__ __forceinline__ int poll_pos(StackSmem& sm, uint32_t q, int e, uint32
         break;
       }
     }
-    if ((i & 15) == 15 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) break;
+    if ((i & 15) == 15 && globaltimer_ns() - t0 > limit_ns) break;
   }
   if (waited != nullptr) *waited += (uint64_t)clock64() - c0;
   return r;
@@ -555,7 +556,7 @@ __device__ bool grid_spin(StackSmem& sm, const StackParams& p, uint32_t target) 
       const uint64_t t0 = globaltimer_ns();
       uint32_t spins = 0;
       while (ld_acquire_u32(p.bar_count) < target) {
-        if ((++spins & 255) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+        if ((++spins & 255) == 0 && globaltimer_ns() - t0 > p.wait_ns) {
           ok0 = false;
           break;
         }
@@ -626,7 +627,7 @@ __device__ bool layer_wait(StackSmem& sm, const StackParams& p, int lm1) {
         uint32_t v;
         asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f + s) : "memory");
         if ((int32_t)(v - seq) >= 0) break;
-        if ((++i & 63) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+        if ((++i & 63) == 0 && globaltimer_ns() - t0 > p.wait_ns) {
           ok0 = false;
           break;
         }
@@ -660,13 +661,14 @@ struct Copy {
 };
 template <int NCP>
 __device__ __forceinline__ void issue_entry(StackSmem& sm, uint8_t* ring, Producer& pr, int l, uint8_t kind, int n,
-                                            int64_t index, const Copy (&cp)[NCP], uint64_t* waited) {
+                                            int64_t index, const Copy (&cp)[NCP], uint64_t* waited,
+                                            uint64_t limit_ns) {
   const uint32_t q = pr.k;
   const int e = (int)(q % (uint32_t)NE);
   const uint32_t round = q / (uint32_t)NE;
   if (round > 0) {
     const uint64_t t0 = (waited != nullptr) ? globaltimer_ns() : 0;
-    if (!mbar_wait(&sm.empty[e], (round - 1) & 1u, WAIT_LIMIT_NS)) {
+    if (!mbar_wait(&sm.empty[e], (round - 1) & 1u, limit_ns)) {
       pr.ok = false;
       return;
     }
@@ -737,7 +739,9 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         bulk_g2s(sm.pbuf, a, abytes, &sm.pbar, 0ull);
         if (bbytes) bulk_g2s(sm.pbuf + boff, b, bbytes, &sm.pbar, 0ull);
       }
-      const bool done = mbar_wait(&sm.pbar, pphase & 1u, WAIT_LIMIT_NS);
+      bool done = mbar_wait(&sm.pbar, pphase & 1u, p.wait_ns);
+      // a copy that outlived a short limit still lands: never leave it in flight
+      if (!done) mbar_wait(&sm.pbar, pphase & 1u, WAIT_LIMIT_NS);
       ++pphase;
       return __all_sync(0xffffffffu, done);
     };
@@ -783,7 +787,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         const uint64_t t0 = globaltimer_ns();
         uint32_t i = 0;
         while (ld_vol(&sm.cons_layer) < l - 1) {
-          if ((++i & 63) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+          if ((++i & 63) == 0 && globaltimer_ns() - t0 > p.wait_ns) {
             ok = false;
             break;
           }
@@ -855,7 +859,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         const uint64_t t0 = globaltimer_ns();
         uint32_t i = 0;
         while (ld_acquire_u32(cnt) < (uint32_t)WD_TILES) {
-          if ((++i & 63) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+          if ((++i & 63) == 0 && globaltimer_ns() - t0 > p.wait_ns) {
             good = false;
             break;
           }
@@ -899,7 +903,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
       // ---- layer 0's own prediction on RMSNorm_0(x_0) (engine.py:422), as for
       // the later layers, once the consumers have x_0's RMS
       const hc_layer_desc& d0l = p.layers[0];
-      if (lane == 0) ok = mbar_wait(&sm.phase0_done, p0phase & 1u, WAIT_LIMIT_NS);
+      if (lane == 0) ok = mbar_wait(&sm.phase0_done, p0phase & 1u, p.wait_ns);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       // the layer-0 arrival is also the one the loop below waits for at l = 0
       if (!next_pred(p, 0)) ++p0phase;
@@ -924,7 +928,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
       if (pred_next) {
         // ---- W_down rows [d0, d1) of layer l+1's predictor on RMSNorm_{l+1}(x_l)
         // (one phase per layer with a next predictor, like wdown_done)
-        if (lane == 0) ok = mbar_wait(&sm.phase0_done, p0phase & 1u, WAIT_LIMIT_NS);
+        if (lane == 0) ok = mbar_wait(&sm.phase0_done, p0phase & 1u, p.wait_ns);
         ++p0phase;
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
@@ -966,7 +970,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
           const uint64_t t0 = globaltimer_ns();
           uint32_t i = 0;
           while (ld_vol(&sm.cons_layer) < l - 2) {
-            if ((++i & 63) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+            if ((++i & 63) == 0 && globaltimer_ns() - t0 > p.wait_ns) {
               pr.ok = false;
               break;
             }
@@ -1002,7 +1006,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
           const uint64_t t0 = globaltimer_ns();
           uint32_t i = 0;
           while (ld_vol(&sm.cons_layer) < l - 1) {
-            if ((++i & 63) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+            if ((++i & 63) == 0 && globaltimer_ns() - t0 > p.wait_ns) {
               pr.ok = false;
               break;
             }
@@ -1017,7 +1021,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
           const uint64_t t0 = globaltimer_ns();
           uint32_t i = 0;
           while (ld_acquire_u32(p.gdone + l % NACC) < (uint32_t)G) {
-            if ((++i & 63) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+            if ((++i & 63) == 0 && globaltimer_ns() - t0 > p.wait_ns) {
               pr.ok = false;
               break;
             }
@@ -1047,7 +1051,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
                 cp[k] = {k < m ? d.cold_records + (size_t)rec[j + k] * REC_BYTES : nullptr,
                          k < m ? (uint32_t)REC_COPY : 0u,
                          (uint32_t)((k >> 1) * HALF_BYTES + (k & 1) * REC_SLOT_OFF)};
-              issue_entry(sm, ring, pr, l, UNIT_COLD, m, (int64_t)(i + j), cp, iwp);
+              issue_entry(sm, ring, pr, l, UNIT_COLD, m, (int64_t)(i + j), cp, iwp, p.wait_ns);
               ++ng;
             }
             cold_taken += n;
@@ -1069,7 +1073,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
           for (int k = 0; k < 2; ++k)
             cp[k] = {k < n ? d.hot + (i + k) * HOT_BYTES : nullptr, k < n ? (uint32_t)HOT_BYTES : 0u,
                      (uint32_t)(k * HALF_BYTES)};
-          issue_entry(sm, ring, pr, l, UNIT_HOT, n, i, cp, iwp);
+          issue_entry(sm, ring, pr, l, UNIT_HOT, n, i, cp, iwp, p.wait_ns);
           ++ng;
           claimed += n;
         }
@@ -1095,7 +1099,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
     if (lane == 0) {
       const uint32_t first = pr.k > (uint32_t)NE ? pr.k - (uint32_t)NE : 0u;
       for (uint32_t q = first; q < pr.k; ++q)
-        if (!mbar_wait(&sm.full[q % (uint32_t)NE], (q / (uint32_t)NE) & 1u, WAIT_LIMIT_NS)) {
+        if (!mbar_wait(&sm.full[q % (uint32_t)NE], (q / (uint32_t)NE) & 1u, WAIT_LIMIT_NS)) {   // copies land by themselves
           atomicOr(p.status, HC_ERR_TIMEOUT);
           break;
         }
@@ -1253,7 +1257,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         uint64_t tb = 0;
         // one poller per subgroup decides; the decision reaches all 128 threads through the barrier
         if (u == 0) {
-          int r = poll_pos(sm, q, e, par, l, gi, tr ? &sm.tstat[0] : nullptr);
+          int r = poll_pos(sm, q, e, par, l, gi, tr ? &sm.tstat[0] : nullptr, p.wait_ns);
           if (ld_vol(&sm.abort) != 0) r = -1;
           if (r < 0) sm.abort = 1;
           sm.sgdec[sg][dbuf] = r;
@@ -1309,7 +1313,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
       // partial y (fixed tree in shared memory) and add it to the layer's accumulator
       if (t == 0) {
         bool okw = true;
-        if (pred_next) okw = mbar_wait(&sm.wdown_done, wd_phase & 1u, WAIT_LIMIT_NS);
+        if (pred_next) okw = mbar_wait(&sm.wdown_done, wd_phase & 1u, p.wait_ns);
         if (!okw) {
           sm.abort = 1;
           atomicOr(p.status, HC_ERR_TIMEOUT);
@@ -1511,6 +1515,7 @@ extern "C" int hc_ffn_stack_tp(const hc_layer_desc* layers, int32_t n_layers, in
   p.xbuf = reinterpret_cast<float*>(ws + WS_XBUF);
   p.status = status;
   p.trace = trace;
+  p.wait_ns = (tp && tp->wait_ns > 0) ? tp->wait_ns : WAIT_LIMIT_NS;
   void* args[] = {&p};
   cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(ffn_stack_kernel), dim3(G),
                                               dim3(STACK_THREADS), args, smem, reinterpret_cast<cudaStream_t>(stream));

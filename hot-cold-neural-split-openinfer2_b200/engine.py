@@ -143,13 +143,16 @@ class FFNStack:
                  predictors: Sequence[Optional[NeuronPredictor]], activation: str = "silu",
                  act_on_both: bool = False, eps: float = 1e-5, threshold: float = 0.5,
                  layer_ids: Optional[Sequence[int]] = None, grid: int = 0, inter: Optional[int] = None,
-                 tp: Optional[TPGroup] = None):
+                 tp: Optional[TPGroup] = None, wait_ns: int = 0):
         """With ``tp``, this GPU takes its share of every layer's neurons: hot
         neurons [r n_hot / N, (r+1) n_hot / N) of each layer's hot list and
         the cold ids of mask words [r W / N, (r+1) W / N); the output is
-        the whole layer stack's, identical on every rank."""
+        the whole layer stack's, identical on every rank.  ``wait_ns``
+        limits every bounded wait inside a launch (0 = the kernel's 2 s);
+        an expired wait ends the launch with HC_ERR_TIMEOUT in the status."""
         self.store = store
         self.tp = tp
+        self.wait_ns = int(wait_ns)
         self.device = store.device
         self.L = len(hot)
         self.layer_ids = list(layer_ids) if layer_ids is not None else list(range(self.L))
@@ -231,8 +234,12 @@ class FFNStack:
         tp = None
         if self.tp is not None and self.tp.size > 1:
             tp = N.TPDesc(size=self.tp.size, rank=self.tp.rank, words_lo=self.words_lo, words_n=self.words_n,
-                          peer_buf=N.ptr(self.tp.peer_buf), seq_base=(self.tp.launches * self.L) & 0xFFFFFFFF)
+                          peer_buf=N.ptr(self.tp.peer_buf), seq_base=(self.tp.launches * self.L) & 0xFFFFFFFF,
+                          wait_ns=self.wait_ns)
             self.tp.launches += 1
+        elif self.wait_ns:
+            tp = N.TPDesc(size=1, rank=0, words_lo=0, words_n=self.words, peer_buf=None, seq_base=0,
+                          wait_ns=self.wait_ns)
         mg = 2 if masks_given == 2 else (1 if masks_given else 0)
         N.check(N.lib.hc_ffn_stack_tp(N.ptr(self.desc_dev), self.L, self.inter, N.ptr(x), N.ptr(self.masks),
                                       mg, N.ptr(out), N.ptr(x_hist), self.eps, self.act,

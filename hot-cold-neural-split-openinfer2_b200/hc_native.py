@@ -23,7 +23,7 @@ HC_ERR_UNSUPPORTED = 16
 
 HC_F32, HC_BF16, HC_F16 = 0, 1, 2
 HC_ACT_SILU, HC_ACT_RELU = 0, 1
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 TABLE_SIZE = 65536
 
@@ -93,7 +93,8 @@ _SIGS = {
 class TPDesc(ctypes.Structure):
     """Mirror of hc_tp_desc (include/hotcold.h)."""
     _fields_ = [("size", ctypes.c_int32), ("rank", ctypes.c_int32), ("words_lo", ctypes.c_int32),
-                ("words_n", ctypes.c_int32), ("peer_buf", ctypes.c_void_p), ("seq_base", ctypes.c_uint32)]
+                ("words_n", ctypes.c_int32), ("peer_buf", ctypes.c_void_p), ("seq_base", ctypes.c_uint32),
+                ("wait_ns", ctypes.c_uint64)]
 
 
 def _load():

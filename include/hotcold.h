@@ -55,7 +55,7 @@ typedef struct CUstream_st* hc_stream_t; /* == cudaStream_t */
 #define HC_ACT_RELU 1
 
 /* Library identity / device checks.  hc_version returns HC_ABI_VERSION. */
-#define HC_ABI_VERSION 1
+#define HC_ABI_VERSION 2
 HC_API int hc_version(void);
 HC_API const char* hc_status_string(int status);
 /* Number of SMs of the current device, or -1 when no CUDA device is usable. */
@@ -294,14 +294,18 @@ HC_API int hc_ffn_stack(const hc_layer_desc* layers, int32_t n_layers, int32_t i
  *   seq_base   launches so far x n_layers; every GPU passes the same value
  * All `size` kernels must be running at the same time (one per GPU, issued
  * by each rank in the same order); a GPU that does not reach a layer within
- * 2 s makes the others return HC_ERR_TIMEOUT.  masks[] rows are written only
- * for the mask words this GPU owns.
+ * `wait_ns` (default 2 s) makes the others return HC_ERR_TIMEOUT: the kernel
+ * ORs it into `status`, waits for its own copies in flight and returns,
+ * leaving the workspace clean and the context usable.  masks[] rows are
+ * written only for the mask words this GPU owns.  A tp with size 1 only
+ * sets the wait limit.
  */
 typedef struct hc_tp_desc {
   int32_t size, rank;
   int32_t words_lo, words_n;
   void* const* peer_buf;
   uint32_t seq_base;
+  uint64_t wait_ns;   /* limit of every bounded wait of the launch; 0 = 2 s */
 } hc_tp_desc;
 
 HC_API int64_t hc_tp_buffer_bytes(int32_t tp_size);

@@ -3,8 +3,9 @@
 Each GPU streams its share of every layer (half of the hot list, half of
 the section's records, packed) and the layers' partial outputs are summed
 with one NCCL all-reduce of [B, 4096] per layer.  The result must match the
-same batch on one GPU (float summation order aside) and be identical on both
-ranks.  Skipped on machines with fewer than two GPUs.
+float64 oracle layer by layer (all hot neurons + the union's cold records),
+match the same batch on one GPU (float summation order aside) and be
+identical on both ranks.  Skipped on machines with fewer than two GPUs.
 """
 import os
 import socket
@@ -22,9 +23,37 @@ def _free_port():
         return s.getsockname()[1]
 
 
+def _oracle_worst(syn, fetch, masks, x0, hist, tol=2e-3):
+    """Worst rel-L2 of every token's layer update against the float64 oracle
+    over all hot neurons + the union of the batch's masks & fetch bits (the
+    batched bar: f16 tensor-core operands)."""
+    import numpy as np
+    from oracle import hotcold_oracle as O
+    L, inter = len(syn.hot), syn.inter
+    ostore = O.ColdStoreOracle(syn.store.image.cpu().numpy().tobytes(), syn.cold_index, {"hidden_dim": 4096})
+    xs = [x0.double().cpu().numpy()] + [hist[l].double().cpu().numpy() for l in range(L)]
+    worst = 0.0
+    for l in range(L):
+        m = masks[l].cpu().numpy()
+        union = np.zeros(inter, bool)
+        for b in range(m.shape[0]):
+            union |= O.mask_from_words(m[b], inter)
+        ids = np.nonzero(union & O.mask_from_words(fetch[l].cpu().numpy(), inter))[0]
+        rows = ostore.read_neurons(l, 0, ids.tolist()) if len(ids) else None
+        hot = tuple(t.double().cpu().numpy() for t in syn.hot[l].decoded())
+        ref = O.ffn_layer(xs[l], syn.norms[l].cpu().numpy(), syn.eps, syn.activation, syn.act_on_both, hot, rows)
+        for b in range(xs[l].shape[0]):
+            d_ref = ref[b] - xs[l][b]
+            rel = np.linalg.norm((xs[l + 1][b] - xs[l][b]) - d_ref) / max(np.linalg.norm(d_ref), 1e-30)
+            worst = max(worst, float(rel))
+            assert rel <= tol, f"layer {l} token {b}: rel-L2 {rel:.3e} against the oracle"
+    return worst
+
+
 def _worker(rank, world, port, out_dir):
     import sys
     sys.path.insert(0, PKG)
+    sys.path.insert(0, REPO)
     import datetime
     import torch.distributed as dist
     dev = torch.device("cuda", rank)
@@ -48,6 +77,7 @@ def _worker(rank, world, port, out_dir):
         res[f"tp{B}"] = hist.cpu().clone()
         res[f"count{B}"] = bst.union_counts().cpu().clone()
         if rank == 0:
+            res[f"oracle{B}"] = _oracle_worst(syn, bst.fetch, masks, x0, hist)
             one = syn.batch_stack(max_batch=64, single_token_stack=False)
             h1 = torch.empty(L, B, 4096, device=dev)
             one.forward(x0, masks=masks, x_hist=h1)
@@ -71,6 +101,7 @@ def test_sharded_batch_matches_one_gpu(tmp_path):
     for B in (1, 40):
         assert torch.equal(r0[f"tp{B}"], r1[f"tp{B}"])                 # the all-reduce leaves identical bits
         assert torch.equal(r0[f"count{B}"], r1[f"count{B}"])
+        assert r0[f"oracle{B}"] <= 2e-3, (B, r0[f"oracle{B}"])        # every layer against the float64 oracle
         x0 = r0[f"x0_{B}"].double()
         prev = x0
         for l in range(r0[f"tp{B}"].shape[0]):

@@ -249,3 +249,61 @@ def test_stack_on_reference_split_end_to_end(M):
     syn.predictors, syn.norms, syn.eps = [reg.get(0), None], nws, cfg["rms_norm_eps"]
     syn.activation, syn.act_on_both = "silu", False
     _check_stack(M, syn, st, x0, x_hist, st.masks.cpu().numpy(), True)
+
+
+def test_config0_single_layer_swiglu_row_scaled(M):
+    """configs[0] at its stated geometry: one 4096/14336 SwiGLU layer, hot 20%
+    FP8 e4m3 with per-row absmax scales, cold 80% INT4 records, one N(0, 1)
+    token, Bernoulli(0.1) active cold mask.
+
+    * The hot FP8 bytes the kernel streams equal an independent encoding of
+      the scaled dense rows (float32 division, torch's e4m3 cast as the
+      reference's splitter.py:223-225 uses), and the checker decodes them with
+      the oracle's own e4m3 table -- not through HotNeurons.
+    * The layer output matches the float64 oracle on the same quantised
+      weights and active set within the kernel's 1e-3 bar (north star: 1e-2).
+    * Against the dense fp32 FFN over the same neurons (hot + active cold),
+      the hot+cold sum is within the reference's own quantisation bound
+      (tests/test_ffn_exactness.py:93-97: rel-L2 < 0.25)."""
+    engine, hc_synth, predictor, splitter = M
+    inter, H = 14336, 4096
+    syn = hc_synth.make_stack(n_layers=1, inter=inter, hot_frac=0.2, activation="silu", act_on_both=False, seed=0,
+                              row_scale=True, predictors=False, keep_dense=True)
+    masks = hc_synth.bernoulli_words(1, 1, inter, 0.1, seed=2)[:, 0].contiguous()
+    x0 = torch.randn(H, device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))
+    st = syn.stack(with_predictors=False)
+    hist = torch.empty(1, H, device="cuda")
+    st.forward(x0, masks=masks, x_hist=hist)
+    st.check()
+    gate, up, down, hot_ids = (t.numpy() for t in syn.extra["dense"][0])
+    hot_ids = hot_ids.astype(np.int64)
+    # hot bytes: absmax / 448 per row, then the e4m3 cast
+    rows = [gate[hot_ids], up[hot_ids], down[:, hot_ids].T]
+    scales = np.stack([np.maximum(np.abs(r).max(axis=1), np.float32(1e-12)) / np.float32(448.0) for r in rows], 1)
+    got_scales = syn.hot[0].scales.cpu().numpy()
+    assert np.array_equal(got_scales, scales.astype(np.float32))
+    packed = syn.hot[0].packed.cpu().numpy()
+    hot64 = []
+    for j, r in enumerate(rows):
+        enc = O.e4m3_encode(r / scales[:, j:j + 1].astype(np.float32))
+        assert np.array_equal(packed[:, j], enc), f"hot FP8 bytes of vector {j} differ"
+        hot64.append(O.e4m3_decode(enc).astype(np.float64) * scales[:, j:j + 1])
+    hg, hu, hd = hot64[0], hot64[1], hot64[2].T
+    # oracle layer on the same quantised weights and active set
+    ostore = O.ColdStoreOracle(syn.store.image.cpu().numpy().tobytes(), syn.cold_index, {"hidden_dim": H})
+    active = O.mask_from_words(masks[0].cpu().numpy(), inter) & O.mask_from_words(st.fetch[0].cpu().numpy(), inter)
+    ids = np.nonzero(active)[0]
+    assert 0.08 * 11469 < len(ids) < 0.12 * 11469
+    x = x0.double().cpu().numpy()
+    nw = syn.norms[0].cpu().numpy()
+    ref = O.ffn_layer_from_records(x, nw, syn.eps, "silu", False, (hg, hu, hd), ostore, 0, ids.tolist())
+    got = hist[0].double().cpu().numpy()
+    rel = np.linalg.norm((got - x) - (ref - x)) / np.linalg.norm(ref - x)
+    assert rel <= TOL, f"rel-L2 against the oracle {rel:.3e}"
+    # quality against the dense fp32 FFN over the same neuron set
+    both = np.concatenate([hot_ids, ids])
+    dense = O.ffn_layer(x.reshape(1, -1), nw, syn.eps, "silu", False,
+                        (gate[both].astype(np.float64), up[both].astype(np.float64),
+                         down[:, both].astype(np.float64)), None)[0]
+    q = np.linalg.norm((got - x) - (dense - x)) / np.linalg.norm(dense - x)
+    assert q < 0.25, f"hot+cold vs dense fp32: rel-L2 {q:.3f}"

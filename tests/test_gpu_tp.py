@@ -1,9 +1,12 @@
 """Tensor parallelism of the fused stack over two GPUs (one process each).
 
 Every layer's neurons are split over the GPUs and each layer's partial
-outputs are exchanged inside the kernel; the result must match the same
-stack run on one GPU (same fetch sets, float summation order aside) and be
-bit-identical on both ranks.  Skipped on machines with fewer than two GPUs.
+outputs are exchanged inside the kernel.  Every layer update of every run
+must match the float64 oracle (sparse_ffn over all hot neurons and the
+cold ids of both ranks' masks, engine.py:173-209), predicted sets must equal
+the exact-logit sets outside the fp32 band, the result must match the same
+stack on one GPU (same fetch sets, float summation order aside), and both
+ranks must hold bit-identical hidden states.  Skipped on machines with fewer than two GPUs.
 """
 import os
 import socket
@@ -21,9 +24,43 @@ def _free_port():
         return s.getsockname()[1]
 
 
+def _oracle_check(syn, st_fetch, x0, hist, masks, check_pred, tol=1e-3):
+    """Every layer update of a run against the float64 oracle: x_{l+1} - x_l
+    = sparse_ffn(RMSNorm(x_l)) over all hot neurons + the cold ids of the
+    whole layer's masks (both ranks' words); predicted masks must equal the
+    exact-logit sets outside the fp32 rounding band.  Returns (worst rel-L2,
+    band flips)."""
+    import numpy as np
+    from oracle import hotcold_oracle as O
+    from predictor import logit_threshold
+    L, inter = len(syn.hot), syn.inter
+    ostore = O.ColdStoreOracle(syn.store.image.cpu().numpy().tobytes(), syn.cold_index, {"hidden_dim": 4096})
+    xs = [x0.double().cpu().numpy()] + [hist[l].double().cpu().numpy() for l in range(L)]
+    thr = logit_threshold(0.5)
+    worst, flips = 0.0, 0
+    for l in range(L):
+        mask = O.mask_from_words(masks[l].cpu().numpy(), inter)
+        if check_pred:
+            p = syn.predictors[l]
+            wd, wu, b = (t.detach().cpu().numpy() for t in (p.down.weight, p.up.weight, p.up.bias))
+            src = xs[0] if l == 0 else xs[l - 1]
+            exact, amb = O.predictor_mask_banded(src, wd, wu, b, thr, norm_w=syn.norms[l].cpu().numpy(), eps=syn.eps)
+            assert np.array_equal(mask[~amb], exact[~amb]), f"layer {l}: predicted set differs"
+            flips += int((mask != exact).sum())
+        ids = np.nonzero(mask & O.mask_from_words(st_fetch[l].cpu().numpy(), inter))[0]
+        hg, hu, hd = (t.double().cpu().numpy() for t in syn.hot[l].decoded())
+        ref = O.ffn_layer_from_records(xs[l], syn.norms[l].cpu().numpy(), syn.eps, syn.activation, syn.act_on_both,
+                                       (hg, hu, hd), ostore, l, ids.tolist())
+        rel = np.linalg.norm((xs[l + 1] - xs[l]) - (ref - xs[l])) / np.linalg.norm(ref - xs[l])
+        worst = max(worst, float(rel))
+        assert rel <= tol, f"layer {l}: rel-L2 {rel:.3e} against the oracle"
+    return worst, flips
+
+
 def _worker(rank, world, port, inter, n_layers, out_dir):
     import sys
     sys.path.insert(0, PKG)
+    sys.path.insert(0, REPO)
     import datetime
     import torch.distributed as dist
     torch.cuda.set_device(rank)
@@ -31,25 +68,30 @@ def _worker(rank, world, port, inter, n_layers, out_dir):
                             timeout=datetime.timedelta(seconds=120))
     import engine
     import hc_synth
-    syn = hc_synth.make_stack(n_layers=n_layers, inter=inter, seed=21, device=f"cuda:{rank}")
-    tp = engine.TPGroup(device=f"cuda:{rank}")
+    dev = f"cuda:{rank}"
+    syn = hc_synth.make_stack(n_layers=n_layers, inter=inter, seed=21, device=dev)
+    tp = engine.TPGroup(device=dev)
     st = syn.stack(tp=tp)
-    x0 = torch.randn(4096, generator=torch.Generator().manual_seed(5)).to(f"cuda:{rank}")
-    res = {}
-    # 1) predictor-driven decode, two tokens in a row
+    x0 = torch.randn(4096, generator=torch.Generator().manual_seed(5)).to(dev)
+    res = {"words": (st.words_lo, st.words_n)}
+    # 1) predictor-driven decode, two tokens in a row (each rank predicts its own words)
     dist.barrier()
     torch.cuda.synchronize()
     for k in range(2):
-        y = st.forward(x0 * (1.0 + 0.1 * k))
+        hist = torch.empty(n_layers, 4096, device=dev)
+        xk = x0 * (1.0 + 0.1 * k)
+        y = st.forward(xk, x_hist=hist)
         torch.cuda.synchronize()
         st.check()
         res[f"pred{k}"] = y.cpu().clone()
-    # 2) fixed fetch sets: compare with the same stack on one GPU
+        res[f"pred{k}_hist"] = hist.cpu().clone()
+        res[f"pred{k}_masks"] = st.masks.cpu().clone()
+    # 2) fixed fetch sets: compare with the oracle and with the same stack on one GPU
     g = torch.Generator().manual_seed(9)
     W = (inter + 31) // 32
     masks = torch.randint(-2**31, 2**31 - 1, (n_layers, W), generator=g, dtype=torch.int64).to(torch.int32)
-    masks = masks.to(f"cuda:{rank}")
-    hist = torch.empty(n_layers, 4096, device=f"cuda:{rank}")
+    masks = masks.to(dev)
+    hist = torch.empty(n_layers, 4096, device=dev)
     dist.barrier()
     torch.cuda.synchronize()
     y = st.forward(x0, masks=masks, x_hist=hist)
@@ -57,15 +99,27 @@ def _worker(rank, world, port, inter, n_layers, out_dir):
     st.check()
     res["given"] = y.cpu().clone()
     res["given_hist"] = hist.cpu().clone()
+    torch.save(res, os.path.join(out_dir, f"rank{rank}.pt"))
+    dist.barrier()
     if rank == 0:
         single = syn.stack()
-        hs = torch.empty(n_layers, 4096, device="cuda:0")
+        hs = torch.empty(n_layers, 4096, device=dev)
         y1 = single.forward(x0, masks=masks, x_hist=hs)
         torch.cuda.synchronize()
         single.check()
         res["single"] = y1.cpu().clone()
         res["single_hist"] = hs.cpu().clone()
-    torch.save(res, os.path.join(out_dir, f"rank{rank}.pt"))
+        # the whole layer's predicted words: each rank wrote the words it owns
+        other = torch.load(os.path.join(out_dir, "rank1.pt"))
+        lo1, n1 = other["words"]
+        checks = {}
+        for k in range(2):
+            full = res[f"pred{k}_masks"].clone()
+            full[:, lo1:lo1 + n1] = other[f"pred{k}_masks"][:, lo1:lo1 + n1]
+            checks[f"pred{k}"] = _oracle_check(syn, st.fetch, x0 * (1.0 + 0.1 * k), res[f"pred{k}_hist"], full, True)
+        checks["given"] = _oracle_check(syn, st.fetch, x0, res["given_hist"], masks.cpu(), False)
+        res["oracle"] = checks
+        torch.save(res, os.path.join(out_dir, "rank0.pt"))
     dist.barrier()
     tp.close()
     dist.destroy_process_group()
@@ -79,9 +133,13 @@ def test_tensor_parallel_stack_matches_one_gpu(tmp_path):
     mp.spawn(_worker, args=(2, _free_port(), inter, n_layers, str(tmp_path)), nprocs=2, join=True)
     r0 = torch.load(tmp_path / "rank0.pt")
     r1 = torch.load(tmp_path / "rank1.pt")
-    for k in ("pred0", "pred1", "given", "given_hist"):
+    for k in ("pred0", "pred1", "pred0_hist", "pred1_hist", "given", "given_hist"):
         assert torch.equal(r0[k], r1[k]), f"{k}: ranks disagree"
         assert torch.isfinite(r0[k]).all()
+    # every layer of every run matches the float64 oracle (checked on rank 0, asserts there)
+    for k in ("pred0", "pred1", "given"):
+        worst, flips = r0["oracle"][k]
+        assert worst <= 1e-3 and flips <= 4 * 4, (k, worst, flips)
     # same fetch sets on one GPU: only the float summation order differs
     d = (r0["given_hist"] - r0["single_hist"]).norm(dim=1) / r0["single_hist"].norm(dim=1)
     assert float(d.max()) < 1e-3, d
