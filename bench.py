@@ -341,6 +341,69 @@ def config0_quality(dev):
             "reference_figure": "9.5-17.5% (mixed FP8/INT4 split vs fp32, reference BENCHMARKS.md:41)"}
 
 
+def full_decode_bench(dev, prompt_len: int = 512, new_tokens: int = 256, layers: int = LAYERS):
+    """Llama-3.1-8B geometry (32 layers, hidden 4096, 32 query / 8
+    key-value heads, vocab 128256, SwiGLU 14336 split 20% FP8 hot / 80% INT4
+    cold, rank-64 predictor per layer), random-init weights, through
+    DesdemonaEngine.generate: a 512-token prompt of uniform random ids, 256
+    greedy tokens.  Attention is fp16 torch code (prefill) and the FP8 GEMV
+    (decode steps); each decode step is one CUDA graph replay."""
+    import torch
+    import engine
+    import hc_synth
+    from predictor import PredictorRegistry
+    vocab, nq, nkv = 128256, 32, 8
+    syn = hc_synth.make_stack(n_layers=layers, inter=INTER, hot_frac=0.2, rank=RANK, activation="silu",
+                              act_on_both=False, seed=3, device=dev)
+    g = torch.Generator(device=dev).manual_seed(33)
+    shared = {}
+    for li in range(layers):
+        for name, rows in (("q_proj", H), ("k_proj", nkv * 128), ("v_proj", nkv * 128), ("o_proj", H)):
+            shared[f"layer_{li:03d}.{name}"] = (torch.randn(rows, H, generator=g, device=dev) * 0.02).to(
+                torch.float8_e4m3fn)
+        shared[f"layer_{li:03d}.input_layernorm"] = torch.ones(H, dtype=torch.float16, device=dev)
+        shared[f"layer_{li:03d}.post_attention_layernorm"] = syn.norms[li].half()
+    shared["embed_tokens"] = torch.randn(vocab, H, generator=g, device=dev).half()
+    shared["lm_head"] = (torch.randn(vocab, H, generator=g, device=dev) * 0.02).half()
+    shared["final_norm"] = torch.ones(H, dtype=torch.float16, device=dev)
+    cfg = {"hidden_dim": H, "intermediate_dim": INTER, "num_layers": layers, "vocab_size": vocab,
+           "num_attention_heads": nq, "num_key_value_heads": nkv, "rope_theta": 500000.0, "rms_norm_eps": 1e-5,
+           "hidden_act": "silu", "act_on_both": False, "max_position_embeddings": 8192, "num_experts": 1}
+    reg = PredictorRegistry.__new__(PredictorRegistry)
+    reg.device = str(dev)
+    reg.predictors = {(li, 0): p for li, p in enumerate(syn.predictors)}
+    eng = engine.DesdemonaEngine.from_parts(cfg, shared, syn.store, syn.hot, reg, device=dev,
+                                            max_seq_len=prompt_len + new_tokens)
+    del shared
+    prompt = torch.randint(0, vocab, (1, prompt_len), generator=torch.Generator().manual_seed(34))
+    eng.generate(prompt.to(dev), max_new_tokens=8, temperature=0.0)        # warm-up: graph capture, workspaces
+    torch.cuda.synchronize()
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    e0.record()
+    logits, cache = eng.forward(prompt.to(dev), eng.new_cache(1, prompt_len + new_tokens))
+    e1.record()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e0b = torch.cuda.Event(enable_timing=True)
+    e0b.record()
+    out = eng.generate(prompt, max_new_tokens=new_tokens, temperature=0.0)   # host prompt ids, host token list
+    e2.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    eng.check()
+    prefill_ms = e0.elapsed_time(e1)
+    total_ms = e0b.elapsed_time(e2)
+    decode_ms = total_ms - prefill_ms
+    return {"workload": "configs[3]: Llama-3.1-8B geometry (32L, 32q/8kv heads, vocab 128256), SwiGLU 4096/14336 "
+                        "20% FP8 hot / 80% INT4 cold with rank-64 predictors (random init), 512-token random prompt, "
+                        "256 greedy tokens through DesdemonaEngine.generate",
+            "tokens": len(out), "generate_tokens_per_s": round(len(out) / (total_ms / 1e3), 1),
+            "decode_tokens_per_s": round((len(out) - 1) / (decode_ms / 1e3), 1),
+            "prefill_ms": round(prefill_ms, 2), "generate_ms": round(total_ms, 2), "generate_wall_s": round(wall, 3),
+            "note": "generate() timed end to end on the device (prefill + 255 graph-replayed decode steps + "
+                    "sampling + one device-to-host read of the tokens); decode = generate - prefill"}
+
+
 def run_gpu(args):
     import torch
     import torch.distributed as dist
@@ -485,6 +548,12 @@ def run_gpu(args):
         bd = batched_decode_bench(syn, args.steps, args.warmup) if ws == 1 else None
         cpu = cpu_reference(4, 0, layers_per_step=2, budget_s=25.0) if ws == 1 else None
         q0 = config0_quality(dev) if ws == 1 else None
+        fd = None
+        if ws == 1:
+            try:
+                fd = full_decode_bench(dev)
+            except Exception as e:          # noqa: BLE001 -- reported in the line, not hidden
+                fd = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
         line = {"metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "e4m3/int4 weights, fp32 accumulate",
@@ -506,6 +575,8 @@ def run_gpu(args):
             line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
         if q0 is not None:
             line["config0_quality"] = q0
+        if fd is not None:
+            line["full_decode"] = fd
         if bd is not None:
             line["batched_decode"] = {"workload": "configs[4] on 1 GPU: 32L 4096/14336 stack, B tokens, per-token "
                                                   "Bernoulli(0.1) masks unioned per layer, tcgen05 GEMMs",

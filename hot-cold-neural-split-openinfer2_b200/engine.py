@@ -589,11 +589,14 @@ def sparse_ffn(x, activation, act_on_both, gate_hot, up_hot, down_hot, gate_cold
 
 
 class SparseFFNLayer(nn.Module):
-    """The reference's SparseFFNLayer (engine.py:212-312) on the fused kernel.
+    """The reference's SparseFFNLayer (engine.py:212-312) on the fused kernels.
 
     ``submit_cold_fetch`` returns the device mask words of the predicted set
-    (no host sync, no thread pool); ``forward`` runs RMSNorm + hot + cold +
-    residual in one launch per token row."""
+    (no host sync, no thread pool).  ``forward`` runs RMSNorm + hot + cold +
+    residual: one token row through the fused stack kernel (one layer), and
+    B * T > 1 rows -- the reference's single sparse_ffn call over all rows
+    with one fetch set (engine.py:292-312) -- through the batched tensor-core
+    layer (hc_ffn_batch_layer), every weight byte read once per 64 rows."""
 
     _EID = 0
 
@@ -614,8 +617,11 @@ class SparseFFNLayer(nn.Module):
         if ffn_norm_weight is not None:
             self.input_layernorm.weight = nn.Parameter(ffn_norm_weight.to(self.device))
         self.input_layernorm.to(self.device)
-        p = Path(hot_dir) / f"layer_{layer_idx:03d}_expert_{self._EID:03d}.pt"
-        if p.exists():
+        hot = hot_dir if isinstance(hot_dir, HotNeurons) else None
+        p = None if hot is not None else Path(hot_dir) / f"layer_{layer_idx:03d}_expert_{self._EID:03d}.pt"
+        if hot is not None:
+            self.hot = hot
+        elif p.exists():
             self.hot = HotNeurons.from_file(str(p), self.device)
         else:
             z8 = torch.zeros(0, HIDDEN_DIM, dtype=torch.float8_e4m3fn)
@@ -625,20 +631,28 @@ class SparseFFNLayer(nn.Module):
         self._norm32 = self.input_layernorm.weight.detach().to(torch.float32).contiguous()
         self._stack = FFNStack(cold_store, [self.hot], [self._norm32], [self._pred], self.activation,
                                self.act_on_both, self.eps, layer_ids=[layer_idx], inter=self.inter_dim)
+        self._batch: Optional[BatchStack] = None
+        self._rows_in = self._rows_out = None
 
     def _query(self, x_normed: torch.Tensor) -> torch.Tensor:
         return x_normed[:, -1, :].mean(0, keepdim=True)          # engine.py:277
 
-    def _mask_words(self, x: torch.Tensor) -> torch.Tensor:
+    def _mask_words(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Predicted-set words for input x [B, T, H] (not yet normalised)."""
         if self._pred is None:
-            return self._stack._all_ones.view(1, -1).clone()
+            w = self._stack._all_ones.view(1, -1)
+            return out.copy_(w) if out is not None else w.clone()
         if x.shape[0] == 1:
-            row = x[0, -1:, :].to(torch.float32).contiguous()
-            return self._pred.predict_words(row, 0.5, norm_w=self._norm32, eps=self.eps)
-        with torch.no_grad():
-            q = self._query(self.input_layernorm(x.to(self._norm32.dtype)))
-        return self._pred.predict_words(q.to(torch.float32), 0.5)
+            row = x[0, -1:, :].to(torch.float32)
+            return self._pred.predict_words(row, 0.5, norm_w=self._norm32, eps=self.eps, mask_out=out)
+        q = self._query(self.normed32(x))
+        return self._pred.predict_words(q, 0.5, mask_out=out)
+
+    def normed32(self, x: torch.Tensor) -> torch.Tensor:
+        """The layer's RMSNorm (post_attention_layernorm, engine.py:246-249) of
+        x in fp32."""
+        xf = x.to(torch.float32)
+        return xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps) * self._norm32
 
     def _cold_ids_for(self, x_normed: torch.Tensor) -> list[int]:
         """engine.py:274-283: host list of the cold ids to fetch."""
@@ -648,16 +662,376 @@ class SparseFFNLayer(nn.Module):
             return [i for i in ids if i not in self._hot_id_set]
         return [i for i in range(self.inter_dim) if i not in self._hot_id_set]
 
-    def submit_cold_fetch(self, x: torch.Tensor):
+    def submit_cold_fetch(self, x: torch.Tensor, out: Optional[torch.Tensor] = None):
         """The lookahead prefetch (engine.py:285-290): device mask words."""
-        return self._mask_words(x)
+        return self._mask_words(x, out)
+
+    def _batched(self, rows: int) -> BatchStack:
+        if self._batch is None or self._batch.max_batch < rows:
+            cap = max(64, 1 << (rows - 1).bit_length())
+            self._batch = BatchStack(self.cold_store, [self.hot], [self._norm32], None, self.activation,
+                                     self.act_on_both, self.eps, layer_ids=[self.layer_idx], inter=self.inter_dim,
+                                     max_batch=cap, single_token_stack=False)
+        return self._batch
 
     def forward(self, x: torch.Tensor, prefetch_future=None) -> torch.Tensor:
         B, T, H = x.shape
         words = prefetch_future if prefetch_future is not None else self._mask_words(x)
-        self._stack.masks.copy_(words.view(1, -1))
         rows = x.reshape(B * T, H).to(torch.float32).contiguous()
-        out = torch.empty_like(rows)
-        for r in range(rows.shape[0]):
-            self._stack.launch(rows[r], masks_given=True, out=out[r])
+        n = rows.shape[0]
+        if n == 1:
+            self._stack.masks.copy_(words.view(1, -1))
+            out = torch.empty_like(rows)
+            self._stack.launch(rows[0], masks_given=True, out=out[0])
+        else:
+            # every row shares the one fetch set (engine.py:297-311)
+            bst = self._batched(n)
+            m = words.view(1, 1, -1).expand(1, n, -1)
+            out = bst.forward(rows, masks=m)
         return out.reshape(B, T, H).to(x.dtype)
+
+    def check(self):
+        self._stack.check()
+        if self._batch is not None:
+            self._batch.check()
+
+
+# ─── Model shell (engine.py:61-158, :317-511) ─────────────────────────────────
+# Attention, RoPE and sampling are torch code (they are not on the sparse-FFN
+# path); the FFN half of every layer runs the kernels above.  The KV cache is
+# preallocated once per sequence, so a decode step has static shapes and the
+# whole step is captured in one CUDA graph.
+def build_rope_cache(max_seq_len: int, head_dim: int, theta: float, device=None):
+    """cos / sin tables [max_seq_len, head_dim // 2] in fp32 for rotary
+    position embedding with base ``theta`` (engine.py:130-140)."""
+    half = head_dim // 2
+    # frequency i = theta^(-i / half), evaluated as 1 / theta^(i / half) in fp32
+    inv = 1.0 / (float(theta) ** (torch.arange(half, device=device).float() / half))
+    ang = torch.arange(max_seq_len, device=device).float()[:, None] * inv[None, :]
+    return torch.cos(ang), torch.sin(ang)
+
+
+def _rotate(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """Rotary embedding of x [B, heads, T, D] (halves rotated as pairs,
+    engine.py:143-158); cos / sin [T, D/2] are cast to x's dtype first."""
+    d = x.shape[-1] // 2
+    c = cos.to(x.dtype)[None, None]
+    s = sin.to(x.dtype)[None, None]
+    a, b = x[..., :d], x[..., d:]
+    return torch.cat((a * c - b * s, a * s + b * c), dim=-1)
+
+
+class KVCache:
+    """Preallocated key / value cache of every layer: [B, n_kv, capacity, D]
+    fp16 per layer and tensor, filled up to ``length`` positions.  Indexing
+    gives the reference's per-layer (k, v) pair (engine.py:111-115), views of
+    the filled part."""
+
+    def __init__(self, n_layers: int, batch: int, n_kv: int, capacity: int, head_dim: int, device,
+                 dtype=torch.float16):
+        self.k = torch.zeros(n_layers, batch, n_kv, capacity, head_dim, dtype=dtype, device=device)
+        self.v = torch.zeros_like(self.k)
+        self.capacity = capacity
+        self.length = 0
+        self.pos = torch.zeros(1, dtype=torch.int64, device=device)     # == length, on the device
+
+    def __len__(self):
+        return self.k.shape[0]
+
+    def __getitem__(self, layer: int):
+        return self.k[layer, :, :, :self.length], self.v[layer, :, :, :self.length]
+
+
+class GroupedQueryAttention(nn.Module):
+    """Grouped-query attention of one layer (engine.py:63-125): FP8-at-rest
+    q/k/v/o weights computed in fp16, the layer's pre-norm, RoPE, causal
+    softmax attention over the cache."""
+
+    def __init__(self, layer_idx: int, weights: dict, cfg: dict, device="cuda", fp8_decode: bool = True):
+        super().__init__()
+        self.layer_idx = layer_idx
+        self.n_q = cfg["num_attention_heads"]
+        self.n_kv = cfg["num_key_value_heads"]
+        self.hidden = cfg["hidden_dim"]
+        self.head_dim = self.hidden // self.n_q
+        pre = f"layer_{layer_idx:03d}."
+        dev = torch.device(device)
+        w16 = lambda n: weights[pre + n].to(dev).to(torch.float16)
+        # q, k and v projections as one [H + 2 n_kv D, H] matrix: one GEMM instead of three
+        self.qkv_weight = torch.cat([w16("q_proj"), w16("k_proj"), w16("v_proj")], dim=0).contiguous()
+        self.o_weight = w16("o_proj").contiguous()
+        # one-token steps read the FP8 bytes themselves (hc_fp8_gemv): half the weight traffic
+        self.fp8_decode = bool(fp8_decode) and self.hidden == 4096 and self.n_q * self.head_dim == 4096
+        if self.fp8_decode:
+            w8 = lambda n: weights[pre + n].to(dev).to(torch.float8_e4m3fn).view(torch.uint8)
+            self.qkv_w8 = torch.cat([w8("q_proj"), w8("k_proj"), w8("v_proj")], dim=0).contiguous()
+            self.o_w8 = w8("o_proj").contiguous()
+        self.norm = nn.RMSNorm(self.hidden, eps=cfg["rms_norm_eps"]).to(dev)
+        nw = weights.get(pre + "input_layernorm")
+        if nw is not None:
+            self.norm.weight = nn.Parameter(nw.to(dev).to(torch.float16))
+        else:
+            self.norm.to(torch.float16)
+
+    def forward(self, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, cache: KVCache,
+                start: Optional[int], pos: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """x [B, T, H] fp16.  ``start`` = the host's cache length (positions
+        start.. start + T - 1), or None for a graph-captured decode step whose
+        position is the device scalar ``pos`` (T = 1): the step then attends
+        over the whole cache capacity with a mask past ``pos``."""
+        B, T, H = x.shape
+        D, nq, nkv = self.head_dim, self.n_q, self.n_kv
+        one = self.fp8_decode and B * T == 1
+        qkv = self._gemv(self.qkv_w8, self.norm(x)) if one else F.linear(self.norm(x), self.qkv_weight)
+        q = qkv[..., :nq * D].view(B, T, nq, D).transpose(1, 2)
+        k = qkv[..., nq * D:(nq + nkv) * D].view(B, T, nkv, D).transpose(1, 2)
+        v = qkv[..., (nq + nkv) * D:].view(B, T, nkv, D).transpose(1, 2)
+        q, k = _rotate(q, cos, sin), _rotate(k, cos, sin)
+        kc, vc = cache.k[self.layer_idx], cache.v[self.layer_idx]
+        if start is not None:
+            kc[:, :, start:start + T] = k
+            vc[:, :, start:start + T] = v
+            n = start + T
+            keys, vals = kc[:, :, :n], vc[:, :, :n]
+            mask = None
+            if T > 1:                    # causal over the new positions (engine.py:121)
+                i = torch.arange(T, device=x.device)[:, None] + start
+                j = torch.arange(n, device=x.device)[None, :]
+                mask = j <= i
+            out = F.scaled_dot_product_attention(q, keys, vals, attn_mask=mask, enable_gqa=True)
+        else:
+            kc.index_copy_(2, pos, k)
+            vc.index_copy_(2, pos, v)
+            j = torch.arange(cache.capacity, device=x.device)
+            mask = (j <= pos).view(1, 1, 1, -1)
+            out = F.scaled_dot_product_attention(q, kc, vc, attn_mask=mask, enable_gqa=True)
+        out = out.transpose(1, 2).reshape(B, T, nq * D)
+        return self._gemv(self.o_w8, out) if one else F.linear(out, self.o_weight)
+
+    @staticmethod
+    def _gemv(w8: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+        """y [1, 1, rows] = W x for one fp16 row x [1, 1, 4096], W e4m3 bytes [rows, 4096]."""
+        xv = x.reshape(-1).contiguous()
+        y = torch.empty(1, 1, w8.shape[0], dtype=torch.float16, device=x.device)
+        N.check(N.lib.hc_fp8_gemv(N.ptr(w8), None, w8.shape[0], w8.shape[1], N.ptr(xv), N.ptr(y),
+                                  N.stream_handle()), "hc_fp8_gemv")
+        return y
+
+
+def _sample(logits: torch.Tensor, temperature: float, top_p: float) -> torch.Tensor:
+    """Greedy at temperature 0, else nucleus sampling (engine.py:493-511):
+    keep the most probable tokens whose preceding cumulative mass is below
+    top_p, renormalise, draw one."""
+    if temperature == 0.0:
+        return logits.argmax(dim=-1)
+    probs = torch.softmax(logits / temperature, dim=-1)
+    p_sorted, order = torch.sort(probs, dim=-1, descending=True)
+    before = torch.cumsum(p_sorted, dim=-1) - p_sorted
+    p_sorted = torch.where(before < top_p, p_sorted, torch.zeros_like(p_sorted))
+    p_sorted = p_sorted / p_sorted.sum(dim=-1, keepdim=True)
+    pick = torch.multinomial(p_sorted, num_samples=1)
+    return order.gather(-1, pick).squeeze(-1)
+
+
+class DesdemonaEngine(nn.Module):
+    """The reference's inference engine (engine.py:317-488) with the sparse
+    FFN on the B200 kernels.
+
+    ``DesdemonaEngine(split_dir, predictor_dir, device, n_threads,
+    max_seq_len)`` reads the same split artefacts (split_config.json,
+    hot_weights/shared.pt, hot_weights/layer_XXX_expert_000.pt,
+    cold_weights.bin + cold_index.npy) and the same predictor files.  The cold
+    store is uploaded to HBM once; every layer's fetch set is predicted on the
+    device (layer l+1's on layer l's post-attention hidden state, the
+    reference's lookahead, engine.py:421-438) and never crosses to the host.
+    ``generate`` prefills eagerly and replays one captured CUDA graph per
+    decode step.  ``n_threads`` is accepted for signature compatibility (no
+    host thread pool is needed)."""
+
+    def __init__(self, split_dir: Optional[str] = None, predictor_dir: Optional[str] = None, device: str = "cuda",
+                 n_threads: int = 8, max_seq_len: int = 8192, *, _parts: Optional[dict] = None):
+        super().__init__()
+        import json
+        self.device = torch.device(device)
+        self.n_threads = n_threads
+        if _parts is None:
+            with open(Path(split_dir) / "split_config.json") as f:
+                self.cfg = json.load(f)
+            if self.cfg.get("num_experts", 1) != 1:
+                raise ValueError(f"split_dir contains a {self.cfg['num_experts']}-expert MoE split; "
+                                 "this engine serves dense split-dense artifacts only.")
+            shared = torch.load(str(Path(split_dir) / "hot_weights" / "shared.pt"), map_location="cpu")
+            self.predictor = None
+            if predictor_dir and Path(predictor_dir).exists():
+                self.predictor = PredictorRegistry(predictor_dir, device=str(self.device))
+            self.cold_store = ColdWeightStore(str(Path(split_dir) / "cold_weights.bin"),
+                                              str(Path(split_dir) / "cold_index.npy"), self.cfg, device=self.device)
+            hots = [str(Path(split_dir) / "hot_weights")] * self.cfg["num_layers"]
+        else:
+            # in-memory artefacts (synthetic models): cfg, shared, cold_store, hot [HotNeurons], predictor
+            self.cfg = _parts["cfg"]
+            shared = _parts["shared"]
+            self.predictor = _parts.get("predictor")
+            self.cold_store = _parts["cold_store"]
+            hots = _parts["hot"]
+        cfg = self.cfg
+        self.num_layers = cfg["num_layers"]
+        H, vocab = cfg["hidden_dim"], cfg["vocab_size"]
+        self.head_dim = H // cfg["num_attention_heads"]
+        self.max_seq = min(max_seq_len, cfg.get("max_position_embeddings", max_seq_len))
+        dev = self.device
+        self.embed_tokens = nn.Embedding(vocab, H).to(dev)
+        self.embed_tokens.weight = nn.Parameter(shared["embed_tokens"].to(dev).to(torch.float16), requires_grad=False)
+        self.lm_head_weight = shared["lm_head"].to(dev).to(torch.float16)
+        self.final_norm = nn.RMSNorm(H, eps=cfg["rms_norm_eps"]).to(dev)
+        if "final_norm" in shared:
+            self.final_norm.weight = nn.Parameter(shared["final_norm"].to(dev).to(torch.float16), requires_grad=False)
+        else:
+            self.final_norm.to(torch.float16)
+        self.attention_layers = nn.ModuleList([GroupedQueryAttention(li, shared, cfg, dev)
+                                               for li in range(self.num_layers)])
+        self.ffn_layers = nn.ModuleList([
+            SparseFFNLayer(li, hots[li], self.cold_store, self.predictor, cfg, dev, None,
+                           ffn_norm_weight=shared.get(f"layer_{li:03d}.post_attention_layernorm"))
+            for li in range(self.num_layers)])
+        del shared
+        self.cos_cache, self.sin_cache = build_rope_cache(self.max_seq, self.head_dim, cfg["rope_theta"], dev)
+        W = (cfg["intermediate_dim"] + 31) // 32
+        self._words = torch.zeros(self.num_layers, 1, W, dtype=torch.int32, device=dev)   # fetch sets in flight
+        self._graph = None
+        self._graph_cache = None
+
+    @classmethod
+    def from_parts(cls, cfg: dict, shared: dict, cold_store: ColdWeightStore, hot: Sequence[HotNeurons],
+                   predictor: Optional[PredictorRegistry] = None, device="cuda", max_seq_len: int = 8192):
+        """An engine over in-memory artefacts (the split's contents without
+        the files): ``shared`` has shared.pt's keys, ``hot`` one HotNeurons per
+        layer."""
+        return cls(None, None, device, max_seq_len=max_seq_len,
+                   _parts={"cfg": cfg, "shared": shared, "cold_store": cold_store, "hot": list(hot),
+                           "predictor": predictor})
+
+    def new_cache(self, batch: int = 1, capacity: Optional[int] = None) -> KVCache:
+        cap = min(capacity or self.max_seq, self.max_seq)
+        return KVCache(self.num_layers, batch, self.cfg["num_key_value_heads"], cap, self.head_dim, self.device)
+
+    def _layers(self, x: torch.Tensor, cos, sin, cache: KVCache, start: Optional[int], pos=None):
+        """Attention + sparse FFN of every layer, with the fetch-set lookahead."""
+        f = self.ffn_layers
+        words = self._words
+        f[0].submit_cold_fetch(x, out=words[0])             # layer 0's set, on the embedding (engine.py:422)
+        for li in range(self.num_layers):
+            x = x + self.attention_layers[li](x, cos, sin, cache, start, pos)
+            if li + 1 < self.num_layers:                     # next layer's set on this post-attention state
+                f[li + 1].submit_cold_fetch(x, out=words[li + 1])
+            x = f[li](x, words[li])
+        return x
+
+    def forward(self, input_ids: torch.Tensor, kv_caches: Optional[KVCache] = None):
+        """(logits [B, T, vocab], cache) for input_ids [B, T], continuing the
+        cache's positions (engine.py:406-442).  A new cache holds up to
+        max_seq_len positions."""
+        B, T = input_ids.shape
+        cache = kv_caches if kv_caches is not None else self.new_cache(B)
+        start = cache.length
+        if start + T > cache.capacity:
+            raise ValueError(f"sequence of {start + T} positions exceeds the cache capacity {cache.capacity}")
+        x = self.embed_tokens(input_ids.to(self.device))
+        x = self._layers(x, self.cos_cache[start:start + T], self.sin_cache[start:start + T], cache, start)
+        cache.length = start + T
+        cache.pos.fill_(cache.length)
+        logits = F.linear(self.final_norm(x), self.lm_head_weight)
+        return logits, cache
+
+    # -- decode step in one CUDA graph -------------------------------------
+    def _decode_body(self, cache: KVCache):
+        pos = cache.pos
+        x = self.embed_tokens(self._tok.view(1, 1))
+        cos = self.cos_cache.index_select(0, pos)
+        sin = self.sin_cache.index_select(0, pos)
+        x = self._layers(x, cos, sin, cache, None, pos)
+        self._logits.copy_(F.linear(self.final_norm(x), self.lm_head_weight)[:, -1])
+        pos.add_(1)
+
+    def _capture(self, cache: KVCache):
+        self._tok = torch.zeros(1, dtype=torch.int64, device=self.device)
+        self._logits = torch.zeros(1, self.cfg["vocab_size"], dtype=torch.float16, device=self.device)
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream())
+        saved = (cache.k.clone(), cache.v.clone(), cache.pos.clone())
+        with torch.cuda.stream(s):
+            self._decode_body(cache)                # warm-up outside capture (allocations, workspaces)
+            torch.cuda.current_stream().synchronize()
+            cache.k.copy_(saved[0])
+            cache.v.copy_(saved[1])
+            cache.pos.copy_(saved[2])
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                self._decode_body(cache)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        cache.k.copy_(saved[0])
+        cache.v.copy_(saved[1])
+        cache.pos.copy_(saved[2])
+        self._graph, self._graph_cache = g, cache
+
+    def decode_step(self, token: torch.Tensor, cache: KVCache) -> torch.Tensor:
+        """Logits [1, vocab] of one new token (device int64 scalar) at the
+        cache's next position, by one replay of the captured step."""
+        if self._graph is None or self._graph_cache is not cache:
+            self._capture(cache)
+        self._tok.copy_(token.view(1))
+        self._graph.replay()
+        cache.length += 1
+        return self._logits
+
+    @torch.inference_mode()
+    def generate(self, input_ids: torch.Tensor, max_new_tokens: int = 200, temperature: float = 0.7,
+                 top_p: float = 0.9, eos_token_id=None, use_graph: bool = True) -> list[int]:
+        """Generated token ids, prompt excluded, with the reference's stopping
+        rule (engine.py:444-484): the first sampled EOS is kept and ends the
+        sequence.  Tokens stay on the device until the end (one host read)."""
+        if eos_token_id is None:
+            eos = set()
+        elif isinstance(eos_token_id, int):
+            eos = {eos_token_id}
+        else:
+            eos = set(eos_token_id)
+        if input_ids.dim() == 1:
+            input_ids = input_ids.view(1, -1)
+        if input_ids.shape[0] != 1:
+            raise ValueError("generate decodes one sequence (batch 1), as the reference does")
+        T = input_ids.shape[1]
+        n_new = max(int(max_new_tokens), 1)
+        cache = self.new_cache(1, T + n_new)
+        logits, cache = self.forward(input_ids, cache)
+        out = torch.empty(n_new, dtype=torch.int64, device=self.device)
+        tok = _sample(logits[:, -1, :], temperature, top_p).view(1)
+        out[0] = tok[0]
+        count = 1
+        while count < n_new:
+            # the host looks at the tokens (for an EOS) only every 16 steps
+            if eos and count % 16 == 0 and any(t in eos for t in out[:count].tolist()):
+                break
+            if use_graph:
+                lg = self.decode_step(tok, cache)
+            else:
+                lg, cache = self.forward(tok.view(1, 1), cache)
+                lg = lg[:, -1, :]
+            tok = _sample(lg, temperature, top_p).view(1)
+            out[count] = tok[0]
+            count += 1
+        ids = out[:count].tolist()
+        if eos:
+            for i, t in enumerate(ids):
+                if t in eos:
+                    return ids[:i + 1]
+        return ids
+
+    def check(self):
+        for f in self.ffn_layers:
+            f.check()
+
+    def close(self):
+        self._graph = None
+        self.cold_store.close()

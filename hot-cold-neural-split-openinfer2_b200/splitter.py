@@ -9,13 +9,17 @@
 * A GPU splitter (:func:`quantize_int4_rows`, :func:`build_records`,
   :func:`build_cold_image`, :func:`hot_from_dense`) that writes byte-identical
   records from device-resident weights, replacing the reference's
-  per-vector Python loop (splitter.py:186-262).
+  per-vector Python loop (splitter.py:186-262), and :func:`split_dense`, the
+  reference's split-dense entry point (splitter.py:129-302) on top of it:
+  the same split directory, file for file.
 
 Everything that computes runs on CUDA; there is no CPU fallback.
 """
 from __future__ import annotations
 
+import json
 import struct
+from pathlib import Path
 from typing import Optional, Sequence
 
 import numpy as np
@@ -302,3 +306,133 @@ def hot_from_dense(gate: torch.Tensor, up: torch.Tensor, down: torch.Tensor, hot
         scales = s / torch.full_like(s, 448.0)
         g, u, d = g / scales[:, 0:1], u / scales[:, 1:2], d / scales[:, 2:3]
     return (g.to(torch.float8_e4m3fn), u.to(torch.float8_e4m3fn), d.t().to(torch.float8_e4m3fn), scales)
+
+
+# ─── split_dense (splitter.py:129-302) ────────────────────────────────────────
+def _load_base_model(base_model, trust_remote_code: bool):
+    """The model object split_dense reads: passed in directly, or loaded from a
+    path the way the reference does (fp16 on the CPU, splitter.py:151-154)."""
+    if not isinstance(base_model, (str, Path)):
+        return base_model
+    from transformers import AutoModelForCausalLM      # only needed for a checkpoint path
+    return AutoModelForCausalLM.from_pretrained(str(base_model), torch_dtype=torch.float16, device_map="cpu",
+                                                trust_remote_code=trust_remote_code)
+
+
+def split_dense(base_model, profile_path: str, output_dir: str, hot_count: int = HOT_COUNT_DENSE,
+                trust_remote_code: bool = False, device="cuda") -> dict:
+    """The reference's split-dense step (splitter.py:129-302) on the GPU.
+
+    ``base_model`` is a checkpoint path (loaded like the reference: fp16 on
+    the CPU) or an already loaded causal-LM object with the same attributes
+    (``config``, ``model.layers[i].self_attn/mlp/norms``, ``model.embed_tokens``,
+    ``model.norm``, ``lm_head``).  Writes the same artefacts into
+    ``output_dir`` -- ``hot_weights/shared.pt``,
+    ``hot_weights/layer_XXX_expert_000.pt``, ``cold_weights.bin``,
+    ``cold_index.npy`` and ``split_config.json`` -- with the same contents:
+    weights taken at fp16 as the reference loads them, hot neurons = top
+    ``hot_count`` of the profile's ``expert_0`` frequencies (torch.topk on the
+    host, as the reference), hot FP8 by direct cast, cold records quantised on
+    the GPU by :func:`build_records` (byte-identical to the reference's
+    per-vector loop).  Raises ValueError where the reference does (hidden size
+    other than 4096, a layer without usable frequencies).  Returns the config
+    dict."""
+    out = Path(output_dir)
+    hot_dir = out / "hot_weights"
+    hot_dir.mkdir(parents=True, exist_ok=True)
+    with open(profile_path) as f:
+        profile = json.load(f)
+    model = _load_base_model(base_model, trust_remote_code)
+    hf = model.config
+    if hf.hidden_size != HIDDEN_DIM:
+        raise ValueError(f"Base model hidden_size={hf.hidden_size} but the cold-record binary layout is sized for "
+                         f"{HIDDEN_DIM}")
+    dev = torch.device(device)
+    f16 = lambda w: w.data.to(torch.float16) if hasattr(w, "data") else torch.as_tensor(w).to(torch.float16)
+    layers = model.model.layers
+    num_layers = hf.num_hidden_layers
+    inter_dim = hf.intermediate_size
+
+    shared = {}
+    for li, layer in enumerate(layers):
+        for name in ("q_proj", "k_proj", "v_proj", "o_proj"):
+            w = f16(getattr(layer.self_attn, name).weight)
+            shared[f"layer_{li:03d}.{name}"] = w.to(dev).to(torch.float8_e4m3fn).cpu()
+        shared[f"layer_{li:03d}.input_layernorm"] = f16(layer.input_layernorm.weight).cpu()
+        shared[f"layer_{li:03d}.post_attention_layernorm"] = f16(layer.post_attention_layernorm.weight).cpu()
+    shared["embed_tokens"] = f16(model.model.embed_tokens.weight).cpu()
+    shared["lm_head"] = f16(model.lm_head.weight).cpu()
+    shared["final_norm"] = f16(model.model.norm.weight).cpu()
+    torch.save(shared, str(hot_dir / "shared.pt"))
+    del shared
+
+    cold_index = np.zeros((num_layers, 1, 2), dtype=np.uint64)
+    total_hot = total_cold = 0
+    cursor = 0
+    with open(out / "cold_weights.bin", "wb") as cold_f:
+        for li in range(num_layers):
+            mlp = layers[li].mlp
+            gate = f16(mlp.gate_proj.weight).to(dev).float()          # (I, H)
+            up = f16(mlp.up_proj.weight).to(dev).float()              # (I, H)
+            down = f16(mlp.down_proj.weight).to(dev).float()          # (H, I)
+            I = gate.shape[0]
+            freq_list = profile["layers"].get(str(li), {}).get("expert_0", [])
+            if not freq_list or len(freq_list) != I:
+                raise ValueError(f"profile has no usable expert_0 frequencies for layer {li} "
+                                 f"(got {len(freq_list)}, need {I})")
+            top = torch.topk(torch.tensor(freq_list), min(hot_count, I)).indices
+            hot_mask = torch.zeros(I, dtype=torch.bool)
+            hot_mask[top] = True
+            hot_ids = hot_mask.nonzero(as_tuple=True)[0]
+            cold_ids = (~hot_mask).nonzero(as_tuple=True)[0]
+            total_hot += len(hot_ids)
+            total_cold += len(cold_ids)
+            hd = hot_ids.to(dev)
+            torch.save({"neuron_ids": hot_ids,
+                        "gate": gate[hd].to(torch.float8_e4m3fn).cpu(),
+                        "up": up[hd].to(torch.float8_e4m3fn).cpu(),
+                        "down": down[:, hd].to(torch.float8_e4m3fn).cpu()},
+                       str(hot_dir / f"layer_{li:03d}_expert_000.pt"))
+            cd = cold_ids.to(dev)
+            start = cursor
+            cold_f.write(struct.pack("<HHIq", li, 0, len(cold_ids), 0))
+            cursor += SECTION_HEADER_BYTES
+            # records in chunks (bounded device memory), in cold-id order
+            for c0 in range(0, len(cold_ids), 4096):
+                ids = cd[c0:c0 + 4096]
+                rec = build_records(ids, gate[ids], up[ids], down[:, ids].t().contiguous())
+                cold_f.write(rec.cpu().numpy().tobytes())
+                cursor += rec.numel()
+            pad = (-cursor) % PAGE_ALIGN
+            if pad:
+                cold_f.write(b"\x00" * pad)
+                cursor += pad
+            cold_index[li, 0] = (start, len(cold_ids))
+            del gate, up, down
+    np.save(str(out / "cold_index.npy"), cold_index)
+    config = {
+        "base_model": str(base_model) if isinstance(base_model, (str, Path)) else getattr(hf, "_name_or_path", ""),
+        "hidden_dim": hf.hidden_size,
+        "intermediate_dim": inter_dim,
+        "expert_inter_dim": inter_dim,
+        "num_experts": 1,
+        "num_layers": num_layers,
+        "vocab_size": hf.vocab_size,
+        "num_attention_heads": hf.num_attention_heads,
+        "num_key_value_heads": hf.num_key_value_heads,
+        "rope_theta": getattr(hf, "rope_theta", 10000.0),
+        "rms_norm_eps": hf.rms_norm_eps,
+        "hidden_act": hf.hidden_act,
+        "act_on_both": getattr(hf, "model_type", "") == "bamboo",
+        "max_position_embeddings": hf.max_position_embeddings,
+        "hot_count": hot_count,
+        "total_hot_neurons": int(total_hot),
+        "total_cold_neurons": int(total_cold),
+        "hot_fraction": total_hot / max(total_hot + total_cold, 1),
+        "cold_file_bytes": cursor,
+        "neuron_record_bytes": NEURON_RECORD_BYTES,
+        "page_align": PAGE_ALIGN,
+    }
+    with open(out / "split_config.json", "w") as f:
+        json.dump(config, f, indent=2)
+    return config

@@ -414,6 +414,24 @@ HC_API int hc_ffn_batch_layer_partial(const hc_layer_desc* layer, const void* pa
 HC_API int64_t hc_batch_pack_bytes(int32_t n_hot, int32_t n_records);
 HC_API int hc_batch_pack(const hc_layer_desc* layer, void* packed, hc_stream_t stream);
 
+/* ======================================================================= */
+/* Decode-step attention projections                                       */
+/* ======================================================================= */
+
+/*
+ * hc_fp8_gemv -- the batch-1 form of the attention projections F.linear(x, W)
+ * in GroupedQueryAttention.forward (engine.py:100-102, :123), whose weights
+ * the reference stores as FP8 e4m3 at rest and casts to fp16 for every call
+ * (engine.py:77-82): y = W x, reading the e4m3 bytes directly.
+ *   w          [rows][cols] e4m3 (row-major, 16-byte aligned); cols == 4096
+ *   row_scale  optional [rows] fp32 per-row scale (NULL = 1, the reference's
+ *              direct cast)
+ *   x          [cols] fp16 (16-byte aligned); y [rows] fp16
+ * fp32 accumulation of exact f16 x f16 products; one launch, no workspace.
+ */
+HC_API int hc_fp8_gemv(const uint8_t* w, const float* row_scale, int64_t rows, int32_t cols, const void* x,
+                       void* y, hc_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

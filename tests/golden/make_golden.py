@@ -25,6 +25,15 @@ here.  What is produced (all from reference code paths, seeds fixed):
 * ``ffn.npz``            engine.sparse_ffn (engine.py:173-209) for SwiGLU and
                          dReLU, and SparseFFNLayer.forward / _cold_ids_for
                          (engine.py:274-312) with the predictor registry.
+* ``engine.npz``         the reference's DesdemonaEngine (engine.py:317-511)
+                         on a split of the 2-layer Llama-geometry stub of
+                         stub_models.py written by the reference's split_dense:
+                         prefill logits, greedy generate() tokens, the logits of
+                         every decode step with the cache, the cold ids each
+                         layer fetched, and the split's small files
+                         (split_config.json, cold_index.npy, a digest of
+                         cold_weights.bin).  ``make_golden.py <ref> engine``
+                         regenerates only this file.
 """
 
 from __future__ import annotations
@@ -223,8 +232,89 @@ def main(ref_dir: str):
     print("golden fixtures written to", HERE)
 
 
+def engine_main(ref_dir: str):
+    """engine.npz: the reference's own engine, run on the CPU in fp16."""
+    import hashlib
+    sys.path.insert(0, ref_dir)
+    sys.path.insert(0, str(HERE))
+    import splitter  # noqa: E402  (reference)
+    import predictor as ref_predictor  # noqa: E402
+    import engine as ref_engine  # noqa: E402
+    import stub_models as SM  # noqa: E402
+
+    n_layers, inter, hot_count, vocab = 2, 64, 16, 64
+    stub = SM.engine_stub_model(11, n_layers, inter, vocab)
+    splitter.AutoModelForCausalLM = types.SimpleNamespace(from_pretrained=lambda *a, **k: stub)
+    work = Path(tempfile.mkdtemp())
+    (work / "profile.json").write_text(json.dumps(SM.engine_stub_profile(12, n_layers, inter)))
+    splitter.split_dense("engine-stub", str(work / "profile.json"), str(work / "split"), hot_count=hot_count)
+    pdir = work / "predictors"
+    pdir.mkdir()
+    for li in range(n_layers):
+        p = ref_predictor.NeuronPredictor(SM.H, inter, rank=16)
+        down, up, bias = SM.engine_stub_predictor_params(li, 13, inter, 16)
+        with torch.no_grad():
+            p.down.weight.copy_(down)
+            p.up.weight.copy_(up)
+            p.up.bias.copy_(bias)
+        p.save(str(pdir / f"layer_{li:03d}_expert_000.pt"))
+
+    fetched = []                           # (layer, ids) of every cold read, in order
+    orig_read = splitter.ColdWeightStore.read_neurons
+
+    def recording_read(self, layer_idx, expert_idx, neuron_ids):
+        fetched.append((layer_idx, list(neuron_ids)))
+        return orig_read(self, layer_idx, expert_idx, neuron_ids)
+    splitter.ColdWeightStore.read_neurons = recording_read
+
+    eng = ref_engine.DesdemonaEngine(str(work / "split"), str(pdir), device="cpu", n_threads=2, max_seq_len=64)
+    g = torch.Generator().manual_seed(14)
+    prompt = torch.randint(0, vocab, (1, 12), generator=g)
+    out = {"prompt": prompt.numpy()}
+    with torch.inference_mode():
+        logits, kv = eng.forward(prompt)
+        out["prefill_logits"] = logits[0].float().numpy()
+        n_prefill = len(fetched)
+        tokens = eng.generate(prompt, max_new_tokens=8, temperature=0.0)
+        out["greedy_tokens"] = np.asarray(tokens, np.int64)
+        # teacher-forced decode: the logits of each generated token's step, with the cache
+        logits, kv = eng.forward(prompt)
+        steps = [logits[0, -1].float().numpy()]
+        fetch_steps = []
+        for t in tokens[:-1]:
+            k0 = len(fetched)
+            logits, kv = eng.forward(torch.tensor([[t]]), kv)
+            steps.append(logits[0, -1].float().numpy())
+            fetch_steps.append(fetched[k0:])
+    out["decode_logits"] = np.stack(steps)
+    for li in range(n_layers):
+        out[f"prefill_fetch_l{li}"] = np.asarray(fetched[li][1] if fetched[li][0] == li else [], np.int64)
+    out["decode_fetch"] = np.asarray([[len(ids) for (_, ids) in st] for st in fetch_steps], np.int64)
+    out["n_prefill_reads"] = np.asarray([n_prefill])
+    split = work / "split"
+    out["split_config"] = np.frombuffer((split / "split_config.json").read_bytes(), np.uint8)
+    out["cold_index"] = np.load(split / "cold_index.npy")
+    out["cold_sha256"] = np.frombuffer(hashlib.sha256((split / "cold_weights.bin").read_bytes()).digest(), np.uint8)
+    hot0 = torch.load(split / "hot_weights" / "layer_000_expert_000.pt")
+    out["hot0_ids"] = hot0["neuron_ids"].numpy()
+    out["hot0_gate_bytes"] = hot0["gate"].view(torch.uint8).numpy()
+    shared = torch.load(split / "hot_weights" / "shared.pt")
+    out["shared_keys"] = np.asarray(sorted(shared.keys()))
+    out["shared_q0_sha256"] = np.frombuffer(hashlib.sha256(
+        shared["layer_000.q_proj"].view(torch.uint8).numpy().tobytes()).digest(), np.uint8)
+    eng.close()
+    splitter.ColdWeightStore.read_neurons = orig_read
+    np.savez_compressed(HERE / "engine.npz", **out)
+    shutil.rmtree(work)
+    print("engine fixture written to", HERE / "engine.npz")
+
+
 if __name__ == "__main__":
     ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("HC_REFERENCE_DIR")
     if not ref:
-        raise SystemExit("usage: make_golden.py <reference checkout dir>  (or set HC_REFERENCE_DIR)")
-    main(ref)
+        raise SystemExit("usage: make_golden.py <reference checkout dir> [engine]  (or set HC_REFERENCE_DIR)")
+    if len(sys.argv) > 2 and sys.argv[2] == "engine":
+        engine_main(ref)
+    else:
+        main(ref)
+        engine_main(ref)
