@@ -106,6 +106,7 @@ struct StackSmem {
   float zred[NWARPS];
   float red[NSG][2][SG_WARPS][2 * NB_COLD];
   int32_t sgdec[NSG][2];            // per-subgroup decision of its poller
+  int32_t sgok[2][NSG];             // per layer parity: subgroup finished its layer without an abort
   uint64_t tstat[8];                // trace counters of subgroup 0's poller
   int32_t plan_list[COLD_LIST];     // nids, then record indices, of this CTA's active cold records
   uint32_t own_words[OWN_WORDS];    // predicted mask words of this CTA's neuron-id range
@@ -123,10 +124,12 @@ struct StackSmem {
   alignas(8) uint64_t wdown_done;   // planner -> consumers: done with the W_down rows in ystage
 };
 constexpr size_t RING_OFF = (sizeof(StackSmem) + 127) / 128 * 128;
+static_assert(RING_OFF + (size_t)NE * ENTRY_BYTES <= 227 * 1024, "stack kernel shared memory exceeds 227 KB");
 
 struct StackParams {
   const hc_layer_desc* layers;
   int n_layers;
+  int n_compute;             // layers computed: n_layers, or n_layers - 1 when the last is only predicted
   int inter;
   int words;                 // ceil(inter / 32)
   int words_lo, words_n;     // mask words (neuron ids / 32) this GPU owns
@@ -489,14 +492,20 @@ __device__ __forceinline__ void sg_hot(StackSmem& sm, const StackParams& p, cons
     }
     a = gated(s * sgs, uu * sus, p.relu, p.both) * sds;
   }
+  // a neuron whose gated activation is exactly zero (dReLU: either branch <= 0)
+  // adds nothing: its down column is skipped (every warp holds the same a's)
   const float a0 = __shfl_sync(0xffffffffu, a, 0), a1 = __shfl_sync(0xffffffffu, a, 1);
-  axpy32_fp8(slot0 + 2 * H + SPT * u, __half_as_ushort(__float2half_rn(a0)), y);
-  if (n > 1) axpy32_fp8(slot1 + 2 * H + SPT * u, __half_as_ushort(__float2half_rn(a1)), y);
+  if (a0 != 0.0f) axpy32_fp8(slot0 + 2 * H + SPT * u, __half_as_ushort(__float2half_rn(a0)), y);
+  if (n > 1 && a1 != 0.0f) axpy32_fp8(slot1 + 2 * H + SPT * u, __half_as_ushort(__float2half_rn(a1)), y);
 }
 
 // Cold group: n (<= NB_COLD) INT4 records, two per slot.
+// The decoded down rows carry a bias (1032 / 1152 per element, int4_pairs):
+// the f16 coefficients are summed into csa / csb and the bias is removed once
+// per layer (cold_bias_out), which keeps it small against fp32's precision.
 __device__ __forceinline__ void sg_cold(StackSmem& sm, const StackParams& p, const uint8_t* slot0,
-                                        const uint8_t* slot1, int n, int sg, int buf, float (&y)[SPT]) {
+                                        const uint8_t* slot1, int n, int sg, int buf, float (&y)[SPT], float& csa,
+                                        float& csb) {
   const int u = threadIdx.x & (SG_THREADS - 1), lane = threadIdx.x & 31;
   XFix xf;
   {
@@ -526,11 +535,11 @@ __device__ __forceinline__ void sg_cold(StackSmem& sm, const StackParams& p, con
   const float uu = __shfl_down_sync(0xffffffffu, s, NB_COLD);
   float a = 0.0f;
   if (lane < n) a = gated(s, uu, p.relu, p.both);
-  float csa = 0.0f, csb = 0.0f;   // sums of the f16 coefficients (the decoded rows carry a bias)
 #pragma unroll
   for (int j = 0; j < NB_COLD; ++j) {
     const float aj = __shfl_sync(0xffffffffu, a, j);
-    if (j < n) {
+    // a zero activation (dReLU) adds nothing: skip the record's down column
+    if (j < n && aj != 0.0f) {
       const __half c16 = __float2half_rn(aj * ld_half(rec[j] + SCALE_OFF + 4 * NGROUPS + gs));
       const __half c16s = __hmul(c16, __float2half(0.0625f));    // exact unless subnormal; csb tracks it
       csa += __half2float(c16);
@@ -538,6 +547,8 @@ __device__ __forceinline__ void sg_cold(StackSmem& sm, const StackParams& p, con
       axpy32_int4(rec[j] + 2 * VEC_BYTES + 16 * u, __half_as_ushort(c16), __half_as_ushort(c16s), y);
     }
   }
+}
+__device__ __forceinline__ void cold_bias_out(float (&y)[SPT], float csa, float csb) {
 #pragma unroll
   for (int k = 0; k < SPT; ++k) y[k] = (k & 1) ? fmaf(-1152.0f, csb, y[k]) : fmaf(-1032.0f, csa, y[k]);
 }
@@ -934,6 +945,9 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         if (!ok) break;
         ok = wdown(dn, l + 1, d0, d1, [&](int r) { return xs[r - d0 * WD_ROWS]; });
         if (!ok) break;
+        // leave ystage all zero: it becomes the layer's y accumulator
+        for (int i = lane; i < (d1 - d0) * WD_ROWS; i += 32) xs[i] = 0.0f;
+        __syncwarp();
         if (lane == 0) mbar_arrive(&sm.wdown_done);       // ystage is the consumers' again
         wdown_count(l + 1, d0, d1);
         preload(l + 1);
@@ -964,7 +978,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
     Producer pr;
     if (lane == 0) {
       pr.pol = l2_evict_first_policy();
-      for (int l = 0; l < p.n_layers && pr.ok; ++l) {
+      for (int l = 0; l < p.n_compute && pr.ok; ++l) {
         // stay at most two layers ahead of the consumers (ngroups is indexed l & 3)
         {
           const uint64_t t0 = globaltimer_ns();
@@ -1014,9 +1028,11 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
           if (!pr.ok) break;
           __threadfence();
         }
-        // Cold records from the layer's pool, COLD_CLAIM per claim (the next
-        // claim is taken before the current one is issued), once every CTA has
-        // published its list.
+        // Once every CTA has published its list, this CTA streams its static
+        // share of the layer: pool entries [c n / G, (c+1) n / G) (cold records),
+        // then hot neurons [c n_hot / G, (c+1) n_hot / G), two per group.  Equal
+        // shares of both kinds give every SM the same bytes, so the layer's CTAs
+        // finish together (no claims, no counter round trips).
         {
           const uint64_t t0 = globaltimer_ns();
           uint32_t i = 0;
@@ -1034,40 +1050,30 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         {
           const uint32_t total = __ldcg(p.gfill + l % NACC);
           const int32_t* pool = p.gpool + (size_t)(l % NACC) * POOL_CAP;
-          uint32_t i = atomicAdd(p.gclaim + l % NACC, (uint32_t)COLD_CLAIM);
-          while (pr.ok && i < total) {
-            const uint32_t inext = atomicAdd(p.gclaim + l % NACC, (uint32_t)COLD_CLAIM);
-            const int n = (int)min((uint32_t)COLD_CLAIM, total - i);
-            int rec[COLD_CLAIM];
+          const uint32_t i0 = (uint32_t)split_lo(total, c, G), i1 = (uint32_t)split_lo(total, c + 1, G);
+          for (uint32_t i = i0; pr.ok && i < i1; i += NB_COLD) {
+            const int m = (int)min((uint32_t)NB_COLD, i1 - i);
+            int rec[NB_COLD];
 #pragma unroll
-            for (int k = 0; k < COLD_CLAIM; ++k) rec[k] = (k < n) ? __ldcg(pool + i + k) : 0;
+            for (int k = 0; k < NB_COLD; ++k) rec[k] = (k < m) ? __ldcg(pool + i + k) : 0;
+            Copy cp[NB_COLD];
 #pragma unroll
-            for (int j = 0; j < COLD_CLAIM; j += NB_COLD) {
-              if (j >= n || !pr.ok) break;
-              const int m = min(NB_COLD, n - j);
-              Copy cp[NB_COLD];
-#pragma unroll
-              for (int k = 0; k < NB_COLD; ++k)
-                cp[k] = {k < m ? d.cold_records + (size_t)rec[j + k] * REC_BYTES : nullptr,
-                         k < m ? (uint32_t)REC_COPY : 0u,
-                         (uint32_t)((k >> 1) * HALF_BYTES + (k & 1) * REC_SLOT_OFF)};
-              issue_entry(sm, ring, pr, l, UNIT_COLD, m, (int64_t)(i + j), cp, iwp, p.wait_ns);
-              ++ng;
-            }
-            cold_taken += n;
-            i = inext;
+            for (int k = 0; k < NB_COLD; ++k)
+              cp[k] = {k < m ? d.cold_records + (size_t)rec[k] * REC_BYTES : nullptr,
+                       k < m ? (uint32_t)REC_COPY : 0u,
+                       (uint32_t)((k >> 1) * HALF_BYTES + (k & 1) * REC_SLOT_OFF)};
+            issue_entry(sm, ring, pr, l, UNIT_COLD, m, (int64_t)i, cp, iwp, p.wait_ns);
+            ++ng;
+            cold_taken += m;
           }
         }
         if (!pr.ok) break;
         trace_ev(p, l, 12);
         trace_ev(p, l, 13);
-        // Hot neurons, two per claim until the layer's counter passes n_hot.
         uint64_t claimed = 0;
-        int64_t next = sp.n_static + (int64_t)atomicAdd(p.hot_next + l % NACC, (uint32_t)NB_HOT);
-        while (pr.ok && next < d.n_hot) {
-          const int64_t i = next;
-          next = sp.n_static + (int64_t)atomicAdd(p.hot_next + l % NACC, (uint32_t)NB_HOT);
-          const int n = (int)min((int64_t)NB_HOT, d.n_hot - i);
+        const int64_t hA = split_lo(d.n_hot, c, G), hB = split_lo(d.n_hot, c + 1, G);
+        for (int64_t i = hA; pr.ok && i < hB; i += NB_HOT) {
+          const int n = (int)min((int64_t)NB_HOT, hB - i);
           Copy cp[2];
 #pragma unroll
           for (int k = 0; k < 2; ++k)
@@ -1112,7 +1118,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
     uint32_t wd_phase = 0;   // layers with a next predictor so far (wdown_done phases)
     int rbuf = 0, dbuf = 0;
     bool ok = true;
-    for (int l = 0; l < p.n_layers && ok; ++l) {
+    for (int l = 0; l < p.n_compute && ok; ++l) {
       const hc_layer_desc d = p.layers[l];
       const bool pred_next = next_pred(p, l);
       if (t == 0 && c == 0 && !p.masks_given && d.pred_w_up != nullptr && !rank_ok(d.rank))
@@ -1175,6 +1181,11 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
 
       // ---- RMSNorm (engine.py:295; torch.nn.RMSNorm) -> f16 and fixed-point copies
       {
+        // the layer's y accumulator starts at zero (the previous layer's last
+        // reads of it are behind the grid barrier); the barriers in cons_sum
+        // order this before the W_down rows below are written into it
+        reinterpret_cast<float4*>(sm.ystage)[2 * t] = make_float4(0.f, 0.f, 0.f, 0.f);
+        reinterpret_cast<float4*>(sm.ystage)[2 * t + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
         float ss = 0.0f;
 #pragma unroll
         for (int i = 0; i < EPT; ++i) ss = fmaf(x[i], x[i], ss);
@@ -1242,6 +1253,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
       float y[SPT];
 #pragma unroll
       for (int k = 0; k < SPT; ++k) y[k] = 0.0f;
+      float csa = 0.0f, csb = 0.0f;      // f16 coefficient sums of the cold rows (bias removed at the end)
       // trace counters (subgroup 0's poller, SM cycles): 0 fill waits, 1 cold,
       // 2 hot, 4 group barrier, 5 group setup, 6 release, 7 start
       const bool tr = p.trace != nullptr && t == 0;
@@ -1278,7 +1290,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         const uint64_t tg0 = tr ? (uint64_t)clock64() : 0;
         if (tr) sm.tstat[5] += tg0 - tb;
         if (inf.kind == UNIT_COLD) {
-          sg_cold(sm, p, s0, s1, inf.n, sg, rbuf, y);
+          sg_cold(sm, p, s0, s1, inf.n, sg, rbuf, y, csa, csb);
           rbuf ^= 1;
         } else {
           sg_hot(sm, p, d.hot_scale, s0, s1, inf.n, inf.index, sg, rbuf, y);
@@ -1309,53 +1321,42 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         trace_set(p, l, 26, sm.tstat[6]);
         trace_set(p, l, 27, (uint64_t)clock64() - sm.tstat[7]);
       }
-      // ---- all subgroups done: one abort decision for everyone, then sum the
-      // partial y (fixed tree in shared memory) and add it to the layer's accumulator
-      if (t == 0) {
-        bool okw = true;
-        if (pred_next) okw = mbar_wait(&sm.wdown_done, wd_phase & 1u, p.wait_ns);
-        if (!okw) {
+      // ---- this subgroup is done with the layer: remove the cold rows' bias and,
+      // once the planner has released ystage (its W_down rows), add the partial y
+      // into ystage with shared-memory atomics (element 32u+k at k*128+u: a warp's
+      // adds hit 32 banks).  Subgroups that finish early do this while the others
+      // stream their last groups.
+      cold_bias_out(y, csa, csb);
+      if (u == 0) {
+        if (pred_next && !mbar_wait(&sm.wdown_done, wd_phase & 1u, p.wait_ns)) {
           sm.abort = 1;
           atomicOr(p.status, HC_ERR_TIMEOUT);
         }
-        sm.flag = ld_vol(&sm.abort) ? 0 : 1;
+        // one decision per subgroup and layer parity, read by every consumer after the
+        // CTA barrier below (rewritten only two layers later, past another CTA barrier)
+        sm.sgok[l & 1][sg] = ld_vol(&sm.abort) ? 0 : 1;
       }
       if (pred_next) ++wd_phase;
+      named_bar(2 + sg, SG_THREADS);
+      if (sm.sgok[l & 1][sg]) {
+#pragma unroll
+        for (int k = 0; k < SPT; ++k) atomicAdd(sm.ystage + k * SG_THREADS + u, y[k]);
+      }
       named_bar(1, CONS_THREADS);
-      if (sm.flag == 0) {
+      if (!(sm.sgok[l & 1][0] & sm.sgok[l & 1][1] & sm.sgok[l & 1][2] & sm.sgok[l & 1][3])) {
         ok = false;
         break;
       }
       base += (uint32_t)ld_vol(&sm.ngroups[l & 3]);
       {
-        float* bufA = sm.ystage;
-        float* bufB = reinterpret_cast<float*>(sm.xh);     // xh + xq: 16 KB, dead until the next layer
-        if (sg >= 2) {
-          float* dst = sg == 2 ? bufA : bufB;
-#pragma unroll
-          for (int k = 0; k < SPT; ++k) dst[k * SG_THREADS + u] = y[k];
-        }
-        named_bar(1, CONS_THREADS);
-        if (sg < 2) {
-          const float* src = sg == 0 ? bufA : bufB;
-#pragma unroll
-          for (int k = 0; k < SPT; ++k) y[k] += src[k * SG_THREADS + u];
-        }
-        named_bar(1, CONS_THREADS);
-        if (sg < 2) {
-          float* dst = sg == 0 ? bufA : bufB;
-#pragma unroll
-          for (int k = 0; k < SPT; ++k) dst[k * SG_THREADS + u] = y[k];
-        }
-        named_bar(1, CONS_THREADS);
-        // element layout: thread t sums elements [8t, 8t+8) (element 32u+k sits at
-        // k*128+u) and stores them in element order for one bulk reduction
+        // element order for one bulk reduction: thread t gathers elements [8t, 8t+8)
+        // into bufB (xh + xq: dead until the next layer's input is normalised)
+        float* bufB = reinterpret_cast<float*>(sm.xh);
         float e[EPT];
         const int eu = t >> 2, ek = EPT * (t & 3);
 #pragma unroll
-        for (int i = 0; i < EPT; ++i) e[i] = bufA[(ek + i) * SG_THREADS + eu] + bufB[(ek + i) * SG_THREADS + eu];
-        named_bar(1, CONS_THREADS);
-        float4* yo = reinterpret_cast<float4*>(bufA + EPT * t);
+        for (int i = 0; i < EPT; ++i) e[i] = sm.ystage[(ek + i) * SG_THREADS + eu];
+        float4* yo = reinterpret_cast<float4*>(bufB + EPT * t);
         yo[0] = make_float4(e[0], e[1], e[2], e[3]);
         yo[1] = make_float4(e[4], e[5], e[6], e[7]);
         fence_proxy_async_smem();
@@ -1363,7 +1364,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         if (t == 0) {
           trace_ev(p, l, 9);
           // y_l += this CTA's partial: the L2 adds 16 KB in one bulk operation
-          bulk_reduce_add_f32(p.yacc + ((size_t)(l % NACC) * YCOPIES + c % YCOPIES) * H, bufA, H * sizeof(float));
+          bulk_reduce_add_f32(p.yacc + ((size_t)(l % NACC) * YCOPIES + c % YCOPIES) * H, bufB, H * sizeof(float));
           bulk_wait_all();
           trace_ev(p, l, 28);
           // then the grid-barrier arrival, ordered after the reduction's writes
@@ -1376,7 +1377,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
     }
     // ---- output: x_L = x_{L-1} + y_{L-1}
     if (ok) {
-      const int L = p.n_layers;
+      const int L = p.n_compute;
       ok = layer_wait(sm, p, L - 1);
       if (ok && c == 0) {
         float xo[EPT];
@@ -1452,6 +1453,8 @@ extern "C" int hc_ffn_stack_tp(const hc_layer_desc* layers, int32_t n_layers, in
   if (!layers || n_layers <= 0 || n_layers > 32767 || !x_in || !masks || !x_out || !workspace || !status)
     return HC_ERR_ARG;
   if (masks_given < 0 || masks_given > 2) return HC_ERR_ARG;
+  // predicting the last layer only needs a layer before it and the kernel's own prediction
+  if (tp && tp->predict_last && (n_layers < 2 || masks_given == 1)) return HC_ERR_ARG;
   if (inter <= 0 || inter > 32768 || (inter & 3) != 0 || (act != HC_ACT_SILU && act != HC_ACT_RELU))
     return HC_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(x_in) & 15) || (reinterpret_cast<uintptr_t>(x_out) & 15) ||
@@ -1483,6 +1486,7 @@ extern "C" int hc_ffn_stack_tp(const hc_layer_desc* layers, int32_t n_layers, in
   StackParams p;
   p.layers = layers;
   p.n_layers = n_layers;
+  p.n_compute = n_layers - ((tp && tp->predict_last) ? 1 : 0);
   p.inter = inter;
   p.words = words;
   p.words_lo = words_lo;

@@ -18,6 +18,7 @@
 from __future__ import annotations
 
 import ctypes
+import math
 from pathlib import Path
 from typing import Optional, Sequence
 
@@ -224,12 +225,14 @@ class FFNStack:
                              mask_out=self.masks[0:1])
 
     def launch(self, x: torch.Tensor, masks_given=False, x_hist: Optional[torch.Tensor] = None,
-               out: Optional[torch.Tensor] = None, trace: Optional[torch.Tensor] = None) -> torch.Tensor:
+               out: Optional[torch.Tensor] = None, trace: Optional[torch.Tensor] = None,
+               predict_last: bool = False) -> torch.Tensor:
         """One hc_ffn_stack launch.  ``masks_given``: False (row 0 of
         ``self.masks`` holds layer 0's set), True (every row given) or 2 (the
-        kernel predicts layer 0 too).  ``trace`` (int64 [L, grid, 40], device)
-        (zeroed) receives per-CTA phase timestamps and waits
-        (see include/hotcold.h)."""
+        kernel predicts layer 0 too).  ``predict_last``: the last layer is
+        not computed, only its mask row predicted (from the input of the layer
+        before it).  ``trace`` (int64 [L, grid, 40], device) (zeroed)
+        receives per-CTA phase timestamps and waits (see include/hotcold.h)."""
         out = self.x_out if out is None else out
         tp = None
         if self.tp is not None and self.tp.size > 1:
@@ -237,9 +240,11 @@ class FFNStack:
                           peer_buf=N.ptr(self.tp.peer_buf), seq_base=(self.tp.launches * self.L) & 0xFFFFFFFF,
                           wait_ns=self.wait_ns)
             self.tp.launches += 1
-        elif self.wait_ns:
+        elif self.wait_ns or predict_last:
             tp = N.TPDesc(size=1, rank=0, words_lo=0, words_n=self.words, peer_buf=None, seq_base=0,
                           wait_ns=self.wait_ns)
+        if tp is not None:
+            tp.predict_last = 1 if predict_last else 0
         mg = 2 if masks_given == 2 else (1 if masks_given else 0)
         N.check(N.lib.hc_ffn_stack_tp(N.ptr(self.desc_dev), self.L, self.inter, N.ptr(x), N.ptr(self.masks),
                                       mg, N.ptr(out), N.ptr(x_hist), self.eps, self.act,
@@ -674,6 +679,32 @@ class SparseFFNLayer(nn.Module):
                                      max_batch=cap, single_token_stack=False)
         return self._batch
 
+    def forward_lookahead(self, x: torch.Tensor, words: torch.Tensor, nxt: "SparseFFNLayer",
+                          next_words: torch.Tensor) -> torch.Tensor:
+        """forward(x, words) for one token row that also predicts the next
+        layer's fetch set from this x (its post-attention hidden state,
+        engine.py:430-438) into ``next_words``, inside the same kernel
+        launch.  ``words`` and ``next_words`` must be consecutive rows of one
+        [L, W] int32 buffer."""
+        pair = getattr(self, "_pair", None)
+        if pair is None or pair[0] is not nxt:
+            st = FFNStack(self.cold_store, [self.hot, nxt.hot], [self._norm32, nxt._norm32], [None, nxt._pred],
+                          self.activation, self.act_on_both, self.eps,
+                          layer_ids=[self.layer_idx, nxt.layer_idx], inter=self.inter_dim)
+            pair = (nxt, st)
+            self._pair = pair
+        st = pair[1]
+        base = words.untyped_storage().data_ptr()
+        if next_words.untyped_storage().data_ptr() != base or \
+                next_words.data_ptr() - words.data_ptr() != 4 * st.words:
+            raise ValueError("words and next_words must be consecutive rows of one buffer")
+        st.masks = words.view(-1).as_strided((2, st.words), (st.words, 1))
+        B, T, H = x.shape
+        rows = x.reshape(B * T, H).to(torch.float32).contiguous()
+        out = torch.empty_like(rows)
+        st.launch(rows[0], masks_given=False, out=out[0], predict_last=True)
+        return out.reshape(B, T, H).to(x.dtype)
+
     def forward(self, x: torch.Tensor, prefetch_future=None) -> torch.Tensor:
         B, T, H = x.shape
         words = prefetch_future if prefetch_future is not None else self._mask_words(x)
@@ -694,6 +725,8 @@ class SparseFFNLayer(nn.Module):
         self._stack.check()
         if self._batch is not None:
             self._batch.check()
+        if getattr(self, "_pair", None) is not None:
+            self._pair[1].check()
 
 
 # ─── Model shell (engine.py:61-158, :317-511) ─────────────────────────────────
@@ -793,20 +826,33 @@ class GroupedQueryAttention(nn.Module):
             vc[:, :, start:start + T] = v
             n = start + T
             keys, vals = kc[:, :, :n], vc[:, :, :n]
-            mask = None
             if T > 1:                    # causal over the new positions (engine.py:121)
                 i = torch.arange(T, device=x.device)[:, None] + start
                 j = torch.arange(n, device=x.device)[None, :]
-                mask = j <= i
-            out = F.scaled_dot_product_attention(q, keys, vals, attn_mask=mask, enable_gqa=True)
+                out = F.scaled_dot_product_attention(q, keys, vals, attn_mask=j <= i, enable_gqa=True)
+            else:
+                out = self._attend_one(q, keys, vals, None)
         else:
             kc.index_copy_(2, pos, k)
             vc.index_copy_(2, pos, v)
             j = torch.arange(cache.capacity, device=x.device)
-            mask = (j <= pos).view(1, 1, 1, -1)
-            out = F.scaled_dot_product_attention(q, kc, vc, attn_mask=mask, enable_gqa=True)
+            out = self._attend_one(q, kc, vc, (j <= pos).view(1, 1, 1, -1))
         out = out.transpose(1, 2).reshape(B, T, nq * D)
         return self._gemv(self.o_w8, out) if one else F.linear(out, self.o_weight)
+
+    def _attend_one(self, q, keys, vals, mask):
+        """Softmax attention of one query position per head, the query heads
+        grouped onto their key-value head (head h reads kv head h // group,
+        the reference's repeat_interleave, engine.py:117-121): two batched
+        products and an fp32 softmax, with no expanded copy of the cache."""
+        B, nq, _, D = q.shape
+        g = nq // self.n_kv
+        qg = q.reshape(B, self.n_kv, g, D)
+        s = torch.matmul(qg, keys.transpose(-1, -2)).float() * (1.0 / math.sqrt(D))     # [B, nkv, g, S]
+        if mask is not None:
+            s = s.masked_fill(~mask, float("-inf"))
+        p = torch.softmax(s, dim=-1).to(vals.dtype)
+        return torch.matmul(p, vals).reshape(B, nq, 1, D)
 
     @staticmethod
     def _gemv(w8: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
@@ -895,9 +941,11 @@ class DesdemonaEngine(nn.Module):
                            ffn_norm_weight=shared.get(f"layer_{li:03d}.post_attention_layernorm"))
             for li in range(self.num_layers)])
         del shared
+        self.requires_grad_(False)
         self.cos_cache, self.sin_cache = build_rope_cache(self.max_seq, self.head_dim, cfg["rope_theta"], dev)
         W = (cfg["intermediate_dim"] + 31) // 32
         self._words = torch.zeros(self.num_layers, 1, W, dtype=torch.int32, device=dev)   # fetch sets in flight
+        self.fused_lookahead = True
         self._graph = None
         self._graph_cache = None
 
@@ -919,14 +967,21 @@ class DesdemonaEngine(nn.Module):
         """Attention + sparse FFN of every layer, with the fetch-set lookahead."""
         f = self.ffn_layers
         words = self._words
+        one = x.shape[0] * x.shape[1] == 1 and self.fused_lookahead
         f[0].submit_cold_fetch(x, out=words[0])             # layer 0's set, on the embedding (engine.py:422)
         for li in range(self.num_layers):
             x = x + self.attention_layers[li](x, cos, sin, cache, start, pos)
-            if li + 1 < self.num_layers:                     # next layer's set on this post-attention state
-                f[li + 1].submit_cold_fetch(x, out=words[li + 1])
+            if li + 1 < self.num_layers:
+                if one:
+                    # one token: this layer's kernel also predicts the next layer's set
+                    # from this post-attention state (engine.py:430-438)
+                    x = f[li].forward_lookahead(x, words[li], f[li + 1], words[li + 1])
+                    continue
+                f[li + 1].submit_cold_fetch(x, out=words[li + 1])     # next layer's set on this state
             x = f[li](x, words[li])
         return x
 
+    @torch.inference_mode()
     def forward(self, input_ids: torch.Tensor, kv_caches: Optional[KVCache] = None):
         """(logits [B, T, vocab], cache) for input_ids [B, T], continuing the
         cache's positions (engine.py:406-442).  A new cache holds up to
@@ -975,6 +1030,7 @@ class DesdemonaEngine(nn.Module):
         cache.pos.copy_(saved[2])
         self._graph, self._graph_cache = g, cache
 
+    @torch.inference_mode()
     def decode_step(self, token: torch.Tensor, cache: KVCache) -> torch.Tensor:
         """Logits [1, vocab] of one new token (device int64 scalar) at the
         cache's next position, by one replay of the captured step."""

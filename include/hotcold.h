@@ -306,6 +306,12 @@ typedef struct hc_tp_desc {
   void* const* peer_buf;
   uint32_t seq_base;
   uint64_t wait_ns;   /* limit of every bounded wait of the launch; 0 = 2 s */
+  /* 1: the last layer of `layers` is not computed, only its mask row is
+   * predicted, on RMSNorm_last(input of the layer before it) -- the engine's
+   * lookahead across an attention block (engine.py:430-438): a launch over
+   * [layer l, layer l+1] computes layer l and predicts layer l+1's set.
+   * Needs n_layers >= 2 and masks_given 0 or 2. */
+  int32_t predict_last;
 } hc_tp_desc;
 
 HC_API int64_t hc_tp_buffer_bytes(int32_t tp_size);

@@ -139,6 +139,9 @@ def test_engine_matches_reference_engine(M, tmp_path):
     # greedy generation: equal tokens wherever the reference's top-2 margin is clear of the error
     margins = [np.sort(v)[-1] - np.sort(v)[-2] for v in ref["decode_logits"]]
     for use_graph in (True, False):
+        # graph replays use the fused lookahead (one kernel per layer also predicts the next
+        # layer's set); the eager steps run the separate predictor launches
+        eng.fused_lookahead = use_graph
         gen = eng.generate(prompt, max_new_tokens=len(toks), temperature=0.0, use_graph=use_graph)
         eng.check()
         assert len(gen) == len(toks)
@@ -146,6 +149,7 @@ def test_engine_matches_reference_engine(M, tmp_path):
             if margins[k] < 0.05:
                 break                           # a near tie: later tokens may legitimately differ
             assert a == b, f"token {k} (graph={use_graph}): {a} != {b}"
+    eng.fused_lookahead = True
     # the reference's stopping rule: the first EOS is kept and ends the sequence
     eos = toks[2]
     gen = eng.generate(prompt, max_new_tokens=len(toks), temperature=0.0, eos_token_id=eos)
@@ -166,11 +170,13 @@ def test_sparse_ffn_layer_batched_rows_match_reference_layer(M):
     nw = torch.from_numpy(norms["layer_000.post_attention_layernorm"]).half()
     layer = engine.SparseFFNLayer(0, os.path.join(d, "hot_weights"), store, reg, cfg, "cuda", None, nw)
     g = torch.Generator().manual_seed(6)
-    x = (torch.randn(2, 8, 4096, generator=g) * 2).half().cuda()
+    x16 = (torch.randn(2, 8, 4096, generator=g) * 2).half().cuda()
+    y16 = layer(x16)
+    assert y16.shape == x16.shape and y16.dtype == torch.float16    # the reference's dtype in and out
+    x = x16.float()                  # fp32 rows: the comparison is not limited by the fp16 output rounding
     y = layer(x)
     torch.cuda.synchronize()
     layer.check()
-    assert y.shape == x.shape and y.dtype == torch.float16
     assert layer._batch is not None                     # the batched path ran
     # the reference semantics on the host: one fetch set from the batch query, all rows through it
     from oracle import hotcold_oracle as O
@@ -185,4 +191,4 @@ def test_sparse_ffn_layer_batched_rows_match_reference_layer(M):
     got = y.reshape(16, 4096).double().cpu().numpy()
     for r in range(16):
         rel = np.linalg.norm((got[r] - xs[r]) - (ref[r] - xs[r])) / np.linalg.norm(ref[r] - xs[r])
-        assert rel < 1e-2, (r, rel)       # the output is fp16, as the reference's
+        assert rel < 2e-3, (r, rel)       # the batched bar: f16 tensor-core operands

@@ -307,3 +307,33 @@ def test_config0_single_layer_swiglu_row_scaled(M):
                          down[:, both].astype(np.float64)), None)[0]
     q = np.linalg.norm((got - x) - (dense - x)) / np.linalg.norm(dense - x)
     assert q < 0.25, f"hot+cold vs dense fp32: rel-L2 {q:.3f}"
+
+
+def test_stack_predict_last_layer_only(M):
+    """A launch over [layer l, layer l+1] with predict_last computes layer l
+    (given set) and only predicts layer l+1's set from layer l's input -- the
+    engine's lookahead across an attention block."""
+    engine, hc_synth, predictor, splitter = M
+    syn = hc_synth.make_stack(n_layers=2, inter=2048, hot_frac=0.2, rank=64, activation="silu", act_on_both=False,
+                              seed=17, norm_std=0.1)
+    st = syn.stack()
+    g = torch.Generator().manual_seed(7)
+    st.masks[0].copy_(splitter.bits_to_words((torch.rand(2048, generator=g) < 0.3).numpy(), 2048).cuda())
+    st.masks[1].zero_()
+    x0 = torch.randn(4096, device="cuda", generator=torch.Generator(device="cuda").manual_seed(9))
+    out = torch.empty(4096, device="cuda")
+    st.launch(x0, False, None, out, predict_last=True)
+    st.check()
+    # layer 0 against the oracle on its given set
+    hist = out.view(1, -1)
+    _check_stack(M, type("S", (), {"hot": syn.hot[:1], "inter": 2048, "store": syn.store, "cold_index": syn.cold_index,
+                                   "predictors": [None], "norms": syn.norms[:1], "eps": syn.eps,
+                                   "activation": "silu", "act_on_both": False})(), st, x0, hist,
+                 st.masks.cpu().numpy()[:1], False)
+    # layer 1's set: the predictor on RMSNorm_1(x0), outside the fp32 band
+    p = syn.predictors[1]
+    wd, wu, b = (t.detach().cpu().numpy() for t in (p.down.weight, p.up.weight, p.up.bias))
+    exact, amb = O.predictor_mask_banded(x0.double().cpu().numpy(), wd, wu, b, predictor.logit_threshold(0.5),
+                                         norm_w=syn.norms[1].cpu().numpy(), eps=syn.eps)
+    got = O.mask_from_words(st.masks[1].cpu().numpy(), 2048)
+    assert np.array_equal(got[~amb], exact[~amb]) and got.sum() > 100

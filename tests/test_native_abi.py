@@ -137,8 +137,8 @@ def test_tensor_parallel_host_pieces():
         got = [split_range(n, r, size) for r in range(size)]
         assert got[0][0] == 0 and got[-1][1] == n
         assert all(got[i][1] == got[i + 1][0] for i in range(size - 1))
-    # hc_tp_desc layout: 4 int32, a pointer, a uint32, a uint64 wait limit
-    assert ctypes.sizeof(N.TPDesc) == 40 and N.TPDesc.peer_buf.offset == 16 and N.TPDesc.seq_base.offset == 24
-    assert N.TPDesc.wait_ns.offset == 32
+    # hc_tp_desc layout: 4 int32, a pointer, a uint32, a uint64 wait limit, an int32 flag
+    assert ctypes.sizeof(N.TPDesc) == 48 and N.TPDesc.peer_buf.offset == 16 and N.TPDesc.seq_base.offset == 24
+    assert N.TPDesc.wait_ns.offset == 32 and N.TPDesc.predict_last.offset == 40
     assert N.lib.hc_tp_buffer_bytes(8) == 256 + 3 * 8 * 4096 * 4
     assert N.lib.hc_tp_buffer_bytes(0) == -1 and N.lib.hc_tp_buffer_bytes(64) == -1
