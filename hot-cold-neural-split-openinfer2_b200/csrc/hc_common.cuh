@@ -162,6 +162,13 @@ __device__ __forceinline__ void int4x8_to_f32(uint32_t w, float f[8]) {
   for (int e = 0; e < 8; ++e) f[e] = static_cast<float>(static_cast<int32_t>(w << (28 - 4 * e)) >> 28);
 }
 
+// two fp32 -> e4m3x2 (round to nearest even, saturating to +-448): a in the low byte
+__device__ __forceinline__ uint32_t f32x2_to_e4m3x2(float a, float b) {
+  unsigned short r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(b), "f"(a));
+  return r;
+}
+
 // e4m3x2 (low byte -> low half) -> f16x2, exact
 __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t w16) {
   uint32_t r;

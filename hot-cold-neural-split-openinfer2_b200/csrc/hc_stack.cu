@@ -14,13 +14,13 @@
 // layer.  CTA c owns a contiguous neuron-id range (its predictor logits and
 // the active cold records in it) and a slice of the next predictor's W_down
 // rows.  Every CTA publishes its ascending list of active cold records into a
-// per-layer global pool; the issuers of all CTAs then take records from that
-// pool, COLD_CLAIM at a time, and afterwards claim hot neurons two at a time
-// from a per-layer counter, so the work of a layer spreads evenly over the
-// SMs whatever the distribution of active ids.  Layer l+1's logits are
-// computed at the end of layer l, once a global counter shows every CTA has
-// added its W_down partials, so layer l+1's cold list is built, and its
-// records are streamed in, while the grid waits at the layer boundary.
+// per-layer global pool; once the pool is complete, CTA c streams the pool
+// entries [c n / G, (c+1) n / G) and then the hot neurons [c n_hot / G, (c+1)
+// n_hot / G), so every SM moves the same bytes whatever the distribution of
+// active ids.  Layer l+1's logits are computed at the end of layer l, once a
+// global counter shows every CTA has added its W_down partials, so layer
+// l+1's cold list is built, and its records are streamed in, while the grid
+// waits at the layer boundary.
 //
 // Roles:
 //  * issuer warp: streams the CTA's groups (cold records, hot neurons)
@@ -34,9 +34,12 @@
 //    it prefetches into L2;
 //  * 4 consumer subgroups of 128 threads: group g of a layer belongs to
 //    subgroup g % 4; thread u owns elements [32u, 32u+32) of every row and of
-//    its subgroup's partial y.  FP8 rows are dotted with RMSNorm(x) in f16
-//    (f16 x f16 products, fp32 sums); INT4 rows with RMSNorm(x) as 16-bit
-//    fixed point (two byte digits per element, dp4a, exact integer sums).
+//    its subgroup's partial y.  Hot FP8 rows are dotted with RMSNorm(x) on the
+//    tensor cores (mma.sync e4m3, RMSNorm(x) carried as three e4m3 components,
+//    fp32 sums); INT4 rows with RMSNorm(x) as 16-bit fixed point (two byte
+//    digits per element, dp4a, exact integer sums); down columns are added
+//    into y with f16 x f16 products and fp32 sums, skipping neurons whose
+//    gated activation is exactly zero.
 // Layer boundary: the subgroups' partial y are summed in shared memory, added
 // to a per-layer global accumulator with one 16 KB bulk reduction
 // (cp.reduce.async.bulk add.f32, performed in L2), and after the grid barrier
@@ -72,13 +75,15 @@ constexpr int OWN_WORDS = COLD_LIST / 32;
 constexpr int HOT_BYTES = 3 * H;        // 12288
 constexpr int NACC = 3;                 // rotating y / z / hot-claim accumulators
 constexpr int YCOPIES = 1;              // CTA c adds its partial y into copy c % YCOPIES
-constexpr int COLD_CLAIM = 8;           // cold records taken from the layer's pool per claim
 constexpr int POOL_CAP = 32768;         // cold-pool entries per layer (>= inter)
 constexpr int WD_TILES = 4096 / 32;     // W_down tiles of a predictor (H / WD_ROWS)
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;   // 2 s: default limit of every wait on another agent
 static_assert(HALF_BYTES % 128 == 0 && REC_SLOT_OFF % 16 == 0, "halves must stay 16-byte aligned");
 static_assert(HOT_BYTES <= HALF_BYTES && REC_SLOT_OFF + REC_COPY <= HALF_BYTES, "half too small");
-static_assert(WU_ROWS * 96 * 4 + WU_ROWS * 4 <= HALF_BYTES, "predictor tiles must fit a half");
+constexpr int PRED_RANK_MAX = 64;       // in-kernel predictors: rank <= 64, a multiple of 8
+constexpr int PBUF_BYTES = WU_ROWS * PRED_RANK_MAX * 4 + WU_ROWS * 4;   // one W_up tile + bias (>= a W_down tile)
+static_assert(WD_ROWS * PRED_RANK_MAX * 4 <= PBUF_BYTES, "predictor tiles must fit the planner buffer");
+constexpr int XC_STRIDE = 4096 + 64;    // e4m3 component rows of RMSNorm(x): +64 B keeps two rows' loads apart
 static_assert(NE > NSG, "the subgroups' entries advance by NSG per group");
 static_assert(SPT == 32 && EPT == 8, "the decoders assume 32 elements per subgroup thread");
 
@@ -95,18 +100,22 @@ struct SlotInfo {
 };
 
 struct StackSmem {
-  alignas(128) uint8_t pbuf[HALF_BYTES];   // planner: one predictor tile (W_down or W_up + bias)
-  __half xh[H];                     // RMSNorm_l(x) as f16 (hot neurons); with xq, a y stage later
-  uint4 xq[CONS_THREADS];           // the same as 16-bit fixed point, byte digits per 8 elements
+  alignas(128) uint8_t pbuf[PBUF_BYTES];   // planner: one predictor tile (W_down or W_up + bias)
+  // RMSNorm_l(x) * 2^e as the sum of three e4m3 values per element (rows c1, c2,
+  // c3): the B operand of the hot neurons' tensor-core dot products; with xq, a
+  // y stage later
+  alignas(16) uint8_t xc[3][XC_STRIDE];
+  uint4 xq[CONS_THREADS];           // RMSNorm_l(x) as 16-bit fixed point, byte digits per 8 elements
   float ystage[H];                  // subgroup partial y (element 32u+k at k*128+u); earlier in the
                                     // layer, the planner's W_down rows RMSNorm_{l+1}(x_l)
   float z[128];                     // planner: bottleneck of the next layer's predictor
   float rstd0;                      // consumers -> planner: 1 / RMS of x_0 (layer 0's own prediction)
   int2 chunk[H / SPT];              // per 32 elements: (-8 * sum of the fixed-point values, bits of 2^-s)
   float zred[NWARPS];
+  float zmax[NWARPS];
+  float xc_inv;                     // 2^-e: undoes the components' scale
   float red[NSG][2][SG_WARPS][2 * NB_COLD];
   int32_t sgdec[NSG][2];            // per-subgroup decision of its poller
-  int32_t sgok[2][NSG];             // per layer parity: subgroup finished its layer without an abort
   uint64_t tstat[8];                // trace counters of subgroup 0's poller
   int32_t plan_list[COLD_LIST];     // nids, then record indices, of this CTA's active cold records
   uint32_t own_words[OWN_WORDS];    // predicted mask words of this CTA's neuron-id range
@@ -184,11 +193,13 @@ constexpr size_t WS_BYTES = WS_POOL + sizeof(int32_t) * NACC * POOL_CAP;
 
 __device__ __forceinline__ int64_t split_lo(int64_t n, int c, int G) { return n * c / G; }
 // predictor tiles must fit a slot and split evenly over 4 threads per neuron
-__device__ __forceinline__ bool rank_ok(int r) { return r > 0 && r <= 96 && (r & 7) == 0; }
+__device__ __forceinline__ bool rank_ok(int r) { return r > 0 && r <= PRED_RANK_MAX && (r & 7) == 0; }
 
 // Exchange buffer of one GPU (tensor-parallel mode): per slot (l % NACC) a
 // flag word per sender, then per slot a partial y [H] per sender.
-constexpr size_t XCHG_FLAGS = 256;     // bytes reserved for NACC x tp_size flags
+constexpr size_t XCHG_FLAGS = 256;     // header: the arrival counter (first word)
+constexpr int TP_MAX = 8;              // GPUs per tensor-parallel group
+constexpr int KP_MAX = 16;             // CTAs that push slices of a GPU's partial to its peers
 __device__ __forceinline__ uint32_t* xchg_flags(void* buf) { return reinterpret_cast<uint32_t*>(buf); }
 __device__ __forceinline__ float* xchg_y(void* buf, int slot, int sender, int tp) {
   return reinterpret_cast<float*>(reinterpret_cast<char*>(buf) + XCHG_FLAGS) + ((size_t)slot * tp + sender) * H;
@@ -293,6 +304,28 @@ __device__ __forceinline__ bool cons_broadcast(StackSmem& sm, bool ok0) {
   if (threadIdx.x == 0) sm.flag = ok0 ? 1 : 0;
   named_bar(1, CONS_THREADS);
   return sm.flag != 0;
+}
+// sum of a and max of b over the 512 consumer threads (results in every thread)
+__device__ __forceinline__ float cons_sum_max(StackSmem& sm, float a, float& b) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, o));
+  }
+  named_bar(1, CONS_THREADS);
+  if ((threadIdx.x & 31) == 0) {
+    sm.zred[threadIdx.x >> 5] = a;
+    sm.zmax[threadIdx.x >> 5] = b;
+  }
+  named_bar(1, CONS_THREADS);
+  a = 0.0f;
+  b = 0.0f;
+#pragma unroll
+  for (int w = 0; w < NWARPS; ++w) {
+    a += sm.zred[w];
+    b = fmaxf(b, sm.zmax[w]);
+  }
+  return a;
 }
 // sum over the 512 consumer threads (result in every thread)
 __device__ __forceinline__ float cons_sum(StackSmem& sm, float a) {
@@ -456,32 +489,60 @@ __device__ __forceinline__ void axpy32_fp8(const uint8_t* row, unsigned short a1
   }
 }
 
-// Hot group: n (<= NB_HOT) FP8 neurons, one per slot.
+// e4m3 tensor-core dot products: D[16 x 8] += A[16 x 32] B[32 x 8], fp32
+// accumulation (rows 8-15 of A are zero here: a1 = a3 = 0)
+__device__ __forceinline__ void mma_e4m3(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+
+// Hot group: n (<= NB_HOT) FP8 neurons, one per slot.  Gate / up dot products
+// on the tensor cores: warp w of the subgroup takes K elements [1024 w, 1024 w +
+// 1024) of the four rows (gate A, gate B, up A, up B = A rows 0-3) against the
+// three e4m3 components of RMSNorm(x) * 2^e (B columns 0-2); the weights are
+// e4m3 already, products are exact and sums fp32.  Lane (g, t) = (lane / 4,
+// lane % 4) feeds A row g and B column g with the 16 bytes [64 P + 16 t, +16)
+// of each 64-element step P: the same permutation of K on both operands.
 __device__ __forceinline__ void sg_hot(StackSmem& sm, const StackParams& p, const float* hot_scale,
                                        const uint8_t* slot0, const uint8_t* slot1, int n, int64_t i0, int sg, int buf,
                                        float (&y)[SPT]) {
-  const int u = threadIdx.x & (SG_THREADS - 1), lane = threadIdx.x & 31;
-  uint32_t xp[16];
-  {
-    const uint4* src = reinterpret_cast<const uint4*>(sm.xh + SPT * u);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint4 v = src[i];
-      xp[4 * i] = v.x; xp[4 * i + 1] = v.y; xp[4 * i + 2] = v.z; xp[4 * i + 3] = v.w;
+  const int u = threadIdx.x & (SG_THREADS - 1), lane = threadIdx.x & 31, w = u >> 5;
+  const int g = lane >> 2, tq = lane & 3;
+  const bool a_live = g < 4 && (n > 1 || (g & 1) == 0);
+  const bool b_live = g < 3;
+  const uint8_t* arow = ((g & 1) ? slot1 : slot0) + ((g & 2) ? H : 0) + 1024 * w + 16 * tq;
+  const uint8_t* brow = sm.xc[b_live ? g : 0] + 1024 * w + 16 * tq;
+  float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+  for (int P = 0; P < 16; P += 2) {
+    uint4 a = make_uint4(0u, 0u, 0u, 0u), b = a, a2 = a, b2 = a;
+    if (a_live) {
+      a = *reinterpret_cast<const uint4*>(arow + 64 * P);
+      a2 = *reinterpret_cast<const uint4*>(arow + 64 * P + 64);
     }
+    if (b_live) {
+      b = *reinterpret_cast<const uint4*>(brow + 64 * P);
+      b2 = *reinterpret_cast<const uint4*>(brow + 64 * P + 64);
+    }
+    mma_e4m3(d0, a.x, a.y, b.x, b.y);
+    mma_e4m3(d0, a.z, a.w, b.z, b.w);
+    mma_e4m3(d1, a2.x, a2.y, b2.x, b2.y);
+    mma_e4m3(d1, a2.z, a2.w, b2.z, b2.w);
   }
-  float v[2 * NB_HOT];
-  v[0] = dot32_fp8(slot0 + SPT * u, xp);
-  v[NB_HOT] = dot32_fp8(slot0 + H + SPT * u, xp);
-  v[1] = 0.0f;
-  v[NB_HOT + 1] = 0.0f;
-  if (n > 1) {
-    v[1] = dot32_fp8(slot1 + SPT * u, xp);
-    v[NB_HOT + 1] = dot32_fp8(slot1 + H + SPT * u, xp);
+  // row g, columns 2t and 2t+1 (components 0-2 sit in columns 0-2, the rest are zero)
+  float v = (d0[0] + d1[0]) + (d0[1] + d1[1]);
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  if (tq == 0 && g < 4) sm.red[sg][buf][w][g] = v * sm.xc_inv;
+  named_bar(2 + sg, SG_THREADS);
+  float s = 0.0f;
+  if (lane < 2 * NB_HOT) {
+#pragma unroll
+    for (int k = 0; k < SG_WARPS; ++k) s += sm.red[sg][buf][k][lane];
   }
-  const float s = sg_reduce<2 * NB_HOT>(sm, sg, buf, v);
   const float uu = __shfl_down_sync(0xffffffffu, s, NB_HOT);   // lane j < n: gate j, lane NB_HOT + j: up j
-  float a = 0.0f;
+  float act = 0.0f;
   if (lane < n) {
     float sgs = 1.0f, sus = 1.0f, sds = 1.0f;
     if (hot_scale != nullptr) {
@@ -490,16 +551,15 @@ __device__ __forceinline__ void sg_hot(StackSmem& sm, const StackParams& p, cons
       sus = __ldg(s3 + 1);
       sds = __ldg(s3 + 2);
     }
-    a = gated(s * sgs, uu * sus, p.relu, p.both) * sds;
+    act = gated(s * sgs, uu * sus, p.relu, p.both) * sds;
   }
   // a neuron whose gated activation is exactly zero (dReLU: either branch <= 0)
-  // adds nothing: its down column is skipped (every warp holds the same a's)
-  const float a0 = __shfl_sync(0xffffffffu, a, 0), a1 = __shfl_sync(0xffffffffu, a, 1);
+  // adds nothing: its down column is skipped (every warp holds the same values)
+  const float a0 = __shfl_sync(0xffffffffu, act, 0), a1 = __shfl_sync(0xffffffffu, act, 1);
   if (a0 != 0.0f) axpy32_fp8(slot0 + 2 * H + SPT * u, __half_as_ushort(__float2half_rn(a0)), y);
   if (n > 1 && a1 != 0.0f) axpy32_fp8(slot1 + 2 * H + SPT * u, __half_as_ushort(__float2half_rn(a1)), y);
 }
 
-// Cold group: n (<= NB_COLD) INT4 records, two per slot.
 // The decoded down rows carry a bias (1032 / 1152 per element, int4_pairs):
 // the f16 coefficients are summed into csa / csb and the bias is removed once
 // per layer (cold_bias_out), which keeps it small against fp32's precision.
@@ -583,67 +643,77 @@ __device__ bool grid_spin(StackSmem& sm, const StackParams& p, uint32_t target) 
   }
   return ok0;
 }
-__device__ bool grid_wait(StackSmem& sm, const StackParams& p, uint32_t target) {
+__device__ bool grid_wait(StackSmem& sm, const StackParams& p, uint32_t target, int lm1) {
   bool ok0 = true;
-  if (threadIdx.x == 0) ok0 = grid_spin(sm, p, target);
+  if (threadIdx.x == 0) {
+    ok0 = grid_spin(sm, p, target);
+    trace_ev(p, lm1, 32);
+  }
   return cons_broadcast(sm, ok0);
 }
 
 // Wait until y of layer lm1 is complete: every CTA of this GPU added its
-// partial; with several GPUs, CTA 0 then copies this GPU's partial into every
-// peer's exchange buffer (NVLink stores) and publishes the sequence number,
-// and every CTA waits (bounded) for all peers' numbers.
+// partial.  With several GPUs, the first kp = min(grid, 16) CTAs then each
+// copy one slice (1/kp) of this GPU's partial into every peer's exchange
+// buffer (plain NVLink stores), issue one system-scope release and add 1 to
+// each peer's arrival counter; every CTA waits (bounded) until its own
+// counter shows all (size - 1) x kp slices of this layer.  The counter only
+// grows: after the layer with sequence number q it holds q (size - 1) kp, so
+// every GPU must run the same grid.
 __device__ bool layer_wait(StackSmem& sm, const StackParams& p, int lm1) {
   const uint32_t target = (uint32_t)(lm1 + 1) * gridDim.x;
-  if (p.tp_size == 1) return grid_wait(sm, p, target);
-  const int t = threadIdx.x, slot = lm1 % NACC;
+  if (p.tp_size == 1) return grid_wait(sm, p, target, lm1);
+  const int t = threadIdx.x, slot = lm1 % NACC, c = blockIdx.x;
+  const int kp = min((int)gridDim.x, KP_MAX);
   const uint32_t seq = p.seq_base + (uint32_t)lm1 + 1u;
   bool ok0 = true;
   if (t == 0) {
     ok0 = grid_spin(sm, p, target);
     trace_ev(p, lm1, 32);
   }
-  if (blockIdx.x == 0) {
+  if (c < kp) {
     named_bar(1, CONS_THREADS);      // thread 0 saw every local partial; so does every thread now
-    float4 a, b;
-    load_y_local(p, lm1, t, a, b);
-    for (int s = 0; s < p.tp_size; ++s) {
-      if (s == p.tp_rank) continue;
-      float4* dst = reinterpret_cast<float4*>(xchg_y(p.peer_buf[s], slot, p.tp_rank, p.tp_size) + 8 * t);
-      dst[0] = a;
-      dst[1] = b;
+    const int lo = c * (H / 4) / kp, hi = (c + 1) * (H / 4) / kp;     // this CTA's float4 slice
+    for (int i = lo + t; i < hi; i += CONS_THREADS) {
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int k = 0; k < YCOPIES; ++k) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(p.yacc + ((size_t)slot * YCOPIES + k) * H) + i);
+        a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
+      }
+      for (int s = 0; s < p.tp_size; ++s) {
+        if (s == p.tp_rank) continue;
+        reinterpret_cast<float4*>(xchg_y(p.peer_buf[s], slot, p.tp_rank, p.tp_size))[i] = a;
+      }
     }
     named_bar(1, CONS_THREADS);
     if (t == 0 && ok0) {           // on a local timeout the peers time out too
       trace_ev(p, lm1, 36);
-      // one release fence (cumulative over the CTA's stores above, ordered by
-      // the barrier) for all peers' flags
+      // one release (cumulative over the CTA's stores above, ordered by the
+      // barrier) before the counters
       asm volatile("fence.acq_rel.sys;" ::: "memory");
       trace_ev(p, lm1, 33);
       for (int s = 0; s < p.tp_size; ++s) {
         if (s == p.tp_rank) continue;
-        uint32_t* f = xchg_flags(p.peer_buf[s]) + slot * p.tp_size + p.tp_rank;
-        asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(f), "r"(seq) : "memory");
+        asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(xchg_flags(p.peer_buf[s])) : "memory");
       }
       trace_ev(p, lm1, 34);
     }
   }
   if (t == 0 && ok0) {
-    const uint32_t* f = xchg_flags(p.peer_buf[p.tp_rank]) + slot * p.tp_size;
+    const uint32_t* f = xchg_flags(p.peer_buf[p.tp_rank]);
+    const uint32_t want = seq * (uint32_t)(p.tp_size - 1) * (uint32_t)kp;
     const uint64_t t0 = globaltimer_ns();
-    for (int s = 0; s < p.tp_size && ok0; ++s) {
-      if (s == p.tp_rank) continue;
-      uint32_t i = 0;
-      while (true) {
-        uint32_t v;
-        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f + s) : "memory");
-        if ((int32_t)(v - seq) >= 0) break;
-        if ((++i & 63) == 0 && globaltimer_ns() - t0 > p.wait_ns) {
-          ok0 = false;
-          break;
-        }
-        __nanosleep(32);
+    uint32_t i = 0;
+    while (true) {
+      uint32_t v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+      if ((int32_t)(v - want) >= 0) break;
+      if ((++i & 63) == 0 && globaltimer_ns() - t0 > p.wait_ns) {
+        ok0 = false;
+        break;
       }
+      __nanosleep(32);
     }
     if (!ok0) {
       sm.abort = 1;
@@ -945,9 +1015,6 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         if (!ok) break;
         ok = wdown(dn, l + 1, d0, d1, [&](int r) { return xs[r - d0 * WD_ROWS]; });
         if (!ok) break;
-        // leave ystage all zero: it becomes the layer's y accumulator
-        for (int i = lane; i < (d1 - d0) * WD_ROWS; i += 32) xs[i] = 0.0f;
-        __syncwarp();
         if (lane == 0) mbar_arrive(&sm.wdown_done);       // ystage is the consumers' again
         wdown_count(l + 1, d0, d1);
         preload(l + 1);
@@ -1181,15 +1248,13 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
 
       // ---- RMSNorm (engine.py:295; torch.nn.RMSNorm) -> f16 and fixed-point copies
       {
-        // the layer's y accumulator starts at zero (the previous layer's last
-        // reads of it are behind the grid barrier); the barriers in cons_sum
-        // order this before the W_down rows below are written into it
-        reinterpret_cast<float4*>(sm.ystage)[2 * t] = make_float4(0.f, 0.f, 0.f, 0.f);
-        reinterpret_cast<float4*>(sm.ystage)[2 * t + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
-        float ss = 0.0f;
+        float ss = 0.0f, mw = 0.0f;
 #pragma unroll
-        for (int i = 0; i < EPT; ++i) ss = fmaf(x[i], x[i], ss);
-        ss = cons_sum(sm, ss);
+        for (int i = 0; i < EPT; ++i) {
+          ss = fmaf(x[i], x[i], ss);
+          mw = fmaxf(mw, fabsf(x[i] * nw[i]));
+        }
+        ss = cons_sum_max(sm, ss, mw);
         const float rstd = rsqrtf(ss / (float)H + p.eps);
         float xn[EPT];
         float am = 0.0f;
@@ -1199,10 +1264,35 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
           am = fmaxf(am, fabsf(xn[i]));
         }
         {
-          __half2 h2[4];
+          // three e4m3 components per element of xn * 2^e, 2^e the power of two that
+          // puts max |xn| in [128, 256): c1 = e4m3(v), c2 = e4m3(v - c1), c3 =
+          // e4m3(v - c1 - c2); the residues are exact in fp32, so the sum carries
+          // ~12 significant bits (and e4m3's subnormal floor far below the maximum)
+          const float mx = mw * rstd * 1.0001f + 1e-30f;
+          const int ex = min(max((int)((__float_as_uint(mx) >> 23) & 255u), 8), 253);   // 2^e, 2^-e normal
+          const float sc = __uint_as_float((uint32_t)(134 - ex + 127) << 23);
+          if (t == 0) sm.xc_inv = __uint_as_float((uint32_t)(ex - 134 + 127) << 23);
+          uint32_t cw[3][2];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) h2[i] = __floats2half2_rn(xn[2 * i], xn[2 * i + 1]);
-          *reinterpret_cast<uint4*>(sm.xh + EPT * t) = *reinterpret_cast<const uint4*>(h2);
+          for (int h = 0; h < 2; ++h) {
+            float r[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) r[i] = xn[4 * h + i] * sc;
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+              const uint32_t lo = f32x2_to_e4m3x2(r[0], r[1]), hi = f32x2_to_e4m3x2(r[2], r[3]);
+              cw[c][h] = lo | (hi << 16);
+              if (c < 2) {
+                float q[4];
+                e4m3x4_to_f32(cw[c][h], q);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) r[i] -= q[i];
+              }
+            }
+          }
+#pragma unroll
+          for (int c = 0; c < 3; ++c)
+            *reinterpret_cast<uint2*>(sm.xc[c] + EPT * t) = make_uint2(cw[c][0], cw[c][1]);
         }
         // 16-bit fixed point per 32 elements (4 threads): |x| * 2^s < 2^15
         am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
@@ -1321,42 +1411,55 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         trace_set(p, l, 26, sm.tstat[6]);
         trace_set(p, l, 27, (uint64_t)clock64() - sm.tstat[7]);
       }
-      // ---- this subgroup is done with the layer: remove the cold rows' bias and,
-      // once the planner has released ystage (its W_down rows), add the partial y
-      // into ystage with shared-memory atomics (element 32u+k at k*128+u: a warp's
-      // adds hit 32 banks).  Subgroups that finish early do this while the others
-      // stream their last groups.
+      // ---- all subgroups done: remove the cold rows' bias, one abort decision for
+      // everyone, then sum the partial y (fixed tree in shared memory) and add it to
+      // the layer's accumulator
       cold_bias_out(y, csa, csb);
-      if (u == 0) {
-        if (pred_next && !mbar_wait(&sm.wdown_done, wd_phase & 1u, p.wait_ns)) {
+      if (t == 0) {
+        bool okw = true;
+        if (pred_next) okw = mbar_wait(&sm.wdown_done, wd_phase & 1u, p.wait_ns);
+        if (!okw) {
           sm.abort = 1;
           atomicOr(p.status, HC_ERR_TIMEOUT);
         }
-        // one decision per subgroup and layer parity, read by every consumer after the
-        // CTA barrier below (rewritten only two layers later, past another CTA barrier)
-        sm.sgok[l & 1][sg] = ld_vol(&sm.abort) ? 0 : 1;
+        sm.flag = ld_vol(&sm.abort) ? 0 : 1;
       }
       if (pred_next) ++wd_phase;
-      named_bar(2 + sg, SG_THREADS);
-      if (sm.sgok[l & 1][sg]) {
-#pragma unroll
-        for (int k = 0; k < SPT; ++k) atomicAdd(sm.ystage + k * SG_THREADS + u, y[k]);
-      }
       named_bar(1, CONS_THREADS);
-      if (!(sm.sgok[l & 1][0] & sm.sgok[l & 1][1] & sm.sgok[l & 1][2] & sm.sgok[l & 1][3])) {
+      if (sm.flag == 0) {
         ok = false;
         break;
       }
       base += (uint32_t)ld_vol(&sm.ngroups[l & 3]);
       {
-        // element order for one bulk reduction: thread t gathers elements [8t, 8t+8)
-        // into bufB (xh + xq: dead until the next layer's input is normalised)
-        float* bufB = reinterpret_cast<float*>(sm.xh);
+        float* bufA = sm.ystage;
+        float* bufB = reinterpret_cast<float*>(sm.xc);     // xc + xq: > 16 KB, dead until the next layer
+        if (sg >= 2) {
+          float* dst = sg == 2 ? bufA : bufB;
+#pragma unroll
+          for (int k = 0; k < SPT; ++k) dst[k * SG_THREADS + u] = y[k];
+        }
+        named_bar(1, CONS_THREADS);
+        if (sg < 2) {
+          const float* src = sg == 0 ? bufA : bufB;
+#pragma unroll
+          for (int k = 0; k < SPT; ++k) y[k] += src[k * SG_THREADS + u];
+        }
+        named_bar(1, CONS_THREADS);
+        if (sg < 2) {
+          float* dst = sg == 0 ? bufA : bufB;
+#pragma unroll
+          for (int k = 0; k < SPT; ++k) dst[k * SG_THREADS + u] = y[k];
+        }
+        named_bar(1, CONS_THREADS);
+        // element layout: thread t sums elements [8t, 8t+8) (element 32u+k sits at
+        // k*128+u) and stores them in element order for one bulk reduction
         float e[EPT];
         const int eu = t >> 2, ek = EPT * (t & 3);
 #pragma unroll
-        for (int i = 0; i < EPT; ++i) e[i] = sm.ystage[(ek + i) * SG_THREADS + eu];
-        float4* yo = reinterpret_cast<float4*>(bufB + EPT * t);
+        for (int i = 0; i < EPT; ++i) e[i] = bufA[(ek + i) * SG_THREADS + eu] + bufB[(ek + i) * SG_THREADS + eu];
+        named_bar(1, CONS_THREADS);
+        float4* yo = reinterpret_cast<float4*>(bufA + EPT * t);
         yo[0] = make_float4(e[0], e[1], e[2], e[3]);
         yo[1] = make_float4(e[4], e[5], e[6], e[7]);
         fence_proxy_async_smem();
@@ -1364,7 +1467,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         if (t == 0) {
           trace_ev(p, l, 9);
           // y_l += this CTA's partial: the L2 adds 16 KB in one bulk operation
-          bulk_reduce_add_f32(p.yacc + ((size_t)(l % NACC) * YCOPIES + c % YCOPIES) * H, bufB, H * sizeof(float));
+          bulk_reduce_add_f32(p.yacc + ((size_t)(l % NACC) * YCOPIES + c % YCOPIES) * H, bufA, H * sizeof(float));
           bulk_wait_all();
           trace_ev(p, l, 28);
           // then the grid-barrier arrival, ordered after the reduction's writes
@@ -1441,7 +1544,7 @@ extern "C" int64_t hc_ffn_stack_workspace_bytes(int32_t grid, int32_t inter) {
 }
 
 extern "C" int64_t hc_tp_buffer_bytes(int32_t tp_size) {
-  if (tp_size < 1 || (size_t)NACC * tp_size * sizeof(uint32_t) > XCHG_FLAGS) return -1;
+  if (tp_size < 1 || tp_size > TP_MAX) return -1;
   return (int64_t)(XCHG_FLAGS + sizeof(float) * (size_t)NACC * tp_size * H);
 }
 

@@ -119,7 +119,7 @@ class TPGroup:
                 self._opened.append(peer.value)
                 ptrs.append(peer.value)
             self.peer_buf = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
-        self.launches = 0
+        self.seq = 0            # layers exchanged so far through these buffers (the same on every rank)
 
     def close(self):
         for ptr in getattr(self, "_opened", []):
@@ -166,6 +166,11 @@ class FFNStack:
         self.hot = list(hot)
         self.norms = [n.to(self.device, torch.float32).contiguous() if n is not None else None for n in norms]
         self.predictors = list(predictors)
+        for l, pr in enumerate(self.predictors[1:], start=1):
+            # layers after the first are predicted inside the kernel (lookahead)
+            if pr is not None and not (0 < pr.rank <= 64 and pr.rank % 8 == 0):
+                raise ValueError(f"layer {l}: the fused kernel predicts with ranks that are multiples of 8 "
+                                 f"up to 64 (got {pr.rank})")
         self.act = N.HC_ACT_RELU if activation == "relu" else N.HC_ACT_SILU
         self.act_on_both = bool(act_on_both)
         self.eps = float(eps)
@@ -212,7 +217,7 @@ class FFNStack:
         """Layer 0's predictor runs inside the stack kernel (hc_ffn_stack with
         masks_given = 2) -- the kernel supports its rank."""
         p0 = self.predictors[0]
-        return p0 is not None and 0 < p0.rank <= 96 and p0.rank % 8 == 0
+        return p0 is not None and 0 < p0.rank <= 64 and p0.rank % 8 == 0
 
     def first_mask(self, x: torch.Tensor):
         """Layer 0's predicted set from RMSNorm_0(x) (engine.py:422), on device
@@ -237,9 +242,9 @@ class FFNStack:
         tp = None
         if self.tp is not None and self.tp.size > 1:
             tp = N.TPDesc(size=self.tp.size, rank=self.tp.rank, words_lo=self.words_lo, words_n=self.words_n,
-                          peer_buf=N.ptr(self.tp.peer_buf), seq_base=(self.tp.launches * self.L) & 0xFFFFFFFF,
+                          peer_buf=N.ptr(self.tp.peer_buf), seq_base=self.tp.seq & 0xFFFFFFFF,
                           wait_ns=self.wait_ns)
-            self.tp.launches += 1
+            self.tp.seq += self.L - (1 if predict_last else 0)
         elif self.wait_ns or predict_last:
             tp = N.TPDesc(size=1, rank=0, words_lo=0, words_n=self.words, peer_buf=None, seq_base=0,
                           wait_ns=self.wait_ns)
@@ -290,6 +295,12 @@ class FFNStack:
         if self.L > 1:
             put("barrier_wait", us[1:, :, 0] - us[:-1, :, 8])
             put("layer", us[1:, :, 0] - us[:-1, :, 0])
+            if not (self.tp is not None and self.tp.size > 1):
+                # split of the barrier wait: the last CTA's arrival, its sighting, the next layer's input
+                last = us[:-1, :, 8].max(dim=1).values[:, None]
+                put("barrier.after_own_arrival_to_last", last - us[:-1, :, 8])
+                put("barrier.last_arrival_to_seen", us[:-1, :, 32] - last)
+                put("barrier.seen_to_layer_start", us[1:, :, 0] - us[:-1, :, 32])
         put("issue_wait_pool", us[:, :, 11] - us[:, :, 10])
         put("issue_cold", us[:, :, 12] - us[:, :, 11])
         put("issue_hot", us[:, :, 14] - us[:, :, 13])

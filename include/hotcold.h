@@ -227,7 +227,7 @@ HC_API int64_t hc_ffn_stack_workspace_bytes(int32_t grid, int32_t inter);
  * (engine.py:421-438: layer l+1's fetch set comes from layer l's input).
  *   layers     [n_layers] hc_layer_desc (device array); every layer has
  *              `inter` neurons (inter % 4 == 0, inter <= 32768); a predictor
- *              rank must be a multiple of 8 and <= 96 (else HC_ERR_UNSUPPORTED,
+ *              rank must be a multiple of 8 and <= 64 (else HC_ERR_UNSUPPORTED,
  *              no predictor); CTA c owns the neuron ids of mask words
  *              [c*W/grid, (c+1)*W/grid), W = ceil(inter/32), and at most 1024
  *              of them, i.e. ceil(W/grid)*32 <= 1024 (else HC_ERR_UNSUPPORTED)
@@ -283,15 +283,18 @@ HC_API int hc_ffn_stack(const hc_layer_desc* layers, int32_t n_layers, int32_t i
  * GPU's partial).  GPU `rank` holds its slice of the hot neurons (its own
  * hc_layer_desc.hot / n_hot), computes the predictor logits and cold records
  * of mask words [words_lo, words_lo + words_n), and runs the full W_down of
- * every predictor.  Per layer, each GPU sums its CTAs' partial y, copies the
- * sum into every peer's exchange buffer over NVLink (plain peer stores, no
- * multicast) and publishes `seq_base + layer + 1` in a flag word; every GPU
- * waits (bounded) for all peers' flags, then adds the partials in GPU order,
- * so all GPUs hold bit-identical hidden states.
+ * every predictor.  Per layer, each GPU sums its CTAs' partial y; its first
+ * kp = min(grid, 16) CTAs each copy one slice of that sum into every peer's
+ * exchange buffer over NVLink (plain peer stores, no multicast), issue one
+ * system-scope release and add 1 to every peer's arrival counter; every GPU
+ * waits (bounded) until its counter reaches (seq_base + layer + 1) x
+ * (size - 1) x kp, then adds the partials in GPU order, so all GPUs hold
+ * bit-identical hidden states.
  *   peer_buf   device array [size] of every GPU's exchange buffer
  *              (hc_tp_buffer_bytes(size) bytes from hc_tp_alloc, zeroed once,
- *              opened in the other processes with hc_ipc_open)
- *   seq_base   launches so far x n_layers; every GPU passes the same value
+ *              opened in the other processes with hc_ipc_open); size <= 8
+ *   seq_base   layers exchanged through these buffers by earlier launches;
+ *              every GPU passes the same value and runs the same grid
  * All `size` kernels must be running at the same time (one per GPU, issued
  * by each rank in the same order); a GPU that does not reach a layer within
  * `wait_ns` (default 2 s) makes the others return HC_ERR_TIMEOUT: the kernel

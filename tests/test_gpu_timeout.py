@@ -1,9 +1,10 @@
 """A bounded device wait that runs out, on one GPU.
 
 The tensor-parallel stack waits, per layer, for every peer GPU's partial
-output (a flag word the peer writes over NVLink).  Here the "peer" exchange
-buffer is a second local allocation that no kernel ever writes, and the wait
-limit is 5 ms, so the first layer boundary's flag wait expires on every CTA.
+output (an arrival counter the peers increment over NVLink).  Here the
+"peer" exchange buffer is a second local allocation whose kernel never runs,
+so nothing ever increments this GPU's counter, and the wait limit is 5 ms:
+the first layer boundary's wait expires on every CTA.
 The launch must come back on its own with HC_ERR_TIMEOUT in the status word,
 leave its workspace counters clean, and the context must stay usable: a
 normal launch right after it passes the oracle parity check.  Nothing here
@@ -28,7 +29,7 @@ class _LocalPeers:
 
     def __init__(self, N):
         self.N = N
-        self.size, self.rank, self.launches = 2, 0, 0
+        self.size, self.rank, self.seq = 2, 0, 0
         nbytes = int(N.lib.hc_tp_buffer_bytes(2))
         self.bufs = []
         for _ in range(2):

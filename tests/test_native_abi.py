@@ -141,4 +141,4 @@ def test_tensor_parallel_host_pieces():
     assert ctypes.sizeof(N.TPDesc) == 48 and N.TPDesc.peer_buf.offset == 16 and N.TPDesc.seq_base.offset == 24
     assert N.TPDesc.wait_ns.offset == 32 and N.TPDesc.predict_last.offset == 40
     assert N.lib.hc_tp_buffer_bytes(8) == 256 + 3 * 8 * 4096 * 4
-    assert N.lib.hc_tp_buffer_bytes(0) == -1 and N.lib.hc_tp_buffer_bytes(64) == -1
+    assert N.lib.hc_tp_buffer_bytes(0) == -1 and N.lib.hc_tp_buffer_bytes(9) == -1
