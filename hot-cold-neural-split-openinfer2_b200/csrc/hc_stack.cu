@@ -34,10 +34,10 @@
 //    it prefetches into L2;
 //  * 4 consumer subgroups of 128 threads: group g of a layer belongs to
 //    subgroup g % 4; thread u owns elements [32u, 32u+32) of every row and of
-//    its subgroup's partial y.  Hot FP8 rows are dotted with RMSNorm(x) on the
-//    tensor cores (mma.sync e4m3, RMSNorm(x) carried as three e4m3 components,
-//    fp32 sums); INT4 rows with RMSNorm(x) as 16-bit fixed point (two byte
-//    digits per element, dp4a, exact integer sums); down columns are added
+//    its subgroup's partial y.  FP8 rows are dotted with RMSNorm(x) in f16
+//    (f16 x f16 products, fp32 sums); INT4 rows with RMSNorm(x) as 16-bit
+//    fixed point (two byte digits per element, dp4a, exact integer sums); down
+//    columns are added
 //    into y with f16 x f16 products and fp32 sums, skipping neurons whose
 //    gated activation is exactly zero.
 // Layer boundary: the subgroups' partial y are summed in shared memory, added
@@ -80,10 +80,9 @@ constexpr int WD_TILES = 4096 / 32;     // W_down tiles of a predictor (H / WD_R
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;   // 2 s: default limit of every wait on another agent
 static_assert(HALF_BYTES % 128 == 0 && REC_SLOT_OFF % 16 == 0, "halves must stay 16-byte aligned");
 static_assert(HOT_BYTES <= HALF_BYTES && REC_SLOT_OFF + REC_COPY <= HALF_BYTES, "half too small");
-constexpr int PRED_RANK_MAX = 64;       // in-kernel predictors: rank <= 64, a multiple of 8
+constexpr int PRED_RANK_MAX = 96;       // in-kernel predictors: rank <= 96, a multiple of 8
 constexpr int PBUF_BYTES = WU_ROWS * PRED_RANK_MAX * 4 + WU_ROWS * 4;   // one W_up tile + bias (>= a W_down tile)
 static_assert(WD_ROWS * PRED_RANK_MAX * 4 <= PBUF_BYTES, "predictor tiles must fit the planner buffer");
-constexpr int XC_STRIDE = 4096 + 64;    // e4m3 component rows of RMSNorm(x): +64 B keeps two rows' loads apart
 static_assert(NE > NSG, "the subgroups' entries advance by NSG per group");
 static_assert(SPT == 32 && EPT == 8, "the decoders assume 32 elements per subgroup thread");
 
@@ -101,19 +100,14 @@ struct SlotInfo {
 
 struct StackSmem {
   alignas(128) uint8_t pbuf[PBUF_BYTES];   // planner: one predictor tile (W_down or W_up + bias)
-  // RMSNorm_l(x) * 2^e as the sum of three e4m3 values per element (rows c1, c2,
-  // c3): the B operand of the hot neurons' tensor-core dot products; with xq, a
-  // y stage later
-  alignas(16) uint8_t xc[3][XC_STRIDE];
-  uint4 xq[CONS_THREADS];           // RMSNorm_l(x) as 16-bit fixed point, byte digits per 8 elements
+  __half xh[H];                     // RMSNorm_l(x) as f16 (hot neurons); with xq, a y stage later
+  uint4 xq[CONS_THREADS];           // the same as 16-bit fixed point, byte digits per 8 elements
   float ystage[H];                  // subgroup partial y (element 32u+k at k*128+u); earlier in the
                                     // layer, the planner's W_down rows RMSNorm_{l+1}(x_l)
   float z[128];                     // planner: bottleneck of the next layer's predictor
   float rstd0;                      // consumers -> planner: 1 / RMS of x_0 (layer 0's own prediction)
   int2 chunk[H / SPT];              // per 32 elements: (-8 * sum of the fixed-point values, bits of 2^-s)
   float zred[NWARPS];
-  float zmax[NWARPS];
-  float xc_inv;                     // 2^-e: undoes the components' scale
   float red[NSG][2][SG_WARPS][2 * NB_COLD];
   int32_t sgdec[NSG][2];            // per-subgroup decision of its poller
   uint64_t tstat[8];                // trace counters of subgroup 0's poller
@@ -205,14 +199,22 @@ __device__ __forceinline__ float* xchg_y(void* buf, int slot, int sender, int tp
   return reinterpret_cast<float*>(reinterpret_cast<char*>(buf) + XCHG_FLAGS) + ((size_t)slot * tp + sender) * H;
 }
 
+// Layout of the y accumulators (shared stage, global accumulator, exchange
+// buffers): the 4 elements [32 u + 4 j, +4) sit at float4 index 8 u + (j ^ (u &
+// 7)).  A subgroup thread u stores its 32 elements as 8 float4 without bank
+// conflicts (a quarter warp's 8 lanes hit 8 different bank groups), and a
+// consumer thread t reads its elements [8t, 8t+8) as 2 float4.
+__device__ __forceinline__ int ypos4(int u, int j) { return 8 * u + (j ^ (u & 7)); }
+__device__ __forceinline__ int ypos4_of_thread(int t, int h) { return ypos4(t >> 2, 2 * (t & 3) + h); }
+
 // This GPU's partial y of layer l (summed over its CTAs): the local accumulator.
 __device__ __forceinline__ void load_y_local(const StackParams& p, int l, int t, float4& a, float4& b) {
   a = make_float4(0.f, 0.f, 0.f, 0.f);
   b = a;
 #pragma unroll
   for (int k = 0; k < YCOPIES; ++k) {
-    const float4* yv = reinterpret_cast<const float4*>(p.yacc + ((size_t)(l % NACC) * YCOPIES + k) * H + 8 * t);
-    const float4 u = __ldcg(yv), v = __ldcg(yv + 1);
+    const float4* yv = reinterpret_cast<const float4*>(p.yacc + ((size_t)(l % NACC) * YCOPIES + k) * H);
+    const float4 u = __ldcg(yv + ypos4_of_thread(t, 0)), v = __ldcg(yv + ypos4_of_thread(t, 1));
     a.x += u.x; a.y += u.y; a.z += u.z; a.w += u.w;
     b.x += v.x; b.y += v.y; b.z += v.z; b.w += v.w;
   }
@@ -228,9 +230,9 @@ __device__ __forceinline__ void load_x(const StackParams& p, int lm1, int t, flo
     if (s == p.tp_rank) {
       load_y_local(p, lm1, t, u, v);
     } else {
-      const float4* yv = reinterpret_cast<const float4*>(xchg_y(p.peer_buf[p.tp_rank], lm1 % NACC, s, p.tp_size) + 8 * t);
-      u = __ldcg(yv);
-      v = __ldcg(yv + 1);
+      const float4* yv = reinterpret_cast<const float4*>(xchg_y(p.peer_buf[p.tp_rank], lm1 % NACC, s, p.tp_size));
+      u = __ldcg(yv + ypos4_of_thread(t, 0));
+      v = __ldcg(yv + ypos4_of_thread(t, 1));
     }
     a.x += u.x; a.y += u.y; a.z += u.z; a.w += u.w;
     b.x += v.x; b.y += v.y; b.z += v.z; b.w += v.w;
@@ -304,28 +306,6 @@ __device__ __forceinline__ bool cons_broadcast(StackSmem& sm, bool ok0) {
   if (threadIdx.x == 0) sm.flag = ok0 ? 1 : 0;
   named_bar(1, CONS_THREADS);
   return sm.flag != 0;
-}
-// sum of a and max of b over the 512 consumer threads (results in every thread)
-__device__ __forceinline__ float cons_sum_max(StackSmem& sm, float a, float& b) {
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) {
-    a += __shfl_xor_sync(0xffffffffu, a, o);
-    b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, o));
-  }
-  named_bar(1, CONS_THREADS);
-  if ((threadIdx.x & 31) == 0) {
-    sm.zred[threadIdx.x >> 5] = a;
-    sm.zmax[threadIdx.x >> 5] = b;
-  }
-  named_bar(1, CONS_THREADS);
-  a = 0.0f;
-  b = 0.0f;
-#pragma unroll
-  for (int w = 0; w < NWARPS; ++w) {
-    a += sm.zred[w];
-    b = fmaxf(b, sm.zmax[w]);
-  }
-  return a;
 }
 // sum over the 512 consumer threads (result in every thread)
 __device__ __forceinline__ float cons_sum(StackSmem& sm, float a) {
@@ -489,60 +469,32 @@ __device__ __forceinline__ void axpy32_fp8(const uint8_t* row, unsigned short a1
   }
 }
 
-// e4m3 tensor-core dot products: D[16 x 8] += A[16 x 32] B[32 x 8], fp32
-// accumulation (rows 8-15 of A are zero here: a1 = a3 = 0)
-__device__ __forceinline__ void mma_e4m3(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
-}
-
-// Hot group: n (<= NB_HOT) FP8 neurons, one per slot.  Gate / up dot products
-// on the tensor cores: warp w of the subgroup takes K elements [1024 w, 1024 w +
-// 1024) of the four rows (gate A, gate B, up A, up B = A rows 0-3) against the
-// three e4m3 components of RMSNorm(x) * 2^e (B columns 0-2); the weights are
-// e4m3 already, products are exact and sums fp32.  Lane (g, t) = (lane / 4,
-// lane % 4) feeds A row g and B column g with the 16 bytes [64 P + 16 t, +16)
-// of each 64-element step P: the same permutation of K on both operands.
+// Hot group: n (<= NB_HOT) FP8 neurons, one per slot.
 __device__ __forceinline__ void sg_hot(StackSmem& sm, const StackParams& p, const float* hot_scale,
                                        const uint8_t* slot0, const uint8_t* slot1, int n, int64_t i0, int sg, int buf,
                                        float (&y)[SPT]) {
-  const int u = threadIdx.x & (SG_THREADS - 1), lane = threadIdx.x & 31, w = u >> 5;
-  const int g = lane >> 2, tq = lane & 3;
-  const bool a_live = g < 4 && (n > 1 || (g & 1) == 0);
-  const bool b_live = g < 3;
-  const uint8_t* arow = ((g & 1) ? slot1 : slot0) + ((g & 2) ? H : 0) + 1024 * w + 16 * tq;
-  const uint8_t* brow = sm.xc[b_live ? g : 0] + 1024 * w + 16 * tq;
-  float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-  for (int P = 0; P < 16; P += 2) {
-    uint4 a = make_uint4(0u, 0u, 0u, 0u), b = a, a2 = a, b2 = a;
-    if (a_live) {
-      a = *reinterpret_cast<const uint4*>(arow + 64 * P);
-      a2 = *reinterpret_cast<const uint4*>(arow + 64 * P + 64);
-    }
-    if (b_live) {
-      b = *reinterpret_cast<const uint4*>(brow + 64 * P);
-      b2 = *reinterpret_cast<const uint4*>(brow + 64 * P + 64);
-    }
-    mma_e4m3(d0, a.x, a.y, b.x, b.y);
-    mma_e4m3(d0, a.z, a.w, b.z, b.w);
-    mma_e4m3(d1, a2.x, a2.y, b2.x, b2.y);
-    mma_e4m3(d1, a2.z, a2.w, b2.z, b2.w);
-  }
-  // row g, columns 2t and 2t+1 (components 0-2 sit in columns 0-2, the rest are zero)
-  float v = (d0[0] + d1[0]) + (d0[1] + d1[1]);
-  v += __shfl_xor_sync(0xffffffffu, v, 1);
-  if (tq == 0 && g < 4) sm.red[sg][buf][w][g] = v * sm.xc_inv;
-  named_bar(2 + sg, SG_THREADS);
-  float s = 0.0f;
-  if (lane < 2 * NB_HOT) {
+  const int u = threadIdx.x & (SG_THREADS - 1), lane = threadIdx.x & 31;
+  uint32_t xp[16];
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(sm.xh + SPT * u);
 #pragma unroll
-    for (int k = 0; k < SG_WARPS; ++k) s += sm.red[sg][buf][k][lane];
+    for (int i = 0; i < 4; ++i) {
+      const uint4 v = src[i];
+      xp[4 * i] = v.x; xp[4 * i + 1] = v.y; xp[4 * i + 2] = v.z; xp[4 * i + 3] = v.w;
+    }
   }
+  float v[2 * NB_HOT];
+  v[0] = dot32_fp8(slot0 + SPT * u, xp);
+  v[NB_HOT] = dot32_fp8(slot0 + H + SPT * u, xp);
+  v[1] = 0.0f;
+  v[NB_HOT + 1] = 0.0f;
+  if (n > 1) {
+    v[1] = dot32_fp8(slot1 + SPT * u, xp);
+    v[NB_HOT + 1] = dot32_fp8(slot1 + H + SPT * u, xp);
+  }
+  const float s = sg_reduce<2 * NB_HOT>(sm, sg, buf, v);
   const float uu = __shfl_down_sync(0xffffffffu, s, NB_HOT);   // lane j < n: gate j, lane NB_HOT + j: up j
-  float act = 0.0f;
+  float a = 0.0f;
   if (lane < n) {
     float sgs = 1.0f, sus = 1.0f, sds = 1.0f;
     if (hot_scale != nullptr) {
@@ -551,15 +503,16 @@ __device__ __forceinline__ void sg_hot(StackSmem& sm, const StackParams& p, cons
       sus = __ldg(s3 + 1);
       sds = __ldg(s3 + 2);
     }
-    act = gated(s * sgs, uu * sus, p.relu, p.both) * sds;
+    a = gated(s * sgs, uu * sus, p.relu, p.both) * sds;
   }
   // a neuron whose gated activation is exactly zero (dReLU: either branch <= 0)
-  // adds nothing: its down column is skipped (every warp holds the same values)
-  const float a0 = __shfl_sync(0xffffffffu, act, 0), a1 = __shfl_sync(0xffffffffu, act, 1);
+  // adds nothing: its down column is skipped (every warp holds the same a's)
+  const float a0 = __shfl_sync(0xffffffffu, a, 0), a1 = __shfl_sync(0xffffffffu, a, 1);
   if (a0 != 0.0f) axpy32_fp8(slot0 + 2 * H + SPT * u, __half_as_ushort(__float2half_rn(a0)), y);
   if (n > 1 && a1 != 0.0f) axpy32_fp8(slot1 + 2 * H + SPT * u, __half_as_ushort(__float2half_rn(a1)), y);
 }
 
+// Cold group: n (<= NB_COLD) INT4 records, two per slot.
 // The decoded down rows carry a bias (1032 / 1152 per element, int4_pairs):
 // the f16 coefficients are summed into csa / csb and the bias is removed once
 // per layer (cold_bias_out), which keeps it small against fp32's precision.
@@ -1248,13 +1201,10 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
 
       // ---- RMSNorm (engine.py:295; torch.nn.RMSNorm) -> f16 and fixed-point copies
       {
-        float ss = 0.0f, mw = 0.0f;
+        float ss = 0.0f;
 #pragma unroll
-        for (int i = 0; i < EPT; ++i) {
-          ss = fmaf(x[i], x[i], ss);
-          mw = fmaxf(mw, fabsf(x[i] * nw[i]));
-        }
-        ss = cons_sum_max(sm, ss, mw);
+        for (int i = 0; i < EPT; ++i) ss = fmaf(x[i], x[i], ss);
+        ss = cons_sum(sm, ss);
         const float rstd = rsqrtf(ss / (float)H + p.eps);
         float xn[EPT];
         float am = 0.0f;
@@ -1264,35 +1214,10 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
           am = fmaxf(am, fabsf(xn[i]));
         }
         {
-          // three e4m3 components per element of xn * 2^e, 2^e the power of two that
-          // puts max |xn| in [128, 256): c1 = e4m3(v), c2 = e4m3(v - c1), c3 =
-          // e4m3(v - c1 - c2); the residues are exact in fp32, so the sum carries
-          // ~12 significant bits (and e4m3's subnormal floor far below the maximum)
-          const float mx = mw * rstd * 1.0001f + 1e-30f;
-          const int ex = min(max((int)((__float_as_uint(mx) >> 23) & 255u), 8), 253);   // 2^e, 2^-e normal
-          const float sc = __uint_as_float((uint32_t)(134 - ex + 127) << 23);
-          if (t == 0) sm.xc_inv = __uint_as_float((uint32_t)(ex - 134 + 127) << 23);
-          uint32_t cw[3][2];
+          __half2 h2[4];
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            float r[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) r[i] = xn[4 * h + i] * sc;
-#pragma unroll
-            for (int c = 0; c < 3; ++c) {
-              const uint32_t lo = f32x2_to_e4m3x2(r[0], r[1]), hi = f32x2_to_e4m3x2(r[2], r[3]);
-              cw[c][h] = lo | (hi << 16);
-              if (c < 2) {
-                float q[4];
-                e4m3x4_to_f32(cw[c][h], q);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) r[i] -= q[i];
-              }
-            }
-          }
-#pragma unroll
-          for (int c = 0; c < 3; ++c)
-            *reinterpret_cast<uint2*>(sm.xc[c] + EPT * t) = make_uint2(cw[c][0], cw[c][1]);
+          for (int i = 0; i < 4; ++i) h2[i] = __floats2half2_rn(xn[2 * i], xn[2 * i + 1]);
+          *reinterpret_cast<uint4*>(sm.xh + EPT * t) = *reinterpret_cast<const uint4*>(h2);
         }
         // 16-bit fixed point per 32 elements (4 threads): |x| * 2^s < 2^15
         am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
@@ -1432,45 +1357,36 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
       }
       base += (uint32_t)ld_vol(&sm.ngroups[l & 3]);
       {
-        float* bufA = sm.ystage;
-        float* bufB = reinterpret_cast<float*>(sm.xc);     // xc + xq: > 16 KB, dead until the next layer
+        // subgroups 2 and 3 stage their partial y; subgroups 0 and 1 add them and
+        // write the pair sums back in place; one bulk reduction per stage adds
+        // both into the layer's accumulator (the ypos4 layout throughout)
+        float4* bufA = reinterpret_cast<float4*>(sm.ystage);
+        float4* bufB = reinterpret_cast<float4*>(sm.xh);   // xh + xq: 16 KB, dead until the next layer
+        float4* mine = (sg & 1) ? bufB : bufA;
         if (sg >= 2) {
-          float* dst = sg == 2 ? bufA : bufB;
 #pragma unroll
-          for (int k = 0; k < SPT; ++k) dst[k * SG_THREADS + u] = y[k];
+          for (int j = 0; j < SPT / 4; ++j)
+            mine[ypos4(u, j)] = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
         }
         named_bar(1, CONS_THREADS);
         if (sg < 2) {
-          const float* src = sg == 0 ? bufA : bufB;
 #pragma unroll
-          for (int k = 0; k < SPT; ++k) y[k] += src[k * SG_THREADS + u];
+          for (int j = 0; j < SPT / 4; ++j) {
+            const float4 o = mine[ypos4(u, j)];
+            mine[ypos4(u, j)] = make_float4(y[4 * j] + o.x, y[4 * j + 1] + o.y, y[4 * j + 2] + o.z, y[4 * j + 3] + o.w);
+          }
         }
-        named_bar(1, CONS_THREADS);
-        if (sg < 2) {
-          float* dst = sg == 0 ? bufA : bufB;
-#pragma unroll
-          for (int k = 0; k < SPT; ++k) dst[k * SG_THREADS + u] = y[k];
-        }
-        named_bar(1, CONS_THREADS);
-        // element layout: thread t sums elements [8t, 8t+8) (element 32u+k sits at
-        // k*128+u) and stores them in element order for one bulk reduction
-        float e[EPT];
-        const int eu = t >> 2, ek = EPT * (t & 3);
-#pragma unroll
-        for (int i = 0; i < EPT; ++i) e[i] = bufA[(ek + i) * SG_THREADS + eu] + bufB[(ek + i) * SG_THREADS + eu];
-        named_bar(1, CONS_THREADS);
-        float4* yo = reinterpret_cast<float4*>(bufA + EPT * t);
-        yo[0] = make_float4(e[0], e[1], e[2], e[3]);
-        yo[1] = make_float4(e[4], e[5], e[6], e[7]);
         fence_proxy_async_smem();
         named_bar(1, CONS_THREADS);
         if (t == 0) {
           trace_ev(p, l, 9);
-          // y_l += this CTA's partial: the L2 adds 16 KB in one bulk operation
-          bulk_reduce_add_f32(p.yacc + ((size_t)(l % NACC) * YCOPIES + c % YCOPIES) * H, bufA, H * sizeof(float));
+          // y_l += this CTA's two pair sums: the L2 adds 2 x 16 KB in bulk operations
+          float* dst = p.yacc + ((size_t)(l % NACC) * YCOPIES + c % YCOPIES) * H;
+          bulk_reduce_add_f32(dst, reinterpret_cast<float*>(bufA), H * sizeof(float));
+          bulk_reduce_add_f32(dst, reinterpret_cast<float*>(bufB), H * sizeof(float));
           bulk_wait_all();
           trace_ev(p, l, 28);
-          // then the grid-barrier arrival, ordered after the reduction's writes
+          // then the grid-barrier arrival, ordered after the reductions' writes
           asm volatile("fence.proxy.async.global;" ::: "memory");
           trace_ev(p, l, 29);
           asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar_count) : "memory");

@@ -168,9 +168,9 @@ class FFNStack:
         self.predictors = list(predictors)
         for l, pr in enumerate(self.predictors[1:], start=1):
             # layers after the first are predicted inside the kernel (lookahead)
-            if pr is not None and not (0 < pr.rank <= 64 and pr.rank % 8 == 0):
+            if pr is not None and not (0 < pr.rank <= 96 and pr.rank % 8 == 0):
                 raise ValueError(f"layer {l}: the fused kernel predicts with ranks that are multiples of 8 "
-                                 f"up to 64 (got {pr.rank})")
+                                 f"up to 96 (got {pr.rank})")
         self.act = N.HC_ACT_RELU if activation == "relu" else N.HC_ACT_SILU
         self.act_on_both = bool(act_on_both)
         self.eps = float(eps)
@@ -217,7 +217,7 @@ class FFNStack:
         """Layer 0's predictor runs inside the stack kernel (hc_ffn_stack with
         masks_given = 2) -- the kernel supports its rank."""
         p0 = self.predictors[0]
-        return p0 is not None and 0 < p0.rank <= 64 and p0.rank % 8 == 0
+        return p0 is not None and 0 < p0.rank <= 96 and p0.rank % 8 == 0
 
     def first_mask(self, x: torch.Tensor):
         """Layer 0's predicted set from RMSNorm_0(x) (engine.py:422), on device

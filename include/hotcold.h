@@ -227,7 +227,7 @@ HC_API int64_t hc_ffn_stack_workspace_bytes(int32_t grid, int32_t inter);
  * (engine.py:421-438: layer l+1's fetch set comes from layer l's input).
  *   layers     [n_layers] hc_layer_desc (device array); every layer has
  *              `inter` neurons (inter % 4 == 0, inter <= 32768); a predictor
- *              rank must be a multiple of 8 and <= 64 (else HC_ERR_UNSUPPORTED,
+ *              rank must be a multiple of 8 and <= 96 (else HC_ERR_UNSUPPORTED,
  *              no predictor); CTA c owns the neuron ids of mask words
  *              [c*W/grid, (c+1)*W/grid), W = ceil(inter/32), and at most 1024
  *              of them, i.e. ceil(W/grid)*32 <= 1024 (else HC_ERR_UNSUPPORTED)
