@@ -199,22 +199,14 @@ __device__ __forceinline__ float* xchg_y(void* buf, int slot, int sender, int tp
   return reinterpret_cast<float*>(reinterpret_cast<char*>(buf) + XCHG_FLAGS) + ((size_t)slot * tp + sender) * H;
 }
 
-// Layout of the y accumulators (shared stage, global accumulator, exchange
-// buffers): the 4 elements [32 u + 4 j, +4) sit at float4 index 8 u + (j ^ (u &
-// 7)).  A subgroup thread u stores its 32 elements as 8 float4 without bank
-// conflicts (a quarter warp's 8 lanes hit 8 different bank groups), and a
-// consumer thread t reads its elements [8t, 8t+8) as 2 float4.
-__device__ __forceinline__ int ypos4(int u, int j) { return 8 * u + (j ^ (u & 7)); }
-__device__ __forceinline__ int ypos4_of_thread(int t, int h) { return ypos4(t >> 2, 2 * (t & 3) + h); }
-
 // This GPU's partial y of layer l (summed over its CTAs): the local accumulator.
 __device__ __forceinline__ void load_y_local(const StackParams& p, int l, int t, float4& a, float4& b) {
   a = make_float4(0.f, 0.f, 0.f, 0.f);
   b = a;
 #pragma unroll
   for (int k = 0; k < YCOPIES; ++k) {
-    const float4* yv = reinterpret_cast<const float4*>(p.yacc + ((size_t)(l % NACC) * YCOPIES + k) * H);
-    const float4 u = __ldcg(yv + ypos4_of_thread(t, 0)), v = __ldcg(yv + ypos4_of_thread(t, 1));
+    const float4* yv = reinterpret_cast<const float4*>(p.yacc + ((size_t)(l % NACC) * YCOPIES + k) * H + 8 * t);
+    const float4 u = __ldcg(yv), v = __ldcg(yv + 1);
     a.x += u.x; a.y += u.y; a.z += u.z; a.w += u.w;
     b.x += v.x; b.y += v.y; b.z += v.z; b.w += v.w;
   }
@@ -230,9 +222,9 @@ __device__ __forceinline__ void load_x(const StackParams& p, int lm1, int t, flo
     if (s == p.tp_rank) {
       load_y_local(p, lm1, t, u, v);
     } else {
-      const float4* yv = reinterpret_cast<const float4*>(xchg_y(p.peer_buf[p.tp_rank], lm1 % NACC, s, p.tp_size));
-      u = __ldcg(yv + ypos4_of_thread(t, 0));
-      v = __ldcg(yv + ypos4_of_thread(t, 1));
+      const float4* yv = reinterpret_cast<const float4*>(xchg_y(p.peer_buf[p.tp_rank], lm1 % NACC, s, p.tp_size) + 8 * t);
+      u = __ldcg(yv);
+      v = __ldcg(yv + 1);
     }
     a.x += u.x; a.y += u.y; a.z += u.z; a.w += u.w;
     b.x += v.x; b.y += v.y; b.z += v.z; b.w += v.w;
@@ -1357,36 +1349,25 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
       }
       base += (uint32_t)ld_vol(&sm.ngroups[l & 3]);
       {
-        // subgroups 2 and 3 stage their partial y; subgroups 0 and 1 add them and
-        // write the pair sums back in place; one bulk reduction per stage adds
-        // both into the layer's accumulator (the ypos4 layout throughout)
-        float4* bufA = reinterpret_cast<float4*>(sm.ystage);
-        float4* bufB = reinterpret_cast<float4*>(sm.xh);   // xh + xq: 16 KB, dead until the next layer
-        float4* mine = (sg & 1) ? bufB : bufA;
-        if (sg >= 2) {
+        // element order for one bulk reduction: thread t gathers elements [8t, 8t+8)
+        // into bufB (xh + xq: dead until the next layer's input is normalised)
+        float* bufB = reinterpret_cast<float*>(sm.xh);
+        float e[EPT];
+        const int eu = t >> 2, ek = EPT * (t & 3);
 #pragma unroll
-          for (int j = 0; j < SPT / 4; ++j)
-            mine[ypos4(u, j)] = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
-        }
-        named_bar(1, CONS_THREADS);
-        if (sg < 2) {
-#pragma unroll
-          for (int j = 0; j < SPT / 4; ++j) {
-            const float4 o = mine[ypos4(u, j)];
-            mine[ypos4(u, j)] = make_float4(y[4 * j] + o.x, y[4 * j + 1] + o.y, y[4 * j + 2] + o.z, y[4 * j + 3] + o.w);
-          }
-        }
+        for (int i = 0; i < EPT; ++i) e[i] = sm.ystage[(ek + i) * SG_THREADS + eu];
+        float4* yo = reinterpret_cast<float4*>(bufB + EPT * t);
+        yo[0] = make_float4(e[0], e[1], e[2], e[3]);
+        yo[1] = make_float4(e[4], e[5], e[6], e[7]);
         fence_proxy_async_smem();
         named_bar(1, CONS_THREADS);
         if (t == 0) {
           trace_ev(p, l, 9);
-          // y_l += this CTA's two pair sums: the L2 adds 2 x 16 KB in bulk operations
-          float* dst = p.yacc + ((size_t)(l % NACC) * YCOPIES + c % YCOPIES) * H;
-          bulk_reduce_add_f32(dst, reinterpret_cast<float*>(bufA), H * sizeof(float));
-          bulk_reduce_add_f32(dst, reinterpret_cast<float*>(bufB), H * sizeof(float));
+          // y_l += this CTA's partial: the L2 adds 16 KB in one bulk operation
+          bulk_reduce_add_f32(p.yacc + ((size_t)(l % NACC) * YCOPIES + c % YCOPIES) * H, bufB, H * sizeof(float));
           bulk_wait_all();
           trace_ev(p, l, 28);
-          // then the grid-barrier arrival, ordered after the reductions' writes
+          // then the grid-barrier arrival, ordered after the reduction's writes
           asm volatile("fence.proxy.async.global;" ::: "memory");
           trace_ev(p, l, 29);
           asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar_count) : "memory");

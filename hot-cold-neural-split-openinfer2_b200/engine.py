@@ -318,7 +318,7 @@ class FFNStack:
         put("sg0_observe", cyc[:, :, 25])
         put("sg0_release", cyc[:, :, 26])
         put("sg0_total", cyc[:, :, 27])
-        if t.shape[2] > 36 and bool((t[:, :, 32] > 0).any()):
+        if self.tp is not None and self.tp.size > 1 and t.shape[2] > 36 and bool((t[:, :, 32] > 0).any()):
             # tensor parallel: local sum seen -> (CTA 0) push, fence, flags -> all peers seen
             put("tp.local_seen_after_arrive", us[:, :, 32] - us[:, :, 8])
             put("tp.cta0_push", us[:, 0, 36] - us[:, 0, 32])
