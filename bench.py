@@ -227,10 +227,11 @@ def batched_decode_bench(syn, steps: int, warmup: int, batches=(1, 8, 32, 64), s
     + hc_ffn_batch_layer per layer, tcgen05 tensor-core GEMMs), captured in one
     CUDA graph per batch size; B = 1 runs the fused batch-1 stack kernel.
     ``shard=(rank, size)`` (every rank calls this): each GPU streams its share
-    of every layer and the partial outputs are summed by one NCCL all-reduce
-    per layer, launched eagerly; times are the max over ranks.  `value` is device-resident; `e2e` adds the
-    pinned host->device copy of the B inputs and the device->host copy of the
-    outputs to every step."""
+    of every layer and the partial outputs are summed by one exchange kernel
+    per layer (hc_xchg_sum: NVLink stores, bounded waits), captured in the same
+    CUDA graph; times are the max over ranks.  `value` is device-resident;
+    `e2e` adds the pinned host->device copy of the B inputs and the
+    device->host copy of the outputs to every step."""
     import torch
     import hc_synth
     peak, _ = _peaks()
@@ -248,13 +249,13 @@ def batched_decode_bench(syn, steps: int, warmup: int, batches=(1, 8, 32, 64), s
         y = torch.empty(B, H, device=dev)
         bst.forward(x_in, masks=masks, out=y)                   # first call outside capture
         torch.cuda.synchronize()
-        # B = 1 runs the fused stack (one cooperative launch per token): launched
-        # directly; larger batches replay one captured graph per step.  Sharded
-        # batches launch eagerly: every all-reduce stays under the process
-        # group's timeout (a collective inside a replayed graph is not watched).
+        # B = 1 on one GPU runs the fused stack (one cooperative launch per token):
+        # launched directly; everything else replays one captured graph per step
+        # (the sharded exchange is a plain kernel with bounded waits, no library
+        # collective)
         g = None
         sharded = shard is not None and shard[1] > 1
-        if B > 1 and not sharded:
+        if B > 1 or sharded:
             g = torch.cuda.CUDAGraph()
             stream.wait_stream(torch.cuda.current_stream())
             try:
@@ -305,6 +306,7 @@ def batched_decode_bench(syn, steps: int, warmup: int, batches=(1, 8, 32, 64), s
                        "algorithmic_gbs": round(gbs, 1), "frac": round(gbs / (peak * n_gpu), 4),
                        "graph": g is not None}
         del g
+    bst.close()
     return out
 
 
@@ -584,8 +586,9 @@ def run_gpu(args):
         if bd_tp is not None:
             line["batched_decode"] = {"workload": f"configs[4] on {ws} GPUs: 32L 4096/14336 stack, B tokens, "
                                                   "per-token Bernoulli(0.1) masks unioned per layer; every layer's "
-                                                  f"hot neurons and cold records split over {ws} GPUs, one NCCL "
-                                                  "all-reduce of the [B, 4096] partial output per layer",
+                                                  f"hot neurons and cold records split over {ws} GPUs, one "
+                                                  "exchange kernel (NVLink stores into the peers' buffers) per "
+                                                  "layer summing the [B, 4096] partial outputs, CUDA graph",
                                       "unit": "tokens/s (whole job)", "peak": peak, "by_B": bd_tp}
         if dq is not None:
             line["cold_dequant"] = {"unit": "GB/s", "peak": peak, "bytes_per_neuron": COLD_BYTES + 3 * H * 2,

@@ -91,14 +91,16 @@ class TPGroup:
     current; call :meth:`close` before destroying the process group.
     """
 
-    def __init__(self, group=None, device=None):
+    def __init__(self, group=None, device=None, nbytes: Optional[int] = None):
+        """``nbytes``: size of each GPU's exchange buffer (default: the fused
+        stack's, hc_tp_buffer_bytes)."""
         import ctypes
         import torch.distributed as dist
         self.size = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         with torch.cuda.device(self.device):
-            nbytes = int(N.lib.hc_tp_buffer_bytes(self.size))
+            nbytes = int(N.lib.hc_tp_buffer_bytes(self.size)) if nbytes is None else int(nbytes)
             if nbytes <= 0:
                 raise ValueError(f"tensor parallelism over {self.size} GPUs is not supported")
             buf = ctypes.c_void_p()
@@ -407,10 +409,15 @@ class BatchStack:
         ``shard=(rank, size)``: this GPU takes hot neurons [rank n_hot / size,
         (rank+1) n_hot / size) of each layer's hot list and the cold records
         with section indices in [rank n_rec / size, (rank+1) n_rec / size);
-        each layer's partial output [B, 4096] is summed over the ``group``
-        (torch.distributed, NCCL) with one all-reduce before x += y, so every
-        rank ends with the whole stack's output.  Sharded batches always
-        stream the packed copy of the share (the union's flags select)."""
+        each layer's partial output [B, 4096] is summed over the GPUs of
+        ``group`` by one exchange kernel (hc_xchg_sum: NVLink stores into the
+        peers' IPC-mapped buffers, bounded waits) that adds the sum into x, so
+        every rank ends with the whole stack's output; a forward holds no
+        library collective and a CUDA graph can capture it.  Sharded batches
+        always stream the packed copy of the share (the union's flags
+        select).  Build it on every rank with the process group initialised
+        (the buffers' IPC handles are exchanged over ``group``) and call
+        :meth:`close` before destroying the group."""
         self.store = store
         self.device = store.device
         self.L = len(hot)
@@ -459,6 +466,13 @@ class BatchStack:
         self.flag_stride = (max(max(self.sec_records), 1) + 15) // 16 * 16
         self.part = torch.zeros(self.max_batch, HIDDEN_DIM, dtype=torch.float32, device=self.device) \
             if size > 1 else None
+        self.xg = None
+        if size > 1:
+            cap = self.max_batch * HIDDEN_DIM
+            self.xg = TPGroup(group, self.device, nbytes=int(N.lib.hc_xchg_buffer_bytes(size, cap)))
+            self.xg_cap = cap
+            self._xdesc = N.TPDesc(size=size, rank=rank, words_lo=0, words_n=0, peer_buf=N.ptr(self.xg.peer_buf),
+                                   seq_base=0, wait_ns=0)
         self.flags = torch.zeros(self.L, self.flag_stride, dtype=torch.uint8, device=self.device)
         # dense mode streams a packed copy of each layer (hc_batch_pack), built once here
         self.packed = [None] * self.L
@@ -537,7 +551,7 @@ class BatchStack:
                                                  1 if self.act_on_both else 0, N.ptr(self.ws), N.ptr(self.status), s),
                         "hc_ffn_batch_layer")
             else:
-                # this GPU's share of the layer into part, then one all-reduce of [B, 4096]
+                # this GPU's share of the layer into part, then y += the sum of every GPU's part
                 part = self.part[:B]
                 part.zero_()
                 N.check(N.lib.hc_ffn_batch_layer_partial(
@@ -545,8 +559,8 @@ class BatchStack:
                     N.ptr(self.count[l:l + 1]), self.max_cold[l], N.ptr(flags[l]) + self.rec_lo[l], self.eps,
                     self.act, 1 if self.act_on_both else 0, N.ptr(self.ws), N.ptr(part), N.ptr(self.status), s),
                     "hc_ffn_batch_layer_partial")
-                torch.distributed.all_reduce(part, group=self.group)
-                y.add_(part)
+                N.check(N.lib.hc_xchg_sum(N.ptr(part), B * HIDDEN_DIM, N.ptr(y), self.xg_cap,
+                                          ctypes.byref(self._xdesc), N.ptr(self.status), s), "hc_xchg_sum")
             if x_hist is not None:
                 x_hist[l].copy_(y)
         return y
@@ -570,6 +584,13 @@ class BatchStack:
         N.read_status(self.status, "hc_ffn_batch_layer")
         if self._single_stack is not None:
             self._single_stack.check()
+
+    def close(self):
+        """Release the exchange buffers of a sharded stack (before the process
+        group is destroyed)."""
+        if self.xg is not None:
+            self.xg.close()
+            self.xg = None
 
     def union_counts(self) -> torch.Tensor:
         """Cold records each layer fetched in the last forward."""

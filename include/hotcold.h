@@ -423,6 +423,27 @@ HC_API int hc_ffn_batch_layer_partial(const hc_layer_desc* layer, const void* pa
 HC_API int64_t hc_batch_pack_bytes(int32_t n_hot, int32_t n_records);
 HC_API int hc_batch_pack(const hc_layer_desc* layer, void* packed, hc_stream_t stream);
 
+/*
+ * hc_xchg_sum -- the one exchange per layer of the neuron-sharded batched
+ * decode (the reference's down_proj is linear in the neuron dimension,
+ * engine.py:184-188): out += sum over the `size` GPUs of their `part`, in GPU
+ * order, so every GPU gets bit-identical sums.  Each GPU stores its partial
+ * into every peer's exchange buffer with plain NVLink stores (CUDA IPC
+ * mappings from hc_tp_alloc / hc_ipc_open), releases once per CTA and adds to
+ * the peers' arrival counters; it then waits (bounded by tp->wait_ns, default
+ * 2 s; HC_ERR_TIMEOUT in `status` and `out` untouched on expiry) for all
+ * peers.  An ordinary kernel: a CUDA graph can hold it.
+ *   part, out   [n] fp32 (16-byte aligned), n % 4 == 0, n <= max_floats
+ *   tp          size (2..8), rank, peer_buf (device array of every GPU's
+ *               buffer of hc_xchg_buffer_bytes(size, max_floats) bytes, zeroed
+ *               once), wait_ns; seq_base is not used: the buffers count the
+ *               exchanges themselves, so a CUDA graph can replay the call
+ * Every GPU of the group must make the same sequence of calls on its buffers.
+ */
+HC_API int64_t hc_xchg_buffer_bytes(int32_t size, int64_t max_floats);
+HC_API int hc_xchg_sum(const float* part, int64_t n, float* out, int64_t max_floats, const hc_tp_desc* tp,
+                       int32_t* status, hc_stream_t stream);
+
 /* ======================================================================= */
 /* Decode-step attention projections                                       */
 /* ======================================================================= */

@@ -2,7 +2,8 @@
 
 Each GPU streams its share of every layer (half of the hot list, half of
 the section's records, packed) and the layers' partial outputs are summed
-with one NCCL all-reduce of [B, 4096] per layer.  The result must match the
+with one exchange kernel per layer (hc_xchg_sum: NVLink stores into the
+peers' buffers, bounded waits).  The result must match the
 float64 oracle layer by layer (all hot neurons + the union's cold records),
 match the same batch on one GPU (float summation order aside) and be
 identical on both ranks.  Skipped on machines with fewer than two GPUs.
@@ -76,6 +77,22 @@ def _worker(rank, world, port, out_dir):
         bst.check()
         res[f"tp{B}"] = hist.cpu().clone()
         res[f"count{B}"] = bst.union_counts().cpu().clone()
+        if B > 1:
+            # the sharded forward holds no library collective: one CUDA graph replays it
+            yg = torch.empty(B, 4096, device=dev)
+            g = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream(device=dev)
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                with torch.cuda.graph(g, stream=s):
+                    bst.forward(x0, masks=masks, out=yg)
+            torch.cuda.current_stream().wait_stream(s)
+            for _ in range(2):
+                g.replay()
+            torch.cuda.synchronize()
+            bst.check()
+            res[f"graph{B}"] = yg.cpu().clone()
+            del g
         if rank == 0:
             res[f"oracle{B}"] = _oracle_worst(syn, bst.fetch, masks, x0, hist)
             one = syn.batch_stack(max_batch=64, single_token_stack=False)
@@ -85,6 +102,7 @@ def _worker(rank, world, port, out_dir):
             one.check()
             res[f"one{B}"] = h1.cpu().clone()
             res[f"x0_{B}"] = x0.cpu().clone()
+        bst.close()
         del bst
     torch.save(res, os.path.join(out_dir, f"rank{rank}.pt"))
     dist.barrier()
@@ -102,6 +120,10 @@ def test_sharded_batch_matches_one_gpu(tmp_path):
         assert torch.equal(r0[f"tp{B}"], r1[f"tp{B}"])                 # the all-reduce leaves identical bits
         assert torch.equal(r0[f"count{B}"], r1[f"count{B}"])
         assert r0[f"oracle{B}"] <= 2e-3, (B, r0[f"oracle{B}"])        # every layer against the float64 oracle
+        if B > 1:
+            assert torch.equal(r0[f"graph{B}"], r1[f"graph{B}"])       # graph replays agree across ranks
+            d = (r0[f"graph{B}"] - r0[f"tp{B}"][-1]).norm() / (r0[f"tp{B}"][-1] - r0[f"x0_{B}"]).norm()
+            assert float(d) < 1e-4, float(d)                           # and with the eager forward
         x0 = r0[f"x0_{B}"].double()
         prev = x0
         for l in range(r0[f"tp{B}"].shape[0]):
