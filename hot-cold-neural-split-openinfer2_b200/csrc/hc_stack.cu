@@ -102,8 +102,8 @@ struct StackSmem {
   alignas(128) uint8_t pbuf[PBUF_BYTES];   // planner: one predictor tile (W_down or W_up + bias)
   __half xh[H];                     // RMSNorm_l(x) as f16 (hot neurons); with xq, a y stage later
   uint4 xq[CONS_THREADS];           // the same as 16-bit fixed point, byte digits per 8 elements
-  float ystage[H];                  // subgroup partial y (element 32u+k at k*128+u); earlier in the
-                                    // layer, the planner's W_down rows RMSNorm_{l+1}(x_l)
+  float ystage[H];                  // partial y stage of the layer-end tree (ypos4 layout); earlier in
+                                    // the layer, the planner's W_down rows RMSNorm_{l+1}(x_l)
   float z[128];                     // planner: bottleneck of the next layer's predictor
   float rstd0;                      // consumers -> planner: 1 / RMS of x_0 (layer 0's own prediction)
   int2 chunk[H / SPT];              // per 32 elements: (-8 * sum of the fixed-point values, bits of 2^-s)
@@ -198,6 +198,13 @@ __device__ __forceinline__ uint32_t* xchg_flags(void* buf) { return reinterpret_
 __device__ __forceinline__ float* xchg_y(void* buf, int slot, int sender, int tp) {
   return reinterpret_cast<float*>(reinterpret_cast<char*>(buf) + XCHG_FLAGS) + ((size_t)slot * tp + sender) * H;
 }
+
+// Shared-memory stage of the partial y: the 4 elements [32 u + 4 j, +4) of
+// subgroup thread u sit at float4 index 8 u + (j ^ (u & 7)), so that u's 8
+// float4 stores and consumer thread t's reads of its elements [8t, 8t+8) (two
+// float4) are free of bank conflicts.
+__device__ __forceinline__ int ypos4(int u, int j) { return 8 * u + (j ^ (u & 7)); }
+__device__ __forceinline__ int ypos4_of_thread(int t, int h) { return ypos4(t >> 2, 2 * (t & 3) + h); }
 
 // This GPU's partial y of layer l (summed over its CTAs): the local accumulator.
 __device__ __forceinline__ void load_y_local(const StackParams& p, int l, int t, float4& a, float4& b) {
@@ -1349,22 +1356,51 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
       }
       base += (uint32_t)ld_vol(&sm.ngroups[l & 3]);
       {
-        // element order for one bulk reduction: thread t gathers elements [8t, 8t+8)
-        // into bufB (xh + xq: dead until the next layer's input is normalised)
-        float* bufB = reinterpret_cast<float*>(sm.xh);
-        float e[EPT];
-        const int eu = t >> 2, ek = EPT * (t & 3);
+        // Fixed tree over the four subgroups' partial y in shared memory (ypos4
+        // layout, conflict-free): subgroups 2 and 3 stage theirs, subgroups 0 and 1
+        // add them in place, then thread t adds the two stages' elements
+        // [8t, 8t+8) and stores them in element order for one bulk reduction.
+        // bufA = ystage (the planner released it: wdown_done above), bufB = xh + xq
+        // (dead until the next layer's input is normalised).
+        float4* bufA = reinterpret_cast<float4*>(sm.ystage);
+        float4* bufB = reinterpret_cast<float4*>(sm.xh);
+        float4* mine = (sg & 1) ? bufB : bufA;
+        if (sg >= 2) {
 #pragma unroll
-        for (int i = 0; i < EPT; ++i) e[i] = sm.ystage[(ek + i) * SG_THREADS + eu];
-        float4* yo = reinterpret_cast<float4*>(bufB + EPT * t);
-        yo[0] = make_float4(e[0], e[1], e[2], e[3]);
-        yo[1] = make_float4(e[4], e[5], e[6], e[7]);
+          for (int j = 0; j < SPT / 4; ++j)
+            mine[ypos4(u, j)] = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+        }
+        named_bar(1, CONS_THREADS);
+        if (sg < 2) {
+#pragma unroll
+          for (int j = 0; j < SPT / 4; ++j) {
+            const float4 o = mine[ypos4(u, j)];
+            mine[ypos4(u, j)] = make_float4(y[4 * j] + o.x, y[4 * j + 1] + o.y, y[4 * j + 2] + o.z,
+                                            y[4 * j + 3] + o.w);
+          }
+        }
+        named_bar(1, CONS_THREADS);
+        float4 e0 = bufA[ypos4_of_thread(t, 0)], e1 = bufA[ypos4_of_thread(t, 1)];
+        {
+          const float4 f0 = bufB[ypos4_of_thread(t, 0)], f1 = bufB[ypos4_of_thread(t, 1)];
+          e0.x += f0.x; e0.y += f0.y; e0.z += f0.z; e0.w += f0.w;
+          e1.x += f1.x; e1.y += f1.y; e1.z += f1.z; e1.w += f1.w;
+        }
+        named_bar(1, CONS_THREADS);       // every stage read before bufA is overwritten
+        {
+          // element order; lanes 4-7 of each quarter warp store their second half
+          // first, so both stores are conflict-free
+          const int f = (t >> 2) & 1;
+          bufA[2 * t + f] = f ? e1 : e0;
+          bufA[2 * t + 1 - f] = f ? e0 : e1;
+        }
         fence_proxy_async_smem();
         named_bar(1, CONS_THREADS);
         if (t == 0) {
           trace_ev(p, l, 9);
           // y_l += this CTA's partial: the L2 adds 16 KB in one bulk operation
-          bulk_reduce_add_f32(p.yacc + ((size_t)(l % NACC) * YCOPIES + c % YCOPIES) * H, bufB, H * sizeof(float));
+          bulk_reduce_add_f32(p.yacc + ((size_t)(l % NACC) * YCOPIES + c % YCOPIES) * H,
+                              reinterpret_cast<const float*>(bufA), H * sizeof(float));
           bulk_wait_all();
           trace_ev(p, l, 28);
           // then the grid-barrier arrival, ordered after the reduction's writes
