@@ -15,8 +15,9 @@
 //      so every GPU computes bit-identical sums.
 //
 // Buffer layout: [256 B header][3 slots][size senders][n max floats].  The
-// header holds the arrival counter (word 0, added to by the peers), this GPU's
-// count of finished exchanges (word 32) and an exit counter (word 64).  The
+// header (64 words) holds the arrival counter (word 0, added to by the peers),
+// this GPU's count of finished exchanges (word 32) and an exit counter (word
+// 48); the arrival counter has its 128-byte line to itself.  The
 // arrival counter only grows: after exchange q it holds q (size - 1) x 128
 // (every exchange runs 128 CTAs).  The exchange number is read from the
 // buffer, not passed in, so a captured CUDA graph can replay the exchange.
@@ -30,6 +31,8 @@ constexpr int SLOTS = 3;
 constexpr int THREADS = 256;
 constexpr int MAX_SIZE = 8;
 constexpr int GRID = 128;            // CTAs of every exchange (the counter arithmetic relies on it)
+constexpr int W_ARRIVE = 0, W_SEQ = 32, W_EXIT = 48;    // header words (HDR / 4 = 64 of them)
+static_assert(W_EXIT < (int)(HDR / 4), "header words must stay inside the header");
 constexpr uint64_t DEFAULT_WAIT_NS = 2000000000ull;
 
 __device__ __forceinline__ float4* slot_row(void* buf, int slot, int sender, int size, int64_t cap) {
@@ -53,7 +56,7 @@ __global__ void __launch_bounds__(THREADS) xchg_sum_kernel(XParams p) {
   __shared__ uint32_t seq_s;
   const int t = threadIdx.x, c = blockIdx.x, G = gridDim.x;
   void* own = p.peer_buf[p.rank];
-  if (t == 0) seq_s = __ldcg(hdr_word(own, 32));    // exchanges finished here so far
+  if (t == 0) seq_s = __ldcg(hdr_word(own, W_SEQ));    // exchanges finished here so far
   __syncthreads();
   const uint32_t seq = seq_s;
   const int slot = (int)(seq % SLOTS);
@@ -71,9 +74,9 @@ __global__ void __launch_bounds__(THREADS) xchg_sum_kernel(XParams p) {
     asm volatile("fence.acq_rel.sys;" ::: "memory");
     for (int s = 0; s < p.size; ++s) {
       if (s == p.rank) continue;
-      asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(p.peer_buf[s]) : "memory");
+      asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(hdr_word(p.peer_buf[s], W_ARRIVE)) : "memory");
     }
-    const uint32_t* f = hdr_word(own, 0);
+    const uint32_t* f = hdr_word(own, W_ARRIVE);
     const uint32_t want = (seq + 1u) * (uint32_t)(p.size - 1) * (uint32_t)G;
     const uint64_t t0 = globaltimer_ns();
     bool ok = true;
@@ -104,9 +107,9 @@ __global__ void __launch_bounds__(THREADS) xchg_sum_kernel(XParams p) {
   // the last CTA to leave counts the exchange (read by the next launch, stream-ordered)
   if (t == 0) {
     __threadfence();
-    if (atomicAdd(hdr_word(own, 64), 1u) == (uint32_t)G - 1) {
-      *hdr_word(own, 64) = 0u;
-      *hdr_word(own, 32) = seq + 1u;
+    if (atomicAdd(hdr_word(own, W_EXIT), 1u) == (uint32_t)G - 1) {
+      *hdr_word(own, W_EXIT) = 0u;
+      *hdr_word(own, W_SEQ) = seq + 1u;
       __threadfence();
     }
   }
