@@ -189,14 +189,26 @@ __device__ __forceinline__ int64_t split_lo(int64_t n, int c, int G) { return n 
 // predictor tiles must fit a slot and split evenly over 4 threads per neuron
 __device__ __forceinline__ bool rank_ok(int r) { return r > 0 && r <= PRED_RANK_MAX && (r & 7) == 0; }
 
-// Exchange buffer of one GPU (tensor-parallel mode): per slot (l % NACC) a
-// flag word per sender, then per slot a partial y [H] per sender.
-constexpr size_t XCHG_FLAGS = 256;     // header: the arrival counter (first word)
+// Exchange buffer of one GPU (tensor-parallel mode): a 256-byte header, then
+// per slot (exchange number % NACC) and sender one row of H words of 8 bytes,
+// (sequence number << 32) | bits of the float.  An aligned 8-byte store is
+// single-copy atomic, so a receiver that reads the exchange's sequence number
+// in a word also reads that word's value: the data carries its own arrival
+// flag, and no fence or counter is needed between the stores and the reads.
+constexpr size_t XCHG_HDR = 256;
 constexpr int TP_MAX = 8;              // GPUs per tensor-parallel group
-constexpr int KP_MAX = 16;             // CTAs that push slices of a GPU's partial to its peers
-__device__ __forceinline__ uint32_t* xchg_flags(void* buf) { return reinterpret_cast<uint32_t*>(buf); }
-__device__ __forceinline__ float* xchg_y(void* buf, int slot, int sender, int tp) {
-  return reinterpret_cast<float*>(reinterpret_cast<char*>(buf) + XCHG_FLAGS) + ((size_t)slot * tp + sender) * H;
+constexpr int KP_MAX = 32;             // CTAs that push slices of a GPU's partial to its peers
+__device__ __forceinline__ unsigned long long* xchg_row(void* buf, int slot, int sender, int tp) {
+  return reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(buf) + XCHG_HDR) +
+         ((size_t)slot * tp + sender) * H;
+}
+__device__ __forceinline__ void st_pair_sys(unsigned long long* dst, unsigned long long a, unsigned long long b) {
+  asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ ulonglong2 ld_pair_sys(const unsigned long long* src) {
+  ulonglong2 v;
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(src) : "memory");
+  return v;
 }
 
 // Shared-memory stage of the partial y: the 4 elements [32 u + 4 j, +4) of
@@ -219,24 +231,67 @@ __device__ __forceinline__ void load_y_local(const StackParams& p, int l, int t,
   }
 }
 
+// Peer s's partial y of the exchange `seq`, elements [8t, 8t+8): poll (bounded)
+// until all 8 words carry seq.  False if the wait ran out.
+__device__ bool load_y_peer(const StackParams& p, int s, uint32_t seq, int t, float4& a, float4& b) {
+  const unsigned long long* src = xchg_row(p.peer_buf[p.tp_rank], (int)(seq % NACC), s, p.tp_size) + 8 * t;
+  ulonglong2 w[4];
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; ++i) {
+    bool all = true;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      w[k] = ld_pair_sys(src + 2 * k);
+      all = all && (uint32_t)(w[k].x >> 32) == seq && (uint32_t)(w[k].y >> 32) == seq;
+    }
+    if (all) break;
+    if (i == 0) t0 = globaltimer_ns();
+    else if ((i & 63) == 0 && globaltimer_ns() - t0 > p.wait_ns) return false;
+    __nanosleep(32);
+  }
+  a = make_float4(__uint_as_float((uint32_t)w[0].x), __uint_as_float((uint32_t)w[0].y),
+                  __uint_as_float((uint32_t)w[1].x), __uint_as_float((uint32_t)w[1].y));
+  b = make_float4(__uint_as_float((uint32_t)w[2].x), __uint_as_float((uint32_t)w[2].y),
+                  __uint_as_float((uint32_t)w[3].x), __uint_as_float((uint32_t)w[3].y));
+  return true;
+}
+
 // x_l[8t, 8t+8) = x_{l-1} + y_{l-1}; with several GPUs, y is the sum of every
-// GPU's partial in GPU order, so all GPUs compute identical bits.
-__device__ __forceinline__ void load_x(const StackParams& p, int lm1, int t, float (&x)[8]) {
+// GPU's partial in GPU order, so all GPUs compute identical bits.  Returns
+// false (in every consumer thread of the CTA) if a peer's partial did not
+// arrive in time; the caller then stops.
+__device__ __forceinline__ bool load_x(StackSmem& sm, const StackParams& p, int lm1, int t, float (&x)[8]) {
   const float4* xv = reinterpret_cast<const float4*>(p.xbuf + (size_t)(lm1 % NACC) * H + 8 * t);
   float4 a = __ldcg(xv), b = __ldcg(xv + 1);
+  bool ok = true;
+  const uint32_t seq = p.seq_base + (uint32_t)lm1 + 1u;
   for (int s = 0; s < p.tp_size; ++s) {
     float4 u, v;
     if (s == p.tp_rank) {
       load_y_local(p, lm1, t, u, v);
-    } else {
-      const float4* yv = reinterpret_cast<const float4*>(xchg_y(p.peer_buf[p.tp_rank], lm1 % NACC, s, p.tp_size) + 8 * t);
-      u = __ldcg(yv);
-      v = __ldcg(yv + 1);
+    } else if (!load_y_peer(p, s, seq, t, u, v)) {
+      ok = false;
+      break;
     }
     a.x += u.x; a.y += u.y; a.z += u.z; a.w += u.w;
     b.x += v.x; b.y += v.y; b.z += v.z; b.w += v.w;
   }
   x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+  if (p.tp_size == 1) return true;
+  if (!ok) {
+    sm.abort = 1;
+    atomicOr(p.status, HC_ERR_TIMEOUT);
+  }
+  uint32_t all;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.and.pred po, 1, %2, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(all)
+      : "r"((uint32_t)ok), "r"(CONS_THREADS)
+      : "memory");
+  return all != 0;
 }
 
 // generic-proxy shared-memory writes -> visible to the bulk-copy (async) proxy
@@ -605,75 +660,38 @@ __device__ bool grid_wait(StackSmem& sm, const StackParams& p, uint32_t target, 
 }
 
 // Wait until y of layer lm1 is complete: every CTA of this GPU added its
-// partial.  With several GPUs, the first kp = min(grid, 16) CTAs then each
-// copy one slice (1/kp) of this GPU's partial into every peer's exchange
-// buffer (plain NVLink stores), issue one system-scope release and add 1 to
-// each peer's arrival counter; every CTA waits (bounded) until its own
-// counter shows all (size - 1) x kp slices of this layer.  The counter only
-// grows: after the layer with sequence number q it holds q (size - 1) kp, so
-// every GPU must run the same grid.
+// partial.  With several GPUs, the first kp = min(grid, 32) CTAs then each
+// store one slice (1/kp) of this GPU's partial, as (sequence number, value)
+// words, into every peer's exchange buffer with plain NVLink stores; load_x
+// reads the peers' partials as their words arrive.
 __device__ bool layer_wait(StackSmem& sm, const StackParams& p, int lm1) {
   const uint32_t target = (uint32_t)(lm1 + 1) * gridDim.x;
-  if (p.tp_size == 1) return grid_wait(sm, p, target, lm1);
-  const int t = threadIdx.x, slot = lm1 % NACC, c = blockIdx.x;
+  const bool ok = grid_wait(sm, p, target, lm1);     // thread 0 saw every local partial; so does every thread
+  if (p.tp_size == 1 || !ok) return ok;              // on a local timeout the peers time out too
+  const int t = threadIdx.x, c = blockIdx.x;
   const int kp = min((int)gridDim.x, KP_MAX);
-  const uint32_t seq = p.seq_base + (uint32_t)lm1 + 1u;
-  bool ok0 = true;
-  if (t == 0) {
-    ok0 = grid_spin(sm, p, target);
-    trace_ev(p, lm1, 32);
-  }
   if (c < kp) {
-    named_bar(1, CONS_THREADS);      // thread 0 saw every local partial; so does every thread now
-    const int lo = c * (H / 4) / kp, hi = (c + 1) * (H / 4) / kp;     // this CTA's float4 slice
+    const uint32_t seq = p.seq_base + (uint32_t)lm1 + 1u;
+    const int slot = (int)(seq % NACC);
+    const unsigned long long tag = (unsigned long long)seq << 32;
+    const int lo = c * (H / 2) / kp, hi = (c + 1) * (H / 2) / kp;      // this CTA's float2 slice
     for (int i = lo + t; i < hi; i += CONS_THREADS) {
-      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+      float2 a = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int k = 0; k < YCOPIES; ++k) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(p.yacc + ((size_t)slot * YCOPIES + k) * H) + i);
-        a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
+      for (int k = 0; k < YCOPIES; ++k) {       // the order of load_y_local: identical sums on every GPU
+        const float2 v = __ldcg(reinterpret_cast<const float2*>(p.yacc + ((size_t)(lm1 % NACC) * YCOPIES + k) * H) + i);
+        a.x += v.x;
+        a.y += v.y;
       }
+      const unsigned long long w0 = tag | __float_as_uint(a.x), w1 = tag | __float_as_uint(a.y);
       for (int s = 0; s < p.tp_size; ++s) {
         if (s == p.tp_rank) continue;
-        reinterpret_cast<float4*>(xchg_y(p.peer_buf[s], slot, p.tp_rank, p.tp_size))[i] = a;
+        st_pair_sys(xchg_row(p.peer_buf[s], slot, p.tp_rank, p.tp_size) + 2 * i, w0, w1);
       }
     }
-    named_bar(1, CONS_THREADS);
-    if (t == 0 && ok0) {           // on a local timeout the peers time out too
-      trace_ev(p, lm1, 36);
-      // one release (cumulative over the CTA's stores above, ordered by the
-      // barrier) before the counters
-      asm volatile("fence.acq_rel.sys;" ::: "memory");
-      trace_ev(p, lm1, 33);
-      for (int s = 0; s < p.tp_size; ++s) {
-        if (s == p.tp_rank) continue;
-        asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(xchg_flags(p.peer_buf[s])) : "memory");
-      }
-      trace_ev(p, lm1, 34);
-    }
+    if (t == 0) trace_ev(p, lm1, 36);
   }
-  if (t == 0 && ok0) {
-    const uint32_t* f = xchg_flags(p.peer_buf[p.tp_rank]);
-    const uint32_t want = seq * (uint32_t)(p.tp_size - 1) * (uint32_t)kp;
-    const uint64_t t0 = globaltimer_ns();
-    uint32_t i = 0;
-    while (true) {
-      uint32_t v;
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-      if ((int32_t)(v - want) >= 0) break;
-      if ((++i & 63) == 0 && globaltimer_ns() - t0 > p.wait_ns) {
-        ok0 = false;
-        break;
-      }
-      __nanosleep(32);
-    }
-    if (!ok0) {
-      sm.abort = 1;
-      atomicOr(p.status, HC_ERR_TIMEOUT);
-    }
-    trace_ev(p, lm1, 35);
-  }
-  return cons_broadcast(sm, ok0);
+  return true;
 }
 
 // --------------------------------------------------------------------------
@@ -1166,7 +1184,9 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
       } else {
         ok = layer_wait(sm, p, l - 1);
         if (!ok) break;
-        load_x(p, l - 1, t, x);
+        ok = load_x(sm, p, l - 1, t, x);
+        if (!ok) break;
+        if (t == 0) trace_ev(p, l - 1, 35);
         if (p.x_hist && c == 0) {
           float4* h = reinterpret_cast<float4*>(p.x_hist + (size_t)(l - 1) * H + EPT * t);
           h[0] = make_float4(x[0], x[1], x[2], x[3]);
@@ -1415,9 +1435,9 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
     if (ok) {
       const int L = p.n_compute;
       ok = layer_wait(sm, p, L - 1);
+      float xo[EPT];
+      if (ok && c == 0) ok = load_x(sm, p, L - 1, t, xo);
       if (ok && c == 0) {
-        float xo[EPT];
-        load_x(p, L - 1, t, xo);
         const float4 o0 = make_float4(xo[0], xo[1], xo[2], xo[3]);
         const float4 o1 = make_float4(xo[4], xo[5], xo[6], xo[7]);
         float4* out = reinterpret_cast<float4*>(p.x_out + EPT * t);
@@ -1478,7 +1498,7 @@ extern "C" int64_t hc_ffn_stack_workspace_bytes(int32_t grid, int32_t inter) {
 
 extern "C" int64_t hc_tp_buffer_bytes(int32_t tp_size) {
   if (tp_size < 1 || tp_size > TP_MAX) return -1;
-  return (int64_t)(XCHG_FLAGS + sizeof(float) * (size_t)NACC * tp_size * H);
+  return (int64_t)(XCHG_HDR + sizeof(unsigned long long) * (size_t)NACC * tp_size * H);
 }
 
 extern "C" int hc_ffn_stack_tp(const hc_layer_desc* layers, int32_t n_layers, int32_t inter, const float* x_in,

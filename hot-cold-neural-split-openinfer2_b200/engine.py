@@ -321,12 +321,10 @@ class FFNStack:
         put("sg0_release", cyc[:, :, 26])
         put("sg0_total", cyc[:, :, 27])
         if self.tp is not None and self.tp.size > 1 and t.shape[2] > 36 and bool((t[:, :, 32] > 0).any()):
-            # tensor parallel: local sum seen -> (CTA 0) push, fence, flags -> all peers seen
+            # tensor parallel: local sum seen -> (CTA 0) its slice pushed -> every peer's words seen
             put("tp.local_seen_after_arrive", us[:, :, 32] - us[:, :, 8])
             put("tp.cta0_push", us[:, 0, 36] - us[:, 0, 32])
-            put("tp.cta0_fence_sys", us[:, 0, 33] - us[:, 0, 36])
-            put("tp.cta0_flags", us[:, 0, 34] - us[:, 0, 33])
-            put("tp.peers_seen_after_local", us[:, :, 35] - us[:, :, 32])
+            put("tp.peers_seen_after_local", us[:-1, :, 35] - us[:-1, :, 32])
         put("issuer_slot_wait", us[:, :, 18])
         put("dynamic_hot_claimed[n]", t[:, :, 15])
         put("cold_listed[n]", t[:, :, 17])

@@ -264,9 +264,9 @@ HC_API int64_t hc_ffn_stack_workspace_bytes(int32_t grid, int32_t inter);
  *              subgroup 0's poller: 16 waiting for fills, 2/3/23 on cold /
  *              hot / predictor groups, 24/25/26 in its group barrier / seeing
  *              the fills / releasing, 27 in total;
- *              under tensor parallelism 32: local partials complete, 35: all
- *              peers' partials seen; CTA 0 only: 36 pushed to the peers, 33
- *              release fence done, 34 flags written;
+ *              32: local partials complete (every CTA); under tensor
+ *              parallelism 35: all peers' partials seen (layers before the
+ *              last), 36: this CTA's slice pushed (pushing CTAs only);
  *              NULL = off
  * The layer outputs are sums of per-CTA float partials added with atomics, so
  * their last bits can differ between launches.
@@ -284,12 +284,13 @@ HC_API int hc_ffn_stack(const hc_layer_desc* layers, int32_t n_layers, int32_t i
  * hc_layer_desc.hot / n_hot), computes the predictor logits and cold records
  * of mask words [words_lo, words_lo + words_n), and runs the full W_down of
  * every predictor.  Per layer, each GPU sums its CTAs' partial y; its first
- * kp = min(grid, 16) CTAs each copy one slice of that sum into every peer's
- * exchange buffer over NVLink (plain peer stores, no multicast), issue one
- * system-scope release and add 1 to every peer's arrival counter; every GPU
- * waits (bounded) until its counter reaches (seq_base + layer + 1) x
- * (size - 1) x kp, then adds the partials in GPU order, so all GPUs hold
- * bit-identical hidden states.
+ * kp = min(grid, 32) CTAs each store one slice of that sum into every peer's
+ * exchange buffer over NVLink (plain peer stores, no multicast) as 8-byte
+ * words (exchange number << 32 | float bits), exchange number q = seq_base +
+ * layer + 1, in slot q % 3.  An aligned 8-byte store is single-copy atomic,
+ * so every word carries its own arrival flag: each CTA polls (bounded) its
+ * elements' words until they show q, then adds the partials in GPU order, so
+ * all GPUs hold bit-identical hidden states.  No fence or counter is used.
  *   peer_buf   device array [size] of every GPU's exchange buffer
  *              (hc_tp_buffer_bytes(size) bytes from hc_tp_alloc, zeroed once,
  *              opened in the other processes with hc_ipc_open); size <= 8

@@ -1,9 +1,9 @@
 """A bounded device wait that runs out, on one GPU.
 
 The tensor-parallel stack waits, per layer, for every peer GPU's partial
-output (an arrival counter the peers increment over NVLink).  Here the
+output (words tagged with the exchange number, stored over NVLink).  Here the
 "peer" exchange buffer is a second local allocation whose kernel never runs,
-so nothing ever increments this GPU's counter, and the wait limit is 5 ms:
+so no tagged word ever reaches this GPU's buffer, and the wait limit is 5 ms:
 the first layer boundary's wait expires on every CTA.
 The launch must come back on its own with HC_ERR_TIMEOUT in the status word,
 leave its workspace counters clean, and the context must stay usable: a
