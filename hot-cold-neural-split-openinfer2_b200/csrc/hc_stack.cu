@@ -109,7 +109,8 @@ struct StackSmem {
   int2 chunk[H / SPT];              // per 32 elements: (-8 * sum of the fixed-point values, bits of 2^-s)
   float zred[NWARPS];
   float red[NSG][2][SG_WARPS][2 * NB_COLD];
-  int32_t sgdec[NSG][2];            // per-subgroup decision of its poller
+  int32_t sgdec[NSG][2][2];         // per-subgroup decision of its poller: (result, claimed group)
+  int32_t gnext[2];                 // next group of layer l to claim (l & 1), shared by the subgroups
   uint64_t tstat[8];                // trace counters of subgroup 0's poller
   int32_t plan_list[COLD_LIST];     // nids, then record indices, of this CTA's active cold records
   uint32_t own_words[OWN_WORDS];    // predicted mask words of this CTA's neuron-id range
@@ -767,6 +768,8 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
     sm.flag = 1;
     sm.sealed = -1;
     sm.cons_layer = -1;
+    sm.gnext[0] = 0;
+    sm.gnext[1] = 0;
     mbar_fence_init();
   }
   __syncthreads();
@@ -1088,8 +1091,11 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
           const uint32_t total = __ldcg(p.gfill + l % NACC);
           const int32_t* pool = p.gpool + (size_t)(l % NACC) * POOL_CAP;
           const uint32_t i0 = (uint32_t)split_lo(total, c, G), i1 = (uint32_t)split_lo(total, c + 1, G);
-          for (uint32_t i = i0; pr.ok && i < i1; i += NB_COLD) {
-            const int m = (int)min((uint32_t)NB_COLD, i1 - i);
+          // groups of up to NB_COLD records, smaller when the CTA has few (at least
+          // 4 cold groups for the 4 subgroups when it has 4 records or more)
+          const uint32_t gsz = max(1u, min((uint32_t)NB_COLD, (i1 - i0) / 4u));
+          for (uint32_t i = i0; pr.ok && i < i1; i += gsz) {
+            const int m = (int)min(gsz, i1 - i);
             int rec[NB_COLD];
 #pragma unroll
             for (int k = 0; k < NB_COLD; ++k) rec[k] = (k < m) ? __ldcg(pool + i + k) : 0;
@@ -1109,8 +1115,9 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         trace_ev(p, l, 13);
         uint64_t claimed = 0;
         const int64_t hA = split_lo(d.n_hot, c, G), hB = split_lo(d.n_hot, c + 1, G);
-        for (int64_t i = hA; pr.ok && i < hB; i += NB_HOT) {
-          const int n = (int)min((int64_t)NB_HOT, hB - i);
+        const int64_t hsz = (hB - hA >= 8) ? NB_HOT : 1;     // single neurons when the CTA has few
+        for (int64_t i = hA; pr.ok && i < hB; i += hsz) {
+          const int n = (int)min(hsz, hB - i);
           Copy cp[2];
 #pragma unroll
           for (int k = 0; k < 2; ++k)
@@ -1276,6 +1283,8 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         }
       }
       if (t == 0) *reinterpret_cast<volatile int32_t*>(&sm.cons_layer) = l;
+      // layer l+1's claim counter: its last users (layer l-1) are done
+      if (t == 1) sm.gnext[(l + 1) & 1] = 0;
       named_bar(1, CONS_THREADS);
       if (t == 0) {
         // the planner's W_down rows (xs), and at layer 0 the RMS of x_0, are written
@@ -1295,18 +1304,21 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         for (int k = 0; k < 7; ++k) sm.tstat[k] = 0;
         sm.tstat[7] = (uint64_t)clock64();
       }
-      // this subgroup's groups sit at ring positions base + sg, base + sg + 4, ...
-      uint32_t q = base + (uint32_t)sg;
-      int e = (int)(q % (uint32_t)NE);
-      uint32_t par = (q / (uint32_t)NE) & 1u;
-      for (int gi = sg;; gi += NSG) {
+      // The subgroups claim the layer's groups in stream order from a shared
+      // counter (ring position base + group), so a subgroup that drew cheap
+      // groups takes more of them and the four finish together.
+      for (;;) {
         uint64_t tb = 0;
-        // one poller per subgroup decides; the decision reaches all 128 threads through the barrier
+        // one poller per subgroup claims and decides; the decision reaches all 128 threads through the barrier
         if (u == 0) {
-          int r = poll_pos(sm, q, e, par, l, gi, tr ? &sm.tstat[0] : nullptr, p.wait_ns);
+          const int gi = atomicAdd(&sm.gnext[l & 1], 1);
+          const uint32_t qc = base + (uint32_t)gi;
+          int r = poll_pos(sm, qc, (int)(qc % (uint32_t)NE), (qc / (uint32_t)NE) & 1u, l, gi,
+                           tr ? &sm.tstat[0] : nullptr, p.wait_ns);
           if (ld_vol(&sm.abort) != 0) r = -1;
           if (r < 0) sm.abort = 1;
-          sm.sgdec[sg][dbuf] = r;
+          sm.sgdec[sg][dbuf][0] = r;
+          sm.sgdec[sg][dbuf][1] = gi;
           if (tr) tb = (uint64_t)clock64();
         }
         named_bar(2 + sg, SG_THREADS);
@@ -1315,7 +1327,8 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
           sm.tstat[4] += now - tb;
           tb = now;
         }
-        const int r = sm.sgdec[sg][dbuf];
+        const int r = sm.sgdec[sg][dbuf][0];
+        const int e = (int)((base + (uint32_t)sm.sgdec[sg][dbuf][1]) % (uint32_t)NE);
         dbuf ^= 1;
         if (r <= 0) break;
         const SlotInfo inf = sm.info[e];
@@ -1337,12 +1350,6 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         }
         sg_release(sm, e);
         if (tr) sm.tstat[6] += (uint64_t)clock64() - tg1;
-        q += NSG;
-        e += NSG;
-        if (e >= NE) {
-          e -= NE;
-          par ^= 1u;
-        }
       }
       if (p.trace != nullptr && u == 0) trace_ev(p, l, 4 + sg);
       if (tr) {
