@@ -407,6 +407,17 @@ __device__ __forceinline__ int poll_pos(StackSmem& sm, uint32_t q, int e, uint32
   if (waited != nullptr) *waited += (uint64_t)clock64() - c0;
   return r;
 }
+// The same test without waiting: 1 / 0 as poll_pos, 2 when position q is not
+// filled yet (the caller then waits with poll_pos once it holds no entry the
+// fill could need).
+__device__ __forceinline__ int poll_once(StackSmem& sm, uint32_t q, int e, uint32_t par, int l, int gi) {
+  if (ld_vol_u(&sm.info[e].pos) == q && mbar_test_wait(&sm.full[e], par)) return (sm.info[e].layer == l) ? 1 : 0;
+  if (ld_vol(&sm.sealed) >= l) {
+    __threadfence_block();
+    if (gi >= ld_vol(&sm.ngroups[l & 3])) return 0;
+  }
+  return 2;
+}
 __device__ __forceinline__ void sg_release(StackSmem& sm, int e) {
   __syncwarp();
   if ((threadIdx.x & 31) == 0) mbar_arrive(&sm.empty[e]);
@@ -415,12 +426,16 @@ __device__ __forceinline__ void sg_release(StackSmem& sm, int e) {
 // Subgroup reduction of V per-thread partials: warp-level multi-value
 // reduction, one subgroup barrier, then lanes j < V of every warp sum the
 // SG_WARPS warp partials of value j.
-template <int V>
-__device__ __forceinline__ float sg_reduce(StackSmem& sm, int sg, int buf, float (&v)[V]) {
+// `before_bar` runs in every thread just before the barrier (the group loop
+// uses it to claim and test the subgroup's next group, whose decision the same
+// barrier then publishes).
+template <int V, class F>
+__device__ __forceinline__ float sg_reduce(StackSmem& sm, int sg, int buf, float (&v)[V], F&& before_bar) {
   const int lane = threadIdx.x & 31, w = (threadIdx.x >> 5) & (SG_WARPS - 1);
   const float r = warp_reduce_multi<V>(v);
   constexpr int SH = 5 - (V == 16 ? 4 : V == 8 ? 3 : V == 4 ? 2 : 1);
   if ((lane & ((1 << SH) - 1)) == 0) sm.red[sg][buf][w][lane >> SH] = r;
+  before_bar();
   named_bar(2 + sg, SG_THREADS);
   float s = 0.0f;
   if (lane < V) {
@@ -525,9 +540,10 @@ __device__ __forceinline__ void axpy32_fp8(const uint8_t* row, unsigned short a1
 }
 
 // Hot group: n (<= NB_HOT) FP8 neurons, one per slot.
+template <class F>
 __device__ __forceinline__ void sg_hot(StackSmem& sm, const StackParams& p, const float* hot_scale,
                                        const uint8_t* slot0, const uint8_t* slot1, int n, int64_t i0, int sg, int buf,
-                                       float (&y)[SPT]) {
+                                       float (&y)[SPT], F&& before_bar) {
   const int u = threadIdx.x & (SG_THREADS - 1), lane = threadIdx.x & 31;
   uint32_t xp[16];
   {
@@ -547,7 +563,7 @@ __device__ __forceinline__ void sg_hot(StackSmem& sm, const StackParams& p, cons
     v[1] = dot32_fp8(slot1 + SPT * u, xp);
     v[NB_HOT + 1] = dot32_fp8(slot1 + H + SPT * u, xp);
   }
-  const float s = sg_reduce<2 * NB_HOT>(sm, sg, buf, v);
+  const float s = sg_reduce<2 * NB_HOT>(sm, sg, buf, v, before_bar);
   const float uu = __shfl_down_sync(0xffffffffu, s, NB_HOT);   // lane j < n: gate j, lane NB_HOT + j: up j
   float a = 0.0f;
   if (lane < n) {
@@ -571,9 +587,10 @@ __device__ __forceinline__ void sg_hot(StackSmem& sm, const StackParams& p, cons
 // The decoded down rows carry a bias (1032 / 1152 per element, int4_pairs):
 // the f16 coefficients are summed into csa / csb and the bias is removed once
 // per layer (cold_bias_out), which keeps it small against fp32's precision.
+template <class F>
 __device__ __forceinline__ void sg_cold(StackSmem& sm, const StackParams& p, const uint8_t* slot0,
                                         const uint8_t* slot1, int n, int sg, int buf, float (&y)[SPT], float& csa,
-                                        float& csb) {
+                                        float& csb, F&& before_bar) {
   const int u = threadIdx.x & (SG_THREADS - 1), lane = threadIdx.x & 31;
   XFix xf;
   {
@@ -599,7 +616,7 @@ __device__ __forceinline__ void sg_cold(StackSmem& sm, const StackParams& p, con
       v[NB_COLD + j] = dot32_int4(rec[j] + VEC_BYTES + 16 * u, xf) * ld_half(rec[j] + SCALE_OFF + 2 * NGROUPS + gs);
     }
   }
-  const float s = sg_reduce<2 * NB_COLD>(sm, sg, buf, v);
+  const float s = sg_reduce<2 * NB_COLD>(sm, sg, buf, v, before_bar);
   const float uu = __shfl_down_sync(0xffffffffu, s, NB_COLD);
   float a = 0.0f;
   if (lane < n) a = gated(s, uu, p.relu, p.both);
@@ -642,7 +659,7 @@ __device__ bool grid_spin(StackSmem& sm, const StackParams& p, uint32_t target) 
         __nanosleep(32);
       }
     }
-    __threadfence();
+    // (the acquire loads order what follows; the consumers' barrier carries it to the CTA)
     if (!ok0 || ld_vol(&sm.abort) != 0) {
       ok0 = false;
       sm.abort = 1;
@@ -1306,15 +1323,19 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
       }
       // The subgroups claim the layer's groups in stream order from a shared
       // counter (ring position base + group), so a subgroup that drew cheap
-      // groups takes more of them and the four finish together.
-      for (;;) {
+      // groups takes more of them and the four finish together.  A subgroup's
+      // poller claims and tests its next group just before the reduction
+      // barrier of the current one, which publishes the decision: one
+      // subgroup barrier per group.  Decisions alternate between two slots
+      // (a slot is rewritten only after the barrier that follows its reads).
+      int r, gi;
+      {
         uint64_t tb = 0;
-        // one poller per subgroup claims and decides; the decision reaches all 128 threads through the barrier
         if (u == 0) {
-          const int gi = atomicAdd(&sm.gnext[l & 1], 1);
+          gi = atomicAdd(&sm.gnext[l & 1], 1);
           const uint32_t qc = base + (uint32_t)gi;
-          int r = poll_pos(sm, qc, (int)(qc % (uint32_t)NE), (qc / (uint32_t)NE) & 1u, l, gi,
-                           tr ? &sm.tstat[0] : nullptr, p.wait_ns);
+          r = poll_pos(sm, qc, (int)(qc % (uint32_t)NE), (qc / (uint32_t)NE) & 1u, l, gi,
+                       tr ? &sm.tstat[0] : nullptr, p.wait_ns);
           if (ld_vol(&sm.abort) != 0) r = -1;
           if (r < 0) sm.abort = 1;
           sm.sgdec[sg][dbuf][0] = r;
@@ -1322,27 +1343,35 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
           if (tr) tb = (uint64_t)clock64();
         }
         named_bar(2 + sg, SG_THREADS);
-        if (tr) {
-          const uint64_t now = (uint64_t)clock64();
-          sm.tstat[4] += now - tb;
-          tb = now;
-        }
-        const int r = sm.sgdec[sg][dbuf][0];
-        const int e = (int)((base + (uint32_t)sm.sgdec[sg][dbuf][1]) % (uint32_t)NE);
+        if (tr) sm.tstat[4] += (uint64_t)clock64() - tb;
+        r = sm.sgdec[sg][dbuf][0];
+        gi = sm.sgdec[sg][dbuf][1];
         dbuf ^= 1;
-        if (r <= 0) break;
+      }
+      while (r > 0) {
+        const int e = (int)((base + (uint32_t)gi) % (uint32_t)NE);
         const SlotInfo inf = sm.info[e];
         const uint8_t* s0 = ring + (size_t)e * ENTRY_BYTES;
         const uint8_t* s1 = s0 + HALF_BYTES;
+        const int db = dbuf;
+        // claim the next group and test it once (published by the reduction barrier)
+        auto claim_next = [&]() {
+          if (u == 0) {
+            const int g2 = atomicAdd(&sm.gnext[l & 1], 1);
+            const uint32_t q2 = base + (uint32_t)g2;
+            int r2 = poll_once(sm, q2, (int)(q2 % (uint32_t)NE), (q2 / (uint32_t)NE) & 1u, l, g2);
+            if (ld_vol(&sm.abort) != 0) r2 = -1;
+            sm.sgdec[sg][db][0] = r2;
+            sm.sgdec[sg][db][1] = g2;
+          }
+        };
         const uint64_t tg0 = tr ? (uint64_t)clock64() : 0;
-        if (tr) sm.tstat[5] += tg0 - tb;
         if (inf.kind == UNIT_COLD) {
-          sg_cold(sm, p, s0, s1, inf.n, sg, rbuf, y, csa, csb);
-          rbuf ^= 1;
+          sg_cold(sm, p, s0, s1, inf.n, sg, rbuf, y, csa, csb, claim_next);
         } else {
-          sg_hot(sm, p, d.hot_scale, s0, s1, inf.n, inf.index, sg, rbuf, y);
-          rbuf ^= 1;
+          sg_hot(sm, p, d.hot_scale, s0, s1, inf.n, inf.index, sg, rbuf, y, claim_next);
         }
+        rbuf ^= 1;
         uint64_t tg1 = 0;
         if (tr) {
           tg1 = (uint64_t)clock64();
@@ -1350,6 +1379,26 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         }
         sg_release(sm, e);
         if (tr) sm.tstat[6] += (uint64_t)clock64() - tg1;
+        r = sm.sgdec[sg][db][0];
+        gi = sm.sgdec[sg][db][1];
+        dbuf ^= 1;
+        if (r == 2) {
+          // not filled at the test: wait for it now (this subgroup holds no entry)
+          uint64_t tb = 0;
+          if (u == 0) {
+            const uint32_t qc = base + (uint32_t)gi;
+            int r3 = poll_pos(sm, qc, (int)(qc % (uint32_t)NE), (qc / (uint32_t)NE) & 1u, l, gi,
+                              tr ? &sm.tstat[0] : nullptr, p.wait_ns);
+            if (ld_vol(&sm.abort) != 0) r3 = -1;
+            sm.sgdec[sg][dbuf][0] = r3;
+            if (tr) tb = (uint64_t)clock64();
+          }
+          named_bar(2 + sg, SG_THREADS);
+          if (tr) sm.tstat[4] += (uint64_t)clock64() - tb;
+          r = sm.sgdec[sg][dbuf][0];
+          dbuf ^= 1;
+        }
+        if (r < 0 && u == 0) sm.abort = 1;
       }
       if (p.trace != nullptr && u == 0) trace_ev(p, l, 4 + sg);
       if (tr) {
