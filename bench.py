@@ -632,6 +632,11 @@ def run_profile(args):
         dist.init_process_group("gloo")
         tp = engine.TPGroup()
     what = args.profile_target
+    if what == "engine":
+        # configs[3] alone: DesdemonaEngine.generate (the bench line's full_decode field)
+        print(json.dumps(full_decode_bench(torch.device("cuda"))))
+        print("profile target done")
+        return
     syn = hc_synth.make_stack(n_layers=args.layers, inter=args.inter, activation="relu", act_on_both=True, seed=0,
                               predictors=what not in ("gather", "batch") and args.masks_p <= 0)
     if what == "stack":
@@ -701,7 +706,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     # profiling targets (not a bench line): one kernel on a small synthetic case
-    ap.add_argument("--profile-target", choices=["stack", "gather", "predictor", "batch"], default=None)
+    ap.add_argument("--profile-target", choices=["stack", "gather", "predictor", "batch", "engine"], default=None)
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--inter", type=int, default=INTER)
     ap.add_argument("--tokens", type=int, default=3)
