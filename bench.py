@@ -667,6 +667,29 @@ def run_profile(args):
             print(f"stack trace: {args.layers} layers, {fetched / args.layers:.0f} cold records per layer")
             for k, (mean, mx) in st.trace_summary(trace).items():
                 print(f"  {k:28s} mean {mean:9.2f}   max {mx:9.2f}")
+        if trace is not None and tp is not None:
+            # across GPUs: per layer, local sum seen (max over CTAs, event 32), slice pushed
+            # (max over the pushing CTAs, event 36) and peers' words seen (max over CTAs, 35)
+            tr = trace.cpu()
+            allt = [None] * ws
+            dist.all_gather_object(allt, tr)
+            if rank == 0:
+                seen = torch.stack([a[:, :, 32].max(dim=1).values for a in allt]).double() / 1e3
+                push = torch.stack([a[:, :32, 36].max(dim=1).values for a in allt]).double() / 1e3
+                got = torch.stack([a[:-1, :, 35].max(dim=1).values for a in allt]).double() / 1e3
+                skew = (seen.max(dim=0).values - seen.min(dim=0).values)[:-1]
+                print(f"  cross-GPU: local-sum skew between GPUs (us) mean {float(skew.mean()):.2f} "
+                      f"max {float(skew.max()):.2f}")
+                if ws == 2:
+                    # transit each way includes the clock offset with opposite signs: the mean cancels it
+                    t01 = got[1] - push[0][:-1]
+                    t10 = got[0] - push[1][:-1]
+                    print(f"  cross-GPU: last push -> peer's last CTA saw it (us), offset-free mean "
+                          f"{float(((t01 + t10) / 2).mean()):.2f}; each way {float(t01.mean()):.2f} / "
+                          f"{float(t10.mean()):.2f}")
+                late = (seen.max(dim=0).values - seen)[:, :-1]
+                print(f"  cross-GPU: per GPU mean lateness behind the last GPU (us) "
+                      f"{[round(float(v), 2) for v in late.mean(dim=1)]}")
         if tp is not None:
             dist.barrier()
             tp.close()
