@@ -30,19 +30,60 @@ __device__ __forceinline__ float dot16(const uint4 w, const uint32_t (&xp)[8]) {
   return a + b;
 }
 
+// With `norm_w`, x is first normalised (RMSNorm: x / sqrt(mean(x^2) + eps)
+// times the weight, rounded to fp16, torch.nn.RMSNorm), computed by every
+// CTA for itself into shared memory; with `residual`, y = residual + W x in
+// one fp16 rounding (the decoder layer's x + attention(x)).
+template <bool NORM>
 __global__ void __launch_bounds__(GEMV_THREADS) fp8_gemv_kernel(const uint8_t* __restrict__ w,
                                                                  const float* __restrict__ row_scale, int64_t rows,
                                                                  const __half* __restrict__ x,
+                                                                 const __half* __restrict__ norm_w, float eps,
+                                                                 const __half* __restrict__ residual,
                                                                  __half* __restrict__ y) {
   const int lane = threadIdx.x & 31;
   const int64_t gw = (int64_t)blockIdx.x * (GEMV_THREADS / 32) + (threadIdx.x >> 5);
   const int64_t nw = (int64_t)gridDim.x * (GEMV_THREADS / 32);
+  const __half* xs = x;
+  if constexpr (NORM) {
+    __shared__ __align__(16) __half xn[GEMV_K];
+    __shared__ float red[GEMV_THREADS / 32];
+    constexpr int PER = GEMV_K / GEMV_THREADS;          // 16 elements a thread
+    const int t = threadIdx.x;
+    float v[PER];
+    float ss = 0.0f;
+    {
+      const uint4* src = reinterpret_cast<const uint4*>(x + PER * t);
+      const uint4 a = __ldg(src), b = __ldg(src + 1);
+      const uint32_t u[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+        ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[t >> 5] = ss;
+    __syncthreads();
+    ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < GEMV_THREADS / 32; ++k) ss += red[k];
+    const float rstd = rsqrtf(ss / (float)GEMV_K + eps);
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      xn[PER * t + i] = __float2half_rn(v[i] * rstd * __half2float(norm_w[PER * t + i]));
+    __syncthreads();
+    xs = xn;
+  }
   // x elements [512 s + 16 lane, +16) for s = 0..7, as f16 pairs
   uint32_t xp[STEPS][8];
 #pragma unroll
   for (int s = 0; s < STEPS; ++s) {
-    const uint4* src = reinterpret_cast<const uint4*>(x + 512 * s + 16 * lane);
-    const uint4 a = __ldg(src), b = __ldg(src + 1);
+    const uint4* src = reinterpret_cast<const uint4*>(xs + 512 * s + 16 * lane);
+    const uint4 a = NORM ? src[0] : __ldg(src), b = NORM ? src[1] : __ldg(src + 1);
     xp[s][0] = a.x; xp[s][1] = a.y; xp[s][2] = a.z; xp[s][3] = a.w;
     xp[s][4] = b.x; xp[s][5] = b.y; xp[s][6] = b.z; xp[s][7] = b.w;
   }
@@ -68,8 +109,14 @@ __global__ void __launch_bounds__(GEMV_THREADS) fp8_gemv_kernel(const uint8_t* _
       s1 += __shfl_xor_sync(0xffffffffu, s1, o);
     }
     if (lane == 0) {
-      y[r] = __float2half_rn(row_scale ? s0 * __ldg(row_scale + r) : s0);
-      if (two) y[r + 1] = __float2half_rn(row_scale ? s1 * __ldg(row_scale + r + 1) : s1);
+      float y0 = row_scale ? s0 * __ldg(row_scale + r) : s0;
+      if (residual) y0 += __half2float(residual[r]);
+      y[r] = __float2half_rn(y0);
+      if (two) {
+        float y1 = row_scale ? s1 * __ldg(row_scale + r + 1) : s1;
+        if (residual) y1 += __half2float(residual[r + 1]);
+        y[r + 1] = __float2half_rn(y1);
+      }
     }
   }
 }
@@ -78,12 +125,20 @@ __global__ void __launch_bounds__(GEMV_THREADS) fp8_gemv_kernel(const uint8_t* _
 
 using namespace hcg;
 
-extern "C" int hc_fp8_gemv(const uint8_t* w, const float* row_scale, int64_t rows, int32_t cols, const void* x,
-                           void* y, hc_stream_t stream) {
+extern "C" int hc_fp8_gemv_ex(const uint8_t* w, const float* row_scale, int64_t rows, int32_t cols, const void* x,
+                              const void* norm_w, float eps, const void* residual, void* y, hc_stream_t stream) {
   if (!w || !x || !y || rows <= 0 || cols != GEMV_K) return HC_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(x) & 15) ||
-      (reinterpret_cast<uintptr_t>(y) & 1))
+      (reinterpret_cast<uintptr_t>(y) & 1) || (reinterpret_cast<uintptr_t>(norm_w) & 1) ||
+      (reinterpret_cast<uintptr_t>(residual) & 1))
     return HC_ERR_ARG;
+  if (norm_w && !(eps >= 0.0f)) return HC_ERR_ARG;
+  // the residual is read after the products: it must not be overwritten by another row of y
+  if (residual && residual != y) {
+    const char* r0 = static_cast<const char*>(residual);
+    const char* y0 = static_cast<const char*>(y);
+    if (r0 < y0 + 2 * rows && y0 < r0 + 2 * rows) return HC_ERR_ARG;
+  }
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
@@ -92,7 +147,19 @@ extern "C" int hc_fp8_gemv(const uint8_t* w, const float* row_scale, int64_t row
   const int64_t warps_needed = (rows + 1) / 2;
   int64_t grid = (warps_needed + GEMV_THREADS / 32 - 1) / (GEMV_THREADS / 32);
   if (grid > 2LL * sms) grid = 2LL * sms;
-  fp8_gemv_kernel<<<(int)grid, GEMV_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      w, row_scale, rows, static_cast<const __half*>(x), static_cast<__half*>(y));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const __half* xh = static_cast<const __half*>(x);
+  const __half* rh = static_cast<const __half*>(residual);
+  __half* yh = static_cast<__half*>(y);
+  if (norm_w)
+    fp8_gemv_kernel<true><<<(int)grid, GEMV_THREADS, 0, s>>>(w, row_scale, rows, xh,
+                                                              static_cast<const __half*>(norm_w), eps, rh, yh);
+  else
+    fp8_gemv_kernel<false><<<(int)grid, GEMV_THREADS, 0, s>>>(w, row_scale, rows, xh, nullptr, 0.0f, rh, yh);
   return cudaGetLastError() == cudaSuccess ? HC_OK : HC_ERR_CUDA;
+}
+
+extern "C" int hc_fp8_gemv(const uint8_t* w, const float* row_scale, int64_t rows, int32_t cols, const void* x,
+                           void* y, hc_stream_t stream) {
+  return hc_fp8_gemv_ex(w, row_scale, rows, cols, x, nullptr, 0.0f, nullptr, y, stream);
 }

@@ -835,6 +835,12 @@ class GroupedQueryAttention(nn.Module):
             self.norm.weight = nn.Parameter(nw.to(dev).to(torch.float16))
         else:
             self.norm.to(torch.float16)
+        # one-token steps as three kernels: RMSNorm + q/k/v GEMV, RoPE + cache write +
+        # attention (hc_attn_decode), o GEMV + residual
+        self.fused_decode = (self.fp8_decode and self.head_dim == 128 and self.n_q % self.n_kv == 0
+                             and self.n_q // self.n_kv <= 8)
+        self._aws = None
+        self.status = N.new_status(dev)
 
     def forward(self, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, cache: KVCache,
                 start: Optional[int], pos: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -869,6 +875,32 @@ class GroupedQueryAttention(nn.Module):
             out = self._attend_one(q, kc, vc, (j <= pos).view(1, 1, 1, -1))
         out = out.transpose(1, 2).reshape(B, T, nq * D)
         return self._gemv(self.o_w8, out) if one else F.linear(out, self.o_weight)
+
+    def decode_residual(self, x: torch.Tensor, cos_t: torch.Tensor, sin_t: torch.Tensor, cache: KVCache,
+                        pos: torch.Tensor) -> torch.Tensor:
+        """x + attention(x) for one token x [1, 1, H] fp16 at the device
+        position ``pos`` (its k / v are written into the cache there), in three
+        launches: hc_fp8_gemv_ex (input_layernorm + q/k/v), hc_attn_decode
+        (RoPE, cache write, grouped-query attention), hc_fp8_gemv_ex (o +
+        residual).  ``cos_t`` / ``sin_t`` are the whole rotary tables."""
+        xv = x.reshape(-1).contiguous()
+        s = N.stream_handle()
+        if self._aws is None:
+            self._aws = torch.zeros(int(N.lib.hc_attn_decode_workspace_bytes(self.n_q, self.n_kv)),
+                                    dtype=torch.uint8, device=x.device)
+        qkv = torch.empty(self.qkv_w8.shape[0], dtype=torch.float16, device=x.device)
+        N.check(N.lib.hc_fp8_gemv_ex(N.ptr(self.qkv_w8), None, self.qkv_w8.shape[0], self.hidden, N.ptr(xv),
+                                     N.ptr(self.norm.weight.data), float(self.norm.eps), None, N.ptr(qkv), s),
+                "hc_fp8_gemv_ex")
+        att = torch.empty(self.n_q * self.head_dim, dtype=torch.float16, device=x.device)
+        kc, vc = cache.k[self.layer_idx], cache.v[self.layer_idx]
+        N.check(N.lib.hc_attn_decode(N.ptr(qkv), N.ptr(cos_t), N.ptr(sin_t), N.ptr(pos), N.ptr(kc), N.ptr(vc),
+                                     cache.capacity, self.n_q, self.n_kv, self.head_dim, N.ptr(att),
+                                     N.ptr(self._aws), N.ptr(self.status), s), "hc_attn_decode")
+        y = torch.empty(1, 1, self.hidden, dtype=torch.float16, device=x.device)
+        N.check(N.lib.hc_fp8_gemv_ex(N.ptr(self.o_w8), None, self.hidden, self.hidden, N.ptr(att), None, 0.0,
+                                     N.ptr(xv), N.ptr(y), s), "hc_fp8_gemv_ex")
+        return y
 
     def _attend_one(self, q, keys, vals, mask):
         """Softmax attention of one query position per head, the query heads
@@ -976,6 +1008,7 @@ class DesdemonaEngine(nn.Module):
         W = (cfg["intermediate_dim"] + 31) // 32
         self._words = torch.zeros(self.num_layers, 1, W, dtype=torch.int32, device=dev)   # fetch sets in flight
         self.fused_lookahead = True
+        self.fused_attention = True     # one-token steps: the three fused attention kernels
         self._graph = None
         self._graph_cache = None
 
@@ -999,8 +1032,14 @@ class DesdemonaEngine(nn.Module):
         words = self._words
         one = x.shape[0] * x.shape[1] == 1 and self.fused_lookahead
         f[0].submit_cold_fetch(x, out=words[0])             # layer 0's set, on the embedding (engine.py:422)
+        fused = x.shape[0] * x.shape[1] == 1 and self.fused_attention
+        dpos = pos if pos is not None else cache.pos      # eager one-token steps: cache.pos == start
         for li in range(self.num_layers):
-            x = x + self.attention_layers[li](x, cos, sin, cache, start, pos)
+            att = self.attention_layers[li]
+            if fused and att.fused_decode:
+                x = att.decode_residual(x, self.cos_cache, self.sin_cache, cache, dpos)
+            else:
+                x = x + att(x, cos, sin, cache, start, pos)
             if li + 1 < self.num_layers:
                 if one:
                     # one token: this layer's kernel also predicts the next layer's set
@@ -1117,6 +1156,8 @@ class DesdemonaEngine(nn.Module):
     def check(self):
         for f in self.ffn_layers:
             f.check()
+        for a in self.attention_layers:
+            N.read_status(a.status, "hc_attn_decode")
 
     def close(self):
         self._graph = None

@@ -23,7 +23,7 @@ HC_ERR_UNSUPPORTED = 16
 
 HC_F32, HC_BF16, HC_F16 = 0, 1, 2
 HC_ACT_SILU, HC_ACT_RELU = 0, 1
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 TABLE_SIZE = 65536
 
@@ -88,6 +88,9 @@ _SIGS = {
     "hc_batch_pack_bytes": (c_i64, [c_i32, c_i32]),
     "hc_batch_pack": (c_i32, [c_p, c_p, c_p]),
     "hc_fp8_gemv": (c_i32, [c_p, c_p, c_i64, c_i32, c_p, c_p, c_p]),
+    "hc_fp8_gemv_ex": (c_i32, [c_p, c_p, c_i64, c_i32, c_p, c_p, ctypes.c_float, c_p, c_p, c_p]),
+    "hc_attn_decode_workspace_bytes": (c_i64, [c_i32, c_i32]),
+    "hc_attn_decode": (c_i32, [c_p, c_p, c_p, c_p, c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_p, c_p, c_p, c_p]),
     "hc_xchg_buffer_bytes": (c_i64, [c_i32, c_i64]),
     "hc_xchg_sum": (c_i32, [c_p, c_i64, c_p, c_i64, c_p, c_p, c_p]),
 }

@@ -55,7 +55,7 @@ typedef struct CUstream_st* hc_stream_t; /* == cudaStream_t */
 #define HC_ACT_RELU 1
 
 /* Library identity / device checks.  hc_version returns HC_ABI_VERSION. */
-#define HC_ABI_VERSION 2
+#define HC_ABI_VERSION 3
 HC_API int hc_version(void);
 HC_API const char* hc_status_string(int status);
 /* Number of SMs of the current device, or -1 when no CUDA device is usable. */
@@ -462,6 +462,45 @@ HC_API int hc_xchg_sum(const float* part, int64_t n, float* out, int64_t max_flo
  */
 HC_API int hc_fp8_gemv(const uint8_t* w, const float* row_scale, int64_t rows, int32_t cols, const void* x,
                        void* y, hc_stream_t stream);
+
+/*
+ * hc_fp8_gemv_ex -- hc_fp8_gemv with the decoder layer's neighbours fused:
+ *   norm_w     optional [cols] fp16: x is first RMS-normalised,
+ *              fp16(x / sqrt(mean(x^2) + eps) * norm_w) (the layer's
+ *              input_layernorm, engine.py:98-100); NULL = x as given
+ *   residual   optional [rows] fp16: y = residual + W x with one rounding (the
+ *              decoder layer's x + attention(x), engine.py:421-429); may be y
+ *              itself, must not otherwise overlap y
+ */
+HC_API int hc_fp8_gemv_ex(const uint8_t* w, const float* row_scale, int64_t rows, int32_t cols, const void* x,
+                          const void* norm_w, float eps, const void* residual, void* y, hc_stream_t stream);
+
+/*
+ * hc_attn_decode -- one token's grouped-query attention of one layer
+ * (LlamaAttention.forward for T = 1, engine.py:100-125, rotary embedding
+ * engine.py:130-158): RoPE on q and k at position *pos, k / v written into the
+ * cache at *pos, causal softmax attention of every query head over cache
+ * positions 0..*pos of its key-value head (query head h reads key-value head
+ * h / (n_q_heads / n_kv_heads)), out = softmax(q k^T / sqrt(d)) v.
+ *   qkv        [(n_q_heads + 2 n_kv_heads) head_dim] fp16: q, k, v before RoPE
+ *   cos_t/sin_t [capacity][head_dim / 2] fp32 rotary tables (angle pos x
+ *              theta^(-i / (head_dim / 2)))
+ *   pos        device int64 scalar (read by the kernel, so a captured graph
+ *              replays the step); *pos outside [0, capacity) -> HC_ERR_RANGE
+ *              in *status and nothing is written
+ *   k_cache / v_cache  this layer's [n_kv_heads][capacity][head_dim] fp16
+ *   out        [n_q_heads head_dim] fp16
+ *   workspace  hc_attn_decode_workspace_bytes(n_q_heads, n_kv_heads) bytes,
+ *              zeroed once; the kernel leaves its counters zeroed
+ * head_dim must be 128 and n_q_heads / n_kv_heads <= 8.  The sequence is
+ * split over 16 CTAs per key-value head; each CTA's partial softmax is
+ * combined by the last CTA of its head (an atomic counter, no waiting), in
+ * fp32.  Launches on one workspace must not overlap.
+ */
+HC_API int64_t hc_attn_decode_workspace_bytes(int32_t n_q_heads, int32_t n_kv_heads);
+HC_API int hc_attn_decode(const void* qkv, const float* cos_t, const float* sin_t, const int64_t* pos,
+                          void* k_cache, void* v_cache, int32_t capacity, int32_t n_q_heads, int32_t n_kv_heads,
+                          int32_t head_dim, void* out, void* workspace, int32_t* status, hc_stream_t stream);
 
 #ifdef __cplusplus
 }
