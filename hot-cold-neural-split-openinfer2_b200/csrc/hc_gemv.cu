@@ -30,12 +30,13 @@ __device__ __forceinline__ float dot16(const uint4 w, const uint32_t (&xp)[8]) {
   return a + b;
 }
 
-// With `norm_w`, x is first normalised (RMSNorm: x / sqrt(mean(x^2) + eps)
-// times the weight, rounded to fp16, torch.nn.RMSNorm), computed by every
-// CTA for itself into shared memory; with `residual`, y = residual + W x in
-// one fp16 rounding (the decoder layer's x + attention(x)).
+// With `norm_w`, x is RMS-normalised first (torch.nn.RMSNorm: x / sqrt(mean(x^2)
+// + eps) times the weight): every warp loads all of x anyway, so it sums the
+// squares itself (no block synchronisation) and uses f16(x * w) as the
+// operand, applying the scalar 1 / rms to its fp32 sums.  With `residual`,
+// y = residual + W x in one fp16 rounding (the decoder layer's x + attention(x)).
 template <bool NORM>
-__global__ void __launch_bounds__(GEMV_THREADS) fp8_gemv_kernel(const uint8_t* __restrict__ w,
+__global__ void __launch_bounds__(GEMV_THREADS, 2) fp8_gemv_kernel(const uint8_t* __restrict__ w,
                                                                  const float* __restrict__ row_scale, int64_t rows,
                                                                  const __half* __restrict__ x,
                                                                  const __half* __restrict__ norm_w, float eps,
@@ -44,48 +45,34 @@ __global__ void __launch_bounds__(GEMV_THREADS) fp8_gemv_kernel(const uint8_t* _
   const int lane = threadIdx.x & 31;
   const int64_t gw = (int64_t)blockIdx.x * (GEMV_THREADS / 32) + (threadIdx.x >> 5);
   const int64_t nw = (int64_t)gridDim.x * (GEMV_THREADS / 32);
-  const __half* xs = x;
-  if constexpr (NORM) {
-    __shared__ __align__(16) __half xn[GEMV_K];
-    __shared__ float red[GEMV_THREADS / 32];
-    constexpr int PER = GEMV_K / GEMV_THREADS;          // 16 elements a thread
-    const int t = threadIdx.x;
-    float v[PER];
-    float ss = 0.0f;
-    {
-      const uint4* src = reinterpret_cast<const uint4*>(x + PER * t);
-      const uint4 a = __ldg(src), b = __ldg(src + 1);
-      const uint32_t u[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
-        v[2 * i] = f.x;
-        v[2 * i + 1] = f.y;
-        ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
-      }
-    }
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) red[t >> 5] = ss;
-    __syncthreads();
-    ss = 0.0f;
-#pragma unroll
-    for (int k = 0; k < GEMV_THREADS / 32; ++k) ss += red[k];
-    const float rstd = rsqrtf(ss / (float)GEMV_K + eps);
-#pragma unroll
-    for (int i = 0; i < PER; ++i)
-      xn[PER * t + i] = __float2half_rn(v[i] * rstd * __half2float(norm_w[PER * t + i]));
-    __syncthreads();
-    xs = xn;
-  }
   // x elements [512 s + 16 lane, +16) for s = 0..7, as f16 pairs
   uint32_t xp[STEPS][8];
+  float ss = 0.0f;
 #pragma unroll
   for (int s = 0; s < STEPS; ++s) {
-    const uint4* src = reinterpret_cast<const uint4*>(xs + 512 * s + 16 * lane);
-    const uint4 a = NORM ? src[0] : __ldg(src), b = NORM ? src[1] : __ldg(src + 1);
+    const uint4* src = reinterpret_cast<const uint4*>(x + 512 * s + 16 * lane);
+    const uint4 a = __ldg(src), b = __ldg(src + 1);
     xp[s][0] = a.x; xp[s][1] = a.y; xp[s][2] = a.z; xp[s][3] = a.w;
     xp[s][4] = b.x; xp[s][5] = b.y; xp[s][6] = b.z; xp[s][7] = b.w;
+    if constexpr (NORM) {
+      const uint4* wsrc = reinterpret_cast<const uint4*>(norm_w + 512 * s + 16 * lane);
+      const uint4 c = __ldg(wsrc), d = __ldg(wsrc + 1);
+      const uint32_t wv[8] = {c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float2 xf = __half22float2(*reinterpret_cast<const __half2*>(&xp[s][i]));
+        const float2 wf = __half22float2(*reinterpret_cast<const __half2*>(&wv[i]));
+        ss = fmaf(xf.x, xf.x, fmaf(xf.y, xf.y, ss));
+        const __half2 z = __floats2half2_rn(xf.x * wf.x, xf.y * wf.y);
+        xp[s][i] = *reinterpret_cast<const uint32_t*>(&z);
+      }
+    }
+  }
+  float rstd = 1.0f;
+  if constexpr (NORM) {
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    rstd = rsqrtf(ss / (float)GEMV_K + eps);
   }
   for (int64_t r = gw * 2; r < rows; r += nw * 2) {
     const bool two = r + 1 < rows;
@@ -109,11 +96,11 @@ __global__ void __launch_bounds__(GEMV_THREADS) fp8_gemv_kernel(const uint8_t* _
       s1 += __shfl_xor_sync(0xffffffffu, s1, o);
     }
     if (lane == 0) {
-      float y0 = row_scale ? s0 * __ldg(row_scale + r) : s0;
+      float y0 = (row_scale ? s0 * __ldg(row_scale + r) : s0) * rstd;
       if (residual) y0 += __half2float(residual[r]);
       y[r] = __float2half_rn(y0);
       if (two) {
-        float y1 = row_scale ? s1 * __ldg(row_scale + r + 1) : s1;
+        float y1 = (row_scale ? s1 * __ldg(row_scale + r + 1) : s1) * rstd;
         if (residual) y1 += __half2float(residual[r + 1]);
         y[r + 1] = __float2half_rn(y1);
       }
@@ -129,7 +116,7 @@ extern "C" int hc_fp8_gemv_ex(const uint8_t* w, const float* row_scale, int64_t 
                               const void* norm_w, float eps, const void* residual, void* y, hc_stream_t stream) {
   if (!w || !x || !y || rows <= 0 || cols != GEMV_K) return HC_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(x) & 15) ||
-      (reinterpret_cast<uintptr_t>(y) & 1) || (reinterpret_cast<uintptr_t>(norm_w) & 1) ||
+      (reinterpret_cast<uintptr_t>(y) & 1) || (reinterpret_cast<uintptr_t>(norm_w) & 15) ||
       (reinterpret_cast<uintptr_t>(residual) & 1))
     return HC_ERR_ARG;
   if (norm_w && !(eps >= 0.0f)) return HC_ERR_ARG;

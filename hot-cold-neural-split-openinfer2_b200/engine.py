@@ -839,7 +839,6 @@ class GroupedQueryAttention(nn.Module):
         # attention (hc_attn_decode), o GEMV + residual
         self.fused_decode = (self.fp8_decode and self.head_dim == 128 and self.n_q % self.n_kv == 0
                              and self.n_q // self.n_kv <= 8)
-        self._aws = None
         self.status = N.new_status(dev)
 
     def forward(self, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, cache: KVCache,
@@ -885,9 +884,6 @@ class GroupedQueryAttention(nn.Module):
         residual).  ``cos_t`` / ``sin_t`` are the whole rotary tables."""
         xv = x.reshape(-1).contiguous()
         s = N.stream_handle()
-        if self._aws is None:
-            self._aws = torch.zeros(int(N.lib.hc_attn_decode_workspace_bytes(self.n_q, self.n_kv)),
-                                    dtype=torch.uint8, device=x.device)
         qkv = torch.empty(self.qkv_w8.shape[0], dtype=torch.float16, device=x.device)
         N.check(N.lib.hc_fp8_gemv_ex(N.ptr(self.qkv_w8), None, self.qkv_w8.shape[0], self.hidden, N.ptr(xv),
                                      N.ptr(self.norm.weight.data), float(self.norm.eps), None, N.ptr(qkv), s),
@@ -896,7 +892,7 @@ class GroupedQueryAttention(nn.Module):
         kc, vc = cache.k[self.layer_idx], cache.v[self.layer_idx]
         N.check(N.lib.hc_attn_decode(N.ptr(qkv), N.ptr(cos_t), N.ptr(sin_t), N.ptr(pos), N.ptr(kc), N.ptr(vc),
                                      cache.capacity, self.n_q, self.n_kv, self.head_dim, N.ptr(att),
-                                     N.ptr(self._aws), N.ptr(self.status), s), "hc_attn_decode")
+                                     N.ptr(self.status), s), "hc_attn_decode")
         y = torch.empty(1, 1, self.hidden, dtype=torch.float16, device=x.device)
         N.check(N.lib.hc_fp8_gemv_ex(N.ptr(self.o_w8), None, self.hidden, self.hidden, N.ptr(att), None, 0.0,
                                      N.ptr(xv), N.ptr(y), s), "hc_fp8_gemv_ex")

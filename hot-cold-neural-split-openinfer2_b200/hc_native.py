@@ -89,8 +89,7 @@ _SIGS = {
     "hc_batch_pack": (c_i32, [c_p, c_p, c_p]),
     "hc_fp8_gemv": (c_i32, [c_p, c_p, c_i64, c_i32, c_p, c_p, c_p]),
     "hc_fp8_gemv_ex": (c_i32, [c_p, c_p, c_i64, c_i32, c_p, c_p, ctypes.c_float, c_p, c_p, c_p]),
-    "hc_attn_decode_workspace_bytes": (c_i64, [c_i32, c_i32]),
-    "hc_attn_decode": (c_i32, [c_p, c_p, c_p, c_p, c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_p, c_p, c_p, c_p]),
+    "hc_attn_decode": (c_i32, [c_p, c_p, c_p, c_p, c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_p, c_p, c_p]),
     "hc_xchg_buffer_bytes": (c_i64, [c_i32, c_i64]),
     "hc_xchg_sum": (c_i32, [c_p, c_i64, c_p, c_i64, c_p, c_p, c_p]),
 }

@@ -465,9 +465,10 @@ HC_API int hc_fp8_gemv(const uint8_t* w, const float* row_scale, int64_t rows, i
 
 /*
  * hc_fp8_gemv_ex -- hc_fp8_gemv with the decoder layer's neighbours fused:
- *   norm_w     optional [cols] fp16: x is first RMS-normalised,
- *              fp16(x / sqrt(mean(x^2) + eps) * norm_w) (the layer's
- *              input_layernorm, engine.py:98-100); NULL = x as given
+ *   norm_w     optional [cols] fp16 (16-byte aligned): x is first RMS-normalised
+ *              (the layer's input_layernorm, engine.py:98-100): the products
+ *              use fp16(x * norm_w) and the fp32 sums are scaled by
+ *              1 / sqrt(mean(x^2) + eps); NULL = x as given
  *   residual   optional [rows] fp16: y = residual + W x with one rounding (the
  *              decoder layer's x + attention(x), engine.py:421-429); may be y
  *              itself, must not otherwise overlap y
@@ -490,17 +491,14 @@ HC_API int hc_fp8_gemv_ex(const uint8_t* w, const float* row_scale, int64_t rows
  *              in *status and nothing is written
  *   k_cache / v_cache  this layer's [n_kv_heads][capacity][head_dim] fp16
  *   out        [n_q_heads head_dim] fp16
- *   workspace  hc_attn_decode_workspace_bytes(n_q_heads, n_kv_heads) bytes,
- *              zeroed once; the kernel leaves its counters zeroed
- * head_dim must be 128 and n_q_heads / n_kv_heads <= 8.  The sequence is
- * split over 16 CTAs per key-value head; each CTA's partial softmax is
- * combined by the last CTA of its head (an atomic counter, no waiting), in
- * fp32.  Launches on one workspace must not overlap.
+ * head_dim must be 128 and n_q_heads / n_kv_heads <= 8.  One cluster of 8
+ * CTAs per key-value head splits the sequence; the CTAs' partial softmaxes
+ * (fp32) are combined through distributed shared memory after a cluster
+ * barrier.  No workspace; launches on one cache must not overlap.
  */
-HC_API int64_t hc_attn_decode_workspace_bytes(int32_t n_q_heads, int32_t n_kv_heads);
 HC_API int hc_attn_decode(const void* qkv, const float* cos_t, const float* sin_t, const int64_t* pos,
                           void* k_cache, void* v_cache, int32_t capacity, int32_t n_q_heads, int32_t n_kv_heads,
-                          int32_t head_dim, void* out, void* workspace, int32_t* status, hc_stream_t stream);
+                          int32_t head_dim, void* out, int32_t* status, hc_stream_t stream);
 
 #ifdef __cplusplus
 }
