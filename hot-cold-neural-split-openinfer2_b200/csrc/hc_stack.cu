@@ -1085,26 +1085,47 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
           if (!pr.ok) break;
           __threadfence();
         }
-        // Once every CTA has published its list, this CTA streams its static
-        // share of the layer: pool entries [c n / G, (c+1) n / G) (cold records),
-        // then hot neurons [c n_hot / G, (c+1) n_hot / G), two per group.  Equal
-        // shares of both kinds give every SM the same bytes, so the layer's CTAs
-        // finish together (no claims, no counter round trips).
-        {
-          const uint64_t t0 = globaltimer_ns();
-          uint32_t i = 0;
-          while (ld_acquire_u32(p.gdone + l % NACC) < (uint32_t)G) {
-            if ((++i & 63) == 0 && globaltimer_ns() - t0 > p.wait_ns) {
-              pr.ok = false;
-              break;
-            }
-            __nanosleep(64);
+        // This CTA streams its static share of the layer: pool entries
+        // [c n / G, (c+1) n / G) of the layer's cold-record pool (once every CTA
+        // has published its list) and hot neurons [c n_hot / G, (c+1) n_hot / G),
+        // two per group.  Equal shares of both kinds give every SM the same
+        // bytes, so the layer's CTAs finish together (no claims, no counter
+        // round trips).  Cold first (the costlier groups early, so the subgroups'
+        // claims even out the end of the layer), except at a launch's first
+        // layer, whose pool the planners are still building: its hot groups,
+        // which need nothing, stream meanwhile.
+        uint64_t claimed = 0, cold_taken = 0;
+        auto issue_hot = [&]() {
+          trace_ev(p, l, 13);
+          const int64_t hA = split_lo(d.n_hot, c, G), hB = split_lo(d.n_hot, c + 1, G);
+          const int64_t hsz = (hB - hA >= 8) ? NB_HOT : 1;     // single neurons when the CTA has few
+          for (int64_t i = hA; pr.ok && i < hB; i += hsz) {
+            const int n = (int)min(hsz, hB - i);
+            Copy cp[2];
+#pragma unroll
+            for (int k = 0; k < 2; ++k)
+              cp[k] = {k < n ? d.hot + (i + k) * HOT_BYTES : nullptr, k < n ? (uint32_t)HOT_BYTES : 0u,
+                       (uint32_t)(k * HALF_BYTES)};
+            issue_entry(sm, ring, pr, l, UNIT_HOT, n, i, cp, iwp, p.wait_ns);
+            ++ng;
+            claimed += n;
           }
-          if (!pr.ok) break;
-        }
-        trace_ev(p, l, 11);
-        uint64_t cold_taken = 0;
-        {
+          trace_ev(p, l, 37);
+        };
+        auto issue_cold = [&]() {
+          {
+            const uint64_t t0 = globaltimer_ns();
+            uint32_t i = 0;
+            while (ld_acquire_u32(p.gdone + l % NACC) < (uint32_t)G) {
+              if ((++i & 63) == 0 && globaltimer_ns() - t0 > p.wait_ns) {
+                pr.ok = false;
+                break;
+              }
+              __nanosleep(64);
+            }
+            if (!pr.ok) return;
+          }
+          trace_ev(p, l, 11);
           const uint32_t total = __ldcg(p.gfill + l % NACC);
           const int32_t* pool = p.gpool + (size_t)(l % NACC) * POOL_CAP;
           const uint32_t i0 = (uint32_t)split_lo(total, c, G), i1 = (uint32_t)split_lo(total, c + 1, G);
@@ -1126,23 +1147,14 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
             ++ng;
             cold_taken += m;
           }
-        }
-        if (!pr.ok) break;
-        trace_ev(p, l, 12);
-        trace_ev(p, l, 13);
-        uint64_t claimed = 0;
-        const int64_t hA = split_lo(d.n_hot, c, G), hB = split_lo(d.n_hot, c + 1, G);
-        const int64_t hsz = (hB - hA >= 8) ? NB_HOT : 1;     // single neurons when the CTA has few
-        for (int64_t i = hA; pr.ok && i < hB; i += hsz) {
-          const int n = (int)min(hsz, hB - i);
-          Copy cp[2];
-#pragma unroll
-          for (int k = 0; k < 2; ++k)
-            cp[k] = {k < n ? d.hot + (i + k) * HOT_BYTES : nullptr, k < n ? (uint32_t)HOT_BYTES : 0u,
-                     (uint32_t)(k * HALF_BYTES)};
-          issue_entry(sm, ring, pr, l, UNIT_HOT, n, i, cp, iwp, p.wait_ns);
-          ++ng;
-          claimed += n;
+          trace_ev(p, l, 12);
+        };
+        if (l == 0) {
+          issue_hot();
+          if (pr.ok) issue_cold();
+        } else {
+          issue_cold();
+          if (pr.ok) issue_hot();
         }
         if (!pr.ok) break;
         sm.ngroups[l & 3] = ng;

@@ -303,9 +303,11 @@ class FFNStack:
                 put("barrier.after_own_arrival_to_last", last - us[:-1, :, 8])
                 put("barrier.last_arrival_to_seen", us[:-1, :, 32] - last)
                 put("barrier.seen_to_layer_start", us[1:, :, 0] - us[:-1, :, 32])
-        put("issue_wait_pool", us[:, :, 11] - us[:, :, 10])
-        put("issue_cold", us[:, :, 12] - us[:, :, 11])
-        put("issue_hot", us[:, :, 14] - us[:, :, 13])
+        # layers after the first: the cold pool, its groups, then the hot groups
+        # (layer 0: hot groups first); stamps 13/37 hot start/end, 11 pool, 12 cold end
+        put("issue_wait_pool", us[1:, :, 11] - us[1:, :, 10])
+        put("issue_cold", us[1:, :, 12] - us[1:, :, 11])
+        put("issue_hot", us[:, :, 37] - us[:, :, 13])
         for name, ev in (("own_words_after_start", 21), ("planner_wake_after_start", 22),
                          ("plan_ready_after_start", 20)):
             stamped = t[:, :, ev] > 0                  # layers where the event happened
