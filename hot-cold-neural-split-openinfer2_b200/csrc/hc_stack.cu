@@ -140,10 +140,11 @@ struct StackParams {
   int tp_size, tp_rank;      // GPUs sharing each layer's neurons, this GPU's index
   void* const* peer_buf;     // [tp_size] every GPU's exchange buffer (device pointers)
   uint32_t seq_base;         // launches so far x n_layers, identical on every GPU
-  const float* x_in;
+  const void* x_in;          // [H] fp32, or fp16 with io_f16
   uint32_t* masks;           // [n_layers][words]
   int masks_given;
-  float* x_out;
+  void* x_out;               // [H] fp32, or fp16 with io_f16
+  int io_f16;
   float* x_hist;
   float eps;
   int relu;
@@ -982,7 +983,9 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
       uint32_t own = 0;
       if (ok)
         ok = wdown(d0l, 0, d0, d1, [&](int r) {
-          return __ldg(p.x_in + r) * rstd0 * (d0l.norm_w ? __ldg(d0l.norm_w + r) : 1.0f);
+          const float xr = p.io_f16 ? __half2float(__ldg(static_cast<const __half*>(p.x_in) + r))
+                                    : __ldg(static_cast<const float*>(p.x_in) + r);
+          return xr * rstd0 * (d0l.norm_w ? __ldg(d0l.norm_w + r) : 1.0f);
         });
       if (ok) wdown_count(0, d0, d1);
       preload(0);
@@ -1214,9 +1217,20 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
       // ---- layer boundary: x_l = x_{l-1} + y_{l-1} once every CTA has added its part
       float x[EPT];
       if (l == 0) {
-        const float4* src = reinterpret_cast<const float4*>(p.x_in + EPT * t);
-        const float4 q0 = __ldg(src), q1 = __ldg(src + 1);
-        x[0] = q0.x; x[1] = q0.y; x[2] = q0.z; x[3] = q0.w; x[4] = q1.x; x[5] = q1.y; x[6] = q1.z; x[7] = q1.w;
+        if (p.io_f16) {
+          const uint4 q = __ldg(reinterpret_cast<const uint4*>(static_cast<const __half*>(p.x_in) + EPT * t));
+          const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&qw[i]));
+            x[2 * i] = f.x;
+            x[2 * i + 1] = f.y;
+          }
+        } else {
+          const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.x_in) + EPT * t);
+          const float4 q0 = __ldg(src), q1 = __ldg(src + 1);
+          x[0] = q0.x; x[1] = q0.y; x[2] = q0.z; x[3] = q0.w; x[4] = q1.x; x[5] = q1.y; x[6] = q1.z; x[7] = q1.w;
+        }
       } else {
         ok = layer_wait(sm, p, l - 1);
         if (!ok) break;
@@ -1508,9 +1522,20 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
       if (ok && c == 0) {
         const float4 o0 = make_float4(xo[0], xo[1], xo[2], xo[3]);
         const float4 o1 = make_float4(xo[4], xo[5], xo[6], xo[7]);
-        float4* out = reinterpret_cast<float4*>(p.x_out + EPT * t);
-        out[0] = o0;
-        out[1] = o1;
+        if (p.io_f16) {
+          const __half2 h0 = __floats2half2_rn(xo[0], xo[1]), h1 = __floats2half2_rn(xo[2], xo[3]);
+          const __half2 h2 = __floats2half2_rn(xo[4], xo[5]), h3 = __floats2half2_rn(xo[6], xo[7]);
+          uint4 q;
+          q.x = *reinterpret_cast<const uint32_t*>(&h0);
+          q.y = *reinterpret_cast<const uint32_t*>(&h1);
+          q.z = *reinterpret_cast<const uint32_t*>(&h2);
+          q.w = *reinterpret_cast<const uint32_t*>(&h3);
+          *reinterpret_cast<uint4*>(static_cast<__half*>(p.x_out) + EPT * t) = q;
+        } else {
+          float4* out = reinterpret_cast<float4*>(static_cast<float*>(p.x_out) + EPT * t);
+          out[0] = o0;
+          out[1] = o1;
+        }
         if (p.x_hist) {
           float4* h = reinterpret_cast<float4*>(p.x_hist + (size_t)(L - 1) * H + EPT * t);
           h[0] = o0;
@@ -1569,8 +1594,8 @@ extern "C" int64_t hc_tp_buffer_bytes(int32_t tp_size) {
   return (int64_t)(XCHG_HDR + sizeof(unsigned long long) * (size_t)NACC * tp_size * H);
 }
 
-extern "C" int hc_ffn_stack_tp(const hc_layer_desc* layers, int32_t n_layers, int32_t inter, const float* x_in,
-                               uint32_t* masks, int32_t masks_given, float* x_out, float* x_hist, float eps,
+extern "C" int hc_ffn_stack_tp(const hc_layer_desc* layers, int32_t n_layers, int32_t inter, const void* x_in,
+                               uint32_t* masks, int32_t masks_given, void* x_out, float* x_hist, float eps,
                                int32_t act, int32_t act_on_both, float logit_threshold, int32_t grid,
                                void* workspace, int32_t* status, uint64_t* trace, const hc_tp_desc* tp,
                                hc_stream_t stream) {
@@ -1624,6 +1649,7 @@ extern "C" int hc_ffn_stack_tp(const hc_layer_desc* layers, int32_t n_layers, in
   p.masks_given = masks_given == 1;
   p.pred0 = masks_given == 2;
   p.x_out = x_out;
+  p.io_f16 = (tp && tp->io_f16) ? 1 : 0;
   p.x_hist = x_hist;
   p.eps = eps;
   p.relu = act == HC_ACT_RELU;

@@ -233,7 +233,7 @@ class FFNStack:
 
     def launch(self, x: torch.Tensor, masks_given=False, x_hist: Optional[torch.Tensor] = None,
                out: Optional[torch.Tensor] = None, trace: Optional[torch.Tensor] = None,
-               predict_last: bool = False) -> torch.Tensor:
+               predict_last: bool = False, io_f16: bool = False) -> torch.Tensor:
         """One hc_ffn_stack launch.  ``masks_given``: False (row 0 of
         ``self.masks`` holds layer 0's set), True (every row given) or 2 (the
         kernel predicts layer 0 too).  ``predict_last``: the last layer is
@@ -247,11 +247,12 @@ class FFNStack:
                           peer_buf=N.ptr(self.tp.peer_buf), seq_base=self.tp.seq & 0xFFFFFFFF,
                           wait_ns=self.wait_ns)
             self.tp.seq += self.L - (1 if predict_last else 0)
-        elif self.wait_ns or predict_last:
+        elif self.wait_ns or predict_last or io_f16:
             tp = N.TPDesc(size=1, rank=0, words_lo=0, words_n=self.words, peer_buf=None, seq_base=0,
                           wait_ns=self.wait_ns)
         if tp is not None:
             tp.predict_last = 1 if predict_last else 0
+            tp.io_f16 = 1 if io_f16 else 0
         mg = 2 if masks_given == 2 else (1 if masks_given else 0)
         N.check(N.lib.hc_ffn_stack_tp(N.ptr(self.desc_dev), self.L, self.inter, N.ptr(x), N.ptr(self.masks),
                                       mg, N.ptr(out), N.ptr(x_hist), self.eps, self.act,
@@ -732,6 +733,12 @@ class SparseFFNLayer(nn.Module):
             raise ValueError("words and next_words must be consecutive rows of one buffer")
         st.masks = words.view(-1).as_strided((2, st.words), (st.words, 1))
         B, T, H = x.shape
+        if x.dtype == torch.float16:
+            # fp16 hidden state in and out of the kernel (it computes in fp32)
+            row = x.reshape(H).contiguous()
+            out = torch.empty_like(row)
+            st.launch(row, masks_given=False, out=out, predict_last=True, io_f16=True)
+            return out.view(B, T, H)
         rows = x.reshape(B * T, H).to(torch.float32).contiguous()
         out = torch.empty_like(rows)
         st.launch(rows[0], masks_given=False, out=out[0], predict_last=True)

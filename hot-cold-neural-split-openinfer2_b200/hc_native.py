@@ -99,7 +99,8 @@ class TPDesc(ctypes.Structure):
     """Mirror of hc_tp_desc (include/hotcold.h)."""
     _fields_ = [("size", ctypes.c_int32), ("rank", ctypes.c_int32), ("words_lo", ctypes.c_int32),
                 ("words_n", ctypes.c_int32), ("peer_buf", ctypes.c_void_p), ("seq_base", ctypes.c_uint32),
-                ("wait_ns", ctypes.c_uint64), ("predict_last", ctypes.c_int32)]
+                ("wait_ns", ctypes.c_uint64), ("predict_last", ctypes.c_int32),
+                ("io_f16", ctypes.c_int32)]
 
 
 def _load():

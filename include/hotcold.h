@@ -317,12 +317,16 @@ typedef struct hc_tp_desc {
    * [layer l, layer l+1] computes layer l and predicts layer l+1's set.
    * Needs n_layers >= 2 and masks_given 0 or 2. */
   int32_t predict_last;
+  /* 1: x_in and x_out are fp16 [4096] (16-byte aligned) instead of fp32 -- the
+   * engine's fp16 hidden state handed over without conversions; the layers
+   * still compute in fp32 and x_hist stays fp32. */
+  int32_t io_f16;
 } hc_tp_desc;
 
 HC_API int64_t hc_tp_buffer_bytes(int32_t tp_size);
 /* tp == NULL is hc_ffn_stack. */
-HC_API int hc_ffn_stack_tp(const hc_layer_desc* layers, int32_t n_layers, int32_t inter, const float* x_in,
-                    uint32_t* masks, int32_t masks_given, float* x_out, float* x_hist, float eps,
+HC_API int hc_ffn_stack_tp(const hc_layer_desc* layers, int32_t n_layers, int32_t inter, const void* x_in,
+                    uint32_t* masks, int32_t masks_given, void* x_out, float* x_hist, float eps,
                     int32_t act, int32_t act_on_both, float logit_threshold, int32_t grid,
                     void* workspace, int32_t* status, uint64_t* trace, const hc_tp_desc* tp,
                     hc_stream_t stream);

@@ -337,3 +337,15 @@ def test_stack_predict_last_layer_only(M):
                                          norm_w=syn.norms[1].cpu().numpy(), eps=syn.eps)
     got = O.mask_from_words(st.masks[1].cpu().numpy(), 2048)
     assert np.array_equal(got[~amb], exact[~amb]) and got.sum() > 100
+    # the same launch with fp16 input and output (the engine's hidden state): the same
+    # fetch set predicted, the output the fp32 one rounded to fp16 (within its rounding)
+    m1 = st.masks[1].clone()
+    st.masks[1].zero_()
+    x16 = x0.half()
+    out16 = torch.empty(4096, dtype=torch.float16, device="cuda")
+    st.launch(x16, False, None, out16, predict_last=True, io_f16=True)
+    st.launch(x16.float(), False, None, out, predict_last=True)
+    st.check()
+    rel = ((out16.float() - out).norm() / out.norm()).item()
+    assert rel < 1e-3, rel
+    assert int((st.masks[1] ^ m1).ne(0).sum()) <= 2      # x0 vs its fp16 rounding: logits on the threshold may flip

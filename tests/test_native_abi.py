@@ -139,6 +139,6 @@ def test_tensor_parallel_host_pieces():
         assert all(got[i][1] == got[i + 1][0] for i in range(size - 1))
     # hc_tp_desc layout: 4 int32, a pointer, a uint32, a uint64 wait limit, an int32 flag
     assert ctypes.sizeof(N.TPDesc) == 48 and N.TPDesc.peer_buf.offset == 16 and N.TPDesc.seq_base.offset == 24
-    assert N.TPDesc.wait_ns.offset == 32 and N.TPDesc.predict_last.offset == 40
+    assert N.TPDesc.wait_ns.offset == 32 and N.TPDesc.predict_last.offset == 40 and N.TPDesc.io_f16.offset == 44
     assert N.lib.hc_tp_buffer_bytes(8) == 256 + 3 * 8 * 4096 * 8      # (seq, value) words
     assert N.lib.hc_tp_buffer_bytes(0) == -1 and N.lib.hc_tp_buffer_bytes(9) == -1
