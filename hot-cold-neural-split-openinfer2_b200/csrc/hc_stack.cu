@@ -100,8 +100,8 @@ struct SlotInfo {
 
 struct StackSmem {
   alignas(128) uint8_t pbuf[PBUF_BYTES];   // planner: one predictor tile (W_down or W_up + bias)
-  __half xh[H];                     // RMSNorm_l(x) as f16 (hot neurons); with xq, a y stage later
-  uint4 xq[CONS_THREADS];           // the same as 16-bit fixed point, byte digits per 8 elements
+  __half xh[H];                     // RMSNorm_l(x) as f16 (hot neurons, xslot order); with xq, a y stage later
+  uint4 xq[CONS_THREADS];           // the same as 16-bit fixed point, byte digits per 8 elements (xslot order)
   float ystage[H];                  // partial y stage of the layer-end tree (ypos4 layout); earlier in
                                     // the layer, the planner's W_down rows RMSNorm_{l+1}(x_l)
   float z[128];                     // planner: bottleneck of the next layer's predictor
@@ -212,6 +212,12 @@ __device__ __forceinline__ ulonglong2 ld_pair_sys(const unsigned long long* src)
   asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(src) : "memory");
   return v;
 }
+
+// Slot of consumer thread t's 8 normalised elements [8t, 8t+8) in the xh / xq
+// arrays (16 bytes each): subgroup thread u = t / 4 owns elements
+// [32u, 32u+32), its j-th 16 bytes at slot j x 128 + u, so that the 128
+// threads' loads of their j-th word are contiguous (no bank conflicts).
+__device__ __forceinline__ int xslot(int t) { return (t & 3) * SG_THREADS + (t >> 2); }
 
 // Shared-memory stage of the partial y: the 4 elements [32 u + 4 j, +4) of
 // subgroup thread u sit at float4 index 8 u + (j ^ (u & 7)), so that u's 8
@@ -548,10 +554,10 @@ __device__ __forceinline__ void sg_hot(StackSmem& sm, const StackParams& p, cons
   const int u = threadIdx.x & (SG_THREADS - 1), lane = threadIdx.x & 31;
   uint32_t xp[16];
   {
-    const uint4* src = reinterpret_cast<const uint4*>(sm.xh + SPT * u);
+    const uint4* src = reinterpret_cast<const uint4*>(sm.xh) + u;        // word i at [i][u] (xslot)
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const uint4 v = src[i];
+      const uint4 v = src[i * SG_THREADS];
       xp[4 * i] = v.x; xp[4 * i + 1] = v.y; xp[4 * i + 2] = v.z; xp[4 * i + 3] = v.w;
     }
   }
@@ -595,10 +601,10 @@ __device__ __forceinline__ void sg_cold(StackSmem& sm, const StackParams& p, con
   const int u = threadIdx.x & (SG_THREADS - 1), lane = threadIdx.x & 31;
   XFix xf;
   {
-    const uint4* src = sm.xq + 4 * u;
+    const uint4* src = sm.xq + u;                                          // word j at [j][u] (xslot)
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const uint4 v = src[j];
+      const uint4 v = src[j * SG_THREADS];
       xf.d[4 * j] = v.x; xf.d[4 * j + 1] = v.y; xf.d[4 * j + 2] = v.z; xf.d[4 * j + 3] = v.w;
     }
     const int2 ch = sm.chunk[u];
@@ -1286,7 +1292,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
           __half2 h2[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) h2[i] = __floats2half2_rn(xn[2 * i], xn[2 * i + 1]);
-          *reinterpret_cast<uint4*>(sm.xh + EPT * t) = *reinterpret_cast<const uint4*>(h2);
+          reinterpret_cast<uint4*>(sm.xh)[xslot(t)] = *reinterpret_cast<const uint4*>(h2);
         }
         // 16-bit fixed point per 32 elements (4 threads): |x| * 2^s < 2^15
         am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
@@ -1308,7 +1314,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
         dq.y = hb(xi[1]) | (hb(xi[3]) << 8) | (hb(xi[5]) << 16) | (hb(xi[7]) << 24);
         dq.z = lb(xi[0]) | (lb(xi[2]) << 8) | (lb(xi[4]) << 16) | (lb(xi[6]) << 24);
         dq.w = lb(xi[1]) | (lb(xi[3]) << 8) | (lb(xi[5]) << 16) | (lb(xi[7]) << 24);
-        sm.xq[t] = dq;
+        sm.xq[xslot(t)] = dq;
         sum += __shfl_xor_sync(0xffffffffu, sum, 1);
         sum += __shfl_xor_sync(0xffffffffu, sum, 2);
         if ((t & 3) == 0) sm.chunk[t >> 2] = make_int2(-8 * sum, __float_as_int(isc));
