@@ -1458,6 +1458,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
       }
       if (pred_next) ++wd_phase;
       named_bar(1, CONS_THREADS);
+      if (t == 0) trace_ev(p, l, 38);
       if (sm.flag == 0) {
         ok = false;
         break;
@@ -1488,6 +1489,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
           }
         }
         named_bar(1, CONS_THREADS);
+        if (t == 0) trace_ev(p, l, 39);
         float4 e0 = bufA[ypos4_of_thread(t, 0)], e1 = bufA[ypos4_of_thread(t, 1)];
         {
           const float4 f0 = bufB[ypos4_of_thread(t, 0)], f1 = bufB[ypos4_of_thread(t, 1)];

@@ -291,6 +291,9 @@ class FFNStack:
             put(f"subgroup{k}", us[:, :, 4 + k] - us[:, :, 1])
         put("subgroup_spread", sg_done.max(dim=2).values - sg_done.min(dim=2).values)
         put("y_sum", us[:, :, 9] - sg_done.max(dim=2).values)
+        put("y_sum.decision", us[:, :, 38] - sg_done.max(dim=2).values)     # bias out, planner check, barrier
+        put("y_sum.stage_add", us[:, :, 39] - us[:, :, 38])                 # two tree steps
+        put("y_sum.final", us[:, :, 9] - us[:, :, 39])                      # last step, fence, barrier
         put("arrive", us[:, :, 8] - us[:, :, 9])
         put("arrive.bulk_reduce", us[:, :, 28] - us[:, :, 9])
         put("arrive.proxy_fence", us[:, :, 29] - us[:, :, 28])
