@@ -145,28 +145,11 @@ __device__ __forceinline__ void named_bar(int id, int nthreads) {
 // ----------------------------------------------------------------------------
 // element decoders
 // ----------------------------------------------------------------------------
-// 4 e4m3 bytes -> 4 fp32 (exact; hardware e4m3x2 -> f16x2 conversion).
-__device__ __forceinline__ void e4m3x4_to_f32(uint32_t w, float f[4]) {
-  uint32_t lo, hi;
-  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(lo) : "h"(static_cast<unsigned short>(w & 0xFFFFu)));
-  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(hi) : "h"(static_cast<unsigned short>(w >> 16)));
-  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&lo));
-  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&hi));
-  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
-}
-
 // 8 packed signed INT4 (element 2i in the low nibble of byte i) -> fp32.
 // Arithmetic shift sign-extends the nibble: 8..15 -> -8..-1 (splitter.py:119-120).
 __device__ __forceinline__ void int4x8_to_f32(uint32_t w, float f[8]) {
 #pragma unroll
   for (int e = 0; e < 8; ++e) f[e] = static_cast<float>(static_cast<int32_t>(w << (28 - 4 * e)) >> 28);
-}
-
-// two fp32 -> e4m3x2 (round to nearest even, saturating to +-448): a in the low byte
-__device__ __forceinline__ uint32_t f32x2_to_e4m3x2(float a, float b) {
-  unsigned short r;
-  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(b), "f"(a));
-  return r;
 }
 
 // e4m3x2 (low byte -> low half) -> f16x2, exact
@@ -190,20 +173,6 @@ __device__ __forceinline__ void fma2_f16f16_f32(float& a, float& b, uint32_t w, 
       "fma.rn.f32.f16 %0, wl, xl, %0;\n\tfma.rn.f32.f16 %1, wh, xh, %1;\n\t}"
       : "+f"(a), "+f"(b)
       : "r"(w), "r"(x));
-}
-
-// warp-level tensor-core dot products (A rows 8..15 are zero: a1 = a3 = 0)
-__device__ __forceinline__ void mma_f16_m16n8k16(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void mma_s8_m16n8k32(int (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
 }
 
 // bytes [2 .. 6) of the 8-byte pair (a, b): the 2-byte shift every record field has
