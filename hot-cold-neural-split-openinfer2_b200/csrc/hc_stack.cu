@@ -780,6 +780,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
   const int c = blockIdx.x;
 
   if (tid == 0) {
+    trace_ev(p, 0, 33);        // the CTA started (layer 0's slot)
     for (int e = 0; e < NE; ++e) {
       mbar_init(&sm.full[e], 1);
       mbar_init(&sm.empty[e], SG_WARPS);
@@ -1558,6 +1559,7 @@ __global__ void __launch_bounds__(STACK_THREADS, 1) ffn_stack_kernel(StackParams
   // Once every CTA is past its last read: reset the barrier counters and clear
   // the accumulators, so the next launch starts from a clean workspace.
   if (tid == 0) {
+    trace_ev(p, 0, 34);        // the CTA is done (layer 0's slot)
     __threadfence();
     sm.last = atomicAdd(p.exit_count, 1u) == (uint32_t)G - 1;
   }

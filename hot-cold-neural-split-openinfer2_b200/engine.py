@@ -298,7 +298,7 @@ class FFNStack:
         put("arrive.bulk_reduce", us[:, :, 28] - us[:, :, 9])
         put("arrive.proxy_fence", us[:, :, 29] - us[:, :, 28])
         put("arrive.release", us[:, :, 8] - us[:, :, 29])
-        if self.L > 1:
+        if t.shape[0] > 1:          # layers with stamps (a traced slice may hold one)
             put("barrier_wait", us[1:, :, 0] - us[:-1, :, 8])
             put("layer", us[1:, :, 0] - us[:-1, :, 0])
             if not (self.tp is not None and self.tp.size > 1):
@@ -309,8 +309,9 @@ class FFNStack:
                 put("barrier.seen_to_layer_start", us[1:, :, 0] - us[:-1, :, 32])
         # layers after the first: the cold pool, its groups, then the hot groups
         # (layer 0: hot groups first); stamps 13/37 hot start/end, 11 pool, 12 cold end
-        put("issue_wait_pool", us[1:, :, 11] - us[1:, :, 10])
-        put("issue_cold", us[1:, :, 12] - us[1:, :, 11])
+        if t.shape[0] > 1:
+            put("issue_wait_pool", us[1:, :, 11] - us[1:, :, 10])
+            put("issue_cold", us[1:, :, 12] - us[1:, :, 11])
         put("issue_hot", us[:, :, 37] - us[:, :, 13])
         for name, ev in (("own_words_after_start", 21), ("planner_wake_after_start", 22),
                          ("plan_ready_after_start", 20)):
@@ -332,6 +333,9 @@ class FFNStack:
             put("tp.cta0_push", us[:, 0, 36] - us[:, 0, 32])
             put("tp.peers_seen_after_local", us[:-1, :, 35] - us[:-1, :, 32])
         put("issuer_slot_wait", us[:, :, 18])
+        # the launch as a whole (layer 0's slot): CTA start -> layer 0 start, last layer's end -> CTA done
+        put("launch.start_to_layer0", us[0, :, 0] - us[0, :, 33])
+        put("launch.span", us[0, :, 34] - us[0, :, 33])
         put("dynamic_hot_claimed[n]", t[:, :, 15])
         put("cold_listed[n]", t[:, :, 17])
         put("cold_taken[n]", t[:, :, 30])

@@ -257,7 +257,8 @@ HC_API int64_t hc_ffn_stack_workspace_bytes(int32_t grid, int32_t inter);
  *              cold pool complete, 12: cold records issued, 13 / 37: hot
  *              groups start / issued (layer 0 of a launch: hot groups before
  *              the cold pool), 14: layer sealed; CTA thread 0 at the layer
- *              end: 38 all subgroups done, 39 tree staged; 21: own mask words ready (stamped at the end of the
+ *              end: 38 all subgroups done, 39 tree staged; layer 0's slot
+ *              also holds 33: the CTA started, 34: the CTA done; 21: own mask words ready (stamped at the end of the
  *              previous layer), 22: planner took them, 20: own cold list
  *              published -- plus 15: hot neurons claimed, 30: cold records
  *              taken from the pool, 17: active cold records of the own id
