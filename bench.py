@@ -177,7 +177,7 @@ def run_reference(args):
     ref = cpu_reference(args.steps, args.warmup, layers_per_step=2, budget_s=120.0)
     line = {"metric": METRIC, "impl": "reference", "value": ref["value"], "unit": "tokens/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / ref["value"],
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
             "data": "synthetic",
             "config": {"workload": WORKLOAD, "layers": LAYERS, "hidden": H, "inter": INTER, "batch": 1,
                        "note": "one step = one token through 2 sampled layers on the host cores, scaled to 32"},
