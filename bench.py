@@ -310,6 +310,43 @@ def batched_decode_bench(syn, steps: int, warmup: int, batches=(1, 8, 32, 64), s
     return out
 
 
+def pinned_tier_bench(syn, pstore, tokens: int = 8):
+    """configs[2] with cold_weights.bin in pinned host memory (the reference's
+    tiering, splitter.py:307-330): per layer the predicted records cross PCIe
+    into the store's staging buffer (hc_union_cold + hc_cold_stage), then the
+    layer's stack launch, which also predicts the next layer's set.  Timed
+    with CUDA events over ``tokens`` decode tokens after one warm-up token."""
+    import torch
+    import engine
+    dev = pstore.device
+    st = engine.FFNStack(pstore, syn.hot, syn.norms, syn.predictors, syn.activation, syn.act_on_both, syn.eps,
+                         inter=syn.inter)
+    g = torch.Generator(device=dev).manual_seed(5)
+    xs = torch.randn(tokens + 1, H, device=dev, generator=g)
+    ys = torch.empty_like(xs)
+    st.forward(xs[tokens], out=ys[tokens])
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for t in range(tokens):
+        st.forward(xs[t], out=ys[t])
+    e1.record()
+    torch.cuda.synchronize()
+    st.check()
+    ms = e0.elapsed_time(e1)
+    staged = 0
+    for t in range(tokens):                      # the records each token fetched (untimed replay)
+        st.forward(xs[t], out=ys[t])
+        staged += int(st.active_counts().sum())
+    rec_read = 6352                              # bytes of a record the kernels read
+    return {"workload": "configs[2] (32L dReLU 4096/14336, rank-64 predictors), cold store in pinned host memory",
+            "tokens": tokens, "tokens_per_s": round(tokens / (ms / 1e3), 2), "ms_per_token": round(ms / tokens, 3),
+            "staged_records_per_token": round(staged / tokens, 1),
+            "bus_gbs": round(staged * rec_read / (ms * 1e-3) / 1e9, 2),
+            "hbm_staging_bytes": int(pstore.stage_bytes()),
+            "launches_per_token": 2 + 3 * LAYERS}     # layer 0 predictor (2), per layer union + stage + stack
+
+
 def config0_quality(dev):
     """one 4096/14336 SwiGLU layer, hot 20% FP8 with per-row absmax
     scales, cold 80% INT4, one N(0, 1) token, Bernoulli(0.1) active cold mask,
@@ -538,6 +575,7 @@ def run_gpu(args):
     if rank == 0:
         dq = cold_dequant_bench(syn.store) if ws == 1 else None
         dq_pinned = None
+        pt = None
         if ws == 1:
             # the same gather with the cold file image in pinned host memory (PCIe-bound)
             from splitter import ColdWeightStore
@@ -546,6 +584,10 @@ def run_gpu(args):
             dq_pinned = cold_dequant_bench(pstore, reps=3, ks=(256, 1024, 4096))
             for v in dq_pinned.values():
                 v.pop("frac", None)            # bound by PCIe, not HBM
+            try:
+                pt = pinned_tier_bench(syn, pstore)
+            except Exception as e:          # noqa: BLE001 -- reported in the line, not hidden
+                pt = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
             del pstore
         bd = batched_decode_bench(syn, args.steps, args.warmup) if ws == 1 else None
         cpu = cpu_reference(4, 0, layers_per_step=2, budget_s=25.0) if ws == 1 else None
@@ -600,6 +642,8 @@ def run_gpu(args):
                 line["cold_dequant"]["cpu_sample"] = "read_neurons of 256 seeded ids per call, repeated for 2 s"
                 for v in dq.values():
                     v["vs_cpu"] = round(v["neurons_per_s"] / rate, 1)
+        if pt is not None:
+            line["pinned_tier"] = pt
         if dq_pinned is not None:
             line["cold_dequant_pinned"] = {"unit": "GB/s", "source": "pinned host memory read over PCIe by the "
                                            "gather kernel; read_gbs = 6336 B per neuron / time",

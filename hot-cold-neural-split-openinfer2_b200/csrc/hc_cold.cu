@@ -6,6 +6,8 @@
 // A record starts 16 B after a page-aligned section header plus r * 6400, so
 // its start is 16-byte aligned, but every field begins 2 bytes later (after
 // the u16 id).  Threads load aligned words and funnel-shift by 16 bits.
+#include <algorithm>
+
 #include "hc_common.cuh"
 
 namespace hc {
@@ -167,9 +169,73 @@ __global__ void __launch_bounds__(256) gather_dequant_kernel(
   }
 }
 
+// --------------------------------------------------------------------------
+// record staging: the cold tier kept outside HBM.  The reference keeps the
+// store on disk / in host memory and reads only the fetched neurons
+// (splitter.py:307-330, :354-403); here a layer's fetched records are copied,
+// raw, from the store's section (pinned host memory read over the bus, or any
+// device-readable memory) to the same record offsets of a device buffer that
+// the fused kernels then read as the layer's section.  One warp per record:
+// every lane issues its 13 16-byte loads before its stores, so a warp keeps a
+// whole record in flight.
+// --------------------------------------------------------------------------
+constexpr int REC_WORDS = REC_COPY / 16;                 // 397 words read per record
+constexpr int STAGE_PER_LANE = (REC_WORDS + 31) / 32;    // 13
+constexpr int STAGE_THREADS = 256;
+constexpr int STAGE_MAX_CTAS = 148 * 8;
+
+__global__ void __launch_bounds__(STAGE_THREADS) stage_records_kernel(
+    const uint8_t* __restrict__ src, int64_t src_bytes, const int32_t* __restrict__ rec_idx,
+    const int32_t* __restrict__ count, int max_count, int n_records, uint8_t* __restrict__ dst, int64_t dst_bytes,
+    int32_t* __restrict__ status) {
+  const int lane = threadIdx.x & 31;
+  const int warp = (blockIdx.x * STAGE_THREADS + threadIdx.x) >> 5;
+  const int nwarps = (gridDim.x * STAGE_THREADS) >> 5;
+  int n = max_count;
+  if (count != nullptr) {
+    const int c = __ldg(count);
+    if (c > max_count && warp == 0 && lane == 0) atomicOr(status, HC_ERR_RANGE);   // list longer than its buffer
+    n = min(max(c, 0), max_count);
+  }
+  for (int k = warp; k < n; k += nwarps) {
+    const int32_t r = __ldg(rec_idx + k);
+    const int64_t off = (int64_t)r * REC_BYTES;
+    if (r < 0 || r >= n_records || off + REC_COPY > src_bytes || off + REC_COPY > dst_bytes) {
+      if (lane == 0) atomicOr(status, HC_ERR_RANGE);
+      continue;
+    }
+    const uint4* s = reinterpret_cast<const uint4*>(src + off);
+    uint4* d = reinterpret_cast<uint4*>(dst + off);
+    uint4 v[STAGE_PER_LANE];
+#pragma unroll
+    for (int i = 0; i < STAGE_PER_LANE; ++i)
+      if (lane + 32 * i < REC_WORDS) v[i] = __ldg(s + lane + 32 * i);
+#pragma unroll
+    for (int i = 0; i < STAGE_PER_LANE; ++i)
+      if (lane + 32 * i < REC_WORDS) d[lane + 32 * i] = v[i];
+  }
+}
+
 }  // namespace hc
 
 using namespace hc;
+
+extern "C" int hc_cold_stage(const void* src_records, int64_t src_bytes, const int32_t* rec_idx,
+                             const int32_t* count, int32_t max_count, int32_t n_records, void* dst_records,
+                             int64_t dst_bytes, int32_t* status, hc_stream_t stream) {
+  if (!src_records || !dst_records || !status || max_count < 0 || n_records < 0 || src_bytes < 0 ||
+      dst_bytes < 0 || (max_count > 0 && !rec_idx))
+    return HC_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(src_records) & 15) || (reinterpret_cast<uintptr_t>(dst_records) & 15))
+    return HC_ERR_ARG;
+  if (max_count == 0) return HC_OK;
+  const int warps = max_count;
+  const int ctas = std::min((warps + STAGE_THREADS / 32 - 1) / (STAGE_THREADS / 32), STAGE_MAX_CTAS);
+  stage_records_kernel<<<ctas, STAGE_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(src_records), src_bytes, rec_idx, count, max_count, n_records,
+      static_cast<uint8_t*>(dst_records), dst_bytes, status);
+  return cudaGetLastError() == cudaSuccess ? HC_OK : HC_ERR_CUDA;
+}
 
 extern "C" int hc_build_record_table(const void* cold_base, int64_t image_bytes, const int64_t* section_offsets,
                                      const int32_t* n_records, int32_t n_layers, int32_t max_records,

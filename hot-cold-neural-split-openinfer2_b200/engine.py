@@ -152,9 +152,20 @@ class FFNStack:
         the cold ids of mask words [r W / N, (r+1) W / N); the output is
         the whole layer stack's, identical on every rank.  ``wait_ns``
         limits every bounded wait inside a launch (0 = the kernel's 2 s);
-        an expired wait ends the launch with HC_ERR_TIMEOUT in the status."""
+        an expired wait ends the launch with HC_ERR_TIMEOUT in the status.
+
+        Over a store in pinned host memory (``source="pinned"``, the
+        reference's cold tier outside the GPU, splitter.py:307-330) every
+        layer fetches its predicted records over the bus into the store's
+        device staging buffer right before it is computed, and the layers run
+        one launch each (the next layer's set is still predicted inside the
+        launch of the layer before it); only the hot rows, predictors and one
+        section's worth of staging live in HBM."""
         self.store = store
         self.tp = tp
+        self.pinned = getattr(store, "source", "device") == "pinned"
+        if self.pinned and tp is not None and tp.size > 1:
+            raise ValueError("a pinned cold store serves one GPU; tensor parallelism needs the store in HBM")
         self.wait_ns = int(wait_ns)
         self.device = store.device
         self.L = len(hot)
@@ -191,7 +202,8 @@ class FFNStack:
             li = self.layer_ids[l]
             p = self.predictors[l]
             wdt = p.down_t() if p is not None else None
-            rec = store.section_records(li)
+            # a pinned store's records reach the kernel through the staging buffer only
+            rec = store.staging() if self.pinned else store.section_records(li)
             self._keep += [rec, wdt]
             descs.append(N.LayerDesc(
                 hot=N.ptr(self.hot[l].packed), hot_scale=N.ptr(self.hot[l].scales), norm_w=N.ptr(self.norms[l]),
@@ -239,22 +251,41 @@ class FFNStack:
         kernel predicts layer 0 too).  ``predict_last``: the last layer is
         not computed, only its mask row predicted (from the input of the layer
         before it).  ``trace`` (int64 [L, grid, 40], device) (zeroed)
-        receives per-CTA phase timestamps and waits (see include/hotcold.h)."""
+        receives per-CTA phase timestamps and waits (see include/hotcold.h).
+
+        Over a pinned store a launch computes one layer (``L == 1``, or
+        ``L == 2`` with ``predict_last``), whose set (mask row 0) is fetched
+        into the staging buffer first."""
+        if self.pinned:
+            if self.L - (1 if predict_last else 0) != 1 or masks_given == 2:
+                raise ValueError("over a pinned cold store a launch computes one layer whose set is given "
+                                 "(forward() runs the layers one launch each)")
+            self._stage(0)
+        mg = 2 if masks_given == 2 else (1 if masks_given else 0)
+        return self._launch_at(0, self.L, x, mg, x_hist, out, trace, predict_last, io_f16)
+
+    def _stage(self, l: int):
+        """Fetch layer l's records (mask row l & fetchable) into the staging buffer."""
+        self.store.fetch_masked(self.layer_ids[l], self.masks[l], self.fetch[l], self.inter)
+
+    def _launch_at(self, first: int, n: int, x: torch.Tensor, mg: int, x_hist, out, trace, predict_last: bool,
+                   io_f16: bool) -> torch.Tensor:
+        """hc_ffn_stack_tp over layers [first, first + n) of this stack."""
         out = self.x_out if out is None else out
         tp = None
         if self.tp is not None and self.tp.size > 1:
             tp = N.TPDesc(size=self.tp.size, rank=self.tp.rank, words_lo=self.words_lo, words_n=self.words_n,
                           peer_buf=N.ptr(self.tp.peer_buf), seq_base=self.tp.seq & 0xFFFFFFFF,
                           wait_ns=self.wait_ns)
-            self.tp.seq += self.L - (1 if predict_last else 0)
+            self.tp.seq += n - (1 if predict_last else 0)
         elif self.wait_ns or predict_last or io_f16:
             tp = N.TPDesc(size=1, rank=0, words_lo=0, words_n=self.words, peer_buf=None, seq_base=0,
                           wait_ns=self.wait_ns)
         if tp is not None:
             tp.predict_last = 1 if predict_last else 0
             tp.io_f16 = 1 if io_f16 else 0
-        mg = 2 if masks_given == 2 else (1 if masks_given else 0)
-        N.check(N.lib.hc_ffn_stack_tp(N.ptr(self.desc_dev), self.L, self.inter, N.ptr(x), N.ptr(self.masks),
+        desc = N.ptr(self.desc_dev) + first * ctypes.sizeof(N.LayerDesc)
+        N.check(N.lib.hc_ffn_stack_tp(desc, n, self.inter, N.ptr(x), N.ptr(self.masks[first]),
                                       mg, N.ptr(out), N.ptr(x_hist), self.eps, self.act,
                                       1 if self.act_on_both else 0, self.thr, self.grid, N.ptr(self.ws),
                                       N.ptr(self.status), N.ptr(trace),
@@ -348,6 +379,8 @@ class FFNStack:
         the fetch set of every layer instead of running the predictors."""
         N.require_cuda(x)
         x = x.to(torch.float32).contiguous().view(-1)
+        if self.pinned:
+            return self._forward_pinned(x, masks, x_hist, out)
         if masks is not None:
             self.masks.copy_(masks)
             return self.launch(x, True, x_hist, out)
@@ -357,6 +390,30 @@ class FFNStack:
         return self.launch(x, False, x_hist, out)
 
     __call__ = forward
+
+    def _forward_pinned(self, x: torch.Tensor, masks, x_hist, out) -> torch.Tensor:
+        """forward() over a pinned store: per layer, fetch its records into
+        the staging buffer, then one launch that computes it and (when the
+        sets are not given) predicts the next layer's set from the same input
+        -- the order of the whole-stack launch (engine.py:421-438)."""
+        out = self.x_out if out is None else out
+        if masks is not None:
+            self.masks.copy_(masks)
+        else:
+            self.first_mask(x)
+        if getattr(self, "_ping", None) is None:
+            self._ping = torch.empty(2, HIDDEN_DIM, dtype=torch.float32, device=self.device)
+        cur = x
+        for l in range(self.L):
+            if masks is None and l > 0 and self.predictors[l] is None:
+                self.masks[l].copy_(self._all_ones)          # no predictor: every cold neuron
+            self._stage(l)
+            pair = masks is None and l + 1 < self.L and self.predictors[l + 1] is not None
+            dst = out if l == self.L - 1 else self._ping[l % 2]
+            self._launch_at(l, 2 if pair else 1, cur, 0, x_hist[l] if x_hist is not None else None, dst, None,
+                            pair, False)
+            cur = dst
+        return out
 
     def decode_host(self, x_host: torch.Tensor, y_host: torch.Tensor) -> torch.Tensor:
         """Decode T tokens given in host memory: x_host [T, H] fp32 (pinned for
@@ -376,6 +433,8 @@ class FFNStack:
 
     def check(self):
         N.read_status(self.status, "hc_ffn_stack")
+        if self.pinned:
+            self.store.check()              # the staging copies
 
     def active_counts(self) -> torch.Tensor:
         """Active cold neurons per layer of the last forward (this GPU's share
@@ -425,8 +484,15 @@ class BatchStack:
         always stream the packed copy of the share (the union's flags
         select).  Build it on every rank with the process group initialised
         (the buffers' IPC handles are exchanged over ``group``) and call
-        :meth:`close` before destroying the group."""
+        :meth:`close` before destroying the group.
+
+        Over a store in pinned host memory each layer's union is fetched over
+        the bus into the store's staging buffer before the layer runs (the
+        gathered mode; no packed copies are made)."""
         self.store = store
+        self.pinned = getattr(store, "source", "device") == "pinned"
+        if self.pinned and shard is not None and int(shard[1]) > 1:
+            raise ValueError("a pinned cold store serves one GPU; sharding needs the store in HBM")
         self.device = store.device
         self.L = len(hot)
         self.layer_ids = list(layer_ids) if layer_ids is not None else list(range(self.L))
@@ -454,7 +520,7 @@ class BatchStack:
         self.descs, self._keep, self.max_cold, self.rec_lo = [], [], [], []
         for l in range(self.L):
             li = self.layer_ids[l]
-            rec = store.section_records(li)
+            rec = store.staging() if self.pinned else store.section_records(li)
             self._keep.append(rec)
             r0, r1 = split_range(int(store.n_rec_host[li]), rank, size)
             self.rec_lo.append(r0)
@@ -471,6 +537,8 @@ class BatchStack:
         self.rec = torch.zeros(self.L, max(max(self.sec_records), 1), dtype=torch.int32, device=self.device)
         self.count = torch.zeros(self.L, dtype=torch.int32, device=self.device)
         self.dense_min_batch = 1 if size > 1 else int(dense_min_batch)
+        if self.pinned:
+            self.dense_min_batch = self.max_batch + 1        # gathered mode only
         self.flag_stride = (max(max(self.sec_records), 1) + 15) // 16 * 16
         self.part = torch.zeros(self.max_batch, HIDDEN_DIM, dtype=torch.float32, device=self.device) \
             if size > 1 else None
@@ -551,6 +619,10 @@ class BatchStack:
                                                    0, N.ptr(self.count[l:l + 1]),
                                                    N.ptr(flags[l]) if dense else None, self.flag_stride, s),
                         "hc_union_cold_layers")
+            if self.pinned:
+                # the union's records over the bus into the staging buffer
+                self.store.stage_records(self.layer_ids[l], self.rec[l, :self.sec_records[l]], self.store.staging(),
+                                         self.count[l:l + 1])
             if self.part is None:
                 N.check(N.lib.hc_ffn_batch_layer(ctypes.byref(self.descs[l]), N.ptr(self.packed[l]), N.ptr(y), B,
                                                  N.ptr(self.rec[l]),
@@ -590,6 +662,8 @@ class BatchStack:
 
     def check(self):
         N.read_status(self.status, "hc_ffn_batch_layer")
+        if self.pinned:
+            self.store.check()              # the staging copies
         if self._single_stack is not None:
             self._single_stack.check()
 
@@ -966,10 +1040,14 @@ class DesdemonaEngine(nn.Module):
     reference's lookahead, engine.py:421-438) and never crosses to the host.
     ``generate`` prefills eagerly and replays one captured CUDA graph per
     decode step.  ``n_threads`` is accepted for signature compatibility (no
-    host thread pool is needed)."""
+    host thread pool is needed).  ``cold_source="pinned"`` keeps
+    cold_weights.bin in pinned host memory instead -- the reference's tiering
+    (README.md:3-9, splitter.py:307-330): each layer's predicted records cross
+    the bus into one shared staging buffer right before the layer runs."""
 
     def __init__(self, split_dir: Optional[str] = None, predictor_dir: Optional[str] = None, device: str = "cuda",
-                 n_threads: int = 8, max_seq_len: int = 8192, *, _parts: Optional[dict] = None):
+                 n_threads: int = 8, max_seq_len: int = 8192, *, cold_source: str = "device",
+                 _parts: Optional[dict] = None):
         super().__init__()
         import json
         self.device = torch.device(device)
@@ -985,7 +1063,8 @@ class DesdemonaEngine(nn.Module):
             if predictor_dir and Path(predictor_dir).exists():
                 self.predictor = PredictorRegistry(predictor_dir, device=str(self.device))
             self.cold_store = ColdWeightStore(str(Path(split_dir) / "cold_weights.bin"),
-                                              str(Path(split_dir) / "cold_index.npy"), self.cfg, device=self.device)
+                                              str(Path(split_dir) / "cold_index.npy"), self.cfg, device=self.device,
+                                              source=cold_source)
             hots = [str(Path(split_dir) / "hot_weights")] * self.cfg["num_layers"]
         else:
             # in-memory artefacts (synthetic models): cfg, shared, cold_store, hot [HotNeurons], predictor

@@ -60,6 +60,7 @@ _SIGS = {
     "hc_map_ids": (c_i32, [c_p, c_i32, c_p, c_p, c_p, c_p, c_p]),
     "hc_cold_gather_dequant": (c_i32, [c_p, c_i64, c_p, c_p, c_i32, c_p, c_i32, c_p, c_i32,
                                        c_p, c_p, c_p, c_p, c_p]),
+    "hc_cold_stage": (c_i32, [c_p, c_i64, c_p, c_p, c_i32, c_i32, c_p, c_i64, c_p, c_p]),
     "hc_predictor_workspace_bytes": (c_i64, [c_i32, c_i32, c_i32]),
     "hc_predictor_forward": (c_i32, [c_p, c_i32, c_p, c_f, c_p, c_p, c_p, c_i32, c_i32, c_f, c_p, c_p, c_p,
                                      c_p, c_p, c_p, c_p, c_p, c_p, c_p, c_p]),

@@ -132,6 +132,7 @@ class ColdWeightStore:
         N.read_status(self.status, "hc_build_record_table")
         # kept for interface parity with the reference (filled on first access)
         self._offset_cache: dict = {}
+        self._staging = None
 
     # -- reference interface ------------------------------------------------
     def _section_table(self, layer_idx: int, expert_idx: int):
@@ -165,6 +166,7 @@ class ColdWeightStore:
     def close(self):
         self.image = None
         self.table = None
+        self._staging = None
 
     # -- device-side interface --------------------------------------------
     def read_records(self, layer_idx: int, rec_idx: torch.Tensor, count: Optional[torch.Tensor] = None,
@@ -206,9 +208,58 @@ class ColdWeightStore:
         N.read_status(self.status, "ColdWeightStore")
 
     def section_records(self, layer_idx: int) -> torch.Tensor:
-        """Device view of the first record of a layer's section (for the fused FFN)."""
+        """View of the first record of a layer's section (for the fused FFN):
+        device memory, or pinned host memory for ``source="pinned"``."""
         off = int(self.index[layer_idx, 0, 0])
         return self.image[off + SECTION_HEADER_BYTES:]
+
+    def stage_bytes(self) -> int:
+        """Size of a device buffer that holds any one section's records at
+        their own offsets (record r at r * 6400)."""
+        return max(int(self.n_rec_host.max(initial=0)), 1) * NEURON_RECORD_BYTES
+
+    def staging(self) -> torch.Tensor:
+        """The store's device staging buffer (:meth:`stage_bytes`, allocated on
+        first use): the section a fused kernel reads for a layer whose
+        records :meth:`fetch_masked` fetched.  Every stack over this store
+        shares it, so their launches must stay in one stream's order."""
+        if self._staging is None:
+            n = max(int(self.n_rec_host.max(initial=0)), 1)
+            self._staging = torch.empty(self.stage_bytes(), dtype=torch.uint8, device=self.device)
+            self._stage_rec = torch.empty(n, dtype=torch.int32, device=self.device)
+            self._stage_count = torch.zeros(1, dtype=torch.int32, device=self.device)
+        return self._staging
+
+    def fetch_masked(self, layer_idx: int, words: torch.Tensor, fetch_bits: torch.Tensor, inter: int,
+                     batch: int = 1) -> torch.Tensor:
+        """Fetch the records of layer ``layer_idx`` whose ids are set in
+        ``words`` (int32 mask words, [batch][ceil(inter/32)] rows: their
+        union) and in ``fetch_bits`` into :meth:`staging`, on the device (no
+        host sync).  Returns the staging buffer."""
+        dst = self.staging()
+        W = (inter + 31) // 32
+        n = max(int(self.n_rec_host[layer_idx]), 1)
+        N.check(N.lib.hc_union_cold(N.ptr(words), batch, words.stride(0) if words.dim() > 1 else W, inter,
+                                    N.ptr(fetch_bits), N.ptr(self.table[layer_idx]), N.ptr(self._stage_rec),
+                                    N.ptr(self._stage_count), N.stream_handle()), "hc_union_cold")
+        self.stage_records(layer_idx, self._stage_rec[:n], dst, self._stage_count)
+        return dst
+
+    def stage_records(self, layer_idx: int, rec_idx: torch.Tensor, dst: torch.Tensor,
+                      count: Optional[torch.Tensor] = None):
+        """The per-layer fetch of the cold tier: copy the raw records
+        ``rec_idx`` (device int32 [K]; the first ``count[0]`` entries when a
+        device ``count`` is given) of layer ``layer_idx`` from the store
+        (pinned host memory over the bus, or HBM) to the same offsets of the
+        device buffer ``dst`` (uint8, at least :meth:`stage_bytes`).  Bad
+        indices flag HC_ERR_RANGE in :meth:`check`; asynchronous."""
+        N.require_cuda(rec_idx, dst)
+        if rec_idx.dtype != torch.int32 or not rec_idx.is_contiguous():
+            raise ValueError("rec_idx must be a contiguous int32 tensor")
+        src = self.section_records(layer_idx)
+        N.check(N.lib.hc_cold_stage(N.ptr(src), src.numel(), N.ptr(rec_idx), N.ptr(count), rec_idx.numel(),
+                                    int(self.n_rec_host[layer_idx]), N.ptr(dst), dst.numel(), N.ptr(self.status),
+                                    N.stream_handle()), "hc_cold_stage")
 
     def fetch_bits(self, layer_idx: int, hot_ids, inter: Optional[int] = None) -> torch.Tensor:
         """uint32 words: bit i set iff id i has a record and is not hot -- the

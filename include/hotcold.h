@@ -116,6 +116,32 @@ HC_API int hc_cold_gather_dequant(const void* cold_base, int64_t image_bytes, co
                            int32_t K, const int32_t* count, int32_t out_dtype, void* gate_out,
                            void* up_out, void* down_out, int32_t* status, hc_stream_t stream);
 
+/*
+ * hc_cold_stage -- the per-layer fetch of a cold tier kept outside HBM.  The
+ * reference keeps cold_weights.bin on disk / in host memory and reads only
+ * the neurons it fetches (ColdWeightStore, splitter.py:307-330, :354-403);
+ * here the fetched records of one layer are copied raw (their first 6352
+ * bytes: id, INT4 fields, scales) from the store's section to the same
+ * offsets of a device buffer, which the fused kernels (hc_ffn_stack,
+ * hc_ffn_batch_layer) are then given as that layer's cold_records.
+ *   src_records  the section's first record (section offset + 16) in device
+ *                memory or mapped pinned host memory (read over the bus);
+ *                16-byte aligned
+ *   src_bytes    host: bytes readable from src_records
+ *   rec_idx      [max_count] int32 record indices (hc_union_cold's list)
+ *   count        optional [1] int32 (device): entries of rec_idx in use;
+ *                NULL = max_count; a count above max_count sets HC_ERR_RANGE
+ *   n_records    host: records in the section; an index outside [0,
+ *                n_records) or past src_bytes / dst_bytes sets HC_ERR_RANGE
+ *                and is skipped
+ *   dst_records  device buffer laid out like the section (record r at
+ *                r * 6400); 16-byte aligned; dst_bytes its size
+ * Records not listed are left untouched.
+ */
+HC_API int hc_cold_stage(const void* src_records, int64_t src_bytes, const int32_t* rec_idx, const int32_t* count,
+                         int32_t max_count, int32_t n_records, void* dst_records, int64_t dst_bytes,
+                         int32_t* status, hc_stream_t stream);
+
 /* ======================================================================= */
 /* Predictor                                                               */
 /* ======================================================================= */

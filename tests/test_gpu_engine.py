@@ -8,7 +8,8 @@
   repository's split_dense writes: every layer's fetch set equals the
   reference's, prefill and per-step decode logits match the reference's CPU
   fp16 run (tests/golden/engine.npz), and generate() returns the reference's
-  greedy tokens, through the captured decode graph and through eager steps.
+  greedy tokens, through the captured decode graph and through eager steps --
+  with the cold store in HBM and in pinned host memory.
 """
 import hashlib
 import json
@@ -96,7 +97,11 @@ def _rel(a, b):
     return float(np.linalg.norm(np.asarray(a, np.float64) - b) / np.linalg.norm(b))
 
 
-def test_engine_matches_reference_engine(M, tmp_path):
+@pytest.mark.parametrize("cold_source", ["device", "pinned"])
+def test_engine_matches_reference_engine(M, tmp_path, cold_source):
+    """cold_source "pinned": cold_weights.bin stays in pinned host memory and
+    every layer's predicted records cross the bus into the staging buffer
+    before the layer runs (the reference's tiering, splitter.py:307-330)."""
     engine, predictor, splitter, SM = M
     ref = np.load(os.path.join(GOLD, "engine.npz"))
     split, pdir = _engine_split(M, tmp_path)
@@ -113,7 +118,8 @@ def test_engine_matches_reference_engine(M, tmp_path):
     assert hashlib.sha256(shared["layer_000.q_proj"].view(torch.uint8).numpy().tobytes()).digest() == \
         ref["shared_q0_sha256"].tobytes()
 
-    eng = engine.DesdemonaEngine(str(split), str(pdir), device="cuda", max_seq_len=64)
+    eng = engine.DesdemonaEngine(str(split), str(pdir), device="cuda", max_seq_len=64, cold_source=cold_source)
+    assert eng.cold_store.source == cold_source
     prompt = torch.from_numpy(ref["prompt"]).cuda()
     logits, cache = eng.forward(prompt)
     torch.cuda.synchronize()

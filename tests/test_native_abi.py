@@ -85,6 +85,17 @@ def test_argument_errors_are_reported_without_a_device():
     assert N.lib.hc_ffn_batch_layer_partial(None, None, None, 4, None, None, 0, None, 1e-5, 0, 0, None, None,
                                             None, None) == N.HC_ERR_ARG
     assert N.lib.hc_batch_pack(None, None, None) == N.HC_ERR_ARG
+    # record staging: missing buffers or status, negative sizes, a list without indices, misaligned addresses
+    a16, st = 1 << 20, 1 << 21                    # never dereferenced: every call below fails its checks
+    assert N.lib.hc_cold_stage(None, 64, a16, None, 1, 1, a16, 64, st, None) == N.HC_ERR_ARG
+    assert N.lib.hc_cold_stage(a16, 64, a16, None, 1, 1, None, 64, st, None) == N.HC_ERR_ARG
+    assert N.lib.hc_cold_stage(a16, 64, a16, None, 1, 1, a16, 64, None, None) == N.HC_ERR_ARG
+    assert N.lib.hc_cold_stage(a16, 64, a16, None, -1, 1, a16, 64, st, None) == N.HC_ERR_ARG
+    assert N.lib.hc_cold_stage(a16, -1, a16, None, 1, 1, a16, 64, st, None) == N.HC_ERR_ARG
+    assert N.lib.hc_cold_stage(a16, 64, None, None, 1, 1, a16, 64, st, None) == N.HC_ERR_ARG
+    assert N.lib.hc_cold_stage(a16 + 8, 64, a16, None, 1, 1, a16, 64, st, None) == N.HC_ERR_ARG
+    assert N.lib.hc_cold_stage(a16, 64, a16, None, 1, 1, a16 + 4, 64, st, None) == N.HC_ERR_ARG
+    assert N.lib.hc_cold_stage(a16, 64, None, None, 0, 1, a16, 64, st, None) == N.HC_OK     # nothing to copy
     # packed copy: 16 KB per hot gate/up step, 8.5 KB per cold one, 8 / 4.1 KB per down step
     assert N.lib.hc_batch_pack_bytes(2867, 11469) >= (23 * 64 * 16384 + 90 * 64 * 8704 + 32 * 46 * 8192
                                                       + 32 * 180 * 4224)
