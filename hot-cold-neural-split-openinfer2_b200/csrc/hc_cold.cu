@@ -87,85 +87,99 @@ __global__ void __launch_bounds__(1024) map_ids_kernel(const int64_t* __restrict
 }
 
 // --------------------------------------------------------------------------
-// gather + dequantise.  128 threads per record, 2 records per CTA.  Thread t
-// owns elements [32t, 32t + 32) of each vector: bytes [2 + 16t, 18 + 16t) of
-// the field, fetched as an aligned uint4 + one word and shifted by 2 bytes.
+// gather + dequantise.  128 threads per record, 2 records per CTA.  A vector's
+// 4096 elements are 512 chunks of 8 (4 bytes of INT4 each); thread t owns
+// chunks t, t + 128, t + 256 and t + 384, so each warp-wide load reads 128
+// contiguous bytes of the field and each warp-wide store writes 512 (bf16) or
+// 2 x 512 (fp32) contiguous bytes of the output row -- whole lines, where a
+// thread owning 32 consecutive elements would leave every store instruction
+// covering a quarter of 16 lines.  A field starts 2 bytes past a 16-byte
+// boundary: chunk m's nibbles are aligned words m and m + 1 of the field's
+// aligned span, funnel-shifted by 16 bits (word m + 1 comes from the next lane).
 // --------------------------------------------------------------------------
 template <typename OutT>
-__device__ __forceinline__ void store32(OutT* dst, const float (&f)[32]);
+__device__ __forceinline__ void store8(OutT* dst, const float (&f)[8]);
 
 template <>
-__device__ __forceinline__ void store32<float>(float* dst, const float (&f)[32]) {
+__device__ __forceinline__ void store8<float>(float* dst, const float (&f)[8]) {
   float4* d = reinterpret_cast<float4*>(dst);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) d[i] = make_float4(f[4 * i], f[4 * i + 1], f[4 * i + 2], f[4 * i + 3]);
+  d[0] = make_float4(f[0], f[1], f[2], f[3]);
+  d[1] = make_float4(f[4], f[5], f[6], f[7]);
 }
 
 template <>
-__device__ __forceinline__ void store32<__nv_bfloat16>(__nv_bfloat16* dst, const float (&f)[32]) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
+__device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16* dst, const float (&f)[8]) {
+  uint32_t w[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint32_t w[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const __nv_bfloat162 b = __floats2bfloat162_rn(f[8 * i + 2 * j], f[8 * i + 2 * j + 1]);
-      w[j] = *reinterpret_cast<const uint32_t*>(&b);
-    }
-    d[i] = make_uint4(w[0], w[1], w[2], w[3]);
+  for (int j = 0; j < 4; ++j) {
+    const __nv_bfloat162 b = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
+    w[j] = *reinterpret_cast<const uint32_t*>(&b);
   }
+  *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
 }
+
+constexpr int GD_CHUNKS = H / 8 / 128;     // 4 chunks of 8 elements per thread and vector
 
 template <typename OutT>
 __global__ void __launch_bounds__(256) gather_dequant_kernel(
     const uint8_t* __restrict__ base, int64_t image_bytes, const int64_t* __restrict__ sec_off,
-    const int32_t* __restrict__ n_rec, const int32_t* __restrict__ rec_idx, int K, const int32_t* __restrict__ count, OutT* __restrict__ gate_out,
-    OutT* __restrict__ up_out, OutT* __restrict__ down_out, int32_t* __restrict__ status) {
+    const int32_t* __restrict__ n_rec, const int32_t* __restrict__ rec_idx, int K, const int32_t* __restrict__ count,
+    OutT* __restrict__ gate_out, OutT* __restrict__ up_out, OutT* __restrict__ down_out,
+    int32_t* __restrict__ status) {
   const int layer = blockIdx.y;
-  const int k = blockIdx.x * 2 + (threadIdx.x >> 7);
-  const int t = threadIdx.x & 127;
+  const int k = blockIdx.x * 2 + (threadIdx.x >> 7);      // uniform over each 128-thread half (4 whole warps)
+  const int t = threadIdx.x & 127, lane = threadIdx.x & 31;
   if (k >= K) return;
   if (count != nullptr && k >= count[layer]) return;
-  const int64_t row = ((int64_t)layer * K + k) * H + 32 * t;
+  const int64_t row = ((int64_t)layer * K + k) * H;
   OutT* outs[3] = {gate_out + row, up_out + row, down_out + row};
   const int32_t r = rec_idx[(int64_t)layer * K + k];
   const int64_t off = sec_off[layer];
   const bool bad_off = off < 0 || (off & 15) != 0;
   if (bad_off || r < 0 || r >= n_rec[layer] ||
       off + SECTION_HEADER + (int64_t)r * REC_BYTES + REC_COPY > image_bytes) {
-    float z[32];
+    float z[8];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) z[i] = 0.0f;
-    for (int v = 0; v < 3; ++v) store32<OutT>(outs[v], z);
+    for (int i = 0; i < 8; ++i) z[i] = 0.0f;
+    for (int v = 0; v < 3; ++v)
+#pragma unroll
+      for (int j = 0; j < GD_CHUNKS; ++j) store8<OutT>(outs[v] + 8 * (t + 128 * j), z);
     if (t == 0) atomicOr(status, bad_off ? HC_ERR_ARG : HC_ERR_RANGE);
     return;
   }
   const uint8_t* rec = base + off + SECTION_HEADER + (int64_t)r * REC_BYTES;
-  // issue all loads first
-  uint4 a[3];
-  uint32_t e[3];
+  const uint32_t* rw = reinterpret_cast<const uint32_t*>(rec);   // 16-byte aligned
+  // issue all loads first: the chunks' words, the last lane's next words, one
+  // group scale per lane (lane g holds group g's)
+  uint32_t w[3][GD_CHUNKS], nx[3][GD_CHUNKS];
   uint16_t s16[3];
 #pragma unroll
   for (int v = 0; v < 3; ++v) {
-    const uint8_t* p = rec + v * VEC_BYTES + 16 * t;
-    a[v] = __ldg(reinterpret_cast<const uint4*>(p));
-    e[v] = __ldg(reinterpret_cast<const uint32_t*>(p + 16));
-    s16[v] = __ldg(reinterpret_cast<const unsigned short*>(rec + SCALE_OFF + v * 2 * NGROUPS + 2 * (t >> 2)));
+#pragma unroll
+    for (int j = 0; j < GD_CHUNKS; ++j) w[v][j] = __ldg(rw + (VEC_BYTES / 4) * v + t + 128 * j);
+    s16[v] = __ldg(reinterpret_cast<const unsigned short*>(rec + SCALE_OFF + v * 2 * NGROUPS + 2 * lane));
+  }
+  if (lane == 31) {
+#pragma unroll
+    for (int v = 0; v < 3; ++v)
+#pragma unroll
+      for (int j = 0; j < GD_CHUNKS; ++j) nx[v][j] = __ldg(rw + (VEC_BYTES / 4) * v + t + 128 * j + 1);
   }
 #pragma unroll
   for (int v = 0; v < 3; ++v) {
-    const float s = __half2float(__ushort_as_half(s16[v]));
-    const uint32_t w[4] = {shift2(a[v].x, a[v].y), shift2(a[v].y, a[v].z), shift2(a[v].z, a[v].w),
-                           shift2(a[v].w, e[v])};
-    float f[32];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < GD_CHUNKS; ++j) {
+      const uint32_t up1 = __shfl_down_sync(0xffffffffu, w[v][j], 1);
+      const uint32_t hi = lane == 31 ? nx[v][j] : up1;
+      const int m = t + 128 * j;                                   // chunk: elements [8m, 8m + 8)
+      const float sc = __half2float(__ushort_as_half(
+          (unsigned short)__shfl_sync(0xffffffffu, (uint32_t)s16[v], m >> 4)));   // group m / 16 (< 32)
       float q[8];
-      int4x8_to_f32(w[j], q);
+      int4x8_to_f32(shift2(w[v][j], hi), q);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) f[8 * j + i] = q[i] * s;   // exact in fp32 (splitter.py:124)
+      for (int i = 0; i < 8; ++i) q[i] *= sc;                      // exact in fp32 (splitter.py:124)
+      store8<OutT>(outs[v] + 8 * m, q);
     }
-    store32<OutT>(outs[v], f);
   }
 }
 
