@@ -198,3 +198,33 @@ def test_sparse_ffn_layer_batched_rows_match_reference_layer(M):
     for r in range(16):
         rel = np.linalg.norm((got[r] - xs[r]) - (ref[r] - xs[r])) / np.linalg.norm(ref[r] - xs[r])
         assert rel < 2e-3, (r, rel)       # the batched bar: f16 tensor-core operands
+
+
+@pytest.mark.parametrize("tag,act,both", [("swiglu", "silu", False), ("drelu", "relu", True)])
+def test_sparse_ffn_compat_form_matches_reference(M, tag, act, both):
+    """engine.sparse_ffn, the reference-signature form for callers that hold
+    dense tensors (engine.py:173-209: hot half in x's dtype, cold half in
+    fp32), on the reference's own inputs: within the bar of the fp16 hot half
+    of the reference's outputs; hot-only and empty calls too.  The fused
+    kernels are the product path; this form never materialises them."""
+    engine, predictor, splitter, SM = M
+    d = os.path.join(GOLD, "split")
+    cfg = json.load(open(os.path.join(d, "split_config.json")))
+    store = splitter.ColdWeightStore(os.path.join(d, "cold_weights.bin"), os.path.join(d, "cold_index.npy"), cfg)
+    hot = torch.load(os.path.join(d, "hot_weights", "layer_000_expert_000.pt"))
+    hot_ids = set(hot["neuron_ids"].tolist())
+    cold_ids = [i for i in range(cfg["intermediate_dim"]) if i not in hot_ids]
+    cg, cu, cd = store.read_neurons(0, 0, cold_ids)          # the GPU gather, fp32
+    f = np.load(os.path.join(GOLD, "ffn.npz"))
+    x = torch.from_numpy(f["x16"]).half().cuda()
+    hg, hu, hd = (hot[k].cuda().half() for k in ("gate", "up", "down"))
+    y = engine.sparse_ffn(x, act, both, hg, hu, hd, cg, cu, cd)
+    assert y.dtype == torch.float16 and y.shape == x.shape
+    for got, key in ((y, f"sparse_{tag}"), (engine.sparse_ffn(x, act, both, hg, hu, hd, None, None, None),
+                                            f"sparse_{tag}_hotonly")):
+        ref = f[key]
+        assert _rel(got.float().cpu().numpy(), ref) < 5e-3, key
+    empty = engine.sparse_ffn(x, "silu", False, None, None, None, None, None, None)
+    assert torch.count_nonzero(empty) == 0 and np.all(f["sparse_empty"] == 0)
+    with pytest.raises(RuntimeError):
+        engine.sparse_ffn(x.cpu(), act, both, hg.cpu(), hu.cpu(), hd.cpu(), None, None, None)   # no CPU fallback
