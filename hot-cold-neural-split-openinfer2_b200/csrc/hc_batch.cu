@@ -256,15 +256,39 @@ __global__ void __launch_bounds__(256) k_norm(const float* __restrict__ x, int n
                                               float eps, uint8_t* __restrict__ xs_nat, uint8_t* __restrict__ xs_perm) {
   __shared__ float red[8];
   const int b = blockIdx.x, t = threadIdx.x;
+  constexpr int NP = H / 8 / 256;               // 8-element pieces per thread: t, t + 256
   pdl_launch_dependents();
+  // the RMSNorm weights do not depend on the previous layer: read them before waiting
+  float wv[NP][8];
+  const bool w16 = (reinterpret_cast<uintptr_t>(w) & 15) == 0;    // vector loads only when aligned
+#pragma unroll
+  for (int j = 0; j < NP; ++j) {
+    if (w && !w16) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) wv[j][e] = __ldg(w + (t + 256 * j) * 8 + e);
+    } else if (w) {
+      const float4 a0 = __ldg(reinterpret_cast<const float4*>(w + (t + 256 * j) * 8));
+      const float4 a1 = __ldg(reinterpret_cast<const float4*>(w + (t + 256 * j) * 8) + 1);
+      wv[j][0] = a0.x; wv[j][1] = a0.y; wv[j][2] = a0.z; wv[j][3] = a0.w;
+      wv[j][4] = a1.x; wv[j][5] = a1.y; wv[j][6] = a1.z; wv[j][7] = a1.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) wv[j][e] = 1.0f;
+    }
+  }
   pdl_wait();                                   // x is the previous layer's output
-  float rstd = 0.0f;
+  // each thread reads its pieces of x once: the sum of squares and the scaled values
+  float v[NP][8];
   if (b < nb) {
-    const float4* src = reinterpret_cast<const float4*>(x + (size_t)b * H);
     float ss = 0.0f;
-    for (int i = t; i < H / 4; i += 256) {
-      const float4 v = src[i];
-      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+      const float4* src = reinterpret_cast<const float4*>(x + (size_t)b * H + (t + 256 * j) * 8);
+      const float4 a0 = src[0], a1 = src[1];
+      v[j][0] = a0.x; v[j][1] = a0.y; v[j][2] = a0.z; v[j][3] = a0.w;
+      v[j][4] = a1.x; v[j][5] = a1.y; v[j][6] = a1.z; v[j][7] = a1.w;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += v[j][e] * v[j][e];
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -273,26 +297,25 @@ __global__ void __launch_bounds__(256) k_norm(const float* __restrict__ x, int n
     ss = 0.0f;
 #pragma unroll
     for (int k = 0; k < 8; ++k) ss += red[k];
-    rstd = rsqrtf(ss / (float)H + eps);
+    const float rstd = rsqrtf(ss / (float)H + eps);
+#pragma unroll
+    for (int j = 0; j < NP; ++j)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[j][e] *= rstd * wv[j][e];
+  } else {
+#pragma unroll
+    for (int j = 0; j < NP; ++j)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[j][e] = 0.0f;
   }
-  for (int piece = t; piece < H / 8; piece += 256) {
-    const int k0 = piece * 8;
-    float v[8];
-    if (b < nb) {
-      const float4 a0 = reinterpret_cast<const float4*>(x + (size_t)b * H + k0)[0];
-      const float4 a1 = reinterpret_cast<const float4*>(x + (size_t)b * H + k0)[1];
-      v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w; v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] *= rstd * (w ? __ldg(w + k0 + e) : 1.0f);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = 0.0f;
-    }
+  for (int j = 0; j < NP; ++j) {
+    const int k0 = (t + 256 * j) * 8;
     __half hn[8], hp[8];
 #pragma unroll
     for (int p = 0; p < 8; ++p) {
-      hn[p] = __float2half_rn(v[p]);
-      hp[p] = __float2half_rn(v[perm8(p)]);
+      hn[p] = __float2half_rn(v[j][p]);
+      hp[p] = __float2half_rn(v[j][perm8(p)]);
     }
     const size_t off = (size_t)(k0 / KC) * N * 128 + (size_t)((k0 % KC) / 8) * 16 * N + (b / 8) * 128 + (b % 8) * 16;
     *reinterpret_cast<uint4*>(xs_nat + off) = *reinterpret_cast<const uint4*>(hn);
